@@ -1,0 +1,537 @@
+// C ABI of the decoder: plan creation (weight packing), the per-step layer
+// schedule and batch decode. Declarations and contracts: include/fast_audiovae_cuda.h.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/fast_audiovae_cuda.h"
+#include "fav_internal.h"
+
+static_assert(FAV_SLOT_FLOATS == fav::kSlotFloats, "slot size");
+
+namespace {
+
+thread_local char g_error[512] = {0};
+
+int32_t fail(int32_t status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int32_t cuda_fail(cudaError_t e, const char* what) {
+  return fail(FAV_DEVICE_ERROR, "%s: %s", what, cudaGetErrorString(e));
+}
+
+std::once_flag g_prepare_once;
+cudaError_t g_prepare_error = cudaSuccess;
+
+cudaError_t prepare_once() {
+  std::call_once(g_prepare_once, [] { g_prepare_error = fav::prepare_kernels(); });
+  return g_prepare_error;
+}
+
+// --------------------------------------------------------------- packing
+// Weight operand B[n][k] of a layer packed as [n_tile][kblock][term][NT rows][128 B],
+// each 64-element row slice in the 128-byte swizzled K-major layout the MMA
+// reads (16-byte chunk j of row r stored at chunk j ^ (r % 8)). K is padded with
+// zeros to a multiple of 64.
+std::vector<uint16_t> pack_operand(int n_total, int k_total, int nt, int mode,
+                                   const std::function<float(int, int)>& value) {
+  const int kblocks = (k_total + fav::kKBlock - 1) / fav::kKBlock;
+  const int terms = mode == fav::kModeSplit ? 2 : 1;
+  const int ntiles = n_total / nt;
+  std::vector<uint16_t> img((size_t)ntiles * kblocks * terms * nt * 64, 0);
+  for (int n = 0; n < n_total; ++n) {
+    const int tile = n / nt, row = n % nt;
+    for (int k = 0; k < kblocks * fav::kKBlock; ++k) {
+      const float v = k < k_total ? value(n, k) : 0.f;
+      const int kb = k / fav::kKBlock, kk = k % fav::kKBlock;
+      const int chunk = (kk >> 3) ^ (row & 7);
+      const size_t within = (size_t)row * 64 + chunk * 8 + (kk & 7);
+      const size_t base = ((size_t)tile * kblocks + kb) * terms * nt * 64;
+      if (mode == fav::kModeSplit) {
+        const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+        const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+        std::memcpy(&img[base + within], &hi, 2);
+        std::memcpy(&img[base + (size_t)nt * 64 + within], &lo, 2);
+      } else {
+        const __half h = __float2half_rn(v);
+        std::memcpy(&img[base + within], &h, 2);
+      }
+    }
+  }
+  return img;
+}
+
+struct DeviceArrays {
+  std::vector<void*> owned;
+  size_t bytes = 0;
+  ~DeviceArrays() {
+    for (void* p : owned) cudaFree(p);
+  }
+  template <class T>
+  T* upload(const T* host, size_t count, cudaError_t* err) {
+    void* p = nullptr;
+    *err = cudaMalloc(&p, count * sizeof(T));
+    if (*err != cudaSuccess) return nullptr;
+    owned.push_back(p);
+    bytes += count * sizeof(T);
+    *err = cudaMemcpy(p, host, count * sizeof(T), cudaMemcpyHostToDevice);
+    return static_cast<T*>(p);
+  }
+};
+
+struct StageDev {
+  int c_in, c_out, rate, n_tile_t;
+  const float *scale, *offset, *alpha, *recip, *tbias;
+  const uint8_t* timg;
+  int state_t;
+  struct Res {
+    int dilation, n_tile;
+    const float *pre_a, *pre_r, *dw_w, *dw_b, *post_a, *post_r, *pw_b;
+    const uint8_t* img;
+    int state_off;
+  } res[3];
+};
+
+}  // namespace
+
+struct fav_plan {
+  int device = 0;
+  DeviceArrays mem;
+  const float *stem_w = nullptr, *stem_b = nullptr, *pw_b = nullptr;
+  const uint8_t* stem_img = nullptr;
+  StageDev stages[fav::kStages];
+  const float *fin_a = nullptr, *fin_r = nullptr, *fin_w = nullptr, *fin_b = nullptr;
+  int state_final = 0;
+};
+
+namespace {
+
+size_t expected_count(int index) {
+  if (index == 0) return 64 * 7;
+  if (index == 1) return 64;
+  if (index == 2) return 2048 * 64;
+  if (index == 3) return 2048;
+  if (index >= 184) {
+    const size_t tail[4] = {32, 32, 32 * 7, 1};
+    return tail[index - 184];
+  }
+  const int i = (index - 4) / 30, o = (index - 4) % 30;
+  const size_t cin = 2048 >> i, cout = cin / 2, s = fav::kRates[i];
+  if (o < 4) return cin;
+  if (o == 4) return cin * cout * 2 * s;
+  if (o == 5) return cout;
+  const int r = (o - 6) % 8;
+  const size_t sizes[8] = {cout, cout, cout * 7, cout, cout, cout, cout * cout, cout};
+  return sizes[r];
+}
+
+int32_t build_plan(fav_plan* plan, const float* const* w) {
+  cudaError_t e = cudaSuccess;
+  auto up = [&](int index) -> const float* {
+    return plan->mem.upload(w[index], expected_count(index), &e);
+  };
+  auto up_img = [&](const std::vector<uint16_t>& img) -> const uint8_t* {
+    return reinterpret_cast<const uint8_t*>(plan->mem.upload(img.data(), img.size(), &e));
+  };
+  // Stem: depthwise coefficients + 1x1 64->2048 (split bf16).
+  plan->stem_w = up(0);
+  plan->stem_b = up(1);
+  {
+    const float* pw = w[2];
+    plan->stem_img = up_img(pack_operand(2048, 64, 256, fav::kModeSplit,
+                                         [pw](int n, int k) { return pw[(size_t)n * 64 + k]; }));
+  }
+  plan->pw_b = up(3);
+  if (e != cudaSuccess) return cuda_fail(e, "plan upload");
+  int off = 6 * fav::kLatentChannels;
+  for (int i = 0; i < fav::kStages; ++i) {
+    StageDev& st = plan->stages[i];
+    const int base = 4 + 30 * i;
+    st.c_in = 2048 >> i;
+    st.c_out = st.c_in / 2;
+    st.rate = fav::kRates[i];
+    const int n_total = st.c_out * st.rate;
+    st.n_tile_t = n_total % 256 == 0 ? 256 : n_total;
+    st.scale = up(base + 0);
+    st.offset = up(base + 1);
+    st.alpha = up(base + 2);
+    st.recip = up(base + 3);
+    {
+      const float* tw = w[base + 4];
+      const int cin = st.c_in, cout = st.c_out, s = st.rate;
+      // n = phase * C_out + o; k < C_in: current tap W[k][o][p], else previous tap W[k-C_in][o][p+s].
+      st.timg = up_img(pack_operand(n_total, 2 * cin, st.n_tile_t, fav::kModeSplit, [=](int n, int k) {
+        const int p = n / cout, o = n % cout;
+        const int i_ch = k < cin ? k : k - cin;
+        const int tap = k < cin ? p : p + s;
+        return tw[((size_t)i_ch * cout + o) * 2 * s + tap];
+      }));
+    }
+    st.tbias = up(base + 5);
+    st.state_t = off;
+    off += st.c_in;
+    for (int j = 0; j < 3; ++j) {
+      const int rb = base + 6 + 8 * j;
+      auto& r = st.res[j];
+      r.dilation = fav::kDilations[j];
+      r.n_tile = st.c_out < 256 ? st.c_out : 256;
+      r.pre_a = up(rb + 0);
+      r.pre_r = up(rb + 1);
+      r.dw_w = up(rb + 2);
+      r.dw_b = up(rb + 3);
+      r.post_a = up(rb + 4);
+      r.post_r = up(rb + 5);
+      const float* pw = w[rb + 6];
+      const int c = st.c_out;
+      r.img = up_img(pack_operand(c, c, r.n_tile, fav::kModeF16,
+                                  [pw, c](int n, int k) { return pw[(size_t)n * c + k]; }));
+      r.pw_b = up(rb + 7);
+      r.state_off = off;
+      off += 6 * r.dilation * st.c_out;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "plan upload");
+  }
+  plan->fin_a = up(184);
+  plan->fin_r = up(185);
+  plan->fin_w = up(186);
+  plan->fin_b = up(187);
+  plan->state_final = off;
+  off += 6 * fav::kFinalChannels;
+  if (e != cudaSuccess) return cuda_fail(e, "plan upload");
+  if (off != fav::kSlotFloats) return fail(FAV_INVALID_ARGUMENT, "internal state layout mismatch (%d)", off);
+  return FAV_OK;
+}
+
+// Launches the 26 kernels of one decoder step. Activations ping-pong between
+// two workspace buffers of n_streams * frames * 61440 floats.
+// Layers are numbered 0 (stem), 1 + 4i (stage i transposed conv), 2 + 4i + j
+// (stage i residual j) and 25 (final conv); the schedule stops after
+// ``last_layer`` and reports the buffer holding that layer's output.
+int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, int frames, const float* z,
+                 int z_stride, int z_offset, float* audio, int audio_stride, int audio_offset, float* ws,
+                 uint32_t* status, cudaStream_t stream, int last_layer = 25, float** last_out = nullptr) {
+  const size_t buf = (size_t)n_streams * frames * 61440;
+  float* cur = ws;
+  float* other = ws + buf;
+  fav::LayerArgs a{};
+  a.state = state;
+  a.status = status;
+  // stem
+  a.kind = fav::kStem;
+  a.mode = fav::kModeSplit;
+  a.rows = n_streams * frames;
+  a.rows_per_stream = frames;
+  a.k_channels = 64;
+  a.num_kblocks = 1;
+  a.n_total = 2048;
+  a.n_tile = 256;
+  a.c_out = 2048;
+  a.x = z;
+  a.z_stride = z_stride;
+  a.z_offset = z_offset;
+  a.out = cur;
+  a.bias = p->pw_b;
+  a.dw_w = p->stem_w;
+  a.dw_b = p->stem_b;
+  a.wimg = p->stem_img;
+  a.state_off = 0;
+  cudaError_t e = fav::launch_gemm_layer(a, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "stem launch");
+  int layer = 0;
+  if (last_out) *last_out = cur;
+  if (layer == last_layer) return FAV_OK;
+  int n = frames;
+  for (int i = 0; i < fav::kStages; ++i) {
+    const StageDev& st = p->stages[i];
+    fav::LayerArgs t{};
+    t.state = state;
+    t.status = status;
+    t.kind = fav::kTconv;
+    t.mode = fav::kModeSplit;
+    t.rows = n_streams * n;
+    t.rows_per_stream = n;
+    t.k_channels = st.c_in;
+    t.num_kblocks = 2 * st.c_in / fav::kKBlock;
+    t.n_total = st.c_out * st.rate;
+    t.n_tile = st.n_tile_t;
+    t.c_out = st.c_out;
+    t.stride = st.rate;
+    t.x = cur;
+    t.out = other;
+    t.bias = st.tbias;
+    t.scale = st.scale;
+    t.offset = st.offset;
+    t.alpha1 = st.alpha;
+    t.recip1 = st.recip;
+    t.wimg = st.timg;
+    t.state_off = st.state_t;
+    if ((e = fav::launch_gemm_layer(t, stream)) != cudaSuccess) return cuda_fail(e, "transpose launch");
+    std::swap(cur, other);
+    n *= st.rate;
+    if (last_out) *last_out = cur;
+    if (++layer == last_layer) return FAV_OK;
+    for (int j = 0; j < 3; ++j) {
+      const auto& r = st.res[j];
+      fav::LayerArgs u{};
+      u.state = state;
+      u.status = status;
+      u.kind = fav::kResidual;
+      u.mode = fav::kModeF16;
+      u.rows = n_streams * n;
+      u.rows_per_stream = n;
+      u.k_channels = st.c_out;
+      u.num_kblocks = st.c_out < fav::kKBlock ? 1 : st.c_out / fav::kKBlock;
+      u.n_total = st.c_out;
+      u.n_tile = r.n_tile;
+      u.c_out = st.c_out;
+      u.dilation = r.dilation;
+      u.x = cur;
+      u.out = other;
+      u.bias = r.pw_b;
+      u.alpha1 = r.pre_a;
+      u.recip1 = r.pre_r;
+      u.alpha2 = r.post_a;
+      u.recip2 = r.post_r;
+      u.dw_w = r.dw_w;
+      u.dw_b = r.dw_b;
+      u.wimg = r.img;
+      u.state_off = r.state_off;
+      if ((e = fav::launch_gemm_layer(u, stream)) != cudaSuccess) return cuda_fail(e, "residual launch");
+      std::swap(cur, other);
+      if (last_out) *last_out = cur;
+      if (++layer == last_layer) return FAV_OK;
+    }
+  }
+  fav::FinalArgs f{};
+  f.rows = n_streams * n;
+  f.rows_per_stream = n;
+  f.x = cur;
+  f.audio = audio;
+  f.audio_stride = audio_stride;
+  f.audio_offset = audio_offset;
+  f.alpha = p->fin_a;
+  f.recip = p->fin_r;
+  f.w = p->fin_w;
+  f.b = p->fin_b;
+  f.state = state;
+  f.state_off = p->state_final;
+  f.status = status;
+  if ((e = fav::launch_final(f, stream)) != cudaSuccess) return cuda_fail(e, "final launch");
+  if (last_out) *last_out = audio;
+  return FAV_OK;
+}
+
+bool overflow_mul(size_t a, size_t b, size_t* out) {
+  if (a && b > SIZE_MAX / a) return true;
+  *out = a * b;
+  return false;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t fav_abi_version(void) { return FAV_ABI_VERSION; }
+
+const char* fav_last_error(void) { return g_error; }
+
+const char* fav_status_string(int32_t s) {
+  switch (s) {
+    case FAV_OK: return "ok";
+    case FAV_INVALID_ARGUMENT: return "invalid argument";
+    case FAV_UNSUPPORTED: return "unsupported";
+    case FAV_OVERLAP: return "overlapping buffers";
+    case FAV_SIZE_OVERFLOW: return "size overflow";
+    case FAV_DEVICE_ERROR: return "device error";
+    case FAV_TIMEOUT: return "device wait timed out";
+    default: return "unknown status";
+  }
+}
+
+int32_t fav_device_supported(void) {
+  int dev = 0, major = 0, minor = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) return 0;
+  return major == 10 && minor == 0;
+}
+
+int32_t fav_plan_create(const float* const* coefficients, int32_t count, int32_t precision, fav_plan** plan_out) {
+  g_error[0] = 0;
+  if (!plan_out) return fail(FAV_INVALID_ARGUMENT, "plan_out is NULL");
+  *plan_out = nullptr;
+  if (!coefficients || count != FAV_NUM_COEFFICIENTS)
+    return fail(FAV_INVALID_ARGUMENT, "expected %d coefficient arrays", FAV_NUM_COEFFICIENTS);
+  if (precision != FAV_PRECISION_BF16) return fail(FAV_UNSUPPORTED, "unsupported precision %d", precision);
+  for (int i = 0; i < count; ++i) {
+    if (!coefficients[i]) return fail(FAV_INVALID_ARGUMENT, "coefficient %d is NULL", i);
+    const size_t nvals = expected_count(i);
+    for (size_t j = 0; j < nvals; ++j)
+      if (!std::isfinite(coefficients[i][j])) return fail(FAV_INVALID_ARGUMENT, "coefficient %d is not finite", i);
+  }
+  if (!fav_device_supported()) return fail(FAV_UNSUPPORTED, "current CUDA device is not an sm_100 (B200) GPU");
+  cudaError_t e = prepare_once();
+  if (e != cudaSuccess) return cuda_fail(e, "kernel attributes");
+  fav_plan* plan = new (std::nothrow) fav_plan();
+  if (!plan) return fail(FAV_DEVICE_ERROR, "out of host memory");
+  cudaGetDevice(&plan->device);
+  const int32_t st = build_plan(plan, coefficients);
+  if (st != FAV_OK) {
+    delete plan;
+    return st;
+  }
+  *plan_out = plan;
+  return FAV_OK;
+}
+
+void fav_plan_destroy(fav_plan* plan) { delete plan; }
+
+size_t fav_plan_bytes(const fav_plan* plan) { return plan ? plan->mem.bytes : 0; }
+
+size_t fav_state_pool_bytes(int32_t num_slots) {
+  if (num_slots <= 0) return 0;
+  return (size_t)2 * num_slots * FAV_SLOT_FLOATS * sizeof(float);
+}
+
+size_t fav_step_workspace_bytes(int32_t n_streams, int32_t frames) {
+  if (n_streams <= 0 || frames <= 0) return 0;
+  size_t rows, bytes;
+  if (overflow_mul((size_t)n_streams, (size_t)frames, &rows)) return 0;
+  if (overflow_mul(rows, (size_t)2 * 61440 * sizeof(float), &bytes)) return 0;
+  return bytes;
+}
+
+int32_t fav_step(const fav_plan* plan, float* state_pool, int32_t num_slots, const int32_t* slot_codes,
+                 int32_t n_streams, int32_t frames, const float* latents, float* audio, void* workspace,
+                 size_t workspace_bytes, uint32_t* status, void* cuda_stream) {
+  g_error[0] = 0;
+  if (!plan) return fail(FAV_INVALID_ARGUMENT, "plan is NULL");
+  if (n_streams < 0 || frames < 0) return fail(FAV_INVALID_ARGUMENT, "negative stream or frame count");
+  if (n_streams == 0 || frames == 0) return FAV_OK;
+  if ((int64_t)n_streams * frames * fav::kHop > INT32_MAX)
+    return fail(FAV_SIZE_OVERFLOW, "step too large: %d streams x %d frames", n_streams, frames);
+  if (!latents || !audio || !workspace) return fail(FAV_INVALID_ARGUMENT, "NULL latents, audio or workspace");
+  if (!state_pool || !slot_codes || num_slots < n_streams)
+    return fail(FAV_INVALID_ARGUMENT, "state pool, slot codes and num_slots >= n_streams are required");
+  const size_t need = fav_step_workspace_bytes(n_streams, frames);
+  if (!need) return fail(FAV_SIZE_OVERFLOW, "workspace size overflow");
+  if (workspace_bytes < need)
+    return fail(FAV_INVALID_ARGUMENT, "workspace too small: %zu < %zu bytes", workspace_bytes, need);
+  fav::StateRef st{state_pool, state_pool, slot_codes, num_slots, 0};
+  return run_step(plan, st, n_streams, frames, latents, frames, 0, audio, frames * fav::kHop, 0,
+                  static_cast<float*>(workspace), status, static_cast<cudaStream_t>(cuda_stream));
+}
+
+size_t fav_batch_workspace_bytes(int32_t n_clips, int32_t chunk_frames) {
+  const size_t act = fav_step_workspace_bytes(n_clips, chunk_frames);
+  if (!act) return 0;
+  return act + fav_state_pool_bytes(n_clips);
+}
+
+int32_t fav_decode_batch(const fav_plan* plan, const float* latents, int32_t n_clips, int32_t frames,
+                         int32_t chunk_frames, float* audio, void* workspace, size_t workspace_bytes,
+                         uint32_t* status, void* cuda_stream) {
+  g_error[0] = 0;
+  if (!plan) return fail(FAV_INVALID_ARGUMENT, "plan is NULL");
+  if (n_clips < 0 || frames < 0 || chunk_frames <= 0) return fail(FAV_INVALID_ARGUMENT, "bad clip/frame counts");
+  if (n_clips == 0 || frames == 0) return FAV_OK;
+  if (!latents || !audio || !workspace) return fail(FAV_INVALID_ARGUMENT, "NULL latents, audio or workspace");
+  if ((int64_t)frames * fav::kHop > INT32_MAX || (int64_t)n_clips * chunk_frames * fav::kHop > INT32_MAX)
+    return fail(FAV_SIZE_OVERFLOW, "clip too large");
+  if (chunk_frames > frames) chunk_frames = frames;
+  const size_t need = fav_batch_workspace_bytes(n_clips, chunk_frames);
+  if (!need || workspace_bytes < need)
+    return fail(FAV_INVALID_ARGUMENT, "workspace too small: %zu < %zu bytes", workspace_bytes, need);
+  float* ws = static_cast<float*>(workspace);
+  float* pool = ws + fav_step_workspace_bytes(n_clips, chunk_frames) / sizeof(float);
+  cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
+  for (int t0 = 0, c = 0; t0 < frames; t0 += chunk_frames, ++c) {
+    const int tc = frames - t0 < chunk_frames ? frames - t0 : chunk_frames;
+    // Chunk c reads history half (c & 1) (zero for the first chunk) and writes the other.
+    fav::StateRef st{c == 0 ? nullptr : pool, pool, nullptr, n_clips, (c & 1)};
+    const int32_t s = run_step(plan, st, n_clips, tc, latents, frames, t0, audio, frames * fav::kHop,
+                               t0 * fav::kHop, ws, status, stream);
+    if (s != FAV_OK) return s;
+  }
+  return FAV_OK;
+}
+
+int32_t fav_debug_step_layers(const fav_plan* plan, float* state_pool, int32_t num_slots, const int32_t* slot_codes,
+                              int32_t n_streams, int32_t frames, const float* latents, void* workspace,
+                              size_t workspace_bytes, uint32_t* status, int32_t last_layer, float** layer_out,
+                              void* cuda_stream) {
+  g_error[0] = 0;
+  if (!plan || !layer_out || last_layer < 0 || last_layer > 24 || n_streams <= 0 || frames <= 0 || !latents ||
+      !workspace)
+    return fail(FAV_INVALID_ARGUMENT, "bad debug step arguments");
+  if (workspace_bytes < fav_step_workspace_bytes(n_streams, frames))
+    return fail(FAV_INVALID_ARGUMENT, "workspace too small");
+  if (state_pool && (!slot_codes || num_slots < n_streams))
+    return fail(FAV_INVALID_ARGUMENT, "slot codes and num_slots >= n_streams are required with a state pool");
+  fav::StateRef st{state_pool, state_pool, state_pool ? slot_codes : nullptr, num_slots, 0};
+  return run_step(plan, st, n_streams, frames, latents, frames, 0, nullptr, 0, 0, static_cast<float*>(workspace),
+                  status, static_cast<cudaStream_t>(cuda_stream), last_layer, layer_out);
+}
+
+int32_t fav_test_gemm(const float* a, int32_t m, int32_t k, const float* b, int32_t n, int32_t mode, float* c,
+                      void* cuda_stream) {
+  g_error[0] = 0;
+  if (!a || !b || !c || m <= 0 || k <= 0 || n <= 0) return fail(FAV_INVALID_ARGUMENT, "bad test GEMM arguments");
+  if (k % 2) return fail(FAV_INVALID_ARGUMENT, "K must be even");
+  int nt = n % 256 == 0 ? 256 : n % 128 == 0 ? 128 : n % 64 == 0 ? 64 : n % 32 == 0 ? 32 : 0;
+  if (!nt) return fail(FAV_INVALID_ARGUMENT, "N must be a multiple of 32");
+  cudaError_t e = prepare_once();
+  if (e != cudaSuccess) return cuda_fail(e, "kernel attributes");
+  const int md = mode ? fav::kModeSplit : fav::kModeF16;
+  auto img = pack_operand(n, k, nt, md, [b, k](int row, int col) { return b[(size_t)row * k + col]; });
+  void* dimg = nullptr;
+  uint32_t* dstatus = nullptr;
+  if ((e = cudaMalloc(&dimg, img.size() * 2)) != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+  if ((e = cudaMalloc(&dstatus, 4)) != cudaSuccess) {
+    cudaFree(dimg);
+    return cuda_fail(e, "cudaMalloc");
+  }
+  cudaMemcpy(dimg, img.data(), img.size() * 2, cudaMemcpyHostToDevice);
+  cudaMemset(dstatus, 0, 4);
+  fav::LayerArgs la{};
+  la.kind = fav::kTestGemm;
+  la.mode = md;
+  la.rows = m;
+  la.rows_per_stream = m;
+  la.k_channels = k;
+  la.num_kblocks = (k + fav::kKBlock - 1) / fav::kKBlock;
+  la.n_total = n;
+  la.n_tile = nt;
+  la.c_out = n;
+  la.x = a;
+  la.out = c;
+  la.wimg = static_cast<const uint8_t*>(dimg);
+  la.status = dstatus;
+  cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
+  e = fav::launch_gemm_layer(la, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  uint32_t hs = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&hs, dstatus, 4, cudaMemcpyDeviceToHost);
+  cudaFree(dimg);
+  cudaFree(dstatus);
+  if (e != cudaSuccess) return cuda_fail(e, "test GEMM");
+  if (hs) return fail(FAV_TIMEOUT, "test GEMM kernel status 0x%x", hs);
+  return FAV_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,205 @@
+// Device-side primitives for the sm_100a decoder kernels: mbarriers with
+// bounded waits, bulk global->shared copies, tcgen05 MMA/TMEM access and the
+// shared-memory operand layout (K-major, 128-byte swizzle) the MMAs read.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace fav {
+
+// Error codes a kernel records in the status word (first error wins).
+enum DeviceError : uint32_t {
+  kDevOk = 0,
+  kDevTimeoutProducer = 0x101,
+  kDevTimeoutLoader = 0x102,
+  kDevTimeoutMma = 0x103,
+  kDevTimeoutEpilogue = 0x104,
+  kDevBadLaunch = 0x105,
+};
+
+// A wait that has not completed after this many polls is a bug; the kernel
+// records the error and returns instead of spinning forever.
+constexpr uint32_t kWaitLimit = 1u << 24;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void record_error(uint32_t* status, uint32_t code) {
+  if (status) atomicCAS(status, 0u, code);
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase with ``parity`` to complete. Returns false (and
+// records ``code``) after kWaitLimit polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t code) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+  record_error(status, code);
+  return false;
+}
+
+// ----------------------------------------------------------- bulk copies
+// 1-D bulk copy global -> own shared memory, completion counted on ``bar``.
+// Source and destination 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Make generic-proxy shared-memory writes visible to the async proxy (MMA).
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+// Named barrier that returns the AND of ``pred`` over all participating threads.
+__device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t threads, bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %3, 0;\n\tbar.red.and.pred p, %1, %2, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(out)
+      : "r"(id), "r"(threads), "r"((uint32_t)pred)
+      : "memory");
+  return out != 0;
+}
+
+// --------------------------------------------------------------- tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (f16 or bf16 operands, fp32 accumulate).
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on ``bar`` when all previously issued MMAs of this thread finish.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+// 32 lanes x 16 consecutive fp32 columns of the accumulator.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ------------------------------------------------------------ descriptors
+// Instruction descriptor, kind::f16: fp32 accumulator, K-major A and B.
+// fmt: 0 = f16, 1 = bf16. M = 128.
+__host__ __device__ constexpr uint32_t instr_desc_f16(uint32_t fmt, uint32_t n) {
+  return (1u << 4)              // D format f32
+         | (fmt << 7)           // A format
+         | (fmt << 10)          // B format
+         | ((n >> 3) << 17)     // N / 8
+         | ((128u >> 4) << 24); // M / 16
+}
+// Shared-memory matrix descriptor for a K-major operand tile stored as rows of
+// 128 bytes (64 sixteen-bit elements) with the 128-byte swizzle; 8-row groups
+// are 1024 bytes apart. ``addr`` is the tile (or K-step) start.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  return (uint64_t)((addr & 0x3FFFFu) >> 4)  // start address
+         | ((uint64_t)1 << 16)               // leading byte offset (unused with swizzle)
+         | ((uint64_t)(1024 >> 4) << 32)     // stride byte offset: 8 rows
+         | ((uint64_t)1 << 46)               // descriptor version (sm100)
+         | ((uint64_t)2 << 61);              // SWIZZLE_128B
+}
+// Byte offset of 16-bit element (row, k) inside such a tile (k < 64).
+__host__ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t k) {
+  const uint32_t chunk = (k >> 3) ^ (row & 7u);
+  return row * 128u + (chunk << 4) + ((k & 7u) << 1);
+}
+
+// --------------------------------------------------------------- numerics
+// Snake with the stored reciprocal: x + r * sin(a*x)^2.
+__device__ __forceinline__ float snake(float x, float a, float r) {
+  const float s = __sinf(a * x);
+  return fmaf(r, s * s, x);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo_elem, float hi_elem) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo_elem, hi_elem);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ uint32_t pack_f16(float lo_elem, float hi_elem) {
+  __half2 v = __floats2half2_rn(lo_elem, hi_elem);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+// Split two fp32 values into bf16 (hi, lo) pairs with v ~= hi + lo.
+__device__ __forceinline__ void split_bf16(float v0, float v1, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat16 h0 = __float2bfloat16_rn(v0), h1 = __float2bfloat16_rn(v1);
+  const float r0 = v0 - __bfloat162float(h0), r1 = v1 - __bfloat162float(h1);
+  __nv_bfloat162 h;
+  h.x = h0;
+  h.y = h1;
+  hi = *reinterpret_cast<uint32_t*>(&h);
+  lo = pack_bf16(r0, r1);
+}
+
+__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+}  // namespace fav

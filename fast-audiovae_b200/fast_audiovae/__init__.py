@@ -1,0 +1,90 @@
+"""AudioVAE2 decoder on NVIDIA B200 (sm_100a): the reference's facade for device="cuda".
+
+Mirrors ``src/fast_audiovae/__init__.py:11-14`` and ``automatic.py:274-284`` of
+bevenky/fast-audiovae: ``load(mode=..., threads=..., device=..., **options)``
+returns a decoder with ``.decode`` (batch), ``.stream()`` (streaming) and
+``.info``. Only ``device="cuda"`` is provided here; the reference's CPU/ONNX
+and Apple routes are outside this package.
+
+Coefficients: the reference loads a checksum-pinned ONNX export
+(``assets.py:6-11``). Without it, ``load`` takes ``weights=`` (a coefficient
+dict, names from ``fast_audiovae.weights.weight_shapes()``), ``source=`` (an
+``.npz`` file with those names) or, by default, the seeded random init of
+``fast_audiovae.weights.seeded_weights(weight_seed)``.
+"""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+
+from . import weights
+
+__all__ = ["load", "setup", "weights"]
+
+_MODES = {"batch": "batch", "streaming": "streaming", "stream": "streaming"}
+
+
+def _options(mode, threads, device):
+    if mode not in _MODES:
+        raise ValueError("mode must be batch or streaming")
+    if device != "cuda":
+        raise ValueError("device must be cuda: this package provides the B200 CUDA decoder only")
+    if type(threads) is not int or threads != 1:
+        raise ValueError("CUDA decoding requires threads=1; CPU worker counts do not control the GPU")
+    return _MODES[mode]
+
+
+def _coefficients(weights_arg, source, weight_seed):
+    if weights_arg is not None and source is not None:
+        raise ValueError("Pass weights or source, not both")
+    if weights_arg is not None:
+        coeffs = {k: np.array(v, dtype=np.float32, copy=True) for k, v in weights_arg.items()}
+        origin = "caller_coefficients"
+    elif source is not None:
+        with np.load(Path(source).expanduser(), allow_pickle=False) as archive:
+            coeffs = {k: np.array(archive[k], dtype=np.float32, copy=True) for k in archive.files}
+        origin = "npz:" + str(Path(source).expanduser().resolve())
+    else:
+        coeffs = weights.seeded_weights(weight_seed)
+        origin = f"seeded_random_init(seed={weight_seed})"
+    weights.validate_weights(coeffs)
+    return coeffs, origin
+
+
+def setup(*, mode="streaming", threads=1, device="cuda", cache_dir=None, source=None, offline=False,
+          prefer_custom=True, weights=None, weight_seed=0, **_ignored):
+    """Validate options and describe the selected route, without building a decoder.
+
+    Mirrors ``gpu.setup_gpu`` (``gpu.py:55-95``): no decoder is instantiated and
+    no inference runs. ``cache_dir``, ``offline`` and ``prefer_custom`` are CPU
+    recipe options of the reference and have no effect on the CUDA route.
+    """
+    selected = _options(mode, threads, device)
+    return {"device": "cuda", "backend": "cuda", "selected": "b200_tcgen05", "recipe": "b200_sm100a_v1",
+            "precision": "split-bf16 transposed/stem projections, f16 residual projections, fp32 accumulate",
+            "mode": selected, "threads": 1, "cpu_only": False, "fallback": False,
+            "reason": "Explicit CUDA request", "sample_rate": weights_module().SAMPLE_RATE,
+            "latent_rate": 25, "latent_channels": 64, "samples_per_latent": weights_module().HOP_SAMPLES,
+            "source": str(source) if source is not None else None, "weight_seed": weight_seed}
+
+
+def weights_module():
+    return weights
+
+
+def load(*, mode="streaming", threads=1, device="cuda", cache_dir=None, source=None, offline=False,
+         prefer_custom=True, weights=None, weight_seed=0, max_streams=256, device_index=0):
+    """Load the CUDA decoder; ``mode="stream"`` is accepted as an alias of ``"streaming"``."""
+    info = setup(mode=mode, threads=threads, device=device, cache_dir=cache_dir, source=source,
+                 offline=offline, prefer_custom=prefer_custom, weight_seed=weight_seed)
+    coeffs, origin = _coefficients(weights, source, weight_seed)
+    from .cuda import CUDADecoder
+    decoder = CUDADecoder(coeffs, {**info, "coefficient_source": origin}, info["mode"],
+                          max_streams=max_streams, device=device_index)
+    import torch
+    props = torch.cuda.get_device_properties(decoder.device)
+    decoder.info.update(device_name=props.name, sm_count=props.multi_processor_count)
+    if decoder.mode == "streaming":
+        decoder.prepare()
+    return decoder

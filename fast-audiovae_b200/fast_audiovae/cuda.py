@@ -1,0 +1,319 @@
+"""Explicit CUDA (B200, sm_100a) decoding: the drop-in for the reference GPU route.
+
+Mirrors ``src/fast_audiovae/gpu.py`` of bevenky/fast-audiovae:
+
+* ``CUDADecoder`` <- ``GPUDecoder`` (``gpu.py:125-199``): immutable device weights
+  shared by independent streams, one lock serialising device work, input
+  validation before any device work (``gpu.py:115-122``), owned CPU-ready fp32
+  output, finite check before commit (``gpu.py:177-179``), mode misuse raises
+  ``RuntimeError`` (``gpu.py:189-198``).
+* ``CUDAStream`` <- ``GPUStream`` (``gpu.py:202-249``): per-stream history that
+  advances only after a successful step (``gpu.py:216-225``), ``reset``,
+  ``flush`` (always ``[1,1,0]``), ``close`` and context management.
+
+Device work runs in ``libfav_cuda.so`` through its C ABI; torch only supplies
+device memory, pinned host buffers and the CUDA stream. There is no CPU path:
+an explicit CUDA request never falls back (``gpu.py:29-41``).
+
+Beyond the reference, ``CUDADecoder.decode_streams`` decodes one chunk for
+many streams in a single step (one kernel launch per layer for all of them),
+and ``decode_many`` batch-decodes several equal-length clips at once.
+"""
+from __future__ import annotations
+
+import ctypes as ct
+import threading
+
+import numpy as np
+
+from . import weights as W
+from ._native import Plan, check, load_library
+
+HOP = W.HOP_SAMPLES
+STATE_BYTES = W.STATE_BYTES_FP32
+_FRESH = 2
+
+
+def _latents(value):
+    """``gpu.py:115-122``: float32 numpy ``[1,64,L]``, finite; owned C-contiguous copy."""
+    if (not isinstance(value, np.ndarray) or value.dtype != np.float32
+            or value.ndim != 3 or value.shape[:2] != (1, 64)):
+        raise ValueError("Latents must be a float32 NumPy array with shape [1,64,L]")
+    if not np.isfinite(value).all():
+        raise ValueError("Latents must contain only finite values")
+    return np.array(value, copy=True, order="C") if value.shape[2] else value
+
+
+def _torch():
+    try:
+        import torch
+    except ImportError as error:  # pragma: no cover - torch is a hard dependency here
+        raise RuntimeError("CUDA decoding requires PyTorch for device buffers") from error
+    if not torch.cuda.is_available():
+        raise RuntimeError("CUDA is unavailable; an explicit CUDA request never falls back to CPU")
+    return torch
+
+
+class _Buffers:
+    """Reusable pinned/device staging buffers keyed by shape."""
+
+    def __init__(self, torch, device):
+        self.torch, self.device = torch, device
+        self.cache = {}
+
+    def get(self, key, shape, dtype, pinned=False):
+        t = self.cache.get(key)
+        numel = int(np.prod(shape))
+        if t is None or t.numel() < numel:
+            if pinned:
+                t = self.torch.empty(numel, dtype=dtype, pin_memory=True)
+            else:
+                t = self.torch.empty(numel, dtype=dtype, device=self.device)
+            self.cache[key] = t
+        return t[:numel].view(*shape)
+
+
+class CUDADecoder:
+    """Immutable CUDA weights shared by independent, serialised streams."""
+
+    def __init__(self, weights, info, mode, *, max_streams=256, device=0, batch_chunk_frames=128):
+        if mode not in ("batch", "streaming"):
+            raise ValueError("mode must be batch or streaming")
+        if type(max_streams) is not int or max_streams < 1:
+            raise ValueError("max_streams must be a positive int")
+        torch = _torch()
+        self._torch = torch
+        self.mode = mode
+        self.device = torch.device("cuda", device)
+        self._lock = threading.Lock()
+        with torch.cuda.device(self.device):
+            self._lib = load_library()
+            if not self._lib.fav_device_supported():
+                raise RuntimeError("CUDA decoding requires an sm_100 (B200) GPU; no fallback is permitted")
+            self._plan = Plan(weights)
+            self._max_streams = max_streams if mode == "streaming" else 1
+            pool_bytes = self._lib.fav_state_pool_bytes(self._max_streams)
+            self._pool = torch.zeros(pool_bytes // 4, dtype=torch.float32, device=self.device)
+            self._status = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self._status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self._free_slots = list(range(self._max_streams - 1, -1, -1))
+        self._buffers = _Buffers(torch, self.device)
+        self._chunk = batch_chunk_frames
+        self.state_bytes = STATE_BYTES
+        self.info = {**info, "mode": mode, "state_bytes_per_stream": STATE_BYTES,
+                     "state_device": "cuda", "output_device": "cpu", "output_ready": True,
+                     "max_streams": self._max_streams, "plan_device_bytes": self._plan.device_bytes}
+
+    # ------------------------------------------------------------ internals
+    def _ptr(self, tensor):
+        return ct.c_void_p(tensor.data_ptr())
+
+    def _stream_handle(self):
+        return ct.c_void_p(self._torch.cuda.current_stream(self.device).cuda_stream)
+
+    def _upload(self, arrays, frames):
+        torch = self._torch
+        n = len(arrays)
+        host = self._buffers.get("z_host", (n, 64, frames), torch.float32, pinned=True)
+        hn = host.numpy()
+        for i, a in enumerate(arrays):
+            hn[i] = a[0]
+        dev = self._buffers.get("z_dev", (n, 64, frames), torch.float32)
+        dev.copy_(host, non_blocking=True)
+        return dev
+
+    def _download(self, audio_dev):
+        torch = self._torch
+        host = self._buffers.get("a_host", tuple(audio_dev.shape), torch.float32, pinned=True)
+        host.copy_(audio_dev, non_blocking=True)
+        self._status_host.copy_(self._status, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        status = int(self._status_host.item())
+        if status:
+            raise RuntimeError("CUDA decoder kernel reported status 0x%x" % status)
+        result = host.numpy().copy()
+        if not np.isfinite(result).all():
+            raise RuntimeError("CUDA model returned nonfinite audio")
+        return result
+
+    def _step(self, streams, arrays, frames):
+        """One fav_step for ``streams``; commits their histories only on success."""
+        torch = self._torch
+        n = len(streams)
+        with torch.cuda.device(self.device):
+            self._status.zero_()
+            z = self._upload(arrays, frames)
+            audio = self._buffers.get("audio_dev", (n, HOP * frames), torch.float32)
+            codes_host = self._buffers.get("codes_host", (n,), torch.int32, pinned=True)
+            codes_host.numpy()[:] = [s._code() for s in streams]
+            codes = self._buffers.get("codes_dev", (n,), torch.int32)
+            codes.copy_(codes_host, non_blocking=True)
+            ws_bytes = int(self._lib.fav_step_workspace_bytes(n, frames))
+            ws = self._buffers.get("workspace", (ws_bytes,), torch.uint8)
+            check(self._lib, self._lib.fav_step(
+                self._plan.handle, self._ptr(self._pool), self._max_streams, self._ptr(codes), n, frames,
+                self._ptr(z), self._ptr(audio), self._ptr(ws), ws_bytes, self._ptr(self._status),
+                self._stream_handle()))
+            result = self._download(audio)
+        for s in streams:
+            s._commit(frames)
+        return [result[i].reshape(1, 1, HOP * frames) for i in range(n)]
+
+    def _acquire_slot(self):
+        with self._lock:
+            if not self._free_slots:
+                raise RuntimeError("All %d CUDA stream slots are in use; close a stream or raise max_streams"
+                                   % self._max_streams)
+            return self._free_slots.pop()
+
+    def _release_slot(self, slot):
+        with self._lock:
+            self._free_slots.append(slot)
+
+    # ------------------------------------------------------------ public API
+    def prepare(self):
+        """Warm the 1- and 2-frame step shapes without advancing any live stream."""
+        if self.mode == "streaming":
+            for frames in (1, 2):
+                with self.stream() as s:
+                    s.decode_chunk(np.zeros((1, 64, frames), np.float32))
+        return self
+
+    def decode(self, latents):
+        """Decode an independent sequence in batch mode, starting with zero history."""
+        if self.mode != "batch":
+            raise RuntimeError("Use decoder.stream() for stateful streaming")
+        latents = _latents(latents)
+        if not latents.shape[2]:
+            return np.empty((1, 1, 0), dtype=np.float32)
+        return self.decode_many([latents])[0]
+
+    def decode_many(self, clips):
+        """Batch-decode equal-length clips ``[1,64,L]`` together (one launch per layer per chunk)."""
+        if self.mode != "batch":
+            raise RuntimeError("Use decoder.stream() for stateful streaming")
+        clips = [_latents(c) for c in clips]
+        if not clips:
+            return []
+        frames = clips[0].shape[2]
+        if any(c.shape[2] != frames for c in clips):
+            raise ValueError("decode_many requires clips of equal length")
+        if not frames:
+            return [np.empty((1, 1, 0), dtype=np.float32) for _ in clips]
+        torch = self._torch
+        n = len(clips)
+        with self._lock, torch.cuda.device(self.device):
+            self._status.zero_()
+            z = self._upload(clips, frames)
+            audio = self._buffers.get("batch_audio", (n, HOP * frames), torch.float32)
+            chunk = min(self._chunk, frames)
+            ws_bytes = int(self._lib.fav_batch_workspace_bytes(n, chunk))
+            ws = self._buffers.get("batch_ws", (ws_bytes,), torch.uint8)
+            check(self._lib, self._lib.fav_decode_batch(
+                self._plan.handle, self._ptr(z), n, frames, chunk, self._ptr(audio), self._ptr(ws), ws_bytes,
+                self._ptr(self._status), self._stream_handle()))
+            result = self._download(audio)
+        return [result[i].reshape(1, 1, HOP * frames) for i in range(n)]
+
+    def stream(self):
+        if self.mode != "streaming":
+            raise RuntimeError("Load mode='streaming' to create an audio stream")
+        return CUDAStream(self)
+
+    def decode_streams(self, streams, chunks):
+        """Decode one chunk for each of ``streams`` in a single step.
+
+        All chunks must have the same frame count; each stream's history
+        advances only if the whole step succeeds.
+        """
+        if self.mode != "streaming":
+            raise RuntimeError("Load mode='streaming' to create an audio stream")
+        if len(streams) != len(chunks):
+            raise ValueError("One chunk per stream required")
+        chunks = [_latents(c) for c in chunks]
+        if not streams:
+            return []
+        if len({id(s) for s in streams}) != len(streams):
+            raise ValueError("A stream may appear only once per step")
+        frames = chunks[0].shape[2]
+        if any(c.shape[2] != frames for c in chunks):
+            raise ValueError("decode_streams requires chunks of equal length")
+        for s in streams:
+            if s._decoder is not self:
+                raise ValueError("Stream belongs to another decoder")
+        locks = sorted(streams, key=id)
+        for s in locks:
+            s._lock.acquire()
+        try:
+            for s in streams:
+                s._check_open()
+            if not frames:
+                return [np.empty((1, 1, 0), dtype=np.float32) for _ in streams]
+            with self._lock:
+                return self._step(streams, chunks, frames)
+        finally:
+            for s in reversed(locks):
+                s._lock.release()
+
+    def close(self):
+        if getattr(self, "_plan", None) is not None:
+            self._plan.close()
+
+
+class CUDAStream:
+    """Per-utterance device history; all returned NumPy audio is ready to use."""
+
+    def __init__(self, decoder):
+        self._decoder = decoder
+        self._lock = threading.Lock()
+        self._slot = decoder._acquire_slot()
+        self._parity = 0
+        self._fresh = True
+        self._closed = False
+        self.frames_decoded = 0
+
+    def _code(self):
+        return (self._slot << 2) | (_FRESH if self._fresh else 0) | self._parity
+
+    def _commit(self, frames):
+        self._parity ^= 1
+        self._fresh = False
+        self.frames_decoded += frames
+
+    def _check_open(self):
+        if self._closed:
+            raise RuntimeError("Decoder stream is closed; create a new stream")
+
+    def decode_chunk(self, latents):
+        latents = _latents(latents)
+        with self._lock:
+            self._check_open()
+            if not latents.shape[2]:
+                return np.empty((1, 1, 0), dtype=np.float32)
+            with self._decoder._lock:
+                return self._decoder._step([self], [latents], latents.shape[2])[0]
+
+    def reset(self):
+        with self._lock:
+            self._check_open()
+            self._fresh = True
+            self.frames_decoded = 0
+
+    def flush(self):
+        with self._lock:
+            self._check_open()
+            return np.empty((1, 1, 0), dtype=np.float32)
+
+    def close(self):
+        with self._lock:
+            if not self._closed:
+                self._closed = True
+                self._decoder._release_slot(self._slot)
+
+    def __enter__(self):
+        with self._lock:
+            self._check_open()
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
