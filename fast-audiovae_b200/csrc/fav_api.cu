@@ -224,7 +224,13 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
 // ``last_layer`` and reports the buffer holding that layer's output.
 int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, int frames, const float* z,
                  int z_stride, int z_offset, float* audio, int audio_stride, int audio_offset, float* ws,
-                 uint32_t* status, cudaStream_t stream, int last_layer = 25, float** last_out = nullptr) {
+                 uint32_t* status, cudaStream_t stream, int last_layer = 25, float** last_out = nullptr,
+                 cudaEvent_t* events = nullptr) {
+  // events (optional, 27): recorded before the stem and after each layer.
+  auto mark = [&](int i) {
+    if (events) cudaEventRecord(events[i], stream);
+  };
+  mark(0);
   const size_t buf = (size_t)n_streams * frames * 61440;
   float* cur = ws;
   float* other = ws + buf;
@@ -253,6 +259,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
   cudaError_t e = fav::launch_gemm_layer(a, stream);
   if (e != cudaSuccess) return cuda_fail(e, "stem launch");
   int layer = 0;
+  mark(1);
   if (last_out) *last_out = cur;
   if (layer == last_layer) return FAV_OK;
   int n = frames;
@@ -284,7 +291,8 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     std::swap(cur, other);
     n *= st.rate;
     if (last_out) *last_out = cur;
-    if (++layer == last_layer) return FAV_OK;
+    mark(++layer + 1);
+    if (layer == last_layer) return FAV_OK;
     for (int j = 0; j < 3; ++j) {
       const auto& r = st.res[j];
       fav::LayerArgs u{};
@@ -314,7 +322,8 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       if ((e = fav::launch_gemm_layer(u, stream)) != cudaSuccess) return cuda_fail(e, "residual launch");
       std::swap(cur, other);
       if (last_out) *last_out = cur;
-      if (++layer == last_layer) return FAV_OK;
+      mark(++layer + 1);
+      if (layer == last_layer) return FAV_OK;
     }
   }
   fav::FinalArgs f{};
@@ -332,6 +341,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
   f.state_off = p->state_final;
   f.status = status;
   if ((e = fav::launch_final(f, stream)) != cudaSuccess) return cuda_fail(e, "final launch");
+  mark(26);
   if (last_out) *last_out = audio;
   return FAV_OK;
 }
@@ -469,6 +479,37 @@ int32_t fav_decode_batch(const fav_plan* plan, const float* latents, int32_t n_c
     if (s != FAV_OK) return s;
   }
   return FAV_OK;
+}
+
+int32_t fav_step_profile(const fav_plan* plan, float* state_pool, int32_t num_slots, const int32_t* slot_codes,
+                         int32_t n_streams, int32_t frames, const float* latents, float* audio, void* workspace,
+                         size_t workspace_bytes, uint32_t* status, float* layer_ms, void* cuda_stream) {
+  g_error[0] = 0;
+  if (!layer_ms) return fail(FAV_INVALID_ARGUMENT, "layer_ms is NULL");
+  if (!plan || n_streams <= 0 || frames <= 0 || !latents || !audio || !workspace || !state_pool || !slot_codes ||
+      num_slots < n_streams)
+    return fail(FAV_INVALID_ARGUMENT, "bad profile step arguments");
+  if (workspace_bytes < fav_step_workspace_bytes(n_streams, frames))
+    return fail(FAV_INVALID_ARGUMENT, "workspace too small");
+  cudaEvent_t ev[27];
+  for (int i = 0; i < 27; ++i) {
+    cudaError_t e = cudaEventCreate(&ev[i]);
+    if (e != cudaSuccess) {
+      for (int j = 0; j < i; ++j) cudaEventDestroy(ev[j]);
+      return cuda_fail(e, "cudaEventCreate");
+    }
+  }
+  fav::StateRef st{state_pool, state_pool, slot_codes, num_slots, 0};
+  cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
+  int32_t r = run_step(plan, st, n_streams, frames, latents, frames, 0, audio, frames * fav::kHop, 0,
+                       static_cast<float*>(workspace), status, stream, 25, nullptr, ev);
+  if (r == FAV_OK) {
+    cudaError_t e = cudaEventSynchronize(ev[26]);
+    for (int i = 0; i < 26 && e == cudaSuccess; ++i) e = cudaEventElapsedTime(&layer_ms[i], ev[i], ev[i + 1]);
+    if (e != cudaSuccess) r = cuda_fail(e, "profile events");
+  }
+  for (int i = 0; i < 27; ++i) cudaEventDestroy(ev[i]);
+  return r;
 }
 
 int32_t fav_debug_step_layers(const fav_plan* plan, float* state_pool, int32_t num_slots, const int32_t* slot_codes,

@@ -19,6 +19,7 @@ from pathlib import Path
 import numpy as np
 
 from . import weights
+from . import weights as _coeffs
 
 __all__ = ["load", "setup", "weights"]
 
@@ -46,9 +47,9 @@ def _coefficients(weights_arg, source, weight_seed):
             coeffs = {k: np.array(archive[k], dtype=np.float32, copy=True) for k in archive.files}
         origin = "npz:" + str(Path(source).expanduser().resolve())
     else:
-        coeffs = weights.seeded_weights(weight_seed)
+        coeffs = _coeffs.seeded_weights(weight_seed)
         origin = f"seeded_random_init(seed={weight_seed})"
-    weights.validate_weights(coeffs)
+    _coeffs.validate_weights(coeffs)
     return coeffs, origin
 
 
@@ -64,13 +65,9 @@ def setup(*, mode="streaming", threads=1, device="cuda", cache_dir=None, source=
     return {"device": "cuda", "backend": "cuda", "selected": "b200_tcgen05", "recipe": "b200_sm100a_v1",
             "precision": "split-bf16 transposed/stem projections, f16 residual projections, fp32 accumulate",
             "mode": selected, "threads": 1, "cpu_only": False, "fallback": False,
-            "reason": "Explicit CUDA request", "sample_rate": weights_module().SAMPLE_RATE,
-            "latent_rate": 25, "latent_channels": 64, "samples_per_latent": weights_module().HOP_SAMPLES,
+            "reason": "Explicit CUDA request", "sample_rate": _coeffs.SAMPLE_RATE,
+            "latent_rate": 25, "latent_channels": 64, "samples_per_latent": _coeffs.HOP_SAMPLES,
             "source": str(source) if source is not None else None, "weight_seed": weight_seed}
-
-
-def weights_module():
-    return weights
 
 
 def load(*, mode="streaming", threads=1, device="cuda", cache_dir=None, source=None, offline=False,
@@ -83,7 +80,7 @@ def load(*, mode="streaming", threads=1, device="cuda", cache_dir=None, source=N
     decoder = CUDADecoder(coeffs, {**info, "coefficient_source": origin}, info["mode"],
                           max_streams=max_streams, device=device_index)
     import torch
-    props = torch.cuda.get_device_properties(decoder.device)
+    props = torch.cuda.get_device_properties(decoder._backend.device)
     decoder.info.update(device_name=props.name, sm_count=props.multi_processor_count)
     if decoder.mode == "streaming":
         decoder.prepare()

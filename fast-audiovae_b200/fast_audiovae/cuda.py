@@ -11,9 +11,12 @@ Mirrors ``src/fast_audiovae/gpu.py`` of bevenky/fast-audiovae:
   advances only after a successful step (``gpu.py:216-225``), ``reset``,
   ``flush`` (always ``[1,1,0]``), ``close`` and context management.
 
-Device work runs in ``libfav_cuda.so`` through its C ABI; torch only supplies
-device memory, pinned host buffers and the CUDA stream. There is no CPU path:
-an explicit CUDA request never falls back (``gpu.py:29-41``).
+Device work runs in ``libfav_cuda.so`` through its C ABI (``DeviceBackend``);
+torch only supplies device memory, pinned host buffers and the CUDA stream.
+There is no CPU path: an explicit CUDA request never falls back
+(``gpu.py:29-41``). As the reference injects its model and torch module into
+``GPUDecoder``, the backend is a constructor argument, which lets the facade
+contract be tested without a GPU.
 
 Beyond the reference, ``CUDADecoder.decode_streams`` decodes one chunk for
 many streams in a single step (one kernel launch per layer for all of them),
@@ -27,7 +30,6 @@ import threading
 import numpy as np
 
 from . import weights as W
-from ._native import Plan, check, load_library
 
 HOP = W.HOP_SAMPLES
 STATE_BYTES = W.STATE_BYTES_FP32
@@ -54,81 +56,70 @@ def _torch():
     return torch
 
 
-class _Buffers:
-    """Reusable pinned/device staging buffers keyed by shape."""
+class DeviceBackend:
+    """Device memory and C-ABI calls for one decoder (one plan, one history pool).
 
-    def __init__(self, torch, device):
-        self.torch, self.device = torch, device
+    ``step(codes, arrays, frames)`` and ``decode_many(arrays, frames)`` return
+    fp32 audio ``[n, 1920*frames]`` after a synchronising download, raising
+    ``RuntimeError`` on any launch, kernel-status or finiteness failure. A
+    failed step may have written the *unread* half of a history slot only.
+    """
+
+    def __init__(self, weights, *, max_streams, device=0, batch_chunk_frames=128):
+        torch = _torch()
+        from ._native import Plan, load_library
+        self.torch = torch
+        self.device = torch.device("cuda", device)
+        self.max_streams = max_streams
+        self.chunk = batch_chunk_frames
+        with torch.cuda.device(self.device):
+            self.lib = load_library()
+            if not self.lib.fav_device_supported():
+                raise RuntimeError("CUDA decoding requires an sm_100 (B200) GPU; no fallback is permitted")
+            self.plan = Plan(weights)
+            self.pool = torch.zeros(self.lib.fav_state_pool_bytes(max_streams) // 4, dtype=torch.float32,
+                                    device=self.device)
+            self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self.status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         self.cache = {}
 
-    def get(self, key, shape, dtype, pinned=False):
+    @property
+    def plan_bytes(self):
+        return self.plan.device_bytes
+
+    def _buffer(self, key, shape, dtype, pinned=False):
         t = self.cache.get(key)
         numel = int(np.prod(shape))
         if t is None or t.numel() < numel:
-            if pinned:
-                t = self.torch.empty(numel, dtype=dtype, pin_memory=True)
-            else:
-                t = self.torch.empty(numel, dtype=dtype, device=self.device)
+            torch = self.torch
+            t = (torch.empty(numel, dtype=dtype, pin_memory=True) if pinned
+                 else torch.empty(numel, dtype=dtype, device=self.device))
             self.cache[key] = t
         return t[:numel].view(*shape)
 
-
-class CUDADecoder:
-    """Immutable CUDA weights shared by independent, serialised streams."""
-
-    def __init__(self, weights, info, mode, *, max_streams=256, device=0, batch_chunk_frames=128):
-        if mode not in ("batch", "streaming"):
-            raise ValueError("mode must be batch or streaming")
-        if type(max_streams) is not int or max_streams < 1:
-            raise ValueError("max_streams must be a positive int")
-        torch = _torch()
-        self._torch = torch
-        self.mode = mode
-        self.device = torch.device("cuda", device)
-        self._lock = threading.Lock()
-        with torch.cuda.device(self.device):
-            self._lib = load_library()
-            if not self._lib.fav_device_supported():
-                raise RuntimeError("CUDA decoding requires an sm_100 (B200) GPU; no fallback is permitted")
-            self._plan = Plan(weights)
-            self._max_streams = max_streams if mode == "streaming" else 1
-            pool_bytes = self._lib.fav_state_pool_bytes(self._max_streams)
-            self._pool = torch.zeros(pool_bytes // 4, dtype=torch.float32, device=self.device)
-            self._status = torch.zeros(1, dtype=torch.int32, device=self.device)
-            self._status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
-        self._free_slots = list(range(self._max_streams - 1, -1, -1))
-        self._buffers = _Buffers(torch, self.device)
-        self._chunk = batch_chunk_frames
-        self.state_bytes = STATE_BYTES
-        self.info = {**info, "mode": mode, "state_bytes_per_stream": STATE_BYTES,
-                     "state_device": "cuda", "output_device": "cpu", "output_ready": True,
-                     "max_streams": self._max_streams, "plan_device_bytes": self._plan.device_bytes}
-
-    # ------------------------------------------------------------ internals
-    def _ptr(self, tensor):
+    @staticmethod
+    def _ptr(tensor):
         return ct.c_void_p(tensor.data_ptr())
 
-    def _stream_handle(self):
-        return ct.c_void_p(self._torch.cuda.current_stream(self.device).cuda_stream)
+    def _stream(self):
+        return ct.c_void_p(self.torch.cuda.current_stream(self.device).cuda_stream)
 
     def _upload(self, arrays, frames):
-        torch = self._torch
         n = len(arrays)
-        host = self._buffers.get("z_host", (n, 64, frames), torch.float32, pinned=True)
+        host = self._buffer("z_host", (n, 64, frames), self.torch.float32, pinned=True)
         hn = host.numpy()
         for i, a in enumerate(arrays):
             hn[i] = a[0]
-        dev = self._buffers.get("z_dev", (n, 64, frames), torch.float32)
+        dev = self._buffer("z_dev", (n, 64, frames), self.torch.float32)
         dev.copy_(host, non_blocking=True)
         return dev
 
     def _download(self, audio_dev):
-        torch = self._torch
-        host = self._buffers.get("a_host", tuple(audio_dev.shape), torch.float32, pinned=True)
+        host = self._buffer("a_host", tuple(audio_dev.shape), self.torch.float32, pinned=True)
         host.copy_(audio_dev, non_blocking=True)
-        self._status_host.copy_(self._status, non_blocking=True)
-        torch.cuda.current_stream(self.device).synchronize()
-        status = int(self._status_host.item())
+        self.status_host.copy_(self.status, non_blocking=True)
+        self.torch.cuda.current_stream(self.device).synchronize()
+        status = int(self.status_host.item())
         if status:
             raise RuntimeError("CUDA decoder kernel reported status 0x%x" % status)
         result = host.numpy().copy()
@@ -136,28 +127,75 @@ class CUDADecoder:
             raise RuntimeError("CUDA model returned nonfinite audio")
         return result
 
-    def _step(self, streams, arrays, frames):
-        """One fav_step for ``streams``; commits their histories only on success."""
-        torch = self._torch
-        n = len(streams)
+    def step(self, codes, arrays, frames):
+        from ._native import check
+        torch, lib = self.torch, self.lib
+        n = len(arrays)
         with torch.cuda.device(self.device):
-            self._status.zero_()
+            self.status.zero_()
             z = self._upload(arrays, frames)
-            audio = self._buffers.get("audio_dev", (n, HOP * frames), torch.float32)
-            codes_host = self._buffers.get("codes_host", (n,), torch.int32, pinned=True)
-            codes_host.numpy()[:] = [s._code() for s in streams]
-            codes = self._buffers.get("codes_dev", (n,), torch.int32)
-            codes.copy_(codes_host, non_blocking=True)
-            ws_bytes = int(self._lib.fav_step_workspace_bytes(n, frames))
-            ws = self._buffers.get("workspace", (ws_bytes,), torch.uint8)
-            check(self._lib, self._lib.fav_step(
-                self._plan.handle, self._ptr(self._pool), self._max_streams, self._ptr(codes), n, frames,
-                self._ptr(z), self._ptr(audio), self._ptr(ws), ws_bytes, self._ptr(self._status),
-                self._stream_handle()))
-            result = self._download(audio)
+            audio = self._buffer("audio_dev", (n, HOP * frames), torch.float32)
+            codes_host = self._buffer("codes_host", (n,), torch.int32, pinned=True)
+            codes_host.numpy()[:] = codes
+            codes_dev = self._buffer("codes_dev", (n,), torch.int32)
+            codes_dev.copy_(codes_host, non_blocking=True)
+            ws_bytes = int(lib.fav_step_workspace_bytes(n, frames))
+            ws = self._buffer("workspace", (ws_bytes,), torch.uint8)
+            check(lib, lib.fav_step(self.plan.handle, self._ptr(self.pool), self.max_streams, self._ptr(codes_dev),
+                                    n, frames, self._ptr(z), self._ptr(audio), self._ptr(ws), ws_bytes,
+                                    self._ptr(self.status), self._stream()))
+            return self._download(audio)
+
+    def decode_many(self, arrays, frames):
+        from ._native import check
+        torch, lib = self.torch, self.lib
+        n = len(arrays)
+        with torch.cuda.device(self.device):
+            self.status.zero_()
+            z = self._upload(arrays, frames)
+            audio = self._buffer("batch_audio", (n, HOP * frames), torch.float32)
+            chunk = min(self.chunk, frames)
+            ws_bytes = int(lib.fav_batch_workspace_bytes(n, chunk))
+            ws = self._buffer("batch_ws", (ws_bytes,), torch.uint8)
+            check(lib, lib.fav_decode_batch(self.plan.handle, self._ptr(z), n, frames, chunk, self._ptr(audio),
+                                            self._ptr(ws), ws_bytes, self._ptr(self.status), self._stream()))
+            return self._download(audio)
+
+    def close(self):
+        if getattr(self, "plan", None) is not None:
+            self.plan.close()
+
+
+class CUDADecoder:
+    """Immutable CUDA weights shared by independent, serialised streams."""
+
+    def __init__(self, weights, info, mode, *, max_streams=256, device=0, batch_chunk_frames=128, backend=None):
+        if mode not in ("batch", "streaming"):
+            raise ValueError("mode must be batch or streaming")
+        if type(max_streams) is not int or max_streams < 1:
+            raise ValueError("max_streams must be a positive int")
+        self.mode = mode
+        self._max_streams = max_streams if mode == "streaming" else 1
+        self._backend = backend if backend is not None else DeviceBackend(
+            weights, max_streams=self._max_streams, device=device, batch_chunk_frames=batch_chunk_frames)
+        self._lock = threading.Lock()
+        self._free_slots = list(range(self._max_streams - 1, -1, -1))
+        self.state_bytes = STATE_BYTES
+        self.info = {**info, "mode": mode, "state_bytes_per_stream": STATE_BYTES,
+                     "state_device": "cuda", "output_device": "cpu", "output_ready": True,
+                     "max_streams": self._max_streams,
+                     "plan_device_bytes": getattr(self._backend, "plan_bytes", None)}
+
+    # ------------------------------------------------------------ internals
+    def _step(self, streams, arrays, frames):
+        """One device step for ``streams``; commits their histories only on success."""
+        audio = self._backend.step([s._code() for s in streams], arrays, frames)
+        if (not isinstance(audio, np.ndarray) or audio.dtype != np.float32
+                or audio.shape != (len(streams), HOP * frames)):
+            raise RuntimeError("CUDA model returned invalid audio")
         for s in streams:
             s._commit(frames)
-        return [result[i].reshape(1, 1, HOP * frames) for i in range(n)]
+        return [audio[i].reshape(1, 1, HOP * frames) for i in range(len(streams))]
 
     def _acquire_slot(self):
         with self._lock:
@@ -200,20 +238,12 @@ class CUDADecoder:
             raise ValueError("decode_many requires clips of equal length")
         if not frames:
             return [np.empty((1, 1, 0), dtype=np.float32) for _ in clips]
-        torch = self._torch
-        n = len(clips)
-        with self._lock, torch.cuda.device(self.device):
-            self._status.zero_()
-            z = self._upload(clips, frames)
-            audio = self._buffers.get("batch_audio", (n, HOP * frames), torch.float32)
-            chunk = min(self._chunk, frames)
-            ws_bytes = int(self._lib.fav_batch_workspace_bytes(n, chunk))
-            ws = self._buffers.get("batch_ws", (ws_bytes,), torch.uint8)
-            check(self._lib, self._lib.fav_decode_batch(
-                self._plan.handle, self._ptr(z), n, frames, chunk, self._ptr(audio), self._ptr(ws), ws_bytes,
-                self._ptr(self._status), self._stream_handle()))
-            result = self._download(audio)
-        return [result[i].reshape(1, 1, HOP * frames) for i in range(n)]
+        with self._lock:
+            audio = self._backend.decode_many(clips, frames)
+        if (not isinstance(audio, np.ndarray) or audio.dtype != np.float32
+                or audio.shape != (len(clips), HOP * frames)):
+            raise RuntimeError("CUDA model returned invalid audio")
+        return [audio[i].reshape(1, 1, HOP * frames) for i in range(len(clips))]
 
     def stream(self):
         if self.mode != "streaming":
@@ -238,11 +268,10 @@ class CUDADecoder:
         frames = chunks[0].shape[2]
         if any(c.shape[2] != frames for c in chunks):
             raise ValueError("decode_streams requires chunks of equal length")
-        for s in streams:
-            if s._decoder is not self:
-                raise ValueError("Stream belongs to another decoder")
-        locks = sorted(streams, key=id)
-        for s in locks:
+        if any(s._decoder is not self for s in streams):
+            raise ValueError("Stream belongs to another decoder")
+        ordered = sorted(streams, key=id)
+        for s in ordered:
             s._lock.acquire()
         try:
             for s in streams:
@@ -252,12 +281,13 @@ class CUDADecoder:
             with self._lock:
                 return self._step(streams, chunks, frames)
         finally:
-            for s in reversed(locks):
+            for s in reversed(ordered):
                 s._lock.release()
 
     def close(self):
-        if getattr(self, "_plan", None) is not None:
-            self._plan.close()
+        close = getattr(self._backend, "close", None)
+        if close:
+            close()
 
 
 class CUDAStream:
@@ -285,6 +315,7 @@ class CUDAStream:
             raise RuntimeError("Decoder stream is closed; create a new stream")
 
     def decode_chunk(self, latents):
+        """Decode fp32 ``[1,64,L]`` new frames; failures leave the history intact."""
         latents = _latents(latents)
         with self._lock:
             self._check_open()

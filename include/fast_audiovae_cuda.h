@@ -129,6 +129,16 @@ FAV_API int32_t fav_decode_batch(const fav_plan *plan, const float *latents, int
                                  int32_t chunk_frames, float *audio, void *workspace, size_t workspace_bytes,
                                  uint32_t *status, void *cuda_stream);
 
+/* fav_step with per-layer timing (no reference counterpart; the reference
+ * profiles ORT operators instead, benchmarks/profile_candidate.py:37-60):
+ * CUDA events recorded on cuda_stream around each of the 26 kernel launches;
+ * layer_ms[26] receives their durations (0 = stem, 1+4i = stage i transposed
+ * conv, 2+4i+j = stage i residual j, 25 = final conv). Synchronises. */
+FAV_API int32_t fav_step_profile(const fav_plan *plan, float *state_pool, int32_t num_slots,
+                                 const int32_t *slot_codes, int32_t n_streams, int32_t frames,
+                                 const float *latents, float *audio, void *workspace, size_t workspace_bytes,
+                                 uint32_t *status, float *layer_ms, void *cuda_stream);
+
 /* Diagnostic (no reference counterpart): run one step's layers 0..last_layer
  * (0 = stem, 1+4i = stage i transposed conv, 2+4i+j = stage i residual j,
  * last_layer <= 24) and return in *layer_out the device pointer, inside the
