@@ -352,6 +352,36 @@ bool overflow_mul(size_t a, size_t b, size_t* out) {
   return false;
 }
 
+// Step workspace for fav_step_static, for callers that cannot allocate device
+// memory (a real-time audio callback, a host that forbids cudaMalloc after
+// start-up). It lives in this file-scope device array, so every GPU that loads
+// the library holds FAV_STATIC_MAX_FRAMES * 2 * 61440 floats (7.5 MiB) until
+// the process exits. Host code must not use the array's name as a device
+// address; fav_step_static looks the address up once per device.
+__device__ __align__(256) float g_static_workspace[(size_t)FAV_STATIC_MAX_FRAMES * 2 * 61440];
+
+std::mutex g_static_mutex;
+constexpr int kMaxDevices = 64;
+void* g_static_address[kMaxDevices] = {};
+
+// Device address of g_static_workspace on the current device, looked up on the
+// first call per device (with that device current) and cached.
+int32_t static_workspace(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(FAV_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (!g_static_address[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_workspace);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static workspace)");
+    g_static_address[dev] = p;
+  }
+  *out = static_cast<float*>(g_static_address[dev]);
+  return FAV_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -445,6 +475,27 @@ int32_t fav_step(const fav_plan* plan, float* state_pool, int32_t num_slots, con
   fav::StateRef st{state_pool, state_pool, slot_codes, num_slots, 0};
   return run_step(plan, st, n_streams, frames, latents, frames, 0, audio, frames * fav::kHop, 0,
                   static_cast<float*>(workspace), status, static_cast<cudaStream_t>(cuda_stream));
+}
+
+int32_t fav_step_static(const fav_plan* plan, float* state_pool, int32_t num_slots, const int32_t* slot_codes,
+                        int32_t n_streams, int32_t frames, const float* latents, float* audio, uint32_t* status,
+                        void* cuda_stream) {
+  g_error[0] = 0;
+  if (!plan) return fail(FAV_INVALID_ARGUMENT, "plan is NULL");
+  if (n_streams < 0 || frames < 0) return fail(FAV_INVALID_ARGUMENT, "negative stream or frame count");
+  if (n_streams == 0 || frames == 0) return FAV_OK;
+  if ((int64_t)n_streams * frames > FAV_STATIC_MAX_FRAMES)
+    return fail(FAV_SIZE_OVERFLOW, "n_streams * frames = %lld exceeds the static workspace limit of %d frames",
+                (long long)n_streams * frames, FAV_STATIC_MAX_FRAMES);
+  if (!latents || !audio) return fail(FAV_INVALID_ARGUMENT, "NULL latents or audio");
+  if (!state_pool || !slot_codes || num_slots < n_streams)
+    return fail(FAV_INVALID_ARGUMENT, "state pool, slot codes and num_slots >= n_streams are required");
+  float* ws = nullptr;
+  const int32_t st = static_workspace(&ws);
+  if (st != FAV_OK) return st;
+  fav::StateRef ref{state_pool, state_pool, slot_codes, num_slots, 0};
+  return run_step(plan, ref, n_streams, frames, latents, frames, 0, audio, frames * fav::kHop, 0, ws, status,
+                  static_cast<cudaStream_t>(cuda_stream));
 }
 
 size_t fav_batch_workspace_bytes(int32_t n_clips, int32_t chunk_frames) {

@@ -33,6 +33,7 @@ SIGNATURES = {
     "fav_state_pool_bytes": ([ct.c_int32], ct.c_size_t),
     "fav_step_workspace_bytes": ([ct.c_int32, ct.c_int32], ct.c_size_t),
     "fav_step": ([_P, _P, ct.c_int32, _P, ct.c_int32, ct.c_int32, _P, _P, _P, ct.c_size_t, _P, _P], ct.c_int32),
+    "fav_step_static": ([_P, _P, ct.c_int32, _P, ct.c_int32, ct.c_int32, _P, _P, _P, _P], ct.c_int32),
     "fav_batch_workspace_bytes": ([ct.c_int32, ct.c_int32], ct.c_size_t),
     "fav_decode_batch": ([_P, _P, ct.c_int32, ct.c_int32, ct.c_int32, _P, _P, ct.c_size_t, _P, _P], ct.c_int32),
     "fav_step_profile": ([_P, _P, ct.c_int32, _P, ct.c_int32, ct.c_int32, _P, _P, _P, ct.c_size_t, _P,

@@ -118,6 +118,29 @@ FAV_API int32_t fav_step(const fav_plan *plan, float *state_pool, int32_t num_sl
                          int32_t n_streams, int32_t frames, const float *latents, float *audio, void *workspace,
                          size_t workspace_bytes, uint32_t *status, void *cuda_stream);
 
+/* Largest n_streams * frames one fav_step_static call accepts. */
+#define FAV_STATIC_MAX_FRAMES 16
+
+/* fav_step without a caller workspace and without any allocation. This entry
+ * point has no counterpart in the reference. It serves callers that cannot
+ * allocate device memory while they decode: a real-time audio callback (a
+ * plugin's render thread, a telephony media loop) must not call cudaMalloc,
+ * which can synchronise the device and block for an unbounded time, and some
+ * hosts own all device memory and forbid allocation after start-up. The caller
+ * still passes the plan, history pool, slot codes, latents and audio.
+ * The step's scratch is a library-owned, file-scope device array sized for
+ * n_streams * frames <= FAV_STATIC_MAX_FRAMES (7.5 MiB, held on every GPU
+ * that loads the library until the process exits); larger calls are rejected
+ * with FAV_SIZE_OVERFLOW. The first call on a device looks up that array's
+ * device address (cudaGetSymbolAddress) with the device current; make that
+ * first call before any stream capture. Every call shares the one array and
+ * it keeps the last call's contents (nothing in it needs to start at zero:
+ * a step writes every scratch element before reading it), so calls that
+ * overlap on the GPU (two streams, two threads) race: serialise them. */
+FAV_API int32_t fav_step_static(const fav_plan *plan, float *state_pool, int32_t num_slots,
+                                const int32_t *slot_codes, int32_t n_streams, int32_t frames,
+                                const float *latents, float *audio, uint32_t *status, void *cuda_stream);
+
 /* Workspace bytes fav_decode_batch needs for n_clips clips decoded in chunks
  * of chunk_frames frames (activations plus a temporary history pool). */
 FAV_API size_t fav_batch_workspace_bytes(int32_t n_clips, int32_t chunk_frames);
