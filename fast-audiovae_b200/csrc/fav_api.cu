@@ -18,6 +18,7 @@
 #include "fav_internal.h"
 
 static_assert(FAV_SLOT_FLOATS == fav::kSlotFloats, "slot size");
+static_assert(FAV_SLOT_STRIDE_FLOATS == fav::kSlotStride, "slot stride");
 
 namespace {
 
@@ -33,6 +34,35 @@ int32_t fail(int32_t status, const char* fmt, ...) {
 
 int32_t cuda_fail(cudaError_t e, const char* what) {
   return fail(FAV_DEVICE_ERROR, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+std::once_flag g_encode_once;
+EncodeTiledFn g_encode = nullptr;
+
+// TMA map of a layer input x [rows][channels] fp32: boxes of min(channels, 64)
+// channels x box_rows rows, zero fill outside the tensor.
+int32_t encode_input_map(CUtensorMap* map, const float* x, int rows, int channels, int box_rows) {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  });
+  if (!g_encode) return fail(FAV_DEVICE_ERROR, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)channels, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)channels * sizeof(float)};
+  const cuuint32_t box[2] = {(cuuint32_t)(channels < fav::kKBlock ? channels : fav::kKBlock), (cuuint32_t)box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(x), dims, strides, box,
+                              elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FAV_DEVICE_ERROR, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return FAV_OK;
 }
 
 std::once_flag g_prepare_once;
@@ -166,7 +196,7 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
     st.c_out = st.c_in / 2;
     st.rate = fav::kRates[i];
     const int n_total = st.c_out * st.rate;
-    st.n_tile_t = n_total % 256 == 0 ? 256 : n_total;
+    st.n_tile_t = n_total % 128 == 0 ? 128 : n_total;
     st.scale = up(base + 0);
     st.offset = up(base + 1);
     st.alpha = up(base + 2);
@@ -192,7 +222,14 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
       r.n_tile = st.c_out < 256 ? st.c_out : 256;
       r.pre_a = up(rb + 0);
       r.pre_r = up(rb + 1);
-      r.dw_w = up(rb + 2);
+      {
+        // Residual depthwise taps stored transposed, [7][C], for four-channel loads.
+        const int c = st.c_out;
+        std::vector<float> wt((size_t)7 * c);
+        for (int ch = 0; ch < c; ++ch)
+          for (int j = 0; j < 7; ++j) wt[(size_t)j * c + ch] = w[rb + 2][(size_t)ch * 7 + j];
+        r.dw_w = plan->mem.upload(wt.data(), wt.size(), &e);
+      }
       r.dw_b = up(rb + 3);
       r.post_a = up(rb + 4);
       r.post_r = up(rb + 5);
@@ -255,7 +292,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
   a.dw_w = p->stem_w;
   a.dw_b = p->stem_b;
   a.wimg = p->stem_img;
-  a.state_off = 0;
+  a.hist = fav::HistRef{0, 0, 6, fav::kLatentChannels};
   cudaError_t e = fav::launch_gemm_layer(a, stream);
   if (e != cudaSuccess) return cuda_fail(e, "stem launch");
   int layer = 0;
@@ -286,7 +323,11 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     t.alpha1 = st.alpha;
     t.recip1 = st.recip;
     t.wimg = st.timg;
-    t.state_off = st.state_t;
+    t.hist = fav::HistRef{1 + 4 * i, 2 * st.state_t, 1, st.c_in};
+    t.box_rows = fav::box_rows_for(fav::kTconv, 0);
+    t.raw_pitch = fav::kKBlock;
+    int32_t es = encode_input_map(&t.tmap, t.x, t.rows, st.c_in, t.box_rows);
+    if (es != FAV_OK) return es;
     if ((e = fav::launch_gemm_layer(t, stream)) != cudaSuccess) return cuda_fail(e, "transpose launch");
     std::swap(cur, other);
     n *= st.rate;
@@ -318,7 +359,11 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       u.dw_w = r.dw_w;
       u.dw_b = r.dw_b;
       u.wimg = r.img;
-      u.state_off = r.state_off;
+      u.hist = fav::HistRef{2 + 4 * i + j, 2 * r.state_off, 6 * r.dilation, st.c_out};
+      u.box_rows = fav::box_rows_for(fav::kResidual, r.dilation);
+      u.raw_pitch = st.c_out < fav::kKBlock ? st.c_out : fav::kKBlock;
+      es = encode_input_map(&u.tmap, u.x, u.rows, st.c_out, u.box_rows);
+      if (es != FAV_OK) return es;
       if ((e = fav::launch_gemm_layer(u, stream)) != cudaSuccess) return cuda_fail(e, "residual launch");
       std::swap(cur, other);
       if (last_out) *last_out = cur;
@@ -338,7 +383,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
   f.w = p->fin_w;
   f.b = p->fin_b;
   f.state = state;
-  f.state_off = p->state_final;
+  f.hist = fav::HistRef{25, 2 * p->state_final, 6, fav::kFinalChannels};
   f.status = status;
   if ((e = fav::launch_final(f, stream)) != cudaSuccess) return cuda_fail(e, "final launch");
   mark(26);
@@ -445,7 +490,7 @@ size_t fav_plan_bytes(const fav_plan* plan) { return plan ? plan->mem.bytes : 0;
 
 size_t fav_state_pool_bytes(int32_t num_slots) {
   if (num_slots <= 0) return 0;
-  return (size_t)2 * num_slots * FAV_SLOT_FLOATS * sizeof(float);
+  return (size_t)num_slots * fav::kSlotStride * sizeof(float);
 }
 
 size_t fav_step_workspace_bytes(int32_t n_streams, int32_t frames) {
@@ -472,7 +517,7 @@ int32_t fav_step(const fav_plan* plan, float* state_pool, int32_t num_slots, con
   if (!need) return fail(FAV_SIZE_OVERFLOW, "workspace size overflow");
   if (workspace_bytes < need)
     return fail(FAV_INVALID_ARGUMENT, "workspace too small: %zu < %zu bytes", workspace_bytes, need);
-  fav::StateRef st{state_pool, state_pool, slot_codes, num_slots, 0};
+  fav::StateRef st{state_pool, slot_codes, num_slots, 0};
   return run_step(plan, st, n_streams, frames, latents, frames, 0, audio, frames * fav::kHop, 0,
                   static_cast<float*>(workspace), status, static_cast<cudaStream_t>(cuda_stream));
 }
@@ -493,7 +538,7 @@ int32_t fav_step_static(const fav_plan* plan, float* state_pool, int32_t num_slo
   float* ws = nullptr;
   const int32_t st = static_workspace(&ws);
   if (st != FAV_OK) return st;
-  fav::StateRef ref{state_pool, state_pool, slot_codes, num_slots, 0};
+  fav::StateRef ref{state_pool, slot_codes, num_slots, 0};
   return run_step(plan, ref, n_streams, frames, latents, frames, 0, audio, frames * fav::kHop, 0, ws, status,
                   static_cast<cudaStream_t>(cuda_stream));
 }
@@ -523,8 +568,8 @@ int32_t fav_decode_batch(const fav_plan* plan, const float* latents, int32_t n_c
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
   for (int t0 = 0, c = 0; t0 < frames; t0 += chunk_frames, ++c) {
     const int tc = frames - t0 < chunk_frames ? frames - t0 : chunk_frames;
-    // Chunk c reads history half (c & 1) (zero for the first chunk) and writes the other.
-    fav::StateRef st{c == 0 ? nullptr : pool, pool, nullptr, n_clips, (c & 1)};
+    // Chunk c reads head table (c & 1) (a fresh, zero history for the first chunk) and writes the other.
+    fav::StateRef st{pool, nullptr, n_clips, (c == 0 ? 2 : 0) | (c & 1)};
     const int32_t s = run_step(plan, st, n_clips, tc, latents, frames, t0, audio, frames * fav::kHop,
                                t0 * fav::kHop, ws, status, stream);
     if (s != FAV_OK) return s;
@@ -550,7 +595,7 @@ int32_t fav_step_profile(const fav_plan* plan, float* state_pool, int32_t num_sl
       return cuda_fail(e, "cudaEventCreate");
     }
   }
-  fav::StateRef st{state_pool, state_pool, slot_codes, num_slots, 0};
+  fav::StateRef st{state_pool, slot_codes, num_slots, 0};
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
   int32_t r = run_step(plan, st, n_streams, frames, latents, frames, 0, audio, frames * fav::kHop, 0,
                        static_cast<float*>(workspace), status, stream, 25, nullptr, ev);
@@ -575,7 +620,7 @@ int32_t fav_debug_step_layers(const fav_plan* plan, float* state_pool, int32_t n
     return fail(FAV_INVALID_ARGUMENT, "workspace too small");
   if (state_pool && (!slot_codes || num_slots < n_streams))
     return fail(FAV_INVALID_ARGUMENT, "slot codes and num_slots >= n_streams are required with a state pool");
-  fav::StateRef st{state_pool, state_pool, state_pool ? slot_codes : nullptr, num_slots, 0};
+  fav::StateRef st{state_pool, state_pool ? slot_codes : nullptr, num_slots, 0};
   return run_step(plan, st, n_streams, frames, latents, frames, 0, nullptr, 0, 0, static_cast<float*>(workspace),
                   status, static_cast<cudaStream_t>(cuda_stream), last_layer, layer_out);
 }

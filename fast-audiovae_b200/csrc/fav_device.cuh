@@ -2,6 +2,7 @@
 // bounded waits, bulk global->shared copies, tcgen05 MMA/TMEM access and the
 // shared-memory operand layout (K-major, 128-byte swizzle) the MMAs read.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -78,6 +79,17 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// 2-D TMA tile load (no multicast) of the box at coordinates (x = innermost,
+// y) into own shared memory, completion counted on ``bar``. Out-of-range
+// coordinates read as zero. ``map`` must live in param/const/global space.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Make generic-proxy shared-memory writes visible to the async proxy (MMA).
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -146,6 +158,20 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 lanes x 32 consecutive fp32 columns of the accumulator (load and wait in
+// one statement, so the values are complete when it returns).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // ------------------------------------------------------------ descriptors
 // Instruction descriptor, kind::f16: fp32 accumulator, K-major A and B.
 // fmt: 0 = f16, 1 = bf16. M = 128.
@@ -196,6 +222,10 @@ __device__ __forceinline__ void split_bf16(float v0, float v1, uint32_t& hi, uin
   h.y = h1;
   hi = *reinterpret_cast<uint32_t*>(&h);
   lo = pack_bf16(r0, r1);
+}
+
+__device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t v0, uint32_t v1) {
+  asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(v0), "r"(v1) : "memory");
 }
 
 __device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {

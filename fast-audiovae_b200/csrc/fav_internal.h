@@ -1,5 +1,6 @@
 // Shared declarations between the kernel translation unit and the C ABI.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stddef.h>
@@ -15,8 +16,19 @@ constexpr int kStages = 6;
 constexpr int kRates[kStages] = {8, 6, 5, 2, 2, 2};
 constexpr int kDilations[3] = {1, 3, 9};
 constexpr int kHop = 1920;
-// floats of causal history per stream (the reference's 647,424 bytes)
-constexpr int kSlotFloats = 161856;
+constexpr int kNumHistories = 26;
+
+// Causal history of one stream ("slot"), the reference's 26 histories
+// (647,424 bytes of window) kept as rings: history L (H_L rows x C_L channels)
+// owns 2*H_L rows at ring offset 2*off_L floats; its window is the H_L rows
+// starting at ring row head_L (mod 2*H_L). A step reads heads from one head
+// table (the slot code's read parity), writes its new rows only into ring rows
+// outside the current window and writes the advanced heads to the other table,
+// so an unsuccessful step leaves the committed window untouched.
+constexpr int kSlotFloats = 161856;                       // window floats (reference state size)
+constexpr int kRingFloats = 2 * kSlotFloats;              // ring rows of all histories
+constexpr int kHeadInts = 32;                             // per head table (26 used)
+constexpr int kSlotStride = kRingFloats + 2 * kHeadInts;  // floats per slot
 
 enum LayerKind : int { kStem = 0, kTconv = 1, kResidual = 2, kTestGemm = 3 };
 
@@ -27,17 +39,24 @@ enum GemmMode : int {
 };
 
 // Stream slot codes passed to a step: (slot << 2) | (fresh << 1) | read_parity.
-// The history of ``slot`` is read from pool half ``read_parity`` (or taken as
-// zero when ``fresh``) and the advanced history is written to the other half.
+// ``fresh`` starts the stream from an all-zero history.
 struct StateRef {
-  const float* pool_in;   // state pool (both halves); nullptr = all histories zero
-  float* pool_out;        // state pool written; nullptr = histories not advanced
+  float* pool;            // history pool, kSlotStride floats per slot; nullptr = zero history, not advanced
   const int* slot_codes;  // device array, one code per stream of the call; nullptr = uniform
-  int num_slots;          // slots per pool half
+  int num_slots;
   int uniform_code;       // with slot_codes == nullptr: stream s uses (s << 2) | uniform_code
 };
 
+// One history of the current layer.
+struct HistRef {
+  int index;   // 0..25 (reference order)
+  int ring;    // float offset of the ring inside a slot
+  int rows;    // H (window rows)
+  int width;   // C (channels per row)
+};
+
 struct LayerArgs {
+  CUtensorMap tmap;     // TMA map of the layer input x [rows][k] fp32 (transposed conv, residual)
   int kind;
   int mode;
   int rows;             // GEMM rows: all streams' time steps at this layer's input
@@ -49,6 +68,8 @@ struct LayerArgs {
   int c_out;            // output channels
   int stride;           // transposed-conv rate
   int dilation;         // residual depthwise dilation
+  int box_rows;         // rows of one TMA input box (tile + causal halo)
+  int raw_pitch;        // floats per staged input row (min(k, 64))
   const float* x;       // input activations [rows][k] fp32 (stem: latents [streams][64][z_stride])
   int z_stride;         // stem: frames per stream in the latent buffer
   int z_offset;         // stem: first frame of this step in the latent buffer
@@ -60,11 +81,11 @@ struct LayerArgs {
   const float* recip1;
   const float* alpha2;  // Snake after the depthwise conv (residual)
   const float* recip2;
-  const float* dw_w;    // depthwise taps [C][7]
+  const float* dw_w;    // depthwise taps: stem [64][7], residual [7][C]
   const float* dw_b;
   const uint8_t* wimg;  // packed weight tiles [n_tile][kblock][term][n_tile rows][128 B]
   StateRef state;
-  int state_off;        // offset of this layer's history inside a slot (floats)
+  HistRef hist;
   uint32_t* status;
 };
 
@@ -80,7 +101,7 @@ struct FinalArgs {
   const float* w;       // [32][7]
   const float* b;       // [1]
   StateRef state;
-  int state_off;
+  HistRef hist;
   uint32_t* status;
 };
 
@@ -89,9 +110,10 @@ cudaError_t launch_gemm_layer(const LayerArgs& a, cudaStream_t stream);
 cudaError_t launch_final(const FinalArgs& a, cudaStream_t stream);
 cudaError_t prepare_kernels();
 
-// Bytes of one packed weight tile set (all terms) for ``n_tile`` rows.
-inline size_t weight_tile_bytes(int n_tile, int mode) {
-  return (size_t)n_tile * 128 * (mode == kModeSplit ? 2 : 1);
+// Rows of the TMA input box for a layer kind: the 128-row tile plus the
+// causal halo (one row for a transposed conv, 6*dilation for a residual unit).
+inline int box_rows_for(int kind, int dilation) {
+  return kind == kTconv ? kTileM + 1 : kind == kResidual ? kTileM + 6 * dilation : 0;
 }
 
 }  // namespace fav

@@ -1,25 +1,40 @@
 // sm_100a kernels of the AudioVAE2 decoder step.
 //
-// One GEMM engine serves every dense layer: rows = time steps of all streams
-// (M tile 128), columns = output channels (N tile 32..256), K = input channels.
-// Warp roles per CTA (320 threads):
-//   warps 0-7  A-operand producers: fused prologue (stage affine + Snake, or
-//              Snake -> depthwise k=7 -> Snake, or the stem depthwise conv)
-//              written straight into the 128-byte-swizzled K-major MMA tile;
-//              afterwards the same warps run the epilogue out of TMEM;
-//   warp 8     weight loader: one bulk copy of pre-swizzled weight tiles per stage;
-//   warp 9     TMEM owner and MMA issuer (tcgen05.mma, one elected lane).
-// Pipelines run through mbarriers; every wait is bounded and records an error
-// code in the caller's status word instead of hanging.
+// One persistent GEMM engine serves every dense layer: rows = time steps of all
+// streams (M tile 128), columns = output channels (N tile 32..256), K = input
+// channels. One CTA per SM loops over output tiles; the K-block pipeline runs
+// across tile boundaries and two TMEM accumulators let the epilogue of one tile
+// overlap the mainloop of the next. Warp roles (448 threads):
+//   warps 0-7   A-operand producers: fused prologue (stage affine + Snake, or
+//               Snake -> depthwise k=7 -> Snake, or the stem depthwise conv)
+//               computed from TMA-staged input rows in shared memory and
+//               written straight into the 128-byte-swizzled K-major MMA tile;
+//   warps 8-11  epilogue: TMEM -> registers -> bias / phase interleave /
+//               residual add -> global (each warp owns one TMEM lane quarter);
+//   warp 12     loaders: lane 0 bulk-copies pre-swizzled weight tiles, lane 1
+//               TMA-loads the input rows (tile + causal halo) of each K block;
+//   warp 13     TMEM owner and MMA issuer (tcgen05.mma, one elected lane).
+// Every wait is bounded and records an error code in the caller's status word
+// instead of hanging.
 #include "fav_device.cuh"
 #include "fav_internal.h"
 
 namespace fav {
 
-constexpr int kThreads = 320;
-constexpr int kProducerThreads = 256;
+constexpr int kProducerWarps = 8;
+constexpr int kEpilogueWarps = 4;
+constexpr int kThreads = (kProducerWarps + kEpilogueWarps + 2) * 32;
+constexpr int kProducerThreads = kProducerWarps * 32;
+constexpr int kLoaderWarp = kProducerWarps + kEpilogueWarps;
+constexpr int kMmaWarp = kLoaderWarp + 1;
 constexpr int kSmemBudget = 227 * 1024;
-constexpr int kMaxHalo = 54;  // 6 * largest dilation
+constexpr int kMaxHalo = 54;                 // 6 * largest dilation
+constexpr int kMaxTileStreams = kTileM + 1;  // streams one 128-row tile can touch
+
+template <int KIND>
+constexpr int raw_bytes() {
+  return KIND == kResidual ? (kTileM + kMaxHalo) * 64 * 4 : KIND == kTconv ? (kTileM + 1) * 64 * 4 : 0;
+}
 
 template <int NT, int MODE, int KIND>
 struct GemmCfg {
@@ -29,51 +44,160 @@ struct GemmCfg {
   static constexpr int kAStage = kTerms * kATile;
   static constexpr int kBStage = kTerms * kBTile;
   static constexpr int kStage = kAStage + kBStage;
-  static constexpr int kStaging = KIND == kResidual ? (kTileM + kMaxHalo) * 64 * 4 : 0;
-  static constexpr int kFixed = 1024 /*align slack*/ + 256 /*barriers*/;
-  static constexpr int kStagesFit = (kSmemBudget - kStaging - kFixed) / kStage;
+  static constexpr int kRaw = raw_bytes<KIND>();
+  static constexpr int kTable = KIND == kTestGemm ? 0 : (((2 * kMaxTileStreams + 2 * kTileM) * 4 + 15) / 16) * 16;
+  static constexpr int kFixed = 1024 /*align slack*/ + 256 /*barriers*/ + kTable;
+  static constexpr int kStagesFit = (kSmemBudget - 2 * kRaw - kFixed) / kStage;
   static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
   static_assert(kStages >= 2, "pipeline needs two stages");
-  static constexpr int kSmem = kFixed + kStages * kStage + kStaging;
-  static constexpr uint32_t kTmemCols = NT < 32 ? 32 : NT;
+  static constexpr int kSmem = kFixed + kStages * kStage + 2 * kRaw;
+  // Two accumulators of NT fp32 columns each.
+  static constexpr uint32_t kTmemCols = 2 * NT < 32 ? 32 : 2 * NT;
   static constexpr uint32_t kIdesc = instr_desc_f16(MODE == kModeSplit ? 1u : 0u, NT);
 };
 
-__device__ __forceinline__ const float* slot_in(const StateRef& st, int s, int off) {
-  if (!st.pool_in) return nullptr;
-  const int code = st.slot_codes ? st.slot_codes[s] : ((s << 2) | st.uniform_code);
-  if (code & 2) return nullptr;  // fresh stream: zero history
-  const int slot = code >> 2, parity = code & 1;
-  return st.pool_in + ((size_t)parity * st.num_slots + slot) * kSlotFloats + off;
-}
-__device__ __forceinline__ float* slot_out(const StateRef& st, int s, int off) {
-  if (!st.pool_out) return nullptr;
-  const int code = st.slot_codes ? st.slot_codes[s] : ((s << 2) | st.uniform_code);
-  const int slot = code >> 2, parity = (code & 1) ^ 1;
-  return st.pool_out + ((size_t)parity * st.num_slots + slot) * kSlotFloats + off;
-}
-
 __device__ __forceinline__ float2 ldg2(const float* p) { return __ldg(reinterpret_cast<const float2*>(p)); }
+__device__ __forceinline__ float2 lds2(const float* p) { return *reinterpret_cast<const float2*>(p); }
 
+// ----------------------------------------------------------- history rings
+// Per-tile tables, filled once per tile by the producers: for each stream the
+// tile touches, its slot code and window head; for each tile row, its stream
+// (table entry, -1 past the last row) and time within the chunk.
+struct StreamTable {
+  int* code;
+  int* head;
+  int* row_e;
+  int* row_t;
+  int s_lo;
+};
+constexpr int kTableInts = 2 * kMaxTileStreams + 2 * kTileM;
+
+__device__ __forceinline__ float* slot_base(const StateRef& st, int code) {
+  return st.pool + (size_t)(code >> 2) * kSlotStride;
+}
+__device__ __forceinline__ int* head_table(float* slot, int parity) {
+  return reinterpret_cast<int*>(slot + kRingFloats) + parity * kHeadInts;
+}
+
+// Producers (all kProducerThreads) fill the tables for the tile starting at m0.
+__device__ void fill_table(const LayerArgs& a, int m0, const StreamTable& tab) {
+  const int N = a.rows_per_stream;
+  const int s_hi = (min(m0 + kTileM, a.rows) - 1) / N;
+  for (int i = threadIdx.x; i <= s_hi - tab.s_lo; i += kProducerThreads) {
+    const int s = tab.s_lo + i;
+    const int code = a.state.slot_codes ? a.state.slot_codes[s] : ((s << 2) | a.state.uniform_code);
+    int head = 0;
+    if (a.state.pool && !(code & 2)) head = head_table(slot_base(a.state, code), code & 1)[a.hist.index];
+    tab.code[i] = code;
+    tab.head[i] = head;
+  }
+  if (threadIdx.x < kTileM) {
+    const int g = m0 + threadIdx.x;
+    int e = -1, t = 0;
+    if (g < a.rows) {
+      const int s = g / N;
+      e = s - tab.s_lo;
+      t = g - s * N;
+    }
+    tab.row_e[threadIdx.x] = e;
+    tab.row_t[threadIdx.x] = t;
+  }
+}
+
+// Window row holding time tp (-H <= tp < 0, relative to the chunk start) of
+// table entry i; nullptr when the history is zero.
+__device__ __forceinline__ const float* hist_row(const LayerArgs& a, const StreamTable& tab, int i, int tp) {
+  const int code = tab.code[i];
+  if (!a.state.pool || (code & 2)) return nullptr;
+  const int H = a.hist.rows;
+  int row = tab.head[i] + H + tp;  // in [head, head + H)
+  if (row >= 2 * H) row -= 2 * H;
+  return slot_base(a.state, code) + a.hist.ring + row * a.hist.width;
+}
+
+// Ring row that receives chunk row tp (tp >= max(0, N - H)).
+__device__ __forceinline__ float* hist_new_row(const StateRef& st, const HistRef& h, int code, int head, int tp,
+                                               int N) {
+  const int H = h.rows;
+  int row = head + H + tp - (N > H ? N - H : 0);
+  row %= 2 * H;
+  return slot_base(st, code) + h.ring + row * h.width;
+}
+
+// Advanced head of the history, written to the other head table.
+__device__ __forceinline__ void hist_commit_head(const StateRef& st, const HistRef& h, int code, int head, int N) {
+  const int H = h.rows;
+  head_table(slot_base(st, code), (code & 1) ^ 1)[h.index] = (head + (N < H ? N : H)) % (2 * H);
+}
+
+__device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float4 snake4(float4 v, float4 al, float4 rc) {
+  return make_float4(snake(v.x, al.x, rc.x), snake(v.y, al.y, rc.y), snake(v.z, al.z, rc.z), snake(v.w, al.w, rc.w));
+}
+
+// A-operand stores use plain shared-memory stores (no compiler barrier), so
+// loads for later rows can be scheduled ahead of them; fence.proxy.async before
+// the stage's barrier arrival publishes them to the tensor core.
 // Writes two adjacent channels (k, k+1) of tile row r in the A operand.
 template <int MODE>
-__device__ __forceinline__ void put_a(uint32_t a_stage, int r, int k, float v0, float v1) {
+__device__ __forceinline__ void put_a(uint8_t* a_stage, int r, int k, float v0, float v1) {
   const uint32_t off = sw128_offset(r, k);
   if (MODE == kModeSplit) {
     uint32_t hi, lo;
     split_bf16(v0, v1, hi, lo);
-    st_shared_u32(a_stage + off, hi);
-    st_shared_u32(a_stage + kTileM * 128 + off, lo);
+    *reinterpret_cast<uint32_t*>(a_stage + off) = hi;
+    *reinterpret_cast<uint32_t*>(a_stage + kTileM * 128 + off) = lo;
   } else {
-    st_shared_u32(a_stage + off, pack_f16(v0, v1));
+    *reinterpret_cast<uint32_t*>(a_stage + off) = pack_f16(v0, v1);
+  }
+}
+
+// Writes four adjacent channels (k..k+3, k % 4 == 0) of tile row r.
+template <int MODE>
+__device__ __forceinline__ void put_a4(uint8_t* a_stage, int r, int k, float4 v) {
+  const uint32_t off = sw128_offset(r, k);
+  if (MODE == kModeSplit) {
+    uint32_t h0, l0, h1, l1;
+    split_bf16(v.x, v.y, h0, l0);
+    split_bf16(v.z, v.w, h1, l1);
+    *reinterpret_cast<uint2*>(a_stage + off) = make_uint2(h0, h1);
+    *reinterpret_cast<uint2*>(a_stage + kTileM * 128 + off) = make_uint2(l0, l1);
+  } else {
+    *reinterpret_cast<uint2*>(a_stage + off) = make_uint2(pack_f16(v.x, v.y), pack_f16(v.z, v.w));
+  }
+}
+
+// Positions 8*half .. 8*half+7 of warp ``warp``'s 16-row share of the tile in
+// residue-class order (rows 0, d, 2d, ..., then 1, 1+d, ...), packed as bytes.
+__device__ __forceinline__ void class_rows(int d, int warp, int half, uint32_t& lo, uint32_t& hi) {
+  int rho = 0, k = 16 * warp + 8 * half;
+  while (k >= (kTileM - rho + d - 1) / d) {
+    k -= (kTileM - rho + d - 1) / d;
+    ++rho;
+  }
+  lo = hi = 0;
+  for (int u = 0; u < 8; ++u) {
+    const uint32_t r = rho + k * d;
+    if (u < 4) lo |= r << (8 * u);
+    else hi |= r << (8 * (u - 4));
+    if (++k >= (kTileM - rho + d - 1) / d) {
+      ++rho;
+      k = 0;
+    }
   }
 }
 
 // ------------------------------------------------------------------ producers
-// Stem: depthwise causal conv k=7 (d=1) on latents [S][64][T]; history = last
-// six raw latent frames [6][64].
+// Transposed-conv and residual producers: lane = (row half rs = lane / 16,
+// channel quad cq = lane % 16), so one warp instruction covers two rows of 64
+// channels; all per-row bookkeeping comes from the per-tile tables.
+
+// Stem: depthwise causal conv k=7 (d=1) on latents [S][64][z_stride]; history =
+// last six raw latent frames [6][64]. Two channels per lane, one row per warp step.
 template <int MODE>
-__device__ void produce_stem(const LayerArgs& a, int m0, uint32_t a_stage, int warp, int lane, bool write_state) {
+__device__ void produce_stem(const LayerArgs& a, int m0, uint8_t* a_stage, int warp, int lane, bool write_state,
+                             const StreamTable& tab) {
   const int c = 2 * lane;
   const int T = a.rows_per_stream;
   float w0[7], w1[7];
@@ -83,300 +207,345 @@ __device__ void produce_stem(const LayerArgs& a, int m0, uint32_t a_stage, int w
     w1[j] = __ldg(a.dw_w + (c + 1) * 7 + j);
   }
   const float b0 = __ldg(a.dw_b + c), b1 = __ldg(a.dw_b + c + 1);
-  for (int r = warp; r < kTileM; r += 8) {
-    const int g = m0 + r;
-    float y0 = 0.f, y1 = 0.f;
-    if (g < a.rows) {
-      const int s = g / T, t = g - s * T;
-      const float* z0 = a.x + ((size_t)s * kLatentChannels + c) * a.z_stride + a.z_offset;
-      const float* z1 = z0 + a.z_stride;
-      const float* hist = slot_in(a.state, s, a.state_off);
-      float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 1
+  for (int i0 = 0; i0 < 16; i0 += 4) {
+    float v0[4][7], v1[4][7];
 #pragma unroll
-      for (int j = 0; j < 7; ++j) {
-        const int tp = t - 6 + j;
-        float v0, v1;
-        if (tp >= 0) {
-          v0 = __ldg(z0 + tp);
-          v1 = __ldg(z1 + tp);
-        } else if (hist) {
-          const float2 h = ldg2(hist + (6 + tp) * kLatentChannels + c);
-          v0 = h.x;
-          v1 = h.y;
-        } else {
-          v0 = v1 = 0.f;
-        }
-        acc0 = j == 0 ? w0[0] * v0 : fmaf(w0[j], v0, acc0);
-        acc1 = j == 0 ? w1[0] * v1 : fmaf(w1[j], v1, acc1);
-      }
-      y0 = acc0 + b0;
-      y1 = acc1 + b1;
-      if (write_state && t == T - 1) {
-        float* dst = slot_out(a.state, s, a.state_off);
-        if (dst) {
-          for (int q = 0; q < 6; ++q) {
-            const int tp = T - 6 + q;
-            float v0, v1;
-            if (tp >= 0) {
-              v0 = __ldg(z0 + tp);
-              v1 = __ldg(z1 + tp);
-            } else if (hist) {
-              const float2 h = ldg2(hist + (6 + tp) * kLatentChannels + c);
-              v0 = h.x;
-              v1 = h.y;
-            } else {
-              v0 = v1 = 0.f;
+    for (int ii = 0; ii < 4; ++ii) {
+      const int r = warp + 8 * (i0 + ii);
+      const int e = tab.row_e[r], t = tab.row_t[r];
+#pragma unroll
+      for (int j = 0; j < 7; ++j) v0[ii][j] = v1[ii][j] = 0.f;
+      if (e >= 0) {
+        const int s = tab.s_lo + e;
+        const float* z0 = a.x + ((size_t)s * kLatentChannels + c) * a.z_stride + a.z_offset;
+#pragma unroll
+        for (int j = 0; j < 7; ++j) {
+          const int tp = t - 6 + j;
+          if (tp >= 0) {
+            v0[ii][j] = __ldg(z0 + tp);
+            v1[ii][j] = __ldg(z0 + a.z_stride + tp);
+          } else {
+            const float* h = hist_row(a, tab, e, tp);
+            if (h) {
+              const float2 hv = ldg2(h + c);
+              v0[ii][j] = hv.x;
+              v1[ii][j] = hv.y;
             }
-            *reinterpret_cast<float2*>(dst + q * kLatentChannels + c) = make_float2(v0, v1);
           }
         }
       }
     }
-    put_a<MODE>(a_stage, r, c, y0, y1);
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      const int r = warp + 8 * (i0 + ii);
+      const int e = tab.row_e[r], t = tab.row_t[r];
+      float y0 = 0.f, y1 = 0.f;
+      if (e >= 0) {
+        float acc0 = w0[0] * v0[ii][0], acc1 = w1[0] * v1[ii][0];
+#pragma unroll
+        for (int j = 1; j < 7; ++j) {
+          acc0 = fmaf(w0[j], v0[ii][j], acc0);
+          acc1 = fmaf(w1[j], v1[ii][j], acc1);
+        }
+        y0 = acc0 + b0;
+        y1 = acc1 + b1;
+        if (write_state && t == T - 1 && a.state.pool) {
+          // New window rows: the last min(T, 6) latent frames; zero the rest of a fresh window.
+          const int code = tab.code[e], head = tab.head[e];
+          const float* z0 = a.x + ((size_t)(tab.s_lo + e) * kLatentChannels + c) * a.z_stride + a.z_offset;
+          for (int tp = T > 6 ? T - 6 : 0; tp < T; ++tp) {
+            float* dst = hist_new_row(a.state, a.hist, code, head, tp, T);
+            *reinterpret_cast<float2*>(dst + c) = make_float2(__ldg(z0 + tp), __ldg(z0 + a.z_stride + tp));
+          }
+          if ((code & 2) && T < 6) {
+            float* ring = slot_base(a.state, code) + a.hist.ring;
+            for (int j = T; j < 6; ++j) *reinterpret_cast<float2*>(ring + j * kLatentChannels + c) = make_float2(0.f, 0.f);
+          }
+          if (lane == 0) hist_commit_head(a.state, a.hist, code, head, T);
+        }
+      }
+      put_a<MODE>(a_stage, r, c, y0, y1);
+    }
   }
 }
 
 // Transposed conv, virtual K block kb: tap 0 reads x[t], tap 1 reads x[t-1];
-// both through affine (x*scale, +offset) and Snake. History = previous
-// activated input [1][C_in].
+// both through affine (x*scale, +offset) and Snake. ``raw`` holds input rows
+// m0-1 .. m0+127 of this K block's 64 channels. History = previous activated
+// input [1][C_in].
 template <int MODE>
-__device__ void produce_tconv(const LayerArgs& a, int m0, int kb, uint32_t a_stage, int warp, int lane,
-                              bool write_state) {
+__device__ void produce_tconv(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, const float* raw, int warp,
+                              int lane, bool write_state, const StreamTable& tab) {
   const int C = a.k_channels;
   const int kpt = C / kKBlock;
   const int tap = kb / kpt;
-  const int c = (kb - tap * kpt) * kKBlock + 2 * lane;
+  const int cq = lane & 15, rs = lane >> 4;
+  const int kl = 4 * cq;
+  const int c = (kb - tap * kpt) * kKBlock + kl;
   const int N = a.rows_per_stream;
-  const float sc0 = __ldg(a.scale + c), sc1 = __ldg(a.scale + c + 1);
-  const float of0 = __ldg(a.offset + c), of1 = __ldg(a.offset + c + 1);
-  const float al0 = __ldg(a.alpha1 + c), al1 = __ldg(a.alpha1 + c + 1);
-  const float rc0 = __ldg(a.recip1 + c), rc1 = __ldg(a.recip1 + c + 1);
-  for (int r = warp; r < kTileM; r += 8) {
-    const int g = m0 + r;
-    float y0 = 0.f, y1 = 0.f;
-    if (g < a.rows) {
-      const int s = g / N, t = g - s * N;
+  const float4 sc = ldg4(a.scale + c), of = ldg4(a.offset + c), al = ldg4(a.alpha1 + c), rc = ldg4(a.recip1 + c);
+  float4 v[8];
+  uint32_t raw_mask = 0;  // bit j: v[j] is a raw input row (needs affine + Snake)
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int r = 2 * (warp + 8 * j) + rs;
+    const int e = tab.row_e[r], t = tab.row_t[r];
+    v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (e >= 0) {
       if (t - tap >= 0) {
-        const float2 v = ldg2(a.x + (size_t)(g - tap) * C + c);
-        const float u0 = __fadd_rn(__fmul_rn(v.x, sc0), of0);
-        const float u1 = __fadd_rn(__fmul_rn(v.y, sc1), of1);
-        y0 = snake(u0, al0, rc0);
-        y1 = snake(u1, al1, rc1);
-        if (write_state && tap == 0 && t == N - 1) {
-          float* dst = slot_out(a.state, s, a.state_off);
-          if (dst) *reinterpret_cast<float2*>(dst + c) = make_float2(y0, y1);
-        }
+        v[j] = lds4(raw + (r + 1 - tap) * kKBlock + kl);
+        raw_mask |= 1u << j;
       } else {
-        const float* hist = slot_in(a.state, s, a.state_off);
-        if (hist) {
-          const float2 h = ldg2(hist + c);
-          y0 = h.x;
-          y1 = h.y;
+        const float* h = hist_row(a, tab, e, -1);
+        if (h) v[j] = ldg4(h + c);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int r = 2 * (warp + 8 * j) + rs;
+    float4 y = v[j];
+    if (raw_mask & (1u << j)) {
+      y = make_float4(__fadd_rn(__fmul_rn(y.x, sc.x), of.x), __fadd_rn(__fmul_rn(y.y, sc.y), of.y),
+                      __fadd_rn(__fmul_rn(y.z, sc.z), of.z), __fadd_rn(__fmul_rn(y.w, sc.w), of.w));
+      y = snake4(y, al, rc);
+      if (write_state && tap == 0 && a.state.pool) {
+        const int e = tab.row_e[r];
+        if (tab.row_t[r] == N - 1) {
+          const int code = tab.code[e], head = tab.head[e];
+          *reinterpret_cast<float4*>(hist_new_row(a.state, a.hist, code, head, N - 1, N) + c) = y;
+          if (cq == 0 && kb == 0) hist_commit_head(a.state, a.hist, code, head, N);
         }
       }
     }
-    put_a<MODE>(a_stage, r, c & (kKBlock - 1), y0, y1);
+    put_a4<MODE>(a_stage, r, kl, y);
   }
 }
 
 // Residual unit, K block kb: Snake -> depthwise causal k=7 (dilation d) ->
-// Snake. Phase 1 stages Snake(x) for the tile's rows and its 6d-row halo in
-// shared memory (fp32); phase 2 walks each channel pair down rows of equal
-// residue mod d so the seven taps slide through registers. History = last 6d
-// Snake(x) rows [6d][C] (the depthwise conv's activated input).
+// Snake. ``raw`` holds input rows m0-H .. m0+127 of the K block (pitch P);
+// phase 1 applies the first Snake in place; phase 2 walks each half-warp down
+// eight rows in residue-class order (packed in walk_lo/hi) so the seven taps
+// slide through registers, reloading them at stream starts. History = last 6d
+// Snake(x) rows [6d][C]. Depthwise taps come transposed, [7][C].
 template <int MODE>
-__device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint32_t a_stage, float* staging, int warp,
-                                 int lane, bool write_state) {
+__device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, float* raw, int warp,
+                                 int lane, bool write_state, const StreamTable& tab, uint32_t walk_lo,
+                                 uint32_t walk_hi) {
   const int C = a.k_channels;
   const int d = a.dilation;
   const int H = 6 * d;
   const int N = a.rows_per_stream;
-  const int kl = 2 * lane;                  // channel pair inside the K block
+  const int P = a.raw_pitch;
+  const int cq = lane & 15, rs = lane >> 4;
+  const int kl = 4 * cq;
   const int c = kb * kKBlock + kl;
-  const bool valid = kl < (C < kKBlock ? C : kKBlock);
-  float a10 = 0.f, a11 = 0.f, r10 = 0.f, r11 = 0.f, a20 = 0.f, a21 = 0.f, r20 = 0.f, r21 = 0.f;
-  float w0[7], w1[7], b0 = 0.f, b1 = 0.f;
-#pragma unroll
-  for (int j = 0; j < 7; ++j) w0[j] = w1[j] = 0.f;
+  const bool valid = kl < P;
+  const int tid = warp * 32 + lane;
+  // Phase 1: raw[i] <- Snake(raw[i]) for the box rows i in [0, 128 + H).
   if (valid) {
-    a10 = __ldg(a.alpha1 + c); a11 = __ldg(a.alpha1 + c + 1);
-    r10 = __ldg(a.recip1 + c); r11 = __ldg(a.recip1 + c + 1);
-    a20 = __ldg(a.alpha2 + c); a21 = __ldg(a.alpha2 + c + 1);
-    r20 = __ldg(a.recip2 + c); r21 = __ldg(a.recip2 + c + 1);
-#pragma unroll
-    for (int j = 0; j < 7; ++j) {
-      w0[j] = __ldg(a.dw_w + c * 7 + j);
-      w1[j] = __ldg(a.dw_w + (c + 1) * 7 + j);
-    }
-    b0 = __ldg(a.dw_b + c);
-    b1 = __ldg(a.dw_b + c + 1);
-  }
-  // Phase 1: staging[i] = Snake(x[m0 - H + i]) for i in [0, 128 + H).
-  for (int i = warp; i < kTileM + H; i += 8) {
-    const int g = m0 - H + i;
-    float2 v = make_float2(0.f, 0.f);
-    if (valid && g >= 0 && g < a.rows) {
-      v = ldg2(a.x + (size_t)g * C + c);
-      v.x = snake(v.x, a10, r10);
-      v.y = snake(v.y, a11, r11);
-    }
-    *reinterpret_cast<float2*>(staging + i * 64 + kl) = v;
-  }
-  named_barrier(1, kProducerThreads);
-  // Advanced history for streams whose last row lies in this tile.
-  if (write_state && valid) {
-    const int g_end = min(m0 + kTileM, a.rows);
-    const int s_lo = m0 / N, s_hi = (g_end - 1) / N;
-    for (int s = s_lo + warp; s <= s_hi; s += 8) {
-      const int last = s * N + N - 1;
-      if (last < m0 || last >= g_end) continue;
-      float* dst = slot_out(a.state, s, a.state_off);
-      if (!dst) continue;
-      const float* hist = slot_in(a.state, s, a.state_off);
-      for (int q = 0; q < H; ++q) {
-        const int tp = N - H + q;
-        float2 v;
-        if (tp >= 0) {
-          v = *reinterpret_cast<const float2*>(staging + (s * N + tp - m0 + H) * 64 + kl);
-        } else {
-          v = hist ? ldg2(hist + (N + q) * C + c) : make_float2(0.f, 0.f);
-        }
-        *reinterpret_cast<float2*>(dst + q * C + c) = v;
+    const float4 al = ldg4(a.alpha1 + c), rc = ldg4(a.recip1 + c);
+    const int rows = kTileM + H;
+#pragma unroll 4
+    for (int j = 0; j < (kTileM + kMaxHalo + 15) / 16; ++j) {
+      const int i = 2 * (warp + 8 * j) + rs;
+      if (i < rows) {
+        float4* p = reinterpret_cast<float4*>(raw + i * P + kl);
+        *p = snake4(*p, al, rc);
       }
     }
   }
-  // Phase 2: 16 rows per warp in residue-class order.
-  int rho = 0, k = 16 * warp;
-  while (true) {
-    const int n_rho = (kTileM - rho + d - 1) / d;
-    if (k < n_rho) break;
-    k -= n_rho;
-    ++rho;
+  named_barrier(1, kProducerThreads);
+  // New window rows of streams whose last row lies in this tile.
+  if (write_state && a.state.pool) {
+    const int g_end = min(m0 + kTileM, a.rows);
+    const int n_new = N < H ? N : H;
+    const int quads = P / 4;
+    for (int e = 0; tab.s_lo + e <= (g_end - 1) / N; ++e) {
+      const int s = tab.s_lo + e;
+      const int last = s * N + N - 1;
+      if (last < m0 || last >= g_end) continue;
+      const int code = tab.code[e], head = tab.head[e];
+      for (int it = tid; it < n_new * quads; it += kProducerThreads) {
+        const int q = it / quads, k4 = 4 * (it - q * quads);
+        const int tp = N - n_new + q;
+        *reinterpret_cast<float4*>(hist_new_row(a.state, a.hist, code, head, tp, N) + kb * kKBlock + k4) =
+            lds4(raw + (s * N + tp - m0 + H) * P + k4);
+      }
+      if ((code & 2) && N < H) {
+        float* ring = slot_base(a.state, code) + a.hist.ring;
+        for (int it = tid; it < (H - N) * quads; it += kProducerThreads) {
+          const int q = it / quads, k4 = 4 * (it - q * quads);
+          *reinterpret_cast<float4*>(ring + (N + q) * C + kb * kKBlock + k4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      if (tid == 0 && kb == 0) hist_commit_head(a.state, a.hist, code, head, N);
+    }
   }
-  float2 win[7];
+  // Phase 2.
+  float4 w[7], bias, al2, rc2;
 #pragma unroll
-  for (int j = 0; j < 7; ++j) win[j] = make_float2(0.f, 0.f);
-  int prev_r = -1000000, prev_s = -1;
-  for (int it = 0; it < 16; ++it) {
-    const int r = rho + k * d;
-    const int g = m0 + r;
-    float y0 = 0.f, y1 = 0.f;
-    if (g < a.rows && valid) {
-      const int s = g / N, t = g - s * N;
-      if (prev_r == r - d && prev_s == s) {
+  for (int j = 0; j < 7; ++j) w[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  bias = al2 = rc2 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (valid) {
+#pragma unroll
+    for (int j = 0; j < 7; ++j) w[j] = ldg4(a.dw_w + j * C + c);
+    bias = ldg4(a.dw_b + c);
+    al2 = ldg4(a.alpha2 + c);
+    rc2 = ldg4(a.recip2 + c);
+  }
+  float4 win[7];
+#pragma unroll
+  for (int j = 0; j < 7; ++j) win[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  int prev_r = -1000000, prev_e = -2;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int r = ((u < 4 ? walk_lo : walk_hi) >> (8 * (u & 3))) & 255;
+    const int e = tab.row_e[r];
+    float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (valid && e >= 0) {
+      if (prev_r == r - d && prev_e == e) {
 #pragma unroll
         for (int j = 0; j < 6; ++j) win[j] = win[j + 1];
       } else {
-        const float* hist = slot_in(a.state, s, a.state_off);
+        const int t = tab.row_t[r];
 #pragma unroll
         for (int j = 0; j < 6; ++j) {
           const int back = (6 - j) * d;
           const int tp = t - back;
           if (tp >= 0) {
-            win[j] = *reinterpret_cast<const float2*>(staging + (r - back + H) * 64 + kl);
+            win[j] = lds4(raw + (r - back + H) * P + kl);
           } else {
-            win[j] = hist ? ldg2(hist + (H + tp) * C + c) : make_float2(0.f, 0.f);
+            const float* h = hist_row(a, tab, e, tp);
+            win[j] = h ? ldg4(h + c) : make_float4(0.f, 0.f, 0.f, 0.f);
           }
         }
       }
-      win[6] = *reinterpret_cast<const float2*>(staging + (r + H) * 64 + kl);
-      float h0 = w0[0] * win[0].x, h1 = w1[0] * win[0].y;
+      win[6] = lds4(raw + (r + H) * P + kl);
+      float4 h;
+      h.x = w[0].x * win[0].x;
+      h.y = w[0].y * win[0].y;
+      h.z = w[0].z * win[0].z;
+      h.w = w[0].w * win[0].w;
 #pragma unroll
       for (int j = 1; j < 7; ++j) {
-        h0 = fmaf(w0[j], win[j].x, h0);
-        h1 = fmaf(w1[j], win[j].y, h1);
+        h.x = fmaf(w[j].x, win[j].x, h.x);
+        h.y = fmaf(w[j].y, win[j].y, h.y);
+        h.z = fmaf(w[j].z, win[j].z, h.z);
+        h.w = fmaf(w[j].w, win[j].w, h.w);
       }
-      h0 += b0;
-      h1 += b1;
-      y0 = snake(h0, a20, r20);
-      y1 = snake(h1, a21, r21);
+      h = make_float4(h.x + bias.x, h.y + bias.y, h.z + bias.z, h.w + bias.w);
+      y = snake4(h, al2, rc2);
       prev_r = r;
-      prev_s = s;
+      prev_e = e;
+    } else {
+      prev_e = -2;
     }
-    put_a<MODE>(a_stage, r, kl, y0, y1);
-    if (++k >= (kTileM - rho + d - 1) / d) {
-      ++rho;
-      k = 0;
-    }
+    put_a4<MODE>(a_stage, r, kl, y);
   }
-  named_barrier(1, kProducerThreads);  // staging reused by the next K block
 }
 
 // Plain GEMM operand for the engine self-test: A [rows][K] fp32 row-major.
 template <int MODE>
-__device__ void produce_test(const LayerArgs& a, int m0, int kb, uint32_t a_stage, int warp, int lane) {
+__device__ void produce_test(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, int warp, int lane) {
   const int c = kb * kKBlock + 2 * lane;
-  for (int r = warp; r < kTileM; r += 8) {
-    const int g = m0 + r;
-    float2 v = make_float2(0.f, 0.f);
-    if (g < a.rows && c < a.k_channels) v = ldg2(a.x + (size_t)g * a.k_channels + c);
-    put_a<MODE>(a_stage, r, 2 * lane, v.x, v.y);
+  float2 v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int g = m0 + warp + 8 * i;
+    v[i] = (g < a.rows && c < a.k_channels) ? ldg2(a.x + (size_t)g * a.k_channels + c) : make_float2(0.f, 0.f);
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) put_a<MODE>(a_stage, warp + 8 * i, 2 * lane, v[i].x, v[i].y);
+}
+
+// ------------------------------------------------------------------ epilogue
+template <int KIND>
+__device__ __forceinline__ void load_skip(const LayerArgs& a, int g, int n, float4 (&x)[8]) {
+  if (KIND == kResidual && g < a.rows) {
+    const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)g * a.c_out + n);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = __ldg(src + i);
   }
 }
 
-// ------------------------------------------------------------------ epilogues
+// 32 accumulator columns of row g starting at output column n: bias, phase
+// interleave (transposed conv), skip add (residual) or plain store.
 template <int KIND>
-__device__ __forceinline__ void epilogue_chunk(const LayerArgs& a, int g, int n, const float (&v)[16]) {
+__device__ __forceinline__ void store_32(const LayerArgs& a, const float (&v)[32], const float4 (&x)[8], int g, int n) {
+  if (g >= a.rows) return;
   if (KIND == kTconv) {
     const int p = n / a.c_out, o = n - p * a.c_out;
-    float* dst = a.out + ((size_t)g * a.stride + p) * a.c_out + o;
+    float4* dst = reinterpret_cast<float4*>(a.out + ((size_t)g * a.stride + p) * a.c_out + o);
+    const float4* bias = reinterpret_cast<const float4*>(a.bias + o);
 #pragma unroll
-    for (int i = 0; i < 16; i += 4) {
-      const float4 b = __ldg(reinterpret_cast<const float4*>(a.bias + o + i));
-      *reinterpret_cast<float4*>(dst + i) = make_float4(v[i] + b.x, v[i + 1] + b.y, v[i + 2] + b.z, v[i + 3] + b.w);
+    for (int i = 0; i < 8; ++i) {
+      const float4 b = __ldg(bias + i);
+      dst[i] = make_float4(v[4 * i] + b.x, v[4 * i + 1] + b.y, v[4 * i + 2] + b.z, v[4 * i + 3] + b.w);
     }
   } else if (KIND == kResidual) {
-    const size_t base = (size_t)g * a.c_out + n;
+    float4* dst = reinterpret_cast<float4*>(a.out + (size_t)g * a.c_out + n);
+    const float4* bias = reinterpret_cast<const float4*>(a.bias + n);
 #pragma unroll
-    for (int i = 0; i < 16; i += 4) {
-      const float4 b = __ldg(reinterpret_cast<const float4*>(a.bias + n + i));
-      const float4 x = __ldg(reinterpret_cast<const float4*>(a.x + base + i));
-      *reinterpret_cast<float4*>(a.out + base + i) =
-          make_float4(x.x + (v[i] + b.x), x.y + (v[i + 1] + b.y), x.z + (v[i + 2] + b.z), x.w + (v[i + 3] + b.w));
+    for (int i = 0; i < 8; ++i) {
+      const float4 b = __ldg(bias + i);
+      dst[i] = make_float4(x[i].x + (v[4 * i] + b.x), x[i].y + (v[4 * i + 1] + b.y), x[i].z + (v[4 * i + 2] + b.z),
+                           x[i].w + (v[4 * i + 3] + b.w));
     }
   } else {
-    const size_t base = (size_t)g * a.n_total + n;
+    float4* dst = reinterpret_cast<float4*>(a.out + (size_t)g * a.n_total + n);
 #pragma unroll
-    for (int i = 0; i < 16; i += 4) {
+    for (int i = 0; i < 8; ++i) {
       float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (a.bias) b = __ldg(reinterpret_cast<const float4*>(a.bias + n + i));
-      *reinterpret_cast<float4*>(a.out + base + i) = make_float4(v[i] + b.x, v[i + 1] + b.y, v[i + 2] + b.z, v[i + 3] + b.w);
+      if (a.bias) b = __ldg(reinterpret_cast<const float4*>(a.bias + n) + i);
+      dst[i] = make_float4(v[4 * i] + b.x, v[4 * i + 1] + b.y, v[4 * i + 2] + b.z, v[4 * i + 3] + b.w);
     }
   }
 }
 
 // --------------------------------------------------------------------- engine
 template <int NT, int MODE, int KIND>
-__global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const LayerArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_constant__ LayerArgs a) {
   using Cfg = GemmCfg<NT, MODE, KIND>;
   constexpr int S = Cfg::kStages;
+  constexpr bool kStaged = KIND == kTconv || KIND == kResidual;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* a_base = smem;
   uint8_t* b_base = a_base + S * Cfg::kAStage;
-  float* staging = reinterpret_cast<float*>(b_base + S * Cfg::kBStage);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(b_base + S * Cfg::kBStage + Cfg::kStaging);
+  uint8_t* raw_base = b_base + S * Cfg::kBStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw_base + 2 * Cfg::kRaw);
   uint64_t* a_full = bars;
   uint64_t* b_full = bars + S;
   uint64_t* empty = bars + 2 * S;
-  uint64_t* acc_full = bars + 3 * S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 1);
+  uint64_t* acc_full = bars + 3 * S;       // [2]
+  uint64_t* acc_empty = bars + 3 * S + 2;  // [2]
+  uint64_t* raw_full = bars + 3 * S + 4;   // [2]
+  uint64_t* raw_empty = bars + 3 * S + 6;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 8);
+  int* table = reinterpret_cast<int*>(bars + 3 * S + 9);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kTileM;
-  const int n_tile = blockIdx.y;
   const int num_kb = a.num_kblocks;
+  const int num_m = (a.rows + kTileM - 1) / kTileM;
+  const int num_tiles = num_m * (a.n_total / NT);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&a_full[s], 8);
+      mbar_init(&a_full[s], kProducerWarps);
       mbar_init(&b_full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpilogueWarps);
+      mbar_init(&raw_full[b], 1);
+      mbar_init(&raw_empty[b], kProducerWarps);
+    }
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
@@ -385,91 +554,157 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const LayerArgs
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < 8) {
+  if (warp < kProducerWarps) {
     // ---- A producers
+    uint32_t g = 0;
     bool ok = true;
-    const bool write_state = n_tile == 0;
-    for (int kb = 0; kb < num_kb && ok; ++kb) {
-      const int s = kb % S;
-      const uint32_t ph = (kb / S) & 1;
-      // All producer threads leave together on a timeout, so none is left
-      // waiting at a named barrier inside a producer.
-      ok = named_barrier_and(2, kProducerThreads, mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer));
-      if (!ok) break;
-      const uint32_t a_stage = smem_u32(a_base + s * Cfg::kAStage);
-      if (KIND == kStem) produce_stem<MODE>(a, m0, a_stage, warp, lane, write_state);
-      else if (KIND == kTconv) produce_tconv<MODE>(a, m0, kb, a_stage, warp, lane, write_state);
-      else if (KIND == kResidual) produce_residual<MODE>(a, m0, kb, a_stage, staging, warp, lane, write_state);
-      else produce_test<MODE>(a, m0, kb, a_stage, warp, lane);
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&a_full[s]);
-    }
-    // ---- epilogue
-    if (ok && mbar_wait(acc_full, 0, a.status, kDevTimeoutEpilogue)) {
-      tc_fence_after();
-      const int q = warp & 3, half = warp >> 2;
-      const int r = q * 32 + lane;
-      const int g = m0 + r;
-      constexpr int kHalfCols = NT / 2;
-      for (int col = half * kHalfCols; col < (half + 1) * kHalfCols; col += 16) {
-        float v[16];
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, v);
-        if (g < a.rows) epilogue_chunk<KIND>(a, g, n_tile * NT + col, v);
+    uint32_t walk_lo = 0, walk_hi = 0;
+    if (KIND == kResidual) class_rows(a.dilation, warp, lane >> 4, walk_lo, walk_hi);
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      const int m0 = (t % num_m) * kTileM;
+      const bool write_state = t / num_m == 0;
+      StreamTable tab{table, table + kMaxTileStreams, table + 2 * kMaxTileStreams,
+                      table + 2 * kMaxTileStreams + kTileM, m0 / a.rows_per_stream};
+      if (KIND != kTestGemm) {
+        named_barrier(1, kProducerThreads);  // previous tile's table readers are done
+        fill_table(a, m0, tab);
+        named_barrier(1, kProducerThreads);
+      }
+      for (int kb = 0; kb < num_kb; ++kb, ++g) {
+        const int s = g % S;
+        const uint32_t ph = (g / S) & 1;
+        const int rb = g & 1;
+        // All producer threads leave together on a timeout, so none is left
+        // waiting at a named barrier inside a producer.
+        bool ready = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer);
+        if (kStaged && ready) ready = mbar_wait(&raw_full[rb], (g >> 1) & 1, a.status, kDevTimeoutProducer);
+        ok = named_barrier_and(2, kProducerThreads, ready);
+        if (!ok) break;
+        uint8_t* a_stage = a_base + s * Cfg::kAStage;
+        float* raw = reinterpret_cast<float*>(raw_base + rb * Cfg::kRaw);
+        if (KIND == kStem) produce_stem<MODE>(a, m0, a_stage, warp, lane, write_state, tab);
+        else if (KIND == kTconv) produce_tconv<MODE>(a, m0, kb, a_stage, raw, warp, lane, write_state, tab);
+        else if (KIND == kResidual)
+          produce_residual<MODE>(a, m0, kb, a_stage, raw, warp, lane, write_state, tab, walk_lo, walk_hi);
+        else produce_test<MODE>(a, m0, kb, a_stage, warp, lane);
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (kStaged) mbar_arrive(&raw_empty[rb]);
+          mbar_arrive(&a_full[s]);
+        }
       }
     }
-  } else if (warp == 8) {
-    // ---- weight loader
+  } else if (warp < kLoaderWarp) {
+    // ---- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    uint32_t i = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
+      const int buf = i & 1;
+      const int m0 = (t % num_m) * kTileM, n0 = (t / num_m) * NT;
+      const int g = m0 + q * 32 + lane;
+      float4 x[8];
+      load_skip<KIND>(a, g, n0, x);
+      if (!mbar_wait(&acc_full[buf], (i >> 1) & 1, a.status, kDevTimeoutEpilogue)) break;
+      tc_fence_after();
+      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * NT);
+#pragma unroll 1
+      for (int col = 0; col < NT; col += 32) {
+        float v[32];
+        tmem_ld32(base + col, v);
+        float4 xn[8];
+        if (col + 32 < NT) load_skip<KIND>(a, g, n0 + col + 32, xn);
+        store_32<KIND>(a, v, x, g, n0 + col);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[j] = xn[j];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  } else if (warp == kLoaderWarp) {
     if (lane == 0) {
-      const uint8_t* src = a.wimg + (size_t)n_tile * num_kb * Cfg::kBStage;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % S;
-        const uint32_t ph = (kb / S) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader)) break;
-        mbar_arrive_expect_tx(&b_full[s], Cfg::kBStage);
-        bulk_g2s(b_base + s * Cfg::kBStage, src + (size_t)kb * Cfg::kBStage, Cfg::kBStage, &b_full[s]);
+      // ---- weight tiles
+      uint32_t g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const uint8_t* src = a.wimg + (size_t)(t / num_m) * num_kb * Cfg::kBStage;
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader))) break;
+          mbar_arrive_expect_tx(&b_full[s], Cfg::kBStage);
+          bulk_g2s(b_base + s * Cfg::kBStage, src + (size_t)kb * Cfg::kBStage, Cfg::kBStage, &b_full[s]);
+        }
+      }
+    } else if (lane == 1 && kStaged) {
+      // ---- input rows (tile + causal halo) of each K block
+      const int halo = a.box_rows - kTileM;
+      const uint32_t bytes = (uint32_t)a.box_rows * a.raw_pitch * 4;
+      const int kpt = KIND == kTconv ? a.k_channels / kKBlock : 1;
+      uint32_t g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int m0 = (t % num_m) * kTileM;
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int rb = g & 1;
+          if (!(ok = mbar_wait(&raw_empty[rb], ((g >> 1) & 1) ^ 1, a.status, kDevTimeoutLoader))) break;
+          const int c0 = (KIND == kTconv ? kb % kpt : kb) * kKBlock;
+          mbar_arrive_expect_tx(&raw_full[rb], bytes);
+          tma_load_2d(raw_base + rb * Cfg::kRaw, &a.tmap, c0, m0 - halo, &raw_full[rb]);
+        }
       }
     }
   } else {
     // ---- MMA issuer
     if (lane == 0) {
+      uint32_t g = 0, i = 0;
       bool ok = true;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % S;
-        const uint32_t ph = (kb / S) & 1;
-        ok = mbar_wait(&a_full[s], ph, a.status, kDevTimeoutMma) &&
-             mbar_wait(&b_full[s], ph, a.status, kDevTimeoutMma);
-        if (!ok) break;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++i) {
+        const int buf = i & 1;
+        if (!(ok = mbar_wait(&acc_empty[buf], ((i >> 1) & 1) ^ 1, a.status, kDevTimeoutMma))) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(a_base + s * Cfg::kAStage);
-        const uint32_t b0 = smem_u32(b_base + s * Cfg::kBStage);
+        const uint32_t d = tmem + (uint32_t)(buf * NT);
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          ok = mbar_wait(&a_full[s], ph, a.status, kDevTimeoutMma) &&
+               mbar_wait(&b_full[s], ph, a.status, kDevTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(a_base + s * Cfg::kAStage);
+          const uint32_t b0 = smem_u32(b_base + s * Cfg::kBStage);
 #pragma unroll
-        for (int k = 0; k < kKBlock / 16; ++k) {
-          const uint32_t ko = k * 32;
-          const uint32_t acc = (kb | k) ? 1u : 0u;
-          mma_f16(tmem, smem_desc_sw128(a0 + ko), smem_desc_sw128(b0 + ko), Cfg::kIdesc, acc);
-          if (MODE == kModeSplit) {
-            mma_f16(tmem, smem_desc_sw128(a0 + ko), smem_desc_sw128(b0 + Cfg::kBTile + ko), Cfg::kIdesc, 1u);
-            mma_f16(tmem, smem_desc_sw128(a0 + Cfg::kATile + ko), smem_desc_sw128(b0 + ko), Cfg::kIdesc, 1u);
+          for (int k = 0; k < kKBlock / 16; ++k) {
+            const uint32_t ko = k * 32;
+            const uint32_t acc = (kb | k) ? 1u : 0u;
+            mma_f16(d, smem_desc_sw128(a0 + ko), smem_desc_sw128(b0 + ko), Cfg::kIdesc, acc);
+            if (MODE == kModeSplit) {
+              mma_f16(d, smem_desc_sw128(a0 + ko), smem_desc_sw128(b0 + Cfg::kBTile + ko), Cfg::kIdesc, 1u);
+              mma_f16(d, smem_desc_sw128(a0 + Cfg::kATile + ko), smem_desc_sw128(b0 + ko), Cfg::kIdesc, 1u);
+            }
           }
+          mma_commit(&empty[s]);
         }
-        mma_commit(&empty[s]);
+        if (ok) mma_commit(&acc_full[buf]);
       }
-      if (ok) mma_commit(acc_full);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
   }
 }
 
+static int g_sm_count = 0;
+
 template <int NT, int MODE, int KIND>
 static cudaError_t launch_cfg(const LayerArgs& a, cudaStream_t stream) {
   using Cfg = GemmCfg<NT, MODE, KIND>;
-  const dim3 grid((a.rows + kTileM - 1) / kTileM, a.n_total / NT);
+  const int tiles = ((a.rows + kTileM - 1) / kTileM) * (a.n_total / NT);
+  const int grid = tiles < g_sm_count ? tiles : g_sm_count;
   gemm_layer_kernel<NT, MODE, KIND><<<grid, kThreads, Cfg::kSmem, stream>>>(a);
   return cudaGetLastError();
 }
@@ -481,10 +716,19 @@ static cudaError_t set_smem() {
                               Cfg::kSmem);
 }
 
+// N tiles instantiated per layer kind: the split transposed conv keeps two
+// 64 KB stages next to its double-buffered input rows, so it stops at 128.
+template <int KIND>
+constexpr int max_nt() {
+  return KIND == kTconv ? 128 : 256;
+}
+
 template <int MODE, int KIND>
 static cudaError_t set_smem_all() {
   cudaError_t e;
-  if ((e = set_smem<256, MODE, KIND>()) != cudaSuccess) return e;
+  if constexpr (max_nt<KIND>() >= 256) {
+    if ((e = set_smem<256, MODE, KIND>()) != cudaSuccess) return e;
+  }
   if ((e = set_smem<128, MODE, KIND>()) != cudaSuccess) return e;
   if ((e = set_smem<64, MODE, KIND>()) != cudaSuccess) return e;
   return set_smem<32, MODE, KIND>();
@@ -493,7 +737,9 @@ static cudaError_t set_smem_all() {
 template <int MODE, int KIND>
 static cudaError_t launch_nt(const LayerArgs& a, cudaStream_t stream) {
   switch (a.n_tile) {
-    case 256: return launch_cfg<256, MODE, KIND>(a, stream);
+    case 256:
+      if constexpr (max_nt<KIND>() >= 256) return launch_cfg<256, MODE, KIND>(a, stream);
+      return cudaErrorInvalidValue;
     case 128: return launch_cfg<128, MODE, KIND>(a, stream);
     case 64: return launch_cfg<64, MODE, KIND>(a, stream);
     case 32: return launch_cfg<32, MODE, KIND>(a, stream);
@@ -502,7 +748,10 @@ static cudaError_t launch_nt(const LayerArgs& a, cudaStream_t stream) {
 }
 
 cudaError_t prepare_kernels() {
-  cudaError_t e;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
   if ((e = set_smem_all<kModeSplit, kStem>()) != cudaSuccess) return e;
   if ((e = set_smem_all<kModeSplit, kTconv>()) != cudaSuccess) return e;
   if ((e = set_smem_all<kModeF16, kResidual>()) != cudaSuccess) return e;
@@ -530,8 +779,14 @@ cudaError_t launch_gemm_layer(const LayerArgs& a, cudaStream_t stream) {
 // ------------------------------------------------------------------ final conv
 // Snake(32) -> causal conv 32->1 (k=7) -> tanh on CUDA cores. 256 output rows
 // per block; Snake values for the rows and a 6-row halo staged in shared memory.
+// A stream has at least 1920 rows here, so a block touches at most two streams.
 constexpr int kFinalRows = 256;
 constexpr int kFinalPitch = 33;
+constexpr int kFinalLoads = ((kFinalRows + 6) * kFinalChannels + kFinalRows - 1) / kFinalRows;
+
+__device__ __forceinline__ int final_code(const StateRef& st, int s) {
+  return st.slot_codes ? st.slot_codes[s] : ((s << 2) | st.uniform_code);
+}
 
 __global__ void __launch_bounds__(kFinalRows) final_kernel(const FinalArgs a) {
   __shared__ float act[(kFinalRows + 6) * kFinalPitch];
@@ -539,42 +794,65 @@ __global__ void __launch_bounds__(kFinalRows) final_kernel(const FinalArgs a) {
   const int g0 = blockIdx.x * kFinalRows;
   const int N = a.rows_per_stream;
   for (int i = threadIdx.x; i < kFinalChannels * 7; i += kFinalRows) wsm[i] = __ldg(a.w + i);
-  for (int i = threadIdx.x; i < (kFinalRows + 6) * kFinalChannels; i += kFinalRows) {
-    const int row = i / kFinalChannels, ch = i - row * kFinalChannels;
-    const int g = g0 - 6 + row;
-    float v = 0.f;
-    if (g >= 0 && g < a.rows) v = snake(__ldg(a.x + (size_t)g * kFinalChannels + ch), __ldg(a.alpha + ch), __ldg(a.recip + ch));
-    act[row * kFinalPitch + ch] = v;
+  const int ch = threadIdx.x & (kFinalChannels - 1);
+  const float al = __ldg(a.alpha + ch), rc = __ldg(a.recip + ch);
+  {
+    float v[kFinalLoads];
+#pragma unroll
+    for (int j = 0; j < kFinalLoads; ++j) {
+      const int i = threadIdx.x + j * kFinalRows;
+      const int g = g0 - 6 + i / kFinalChannels;
+      v[j] = (i < (kFinalRows + 6) * kFinalChannels && g >= 0 && g < a.rows)
+                 ? __ldg(a.x + (size_t)g * kFinalChannels + ch)
+                 : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < kFinalLoads; ++j) {
+      const int i = threadIdx.x + j * kFinalRows;
+      if (i < (kFinalRows + 6) * kFinalChannels) act[(i / kFinalChannels) * kFinalPitch + ch] = snake(v[j], al, rc);
+    }
   }
   __syncthreads();
   const int g_end = min(g0 + kFinalRows, a.rows);
-  // Advanced history (last six activated rows) of streams ending in this block.
-  if (a.state.pool_out) {
+  const HistRef& h = a.hist;
+  // New window (last six activated rows) of streams ending in this block.
+  if (a.state.pool) {
     const int s_lo = g0 / N, s_hi = (g_end - 1) / N;
     for (int s = s_lo; s <= s_hi; ++s) {
       const int last = s * N + N - 1;
       if (last < g0 || last >= g_end) continue;
-      float* dst = slot_out(a.state, s, a.state_off);
+      const int code = final_code(a.state, s);
+      const int head = (code & 2) ? 0 : head_table(slot_base(a.state, code), code & 1)[h.index];
       for (int i = threadIdx.x; i < 6 * kFinalChannels; i += kFinalRows) {
-        const int q = i / kFinalChannels, ch = i - q * kFinalChannels;
-        dst[q * kFinalChannels + ch] = act[(last - 5 + q - g0 + 6) * kFinalPitch + ch];
+        const int q = i / kFinalChannels, c = i - q * kFinalChannels;
+        hist_new_row(a.state, h, code, head, N - 6 + q, N)[c] = act[(last - 5 + q - g0 + 6) * kFinalPitch + c];
       }
+      if (threadIdx.x == 0) hist_commit_head(a.state, h, code, head, N);
     }
   }
   const int g = g0 + threadIdx.x;
   if (g < a.rows) {
     const int s = g / N, t = g - s * N;
-    const float* hist = slot_in(a.state, s, a.state_off);
+    const float* hist = nullptr;
+    int head = 0;
+    if (t < 6 && a.state.pool) {
+      const int code = final_code(a.state, s);
+      if (!(code & 2)) {
+        head = head_table(slot_base(a.state, code), code & 1)[h.index];
+        hist = slot_base(a.state, code) + h.ring;
+      }
+    }
     float acc = 0.f;
 #pragma unroll
     for (int j = 0; j < 7; ++j) {
       const int tp = t - 6 + j;
       const float* row = act + (threadIdx.x + j) * kFinalPitch;
-      for (int ch = 0; ch < kFinalChannels; ++ch) {
-        float v;
-        if (tp >= 0) v = row[ch];
-        else v = hist ? __ldg(hist + (6 + tp) * kFinalChannels + ch) : 0.f;
-        acc = fmaf(wsm[ch * 7 + j], v, acc);
+      const float* hrow = nullptr;
+      if (tp < 0 && hist) hrow = hist + ((head + 6 + tp) % 12) * kFinalChannels;
+#pragma unroll 8
+      for (int c = 0; c < kFinalChannels; ++c) {
+        const float v = tp >= 0 ? row[c] : (hrow ? __ldg(hrow + c) : 0.f);
+        acc = fmaf(wsm[c * 7 + j], v, acc);
       }
     }
     a.audio[(size_t)s * a.audio_stride + a.audio_offset + t] = tanhf(acc + __ldg(a.b));

@@ -15,6 +15,7 @@ from . import weights as W
 LIBRARY = Path(__file__).resolve().parent / "libfav_cuda.so"
 ABI_VERSION = 1
 SLOT_FLOATS = 161856
+SLOT_STRIDE_FLOATS = 2 * SLOT_FLOATS + 64
 NUM_COEFFICIENTS = 188
 
 STATUS = {0: "FAV_OK", 1: "FAV_INVALID_ARGUMENT", 2: "FAV_UNSUPPORTED", 3: "FAV_OVERLAP",

@@ -19,11 +19,16 @@
  *     expired) are reported through the caller's device status word.
  *   - Layouts: latents [streams][64][frames] fp32 (the reference's [1,64,L]
  *     per stream); audio [streams][1920*frames] fp32.
- *   - Causal history ("state") lives in a caller-allocated device pool of two
- *     halves x num_slots x FAV_SLOT_FLOATS fp32. A step reads each stream's
- *     history from one half and writes the advanced history to the other, so
- *     a failed step leaves the committed history untouched; the caller flips
- *     the stream's parity only after the step succeeded.
+ *   - Causal history ("state") lives in a caller-allocated device pool of
+ *     num_slots x FAV_SLOT_STRIDE_FLOATS fp32 (zero-initialised is not
+ *     required). Each of a stream's 26 histories (H rows x C channels, the
+ *     reference's inventory, mps_decoder.py:174-181) is a ring of 2H rows whose
+ *     window starts at a head index; every slot ends in two head tables. A step
+ *     reads the heads of the table its slot code names, writes new rows only
+ *     into ring rows outside the current window and writes the advanced heads
+ *     to the other table, so a failed step leaves the committed history
+ *     untouched; the caller flips the stream's read table only after the step
+ *     succeeded.
  */
 #ifndef FAST_AUDIOVAE_CUDA_H
 #define FAST_AUDIOVAE_CUDA_H
@@ -41,9 +46,12 @@ extern "C" {
 #endif
 
 #define FAV_ABI_VERSION 1
-/* Floats of causal history per stream: the reference's 26 histories,
+/* Floats of causal history window per stream: the reference's 26 histories,
  * 647,424 bytes (mps_decoder.py:174-181, :280). */
 #define FAV_SLOT_FLOATS 161856
+/* Floats one stream slot occupies in a history pool: rings of twice the
+ * window plus two head tables of 32 int32. */
+#define FAV_SLOT_STRIDE_FLOATS (2 * FAV_SLOT_FLOATS + 64)
 /* Number of coefficient arrays create_plan expects (order below). */
 #define FAV_NUM_COEFFICIENTS 188
 
@@ -98,7 +106,7 @@ FAV_API void fav_plan_destroy(fav_plan *plan);
 /* Device bytes held by the plan (packed weights and coefficients). */
 FAV_API size_t fav_plan_bytes(const fav_plan *plan);
 
-/* Bytes of a state pool with num_slots streams (two halves). */
+/* Bytes of a history pool with num_slots stream slots. */
 FAV_API size_t fav_state_pool_bytes(int32_t num_slots);
 /* Workspace bytes one fav_step with n_streams x frames needs. */
 FAV_API size_t fav_step_workspace_bytes(int32_t n_streams, int32_t frames);
@@ -106,9 +114,9 @@ FAV_API size_t fav_step_workspace_bytes(int32_t n_streams, int32_t frames);
 /* One decoder step for n_streams independent streams, each decoding `frames`
  * new latent frames (the reference's MPSModel.decode(z, states) for a batch of
  * streams; mps_decoder.py:309-325, gpu.py:157-185).
- *   slot_codes (device int32[n_streams]): (slot << 2) | (fresh << 1) | read_half.
+ *   slot_codes (device int32[n_streams]): (slot << 2) | (fresh << 1) | read_table.
  *     fresh=1 starts the stream from zero history (reference decode(z, {})).
- *     The advanced history is written to half (read_half ^ 1) of `slot`.
+ *     The advanced heads are written to head table (read_table ^ 1) of `slot`.
  *   latents [n_streams][64][frames], audio [n_streams][1920*frames] (device).
  *   workspace: >= fav_step_workspace_bytes(n_streams, frames) device bytes.
  *   status: device uint32 word, 0 on entry; nonzero after the step means a

@@ -231,10 +231,15 @@ def test_decode_many_equals_single_decodes(batch_dec):
 
 
 def test_histories_hold_reference_values(lib, plan, oracle0):
-    """After one step the device history slot holds the reference's 26 histories (channels last)."""
+    """After one step the slot's history windows hold the reference's 26 histories.
+
+    Pool layout: per slot, rings of 2H rows (channels last) for each history at
+    twice its reference offset, then two head tables of 32 int32; a step from
+    read table 0 writes its heads to table 1.
+    """
     z = W.seeded_latents(21, 3)
     pool = torch.zeros(lib.fav_state_pool_bytes(2) // 4, device="cuda")
-    codes = torch.tensor([(1 << 2) | 2 | 0], dtype=torch.int32, device="cuda")  # slot 1, fresh, read half 0
+    codes = torch.tensor([(1 << 2) | 2 | 0], dtype=torch.int32, device="cuda")  # slot 1, fresh, read table 0
     zd = torch.from_numpy(z).cuda()
     audio = torch.empty(1920 * 3, device="cuda")
     ws_bytes = lib.fav_step_workspace_bytes(1, 3)
@@ -245,16 +250,21 @@ def test_histories_hold_reference_values(lib, plan, oracle0):
     torch.cuda.synchronize()
     assert status.item() == 0
     _, states = oracle0.decode(z)
-    slot = pool.view(2, 2, _native.SLOT_FLOATS)[1, 1].cpu().numpy()  # written half 1 of slot 1
-    assert not pool.view(2, 2, -1)[0].any() and not pool.view(2, 2, -1)[1, 0].any()
+    slots = pool.view(2, _native.SLOT_STRIDE_FLOATS)
+    assert not slots[0].any()
+    slot = slots[1].cpu()
+    heads = slot[2 * _native.SLOT_FLOATS:].view(torch.int32)[32:64].numpy()
+    rings = slot[:2 * _native.SLOT_FLOATS].numpy()
     off = 0
-    for name, shape in W.state_shapes().items():
-        count = int(np.prod(shape))
-        got = slot[off:off + count].reshape(shape[2], shape[1]).T[None]
+    for index, (name, shape) in enumerate(W.state_shapes().items()):
+        _, channels, rows = shape
+        ring = rings[2 * off:2 * off + 2 * rows * channels].reshape(2 * rows, channels)
+        window = ring[(heads[index] + np.arange(rows)) % (2 * rows)]
+        got = window.T[None]
         ref = states[name].numpy()
         scale = max(1.0, float(np.abs(ref).max()))
         assert np.abs(got - ref).max() <= 2e-3 * scale, name
-        off += count
+        off += rows * channels
     assert off == _native.SLOT_FLOATS
 
 
