@@ -65,6 +65,30 @@ int32_t encode_input_map(CUtensorMap* map, const float* x, int rows, int channel
   return FAV_OK;
 }
 
+// TMA map of an fp32 output (or skip input) viewed as [rows][channels], or as
+// [rows][phases][channels] when phases > 1 (a transposed conv's interleaved
+// output), read and written in boxes of 32 channels x 32 rows, 128-byte swizzle.
+int32_t encode_box_map(CUtensorMap* map, const float* base, int rows, int channels, int phases) {
+  if (!g_encode) {
+    CUtensorMap probe;
+    const int32_t st = encode_input_map(&probe, base, rows > 0 ? rows : 1, channels, 1);
+    if (st != FAV_OK) return st;
+  }
+  const cuuint64_t dims3[3] = {(cuuint64_t)channels, (cuuint64_t)phases, (cuuint64_t)rows};
+  const cuuint64_t strides3[2] = {(cuuint64_t)channels * 4, (cuuint64_t)channels * phases * 4};
+  const cuuint64_t dims2[2] = {(cuuint64_t)channels * phases, (cuuint64_t)rows};
+  const cuuint64_t strides2[1] = {(cuuint64_t)channels * phases * 4};
+  const cuuint32_t box3[3] = {32, 1, 32}, box2[2] = {32, 32};
+  const cuuint32_t elem[3] = {1, 1, 1};
+  const bool three = phases > 1;
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, three ? 3 : 2, const_cast<float*>(base),
+                              three ? dims3 : dims2, three ? strides3 : strides2, three ? box3 : box2, elem,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FAV_DEVICE_ERROR, "cuTensorMapEncodeTiled (box map) failed (%d)", (int)r);
+  return FAV_OK;
+}
+
 std::once_flag g_prepare_once;
 cudaError_t g_prepare_error = cudaSuccess;
 
@@ -126,12 +150,12 @@ struct DeviceArrays {
 
 struct StageDev {
   int c_in, c_out, rate, n_tile_t;
-  const float *scale, *offset, *alpha, *recip, *tbias;
+  const float *scale, *offset, *alpha, *recip, *tbias, *tcoef;
   const uint8_t* timg;
   int state_t;
   struct Res {
     int dilation, n_tile;
-    const float *pre_a, *pre_r, *dw_w, *dw_b, *post_a, *post_r, *pw_b;
+    const float *pre_a, *pre_r, *dw_w, *dw_b, *post_a, *post_r, *pw_b, *coef;
     const uint8_t* img;
     int state_off;
   } res[3];
@@ -202,6 +226,16 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
     st.alpha = up(base + 2);
     st.recip = up(base + 3);
     {
+      // [block][scale, offset, alpha, recip][64]
+      const int blocks = st.c_in / fav::kKBlock;
+      std::vector<float> cf((size_t)blocks * fav::kCoefTconv * 64);
+      for (int b = 0; b < blocks; ++b)
+        for (int v = 0; v < fav::kCoefTconv; ++v)
+          for (int ch = 0; ch < 64; ++ch)
+            cf[((size_t)b * fav::kCoefTconv + v) * 64 + ch] = w[base + v][b * 64 + ch];
+      st.tcoef = plan->mem.upload(cf.data(), cf.size(), &e);
+    }
+    {
       const float* tw = w[base + 4];
       const int cin = st.c_in, cout = st.c_out, s = st.rate;
       // n = phase * C_out + o; k < C_in: current tap W[k][o][p], else previous tap W[k-C_in][o][p+s].
@@ -238,6 +272,23 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
       r.img = up_img(pack_operand(c, c, r.n_tile, fav::kModeF16,
                                   [pw, c](int n, int k) { return pw[(size_t)n * c + k]; }));
       r.pw_b = up(rb + 7);
+      {
+        // [block][alpha1, recip1, w0..w6, bias, alpha2, recip2][64], zero padded past C
+        const int c = st.c_out, blocks = (c + 63) / 64;
+        std::vector<float> cf((size_t)blocks * fav::kCoefResidual * 64, 0.f);
+        for (int b = 0; b < blocks; ++b)
+          for (int ch = 0; ch < 64 && b * 64 + ch < c; ++ch) {
+            const int cc = b * 64 + ch;
+            float* o = &cf[(size_t)b * fav::kCoefResidual * 64 + ch];
+            o[0 * 64] = w[rb + 0][cc];
+            o[1 * 64] = w[rb + 1][cc];
+            for (int j = 0; j < 7; ++j) o[(2 + j) * 64] = w[rb + 2][(size_t)cc * 7 + j];
+            o[9 * 64] = w[rb + 3][cc];
+            o[10 * 64] = w[rb + 4][cc];
+            o[11 * 64] = w[rb + 5][cc];
+          }
+        r.coef = plan->mem.upload(cf.data(), cf.size(), &e);
+      }
       r.state_off = off;
       off += 6 * r.dilation * st.c_out;
     }
@@ -293,6 +344,8 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
   a.dw_b = p->stem_b;
   a.wimg = p->stem_img;
   a.hist = fav::HistRef{0, 0, 6, fav::kLatentChannels};
+  int32_t es = encode_box_map(&a.tmap_out, a.out, a.rows, 2048, 1);
+  if (es != FAV_OK) return es;
   cudaError_t e = fav::launch_gemm_layer(a, stream);
   if (e != cudaSuccess) return cuda_fail(e, "stem launch");
   int layer = 0;
@@ -323,10 +376,12 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     t.alpha1 = st.alpha;
     t.recip1 = st.recip;
     t.wimg = st.timg;
+    t.coef = st.tcoef;
     t.hist = fav::HistRef{1 + 4 * i, 2 * st.state_t, 1, st.c_in};
     t.box_rows = fav::box_rows_for(fav::kTconv, 0);
     t.raw_pitch = fav::kKBlock;
-    int32_t es = encode_input_map(&t.tmap, t.x, t.rows, st.c_in, t.box_rows);
+    es = encode_input_map(&t.tmap, t.x, t.rows, st.c_in, t.box_rows);
+    if (es == FAV_OK) es = encode_box_map(&t.tmap_out, t.out, t.rows, st.c_out, st.rate);
     if (es != FAV_OK) return es;
     if ((e = fav::launch_gemm_layer(t, stream)) != cudaSuccess) return cuda_fail(e, "transpose launch");
     std::swap(cur, other);
@@ -359,10 +414,13 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       u.dw_w = r.dw_w;
       u.dw_b = r.dw_b;
       u.wimg = r.img;
+      u.coef = r.coef;
       u.hist = fav::HistRef{2 + 4 * i + j, 2 * r.state_off, 6 * r.dilation, st.c_out};
       u.box_rows = fav::box_rows_for(fav::kResidual, r.dilation);
       u.raw_pitch = st.c_out < fav::kKBlock ? st.c_out : fav::kKBlock;
       es = encode_input_map(&u.tmap, u.x, u.rows, st.c_out, u.box_rows);
+      if (es == FAV_OK) es = encode_box_map(&u.tmap_out, u.out, u.rows, st.c_out, 1);
+      if (es == FAV_OK) es = encode_box_map(&u.tmap_skip, u.x, u.rows, st.c_out, 1);
       if (es != FAV_OK) return es;
       if ((e = fav::launch_gemm_layer(u, stream)) != cudaSuccess) return cuda_fail(e, "residual launch");
       std::swap(cur, other);
@@ -660,6 +718,11 @@ int32_t fav_test_gemm(const float* a, int32_t m, int32_t k, const float* b, int3
   la.wimg = static_cast<const uint8_t*>(dimg);
   la.status = dstatus;
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
+  if (encode_box_map(&la.tmap_out, c, m, n, 1) != FAV_OK) {
+    cudaFree(dimg);
+    cudaFree(dstatus);
+    return FAV_DEVICE_ERROR;
+  }
   e = fav::launch_gemm_layer(la, stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
   uint32_t hs = 0;

@@ -90,6 +90,32 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// TMA tile stores (shared -> global, bulk-group completion). Coordinates past
+// the tensor's extent are clipped; coordinates must not be negative.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed store groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until at most N committed store groups are incomplete.
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Make generic-proxy shared-memory writes visible to the async proxy (MMA).
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -215,13 +241,9 @@ __device__ __forceinline__ uint32_t pack_f16(float lo_elem, float hi_elem) {
 }
 // Split two fp32 values into bf16 (hi, lo) pairs with v ~= hi + lo.
 __device__ __forceinline__ void split_bf16(float v0, float v1, uint32_t& hi, uint32_t& lo) {
-  const __nv_bfloat16 h0 = __float2bfloat16_rn(v0), h1 = __float2bfloat16_rn(v1);
-  const float r0 = v0 - __bfloat162float(h0), r1 = v1 - __bfloat162float(h1);
-  __nv_bfloat162 h;
-  h.x = h0;
-  h.y = h1;
-  hi = *reinterpret_cast<uint32_t*>(&h);
-  lo = pack_bf16(r0, r1);
+  hi = pack_bf16(v0, v1);
+  const float h0 = __uint_as_float(hi << 16), h1 = __uint_as_float(hi & 0xffff0000u);
+  lo = pack_bf16(v0 - h0, v1 - h1);
 }
 
 __device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t v0, uint32_t v1) {

@@ -56,7 +56,10 @@ struct HistRef {
 };
 
 struct LayerArgs {
-  CUtensorMap tmap;     // TMA map of the layer input x [rows][k] fp32 (transposed conv, residual)
+  CUtensorMap tmap;       // TMA map of the layer input x [rows][k] fp32 (transposed conv, residual)
+  CUtensorMap tmap_out;   // TMA map of the output, 32 x 32 fp32 boxes, 128-byte swizzle
+                          // (transposed conv: 3-D view [rows][rate][c_out], boxes 32 x 1 x 32)
+  CUtensorMap tmap_skip;  // residual: TMA map of x for the skip add, 32 x 32 boxes, 128-byte swizzle
   int kind;
   int mode;
   int rows;             // GEMM rows: all streams' time steps at this layer's input
@@ -83,6 +86,10 @@ struct LayerArgs {
   const float* recip2;
   const float* dw_w;    // depthwise taps: stem [64][7], residual [7][C]
   const float* dw_b;
+  // Per-64-channel-block coefficients, packed for one bulk copy per K block:
+  // transposed conv [block][scale, offset, alpha, recip][64]; residual
+  // [block][alpha1, recip1, w0..w6, bias, alpha2, recip2][64] (zero padded).
+  const float* coef;
   const uint8_t* wimg;  // packed weight tiles [n_tile][kblock][term][n_tile rows][128 B]
   StateRef state;
   HistRef hist;
@@ -109,6 +116,9 @@ struct FinalArgs {
 cudaError_t launch_gemm_layer(const LayerArgs& a, cudaStream_t stream);
 cudaError_t launch_final(const FinalArgs& a, cudaStream_t stream);
 cudaError_t prepare_kernels();
+
+constexpr int kCoefTconv = 4;      // coefficient vectors per channel block
+constexpr int kCoefResidual = 12;
 
 // Rows of the TMA input box for a layer kind: the 128-row tile plus the
 // causal halo (one row for a transposed conv, 6*dilation for a residual unit).

@@ -23,17 +23,29 @@ namespace fav {
 
 constexpr int kProducerWarps = 8;
 constexpr int kEpilogueWarps = 4;
-constexpr int kThreads = (kProducerWarps + kEpilogueWarps + 2) * 32;
+constexpr int kThreads = (kProducerWarps + kEpilogueWarps + 3) * 32;
 constexpr int kProducerThreads = kProducerWarps * 32;
 constexpr int kLoaderWarp = kProducerWarps + kEpilogueWarps;
 constexpr int kMmaWarp = kLoaderWarp + 1;
+constexpr int kSchedWarp = kMmaWarp + 1;
 constexpr int kSmemBudget = 227 * 1024;
 constexpr int kMaxHalo = 54;                 // 6 * largest dilation
 constexpr int kMaxTileStreams = kTileM + 1;  // streams one 128-row tile can touch
+constexpr uint32_t kEpiBoxBytes = 32 * 32 * 4;
+constexpr int kTableInts = 2 * kMaxTileStreams + 2 * kTileM;  // one tile's stream and row tables
 
+// Input rows of one K block staged by TMA (the box), followed by that block's coefficients.
 template <int KIND>
-constexpr int raw_bytes() {
+__host__ __device__ constexpr int box_bytes() {
   return KIND == kResidual ? (kTileM + kMaxHalo) * 64 * 4 : KIND == kTconv ? (kTileM + 1) * 64 * 4 : 0;
+}
+template <int KIND>
+__host__ __device__ constexpr int coef_floats() {
+  return KIND == kResidual ? kCoefResidual * 64 : KIND == kTconv ? kCoefTconv * 64 : 0;
+}
+template <int KIND>
+__host__ __device__ constexpr int raw_bytes() {
+  return box_bytes<KIND>() + coef_floats<KIND>() * 4;
 }
 
 template <int NT, int MODE, int KIND>
@@ -45,12 +57,17 @@ struct GemmCfg {
   static constexpr int kBStage = kTerms * kBTile;
   static constexpr int kStage = kAStage + kBStage;
   static constexpr int kRaw = raw_bytes<KIND>();
-  static constexpr int kTable = KIND == kTestGemm ? 0 : (((2 * kMaxTileStreams + 2 * kTileM) * 4 + 15) / 16) * 16;
-  static constexpr int kFixed = 1024 /*align slack*/ + 256 /*barriers*/ + kTable;
-  static constexpr int kStagesFit = (kSmemBudget - 2 * kRaw - kFixed) / kStage;
+  static constexpr int kTable = KIND == kTestGemm ? 0 : 2 * ((kTableInts * 4 + 15) / 16) * 16;  // two tiles
+  static constexpr int kFixed = 1024 /*align slack*/ + 512 /*barriers*/ + kTable;
+  // Epilogue staging: per epilogue warp, one or two 32 x 32 fp32 boxes.
+  static constexpr int kEpiBox = 32 * 32 * 4;
+  static constexpr int kEpiBufs =
+      (kSmemBudget - 2 * kRaw - kFixed - kEpilogueWarps * 2 * kEpiBox) / kStage >= 2 ? 2 : 1;
+  static constexpr int kEpi = kEpilogueWarps * kEpiBufs * kEpiBox;
+  static constexpr int kStagesFit = (kSmemBudget - 2 * kRaw - kFixed - kEpi) / kStage;
   static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
   static_assert(kStages >= 2, "pipeline needs two stages");
-  static constexpr int kSmem = kFixed + kStages * kStage + 2 * kRaw;
+  static constexpr int kSmem = kFixed + kStages * kStage + kEpi + 2 * kRaw;
   // Two accumulators of NT fp32 columns each.
   static constexpr uint32_t kTmemCols = 2 * NT < 32 ? 32 : 2 * NT;
   static constexpr uint32_t kIdesc = instr_desc_f16(MODE == kModeSplit ? 1u : 0u, NT);
@@ -70,7 +87,6 @@ struct StreamTable {
   int* row_t;
   int s_lo;
 };
-constexpr int kTableInts = 2 * kMaxTileStreams + 2 * kTileM;
 
 __device__ __forceinline__ float* slot_base(const StateRef& st, int code) {
   return st.pool + (size_t)(code >> 2) * kSlotStride;
@@ -79,11 +95,11 @@ __device__ __forceinline__ int* head_table(float* slot, int parity) {
   return reinterpret_cast<int*>(slot + kRingFloats) + parity * kHeadInts;
 }
 
-// Producers (all kProducerThreads) fill the tables for the tile starting at m0.
-__device__ void fill_table(const LayerArgs& a, int m0, const StreamTable& tab) {
+// The scheduler warp fills the tables for the tile starting at m0.
+__device__ void fill_table(const LayerArgs& a, int m0, const StreamTable& tab, int lane) {
   const int N = a.rows_per_stream;
   const int s_hi = (min(m0 + kTileM, a.rows) - 1) / N;
-  for (int i = threadIdx.x; i <= s_hi - tab.s_lo; i += kProducerThreads) {
+  for (int i = lane; i <= s_hi - tab.s_lo; i += 32) {
     const int s = tab.s_lo + i;
     const int code = a.state.slot_codes ? a.state.slot_codes[s] : ((s << 2) | a.state.uniform_code);
     int head = 0;
@@ -91,16 +107,16 @@ __device__ void fill_table(const LayerArgs& a, int m0, const StreamTable& tab) {
     tab.code[i] = code;
     tab.head[i] = head;
   }
-  if (threadIdx.x < kTileM) {
-    const int g = m0 + threadIdx.x;
+  for (int r = lane; r < kTileM; r += 32) {
+    const int g = m0 + r;
     int e = -1, t = 0;
     if (g < a.rows) {
       const int s = g / N;
       e = s - tab.s_lo;
       t = g - s * N;
     }
-    tab.row_e[threadIdx.x] = e;
-    tab.row_t[threadIdx.x] = t;
+    tab.row_e[r] = e;
+    tab.row_t[r] = t;
   }
 }
 
@@ -168,16 +184,17 @@ __device__ __forceinline__ void put_a4(uint8_t* a_stage, int r, int k, float4 v)
   }
 }
 
-// Positions 8*half .. 8*half+7 of warp ``warp``'s 16-row share of the tile in
-// residue-class order (rows 0, d, 2d, ..., then 1, 1+d, ...), packed as bytes.
-__device__ __forceinline__ void class_rows(int d, int warp, int half, uint32_t& lo, uint32_t& hi) {
-  int rho = 0, k = 16 * warp + 8 * half;
+// Positions n*group .. n*group+n-1 (n <= 8) of warp ``warp``'s 16-row share of
+// the tile in residue-class order (rows 0, d, 2d, ..., then 1, 1+d, ...),
+// packed as bytes.
+__device__ __forceinline__ void class_rows(int d, int warp, int group, int n, uint32_t& lo, uint32_t& hi) {
+  int rho = 0, k = 16 * warp + n * group;
   while (k >= (kTileM - rho + d - 1) / d) {
     k -= (kTileM - rho + d - 1) / d;
     ++rho;
   }
   lo = hi = 0;
-  for (int u = 0; u < 8; ++u) {
+  for (int u = 0; u < n; ++u) {
     const uint32_t r = rho + k * d;
     if (u < 4) lo |= r << (8 * u);
     else hi |= r << (8 * (u - 4));
@@ -186,6 +203,10 @@ __device__ __forceinline__ void class_rows(int d, int warp, int half, uint32_t& 
       k = 0;
     }
   }
+}
+
+__device__ __forceinline__ int walk_row(uint32_t lo, uint32_t hi, int u) {
+  return ((u < 4 ? lo : hi) >> (8 * (u & 3))) & 255;
 }
 
 // ------------------------------------------------------------------ producers
@@ -284,7 +305,8 @@ __device__ void produce_tconv(const LayerArgs& a, int m0, int kb, uint8_t* a_sta
   const int kl = 4 * cq;
   const int c = (kb - tap * kpt) * kKBlock + kl;
   const int N = a.rows_per_stream;
-  const float4 sc = ldg4(a.scale + c), of = ldg4(a.offset + c), al = ldg4(a.alpha1 + c), rc = ldg4(a.recip1 + c);
+  const float* cf = raw + box_bytes<kTconv>() / 4 + kl;
+  const float4 sc = lds4(cf), of = lds4(cf + 64), al = lds4(cf + 128), rc = lds4(cf + 192);
   float4 v[8];
   uint32_t raw_mask = 0;  // bit j: v[j] is a raw input row (needs affine + Snake)
 #pragma unroll
@@ -329,27 +351,32 @@ __device__ void produce_tconv(const LayerArgs& a, int m0, int kb, uint8_t* a_sta
 // eight rows in residue-class order (packed in walk_lo/hi) so the seven taps
 // slide through registers, reloading them at stream starts. History = last 6d
 // Snake(x) rows [6d][C]. Depthwise taps come transposed, [7][C].
-template <int MODE>
+// LPR lanes cover one row (16 for 64-channel K blocks, 8 for C = 32), so a
+// warp instruction covers 32/LPR rows and each lane group walks 16*LPR/32 rows.
+template <int MODE, int LPR>
 __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, float* raw, int warp,
                                  int lane, bool write_state, const StreamTable& tab, uint32_t walk_lo,
-                                 uint32_t walk_hi) {
+                                 uint32_t walk_hi, bool regular) {
+  constexpr int kRpi = 32 / LPR;   // rows per warp instruction
+  constexpr int kRpg = 16 / kRpi;  // rows walked per lane group
   const int C = a.k_channels;
   const int d = a.dilation;
   const int H = 6 * d;
   const int N = a.rows_per_stream;
   const int P = a.raw_pitch;
-  const int cq = lane & 15, rs = lane >> 4;
+  const int cq = lane % LPR, rs = lane / LPR;
   const int kl = 4 * cq;
   const int c = kb * kKBlock + kl;
   const bool valid = kl < P;
   const int tid = warp * 32 + lane;
   // Phase 1: raw[i] <- Snake(raw[i]) for the box rows i in [0, 128 + H).
+  const float* cf = raw + box_bytes<kResidual>() / 4 + kl;
   if (valid) {
-    const float4 al = ldg4(a.alpha1 + c), rc = ldg4(a.recip1 + c);
+    const float4 al = lds4(cf), rc = lds4(cf + 64);
     const int rows = kTileM + H;
-#pragma unroll 4
-    for (int j = 0; j < (kTileM + kMaxHalo + 15) / 16; ++j) {
-      const int i = 2 * (warp + 8 * j) + rs;
+#pragma unroll
+    for (int j = 0; j < (kTileM + kMaxHalo + 8 * kRpi - 1) / (8 * kRpi); ++j) {
+      const int i = kRpi * (warp + 8 * j) + rs;
       if (i < rows) {
         float4* p = reinterpret_cast<float4*>(raw + i * P + kl);
         *p = snake4(*p, al, rc);
@@ -390,18 +417,48 @@ __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_
   bias = al2 = rc2 = make_float4(0.f, 0.f, 0.f, 0.f);
   if (valid) {
 #pragma unroll
-    for (int j = 0; j < 7; ++j) w[j] = ldg4(a.dw_w + j * C + c);
-    bias = ldg4(a.dw_b + c);
-    al2 = ldg4(a.alpha2 + c);
-    rc2 = ldg4(a.recip2 + c);
+    for (int j = 0; j < 7; ++j) w[j] = lds4(cf + (2 + j) * 64);
+    bias = lds4(cf + 9 * 64);
+    al2 = lds4(cf + 10 * 64);
+    rc2 = lds4(cf + 11 * 64);
   }
   float4 win[7];
+  if (regular) {
+    // The lane group's rows are r0, r0+d, ..., r0+(kRpg-1)d of one stream with
+    // every tap inside the chunk: a branch-free sliding window.
+    const int r0 = walk_lo & 255;
+    const float* base = raw + (r0 - 6 * d + H) * P + kl;
+    const int step = d * P;
+#pragma unroll
+    for (int j = 0; j < 6; ++j) win[j] = valid ? lds4(base + j * step) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < kRpg; ++u) {
+      win[6] = valid ? lds4(base + (6 + u) * step) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 h;
+      h.x = w[0].x * win[0].x;
+      h.y = w[0].y * win[0].y;
+      h.z = w[0].z * win[0].z;
+      h.w = w[0].w * win[0].w;
+#pragma unroll
+      for (int j = 1; j < 7; ++j) {
+        h.x = fmaf(w[j].x, win[j].x, h.x);
+        h.y = fmaf(w[j].y, win[j].y, h.y);
+        h.z = fmaf(w[j].z, win[j].z, h.z);
+        h.w = fmaf(w[j].w, win[j].w, h.w);
+      }
+      h = make_float4(h.x + bias.x, h.y + bias.y, h.z + bias.z, h.w + bias.w);
+      put_a4<MODE>(a_stage, r0 + u * d, kl, valid ? snake4(h, al2, rc2) : make_float4(0.f, 0.f, 0.f, 0.f));
+#pragma unroll
+      for (int j = 0; j < 6; ++j) win[j] = win[j + 1];
+    }
+    return;
+  }
 #pragma unroll
   for (int j = 0; j < 7; ++j) win[j] = make_float4(0.f, 0.f, 0.f, 0.f);
   int prev_r = -1000000, prev_e = -2;
-#pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    const int r = ((u < 4 ? walk_lo : walk_hi) >> (8 * (u & 3))) & 255;
+#pragma unroll 1
+  for (int u = 0; u < kRpg; ++u) {
+    const int r = walk_row(walk_lo, walk_hi, u);
     const int e = tab.row_e[r];
     float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
     if (valid && e >= 0) {
@@ -460,50 +517,6 @@ __device__ void produce_test(const LayerArgs& a, int m0, int kb, uint8_t* a_stag
   for (int i = 0; i < 16; ++i) put_a<MODE>(a_stage, warp + 8 * i, 2 * lane, v[i].x, v[i].y);
 }
 
-// ------------------------------------------------------------------ epilogue
-template <int KIND>
-__device__ __forceinline__ void load_skip(const LayerArgs& a, int g, int n, float4 (&x)[8]) {
-  if (KIND == kResidual && g < a.rows) {
-    const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)g * a.c_out + n);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) x[i] = __ldg(src + i);
-  }
-}
-
-// 32 accumulator columns of row g starting at output column n: bias, phase
-// interleave (transposed conv), skip add (residual) or plain store.
-template <int KIND>
-__device__ __forceinline__ void store_32(const LayerArgs& a, const float (&v)[32], const float4 (&x)[8], int g, int n) {
-  if (g >= a.rows) return;
-  if (KIND == kTconv) {
-    const int p = n / a.c_out, o = n - p * a.c_out;
-    float4* dst = reinterpret_cast<float4*>(a.out + ((size_t)g * a.stride + p) * a.c_out + o);
-    const float4* bias = reinterpret_cast<const float4*>(a.bias + o);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 b = __ldg(bias + i);
-      dst[i] = make_float4(v[4 * i] + b.x, v[4 * i + 1] + b.y, v[4 * i + 2] + b.z, v[4 * i + 3] + b.w);
-    }
-  } else if (KIND == kResidual) {
-    float4* dst = reinterpret_cast<float4*>(a.out + (size_t)g * a.c_out + n);
-    const float4* bias = reinterpret_cast<const float4*>(a.bias + n);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 b = __ldg(bias + i);
-      dst[i] = make_float4(x[i].x + (v[4 * i] + b.x), x[i].y + (v[4 * i + 1] + b.y), x[i].z + (v[4 * i + 2] + b.z),
-                           x[i].w + (v[4 * i + 3] + b.w));
-    }
-  } else {
-    float4* dst = reinterpret_cast<float4*>(a.out + (size_t)g * a.n_total + n);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (a.bias) b = __ldg(reinterpret_cast<const float4*>(a.bias + n) + i);
-      dst[i] = make_float4(v[4 * i] + b.x, v[4 * i + 1] + b.y, v[4 * i + 2] + b.z, v[4 * i + 3] + b.w);
-    }
-  }
-}
-
 // --------------------------------------------------------------------- engine
 template <int NT, int MODE, int KIND>
 __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_constant__ LayerArgs a) {
@@ -514,7 +527,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* a_base = smem;
   uint8_t* b_base = a_base + S * Cfg::kAStage;
-  uint8_t* raw_base = b_base + S * Cfg::kBStage;
+  uint8_t* epi_base = b_base + S * Cfg::kBStage;
+  uint8_t* raw_base = epi_base + Cfg::kEpi;
   uint64_t* bars = reinterpret_cast<uint64_t*>(raw_base + 2 * Cfg::kRaw);
   uint64_t* a_full = bars;
   uint64_t* b_full = bars + S;
@@ -523,8 +537,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   uint64_t* acc_empty = bars + 3 * S + 2;  // [2]
   uint64_t* raw_full = bars + 3 * S + 4;   // [2]
   uint64_t* raw_empty = bars + 3 * S + 6;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 8);
-  int* table = reinterpret_cast<int*>(bars + 3 * S + 9);
+  uint64_t* skip_full = bars + 3 * S + 8;     // [epilogue warp][2]
+  uint64_t* table_full = bars + 3 * S + 16;   // [2]
+  uint64_t* table_empty = bars + 3 * S + 18;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 20);
+  int* table = reinterpret_cast<int*>(bars + 3 * S + 22);
+  constexpr int kLpr = NT == 32 ? 8 : 16;  // residual lanes per row (C = 32 uses eight)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_kb = a.num_kblocks;
@@ -543,6 +561,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       mbar_init(&raw_full[b], 1);
       mbar_init(&raw_empty[b], kProducerWarps);
     }
+    for (int b = 0; b < 2 * kEpilogueWarps; ++b) mbar_init(&skip_full[b], 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&table_full[b], 1);
+      mbar_init(&table_empty[b], kProducerWarps);
+    }
     fence_mbar_init();
   }
   if (warp == kMmaWarp) {
@@ -556,19 +579,38 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
 
   if (warp < kProducerWarps) {
     // ---- A producers
-    uint32_t g = 0;
+    if (KIND == kResidual && kLpr == 8) {
+      // C = 32: channels 32-63 of every A stage stay zero.
+      for (int s = 0; s < S; ++s)
+        for (int r = threadIdx.x; r < kTileM; r += kProducerThreads)
+          for (int k = 32; k < 64; k += 4) put_a4<MODE>(a_base + s * Cfg::kAStage, r, k, make_float4(0.f, 0.f, 0.f, 0.f));
+    }
+    uint32_t g = 0, ti = 0;
     bool ok = true;
     uint32_t walk_lo = 0, walk_hi = 0;
-    if (KIND == kResidual) class_rows(a.dilation, warp, lane >> 4, walk_lo, walk_hi);
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+    constexpr int kRpg = 16 * kLpr / 32;
+    bool chain = false;  // this lane group's rows form one arithmetic chain of step d
+    if (KIND == kResidual) {
+      class_rows(a.dilation, warp, lane / kLpr, kRpg, walk_lo, walk_hi);
+      chain = true;
+      for (int u = 1; u < kRpg; ++u)
+        chain = chain && walk_row(walk_lo, walk_hi, u) == (int)(walk_lo & 255) + u * a.dilation;
+    }
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++ti) {
       const int m0 = (t % num_m) * kTileM;
       const bool write_state = t / num_m == 0;
-      StreamTable tab{table, table + kMaxTileStreams, table + 2 * kMaxTileStreams,
-                      table + 2 * kMaxTileStreams + kTileM, m0 / a.rows_per_stream};
+      int* tb = table + (ti & 1) * kTableInts;
+      StreamTable tab{tb, tb + kMaxTileStreams, tb + 2 * kMaxTileStreams, tb + 2 * kMaxTileStreams + kTileM,
+                      m0 / a.rows_per_stream};
+      bool regular = false;
       if (KIND != kTestGemm) {
-        named_barrier(1, kProducerThreads);  // previous tile's table readers are done
-        fill_table(a, m0, tab);
-        named_barrier(1, kProducerThreads);
+        ok = named_barrier_and(2, kProducerThreads,
+                               mbar_wait(&table_full[ti & 1], (ti >> 1) & 1, a.status, kDevTimeoutProducer));
+        if (!ok) break;
+        if (KIND == kResidual && chain) {
+          const int r0 = walk_lo & 255, rl = walk_row(walk_lo, walk_hi, kRpg - 1), e0 = tab.row_e[r0];
+          regular = e0 >= 0 && e0 == tab.row_e[rl] && tab.row_t[r0] >= 6 * a.dilation;
+        }
       }
       for (int kb = 0; kb < num_kb; ++kb, ++g) {
         const int s = g % S;
@@ -585,7 +627,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         if (KIND == kStem) produce_stem<MODE>(a, m0, a_stage, warp, lane, write_state, tab);
         else if (KIND == kTconv) produce_tconv<MODE>(a, m0, kb, a_stage, raw, warp, lane, write_state, tab);
         else if (KIND == kResidual)
-          produce_residual<MODE>(a, m0, kb, a_stage, raw, warp, lane, write_state, tab, walk_lo, walk_hi);
+          produce_residual<MODE, kLpr>(a, m0, kb, a_stage, raw, warp, lane, write_state, tab, walk_lo, walk_hi,
+                                       regular);
         else produce_test<MODE>(a, m0, kb, a_stage, warp, lane);
         fence_async_smem();
         __syncwarp();
@@ -594,34 +637,92 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           mbar_arrive(&a_full[s]);
         }
       }
+      __syncwarp();
+      if (KIND != kTestGemm && lane == 0) mbar_arrive(&table_empty[ti & 1]);
     }
   } else if (warp < kLoaderWarp) {
-    // ---- epilogue
+    // ---- epilogue: per 32-column chunk, TMEM -> registers -> (+ bias, + skip)
+    // -> 128-byte-swizzled box in shared memory -> TMA store. Residual skip
+    // inputs are TMA-loaded into the same box (one chunk ahead when two boxes fit).
+    constexpr int kChunks = NT / 32;
+    constexpr int kBufs = Cfg::kEpiBufs;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    uint32_t i = 0;
+    float* boxes = reinterpret_cast<float*>(epi_base) + q * kBufs * 1024;
+    uint64_t* sbar = skip_full + 2 * q;
+    uint32_t i = 0, k = 0;  // tile and chunk counters
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
       const int buf = i & 1;
       const int m0 = (t % num_m) * kTileM, n0 = (t / num_m) * NT;
-      const int g = m0 + q * 32 + lane;
-      float4 x[8];
-      load_skip<KIND>(a, g, n0, x);
+      const int row0 = m0 + q * 32;
+      auto issue_skip = [&](uint32_t kk, int col) {
+        mbar_arrive_expect_tx(&sbar[kk % kBufs], kEpiBoxBytes);
+        tma_load_2d(boxes + (kk % kBufs) * 1024, &a.tmap_skip, n0 + col, row0, &sbar[kk % kBufs]);
+      };
+      if (KIND == kResidual && kBufs == 2 && lane == 0) {
+        bulk_wait_read<0>();
+        issue_skip(k, 0);
+      }
       if (!mbar_wait(&acc_full[buf], (i >> 1) & 1, a.status, kDevTimeoutEpilogue)) break;
       tc_fence_after();
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * NT);
+      bool ok = true;
 #pragma unroll 1
-      for (int col = 0; col < NT; col += 32) {
+      for (int c = 0; c < kChunks; ++c, ++k) {
+        float* box = boxes + (k % kBufs) * 1024;
+        if (lane == 0) {
+          if (KIND == kResidual) {
+            if (kBufs == 2) {
+              if (c + 1 < kChunks) {
+                bulk_wait_read<0>();
+                issue_skip(k + 1, (c + 1) * 32);
+              }
+            } else {
+              bulk_wait_read<0>();
+              issue_skip(k, c * 32);
+            }
+          } else if (kBufs == 2) {
+            bulk_wait_read<1>();
+          } else {
+            bulk_wait_read<0>();
+          }
+        }
+        __syncwarp();
+        if (KIND == kResidual && !(ok = mbar_wait(&sbar[k % kBufs], (k / kBufs) & 1, a.status, kDevTimeoutEpilogue)))
+          break;
         float v[32];
-        tmem_ld32(base + col, v);
-        float4 xn[8];
-        if (col + 32 < NT) load_skip<KIND>(a, g, n0 + col + 32, xn);
-        store_32<KIND>(a, v, x, g, n0 + col);
+        tmem_ld32(base + c * 32, v);
+        const int n = n0 + c * 32;
+        const int bias_col = KIND == kTconv ? n % a.c_out : n;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) x[j] = xn[j];
+        for (int j = 0; j < 8; ++j) {
+          float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (a.bias) b = ldg4(a.bias + bias_col + 4 * j);
+          float4* p = reinterpret_cast<float4*>(box + lane * 32 + ((j ^ (lane & 7)) << 2));
+          float4 o = make_float4(v[4 * j] + b.x, v[4 * j + 1] + b.y, v[4 * j + 2] + b.z, v[4 * j + 3] + b.w);
+          if (KIND == kResidual) {
+            const float4 x = *p;
+            o = make_float4(x.x + o.x, x.y + o.y, x.z + o.z, x.w + o.w);
+          }
+          *p = o;
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (KIND == kTconv) {
+            const int ph = n / a.c_out;
+            tma_store_3d(&a.tmap_out, box, n - ph * a.c_out, ph, row0);
+          } else {
+            tma_store_2d(&a.tmap_out, box, n, row0);
+          }
+          bulk_commit();
+        }
       }
+      if (!ok) break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
+    if (lane == 0) bulk_wait<0>();
   } else if (warp == kLoaderWarp) {
     if (lane == 0) {
       // ---- weight tiles
@@ -641,6 +742,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       // ---- input rows (tile + causal halo) of each K block
       const int halo = a.box_rows - kTileM;
       const uint32_t bytes = (uint32_t)a.box_rows * a.raw_pitch * 4;
+      constexpr uint32_t kCoefBytes = coef_floats<KIND>() * 4;
       const int kpt = KIND == kTconv ? a.k_channels / kKBlock : 1;
       uint32_t g = 0;
       bool ok = true;
@@ -649,10 +751,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
           const int rb = g & 1;
           if (!(ok = mbar_wait(&raw_empty[rb], ((g >> 1) & 1) ^ 1, a.status, kDevTimeoutLoader))) break;
-          const int c0 = (KIND == kTconv ? kb % kpt : kb) * kKBlock;
-          mbar_arrive_expect_tx(&raw_full[rb], bytes);
-          tma_load_2d(raw_base + rb * Cfg::kRaw, &a.tmap, c0, m0 - halo, &raw_full[rb]);
+          const int blk = KIND == kTconv ? kb % kpt : kb;
+          uint8_t* dst = raw_base + rb * Cfg::kRaw;
+          mbar_arrive_expect_tx(&raw_full[rb], bytes + kCoefBytes);
+          tma_load_2d(dst, &a.tmap, blk * kKBlock, m0 - halo, &raw_full[rb]);
+          bulk_g2s(dst + box_bytes<KIND>(), a.coef + (size_t)blk * coef_floats<KIND>(), kCoefBytes, &raw_full[rb]);
         }
+      }
+    }
+  } else if (warp == kSchedWarp) {
+    // ---- scheduler: per-tile stream/row tables, one tile ahead of the producers
+    if (KIND != kTestGemm) {
+      uint32_t ti = 0;
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++ti) {
+        const int m0 = (t % num_m) * kTileM;
+        if (!mbar_wait(&table_empty[ti & 1], ((ti >> 1) & 1) ^ 1, a.status, kDevTimeoutProducer)) break;
+        int* tb = table + (ti & 1) * kTableInts;
+        StreamTable tab{tb, tb + kMaxTileStreams, tb + 2 * kMaxTileStreams, tb + 2 * kMaxTileStreams + kTileM,
+                        m0 / a.rows_per_stream};
+        fill_table(a, m0, tab, lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&table_full[ti & 1]);
       }
     }
   } else {
