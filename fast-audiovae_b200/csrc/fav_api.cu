@@ -43,9 +43,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 std::once_flag g_encode_once;
 EncodeTiledFn g_encode = nullptr;
 
-// TMA map of a layer input x [rows][channels] fp32: boxes of min(channels, 64)
-// channels x box_rows rows, zero fill outside the tensor.
-int32_t encode_input_map(CUtensorMap* map, const float* x, int rows, int channels, int box_rows) {
+bool load_encoder() {
   std::call_once(g_encode_once, [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -53,40 +51,57 @@ int32_t encode_input_map(CUtensorMap* map, const float* x, int rows, int channel
         q == cudaDriverEntryPointSuccess)
       g_encode = reinterpret_cast<EncodeTiledFn>(fn);
   });
-  if (!g_encode) return fail(FAV_DEVICE_ERROR, "cuTensorMapEncodeTiled is unavailable");
-  const cuuint64_t dims[2] = {(cuuint64_t)channels, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)channels * sizeof(float)};
-  const cuuint32_t box[2] = {(cuuint32_t)(channels < fav::kKBlock ? channels : fav::kKBlock), (cuuint32_t)box_rows};
-  const cuuint32_t elem[2] = {1, 1};
-  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(x), dims, strides, box,
-                              elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(FAV_DEVICE_ERROR, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return g_encode != nullptr;
+}
+
+// Tiled TMA map over a dense tensor of ``rank`` dimensions (innermost first),
+// zero fill outside the tensor.
+int32_t encode_map(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes, const void* base, int rank,
+                   const cuuint64_t* dims, const cuuint32_t* box, CUtensorMapSwizzle swizzle, const char* what) {
+  if (!load_encoder()) return fail(FAV_DEVICE_ERROR, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t strides[4];
+  cuuint64_t pitch = (cuuint64_t)elem_bytes;
+  for (int i = 0; i + 1 < rank; ++i) strides[i] = pitch *= dims[i];
+  const cuuint32_t elem[5] = {1, 1, 1, 1, 1};
+  const CUresult r = g_encode(map, type, rank, const_cast<void*>(base), dims, strides, box, elem,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FAV_DEVICE_ERROR, "cuTensorMapEncodeTiled (%s) failed (%d)", what, (int)r);
   return FAV_OK;
 }
 
-// TMA map of an fp32 output (or skip input) viewed as [rows][channels], or as
-// [rows][phases][channels] when phases > 1 (a transposed conv's interleaved
-// output), read and written in boxes of 32 channels x 32 rows, 128-byte swizzle.
-int32_t encode_box_map(CUtensorMap* map, const float* base, int rows, int channels, int phases) {
-  if (!g_encode) {
-    CUtensorMap probe;
-    const int32_t st = encode_input_map(&probe, base, rows > 0 ? rows : 1, channels, 1);
-    if (st != FAV_OK) return st;
+// Residual input s [rows][channels] fp32: boxes of min(channels, 64) channels x
+// box_rows rows, unswizzled (the producers read it row by row).
+int32_t encode_input_map(CUtensorMap* map, const float* x, int rows, int channels, int box_rows) {
+  const cuuint64_t dims[2] = {(cuuint64_t)channels, (cuuint64_t)rows};
+  const cuuint32_t box[2] = {(cuuint32_t)(channels < fav::kKBlock ? channels : fav::kKBlock), (cuuint32_t)box_rows};
+  return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_NONE, "input");
+}
+
+// Epilogue output y or Snake(y), fp32, viewed as [rows][channels] or, with
+// phases > 1 (a transposed conv's interleaved output), [rows][phases][channels];
+// written in boxes of 16 channels x 32 rows, 64-byte swizzle.
+int32_t encode_out_map(CUtensorMap* map, const float* base, int rows, int channels, int phases) {
+  if (phases > 1) {
+    const cuuint64_t dims[3] = {(cuuint64_t)channels, (cuuint64_t)phases, (cuuint64_t)rows};
+    const cuuint32_t box[3] = {16, 1, 32};
+    return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, 3, dims, box, CU_TENSOR_MAP_SWIZZLE_64B,
+                      "output");
   }
-  const cuuint64_t dims3[3] = {(cuuint64_t)channels, (cuuint64_t)phases, (cuuint64_t)rows};
-  const cuuint64_t strides3[2] = {(cuuint64_t)channels * 4, (cuuint64_t)channels * phases * 4};
-  const cuuint64_t dims2[2] = {(cuuint64_t)channels * phases, (cuuint64_t)rows};
-  const cuuint64_t strides2[1] = {(cuuint64_t)channels * phases * 4};
-  const cuuint32_t box3[3] = {32, 1, 32}, box2[2] = {32, 32};
-  const cuuint32_t elem[3] = {1, 1, 1};
-  const bool three = phases > 1;
-  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, three ? 3 : 2, const_cast<float*>(base),
-                              three ? dims3 : dims2, three ? strides3 : strides2, three ? box3 : box2, elem,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(FAV_DEVICE_ERROR, "cuTensorMapEncodeTiled (box map) failed (%d)", (int)r);
-  return FAV_OK;
+  const cuuint64_t dims[2] = {(cuuint64_t)channels, (cuuint64_t)rows};
+  const cuuint32_t box[2] = {16, 32};
+  return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_64B, "output");
+}
+
+// Split-bf16 planes [2][rows][channels] (hi, then lo) of a transposed conv's
+// activated input. The writer stores boxes of 16 channels x 32 rows (32-byte
+// swizzle); the transposed conv loads 64 x 128 boxes in the 128-byte swizzle,
+// which is the MMA's K-major A layout.
+int32_t encode_plane_map(CUtensorMap* map, const void* planes, int rows, int channels, bool load) {
+  const cuuint64_t dims[3] = {(cuuint64_t)channels, (cuuint64_t)rows, 2};
+  const cuuint32_t store_box[3] = {16, 32, 1}, load_box[3] = {(cuuint32_t)fav::kKBlock, (cuuint32_t)fav::kTileM, 1};
+  return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, planes, 3, dims, load ? load_box : store_box,
+                    load ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B, "planes");
 }
 
 std::once_flag g_prepare_once;
@@ -150,12 +165,12 @@ struct DeviceArrays {
 
 struct StageDev {
   int c_in, c_out, rate, n_tile_t;
-  const float *scale, *offset, *alpha, *recip, *tbias, *tcoef;
+  const float *scale, *offset, *alpha, *recip, *tbias;
   const uint8_t* timg;
   int state_t;
   struct Res {
     int dilation, n_tile;
-    const float *pre_a, *pre_r, *dw_w, *dw_b, *post_a, *post_r, *pw_b, *coef;
+    const float *pre_a, *pre_r, *pw_b, *coef;
     const uint8_t* img;
     int state_off;
   } res[3];
@@ -226,16 +241,6 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
     st.alpha = up(base + 2);
     st.recip = up(base + 3);
     {
-      // [block][scale, offset, alpha, recip][64]
-      const int blocks = st.c_in / fav::kKBlock;
-      std::vector<float> cf((size_t)blocks * fav::kCoefTconv * 64);
-      for (int b = 0; b < blocks; ++b)
-        for (int v = 0; v < fav::kCoefTconv; ++v)
-          for (int ch = 0; ch < 64; ++ch)
-            cf[((size_t)b * fav::kCoefTconv + v) * 64 + ch] = w[base + v][b * 64 + ch];
-      st.tcoef = plan->mem.upload(cf.data(), cf.size(), &e);
-    }
-    {
       const float* tw = w[base + 4];
       const int cin = st.c_in, cout = st.c_out, s = st.rate;
       // n = phase * C_out + o; k < C_in: current tap W[k][o][p], else previous tap W[k-C_in][o][p+s].
@@ -256,36 +261,24 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
       r.n_tile = st.c_out < 256 ? st.c_out : 256;
       r.pre_a = up(rb + 0);
       r.pre_r = up(rb + 1);
-      {
-        // Residual depthwise taps stored transposed, [7][C], for four-channel loads.
-        const int c = st.c_out;
-        std::vector<float> wt((size_t)7 * c);
-        for (int ch = 0; ch < c; ++ch)
-          for (int j = 0; j < 7; ++j) wt[(size_t)j * c + ch] = w[rb + 2][(size_t)ch * 7 + j];
-        r.dw_w = plan->mem.upload(wt.data(), wt.size(), &e);
-      }
-      r.dw_b = up(rb + 3);
-      r.post_a = up(rb + 4);
-      r.post_r = up(rb + 5);
       const float* pw = w[rb + 6];
       const int c = st.c_out;
       r.img = up_img(pack_operand(c, c, r.n_tile, fav::kModeF16,
                                   [pw, c](int n, int k) { return pw[(size_t)n * c + k]; }));
       r.pw_b = up(rb + 7);
       {
-        // [block][alpha1, recip1, w0..w6, bias, alpha2, recip2][64], zero padded past C
+        // [block][w0..w6, bias, alpha2, recip2][64], zero padded past C. The
+        // first Snake's alpha1/recip1 go to the previous layer's epilogue.
         const int c = st.c_out, blocks = (c + 63) / 64;
         std::vector<float> cf((size_t)blocks * fav::kCoefResidual * 64, 0.f);
         for (int b = 0; b < blocks; ++b)
           for (int ch = 0; ch < 64 && b * 64 + ch < c; ++ch) {
             const int cc = b * 64 + ch;
             float* o = &cf[(size_t)b * fav::kCoefResidual * 64 + ch];
-            o[0 * 64] = w[rb + 0][cc];
-            o[1 * 64] = w[rb + 1][cc];
-            for (int j = 0; j < 7; ++j) o[(2 + j) * 64] = w[rb + 2][(size_t)cc * 7 + j];
-            o[9 * 64] = w[rb + 3][cc];
-            o[10 * 64] = w[rb + 4][cc];
-            o[11 * 64] = w[rb + 5][cc];
+            for (int j = 0; j < 7; ++j) o[j * 64] = w[rb + 2][(size_t)cc * 7 + j];
+            o[7 * 64] = w[rb + 3][cc];
+            o[8 * 64] = w[rb + 4][cc];
+            o[9 * 64] = w[rb + 5][cc];
           }
         r.coef = plan->mem.upload(cf.data(), cf.size(), &e);
       }
@@ -305,11 +298,17 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
   return FAV_OK;
 }
 
-// Launches the 26 kernels of one decoder step. Activations ping-pong between
-// two workspace buffers of n_streams * frames * 61440 floats.
-// Layers are numbered 0 (stem), 1 + 4i (stage i transposed conv), 2 + 4i + j
-// (stage i residual j) and 25 (final conv); the schedule stops after
-// ``last_layer`` and reports the buffer holding that layer's output.
+// Workspace regions of one step, each n_streams * frames * 61440 floats (the
+// largest activation, [rows][channels], of any layer): y and Snake(y) of the
+// residual chain in ping-pong pairs, and the split-bf16 planes a transposed
+// conv reads.
+constexpr int kWorkspaceRegions = 5;
+constexpr size_t kRegionFloatsPerFrame = 61440;
+
+// Launches the 26 kernels of one decoder step. Layers are numbered 0 (stem),
+// 1 + 4i (stage i transposed conv), 2 + 4i + j (stage i residual j) and 25
+// (final conv); the schedule stops after ``last_layer`` and reports the buffer
+// holding that layer's output y (a layer whose y nothing reads writes it only then).
 int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, int frames, const float* z,
                  int z_stride, int z_offset, float* audio, int audio_stride, int audio_offset, float* ws,
                  uint32_t* status, cudaStream_t stream, int last_layer = 25, float** last_out = nullptr,
@@ -319,38 +318,48 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     if (events) cudaEventRecord(events[i], stream);
   };
   mark(0);
-  const size_t buf = (size_t)n_streams * frames * 61440;
-  float* cur = ws;
-  float* other = ws + buf;
-  fav::LayerArgs a{};
-  a.state = state;
-  a.status = status;
-  // stem
-  a.kind = fav::kStem;
-  a.mode = fav::kModeSplit;
-  a.rows = n_streams * frames;
-  a.rows_per_stream = frames;
-  a.k_channels = 64;
-  a.num_kblocks = 1;
-  a.n_total = 2048;
-  a.n_tile = 256;
-  a.c_out = 2048;
-  a.x = z;
-  a.z_stride = z_stride;
-  a.z_offset = z_offset;
-  a.out = cur;
-  a.bias = p->pw_b;
-  a.dw_w = p->stem_w;
-  a.dw_b = p->stem_b;
-  a.wimg = p->stem_img;
-  a.hist = fav::HistRef{0, 0, 6, fav::kLatentChannels};
-  int32_t es = encode_box_map(&a.tmap_out, a.out, a.rows, 2048, 1);
-  if (es != FAV_OK) return es;
-  cudaError_t e = fav::launch_gemm_layer(a, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "stem launch");
+  const size_t region = (size_t)n_streams * frames * kRegionFloatsPerFrame;
+  float* X[2] = {ws, ws + region};
+  float* S[2] = {ws + 2 * region, ws + 3 * region};
+  float* planes = ws + 4 * region;
+  int32_t es = FAV_OK;
+  cudaError_t e = cudaSuccess;
+  // stem: depthwise k=7 -> 1x1 64->2048; epilogue writes stage 0's activated planes.
+  {
+    fav::LayerArgs a{};
+    a.state = state;
+    a.status = status;
+    a.kind = fav::kStem;
+    a.mode = fav::kModeSplit;
+    a.epi = fav::kEpiPlanes | (last_layer == 0 ? fav::kEpiX : 0);
+    a.rows = n_streams * frames;
+    a.rows_per_stream = frames;
+    a.k_channels = 64;
+    a.num_kblocks = 1;
+    a.n_total = 2048;
+    a.n_tile = 256;
+    a.c_out = 2048;
+    a.x = z;
+    a.z_stride = z_stride;
+    a.z_offset = z_offset;
+    a.bias = p->pw_b;
+    a.dw_w = p->stem_w;
+    a.dw_b = p->stem_b;
+    a.wimg = p->stem_img;
+    const StageDev& next = p->stages[0];
+    a.next_scale = next.scale;
+    a.next_offset = next.offset;
+    a.next_alpha = next.alpha;
+    a.next_recip = next.recip;
+    a.hist = fav::HistRef{0, 0, 6, fav::kLatentChannels};
+    es = encode_out_map(&a.tmap_out, X[0], a.rows, 2048, 1);
+    if (es == FAV_OK) es = encode_plane_map(&a.tmap_out2, planes, a.rows, 2048, false);
+    if (es != FAV_OK) return es;
+    if ((e = fav::launch_gemm_layer(a, stream)) != cudaSuccess) return cuda_fail(e, "stem launch");
+  }
   int layer = 0;
   mark(1);
-  if (last_out) *last_out = cur;
+  if (last_out) *last_out = X[0];
   if (layer == last_layer) return FAV_OK;
   int n = frames;
   for (int i = 0; i < fav::kStages; ++i) {
@@ -360,6 +369,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     t.status = status;
     t.kind = fav::kTconv;
     t.mode = fav::kModeSplit;
+    t.epi = fav::kEpiX | fav::kEpiS;
     t.rows = n_streams * n;
     t.rows_per_stream = n;
     t.k_channels = st.c_in;
@@ -368,29 +378,26 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     t.n_tile = st.n_tile_t;
     t.c_out = st.c_out;
     t.stride = st.rate;
-    t.x = cur;
-    t.out = other;
     t.bias = st.tbias;
-    t.scale = st.scale;
-    t.offset = st.offset;
-    t.alpha1 = st.alpha;
-    t.recip1 = st.recip;
+    t.next_alpha = st.res[0].pre_a;
+    t.next_recip = st.res[0].pre_r;
     t.wimg = st.timg;
-    t.coef = st.tcoef;
     t.hist = fav::HistRef{1 + 4 * i, 2 * st.state_t, 1, st.c_in};
-    t.box_rows = fav::box_rows_for(fav::kTconv, 0);
-    t.raw_pitch = fav::kKBlock;
-    es = encode_input_map(&t.tmap, t.x, t.rows, st.c_in, t.box_rows);
-    if (es == FAV_OK) es = encode_box_map(&t.tmap_out, t.out, t.rows, st.c_out, st.rate);
+    es = encode_plane_map(&t.tmap, planes, t.rows, st.c_in, true);
+    if (es == FAV_OK) es = encode_out_map(&t.tmap_out, X[0], t.rows, st.c_out, st.rate);
+    if (es == FAV_OK) es = encode_out_map(&t.tmap_out2, S[0], t.rows, st.c_out, st.rate);
     if (es != FAV_OK) return es;
     if ((e = fav::launch_gemm_layer(t, stream)) != cudaSuccess) return cuda_fail(e, "transpose launch");
-    std::swap(cur, other);
     n *= st.rate;
-    if (last_out) *last_out = cur;
+    if (last_out) *last_out = X[0];
     mark(++layer + 1);
     if (layer == last_layer) return FAV_OK;
+    // Residual unit j reads y and Snake_pre(y) from pair j % 2 and writes pair
+    // (j + 1) % 2; the last unit writes the next stage's planes instead (stage 5:
+    // Snake_final(y) for the final conv).
     for (int j = 0; j < 3; ++j) {
       const auto& r = st.res[j];
+      const int in = j & 1, out = in ^ 1;
       fav::LayerArgs u{};
       u.state = state;
       u.status = status;
@@ -404,40 +411,50 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       u.n_tile = r.n_tile;
       u.c_out = st.c_out;
       u.dilation = r.dilation;
-      u.x = cur;
-      u.out = other;
+      u.x = X[in];
       u.bias = r.pw_b;
-      u.alpha1 = r.pre_a;
-      u.recip1 = r.pre_r;
-      u.alpha2 = r.post_a;
-      u.recip2 = r.post_r;
-      u.dw_w = r.dw_w;
-      u.dw_b = r.dw_b;
       u.wimg = r.img;
       u.coef = r.coef;
       u.hist = fav::HistRef{2 + 4 * i + j, 2 * r.state_off, 6 * r.dilation, st.c_out};
       u.box_rows = fav::box_rows_for(fav::kResidual, r.dilation);
       u.raw_pitch = st.c_out < fav::kKBlock ? st.c_out : fav::kKBlock;
-      es = encode_input_map(&u.tmap, u.x, u.rows, st.c_out, u.box_rows);
-      if (es == FAV_OK) es = encode_box_map(&u.tmap_out, u.out, u.rows, st.c_out, 1);
-      if (es == FAV_OK) es = encode_box_map(&u.tmap_skip, u.x, u.rows, st.c_out, 1);
+      const bool debug_y = layer + 1 == last_layer;
+      if (j < 2) {
+        u.epi = fav::kEpiX | fav::kEpiS;
+        u.next_alpha = st.res[j + 1].pre_a;
+        u.next_recip = st.res[j + 1].pre_r;
+      } else if (i + 1 < fav::kStages) {
+        const StageDev& nx = p->stages[i + 1];
+        u.epi = fav::kEpiPlanes | (debug_y ? fav::kEpiX : 0);
+        u.next_scale = nx.scale;
+        u.next_offset = nx.offset;
+        u.next_alpha = nx.alpha;
+        u.next_recip = nx.recip;
+      } else {
+        u.epi = fav::kEpiS | (debug_y ? fav::kEpiX : 0);
+        u.next_alpha = p->fin_a;
+        u.next_recip = p->fin_r;
+      }
+      es = encode_input_map(&u.tmap, S[in], u.rows, st.c_out, u.box_rows);
+      if (es == FAV_OK) es = encode_out_map(&u.tmap_out, X[out], u.rows, st.c_out, 1);
+      if (es == FAV_OK)
+        es = (u.epi & fav::kEpiPlanes) ? encode_plane_map(&u.tmap_out2, planes, u.rows, st.c_out, false)
+                                       : encode_out_map(&u.tmap_out2, S[out], u.rows, st.c_out, 1);
       if (es != FAV_OK) return es;
       if ((e = fav::launch_gemm_layer(u, stream)) != cudaSuccess) return cuda_fail(e, "residual launch");
-      std::swap(cur, other);
-      if (last_out) *last_out = cur;
+      if (last_out) *last_out = X[out];
       mark(++layer + 1);
       if (layer == last_layer) return FAV_OK;
     }
   }
+  // Stage 5's last unit (j = 2) wrote Snake_final(y) to S[1].
   fav::FinalArgs f{};
   f.rows = n_streams * n;
   f.rows_per_stream = n;
-  f.x = cur;
+  f.x = S[1];
   f.audio = audio;
   f.audio_stride = audio_stride;
   f.audio_offset = audio_offset;
-  f.alpha = p->fin_a;
-  f.recip = p->fin_r;
   f.w = p->fin_w;
   f.b = p->fin_b;
   f.state = state;
@@ -458,10 +475,11 @@ bool overflow_mul(size_t a, size_t b, size_t* out) {
 // Step workspace for fav_step_static, for callers that cannot allocate device
 // memory (a real-time audio callback, a host that forbids cudaMalloc after
 // start-up). It lives in this file-scope device array, so every GPU that loads
-// the library holds FAV_STATIC_MAX_FRAMES * 2 * 61440 floats (7.5 MiB) until
+// the library holds FAV_STATIC_MAX_FRAMES * 5 * 61440 floats (18.75 MiB) until
 // the process exits. Host code must not use the array's name as a device
 // address; fav_step_static looks the address up once per device.
-__device__ __align__(256) float g_static_workspace[(size_t)FAV_STATIC_MAX_FRAMES * 2 * 61440];
+__device__ __align__(256) float g_static_workspace[(size_t)FAV_STATIC_MAX_FRAMES * kWorkspaceRegions *
+                                                  kRegionFloatsPerFrame];
 
 std::mutex g_static_mutex;
 constexpr int kMaxDevices = 64;
@@ -555,7 +573,7 @@ size_t fav_step_workspace_bytes(int32_t n_streams, int32_t frames) {
   if (n_streams <= 0 || frames <= 0) return 0;
   size_t rows, bytes;
   if (overflow_mul((size_t)n_streams, (size_t)frames, &rows)) return 0;
-  if (overflow_mul(rows, (size_t)2 * 61440 * sizeof(float), &bytes)) return 0;
+  if (overflow_mul(rows, kWorkspaceRegions * kRegionFloatsPerFrame * sizeof(float), &bytes)) return 0;
   return bytes;
 }
 
@@ -713,12 +731,12 @@ int32_t fav_test_gemm(const float* a, int32_t m, int32_t k, const float* b, int3
   la.n_total = n;
   la.n_tile = nt;
   la.c_out = n;
+  la.epi = fav::kEpiX;
   la.x = a;
-  la.out = c;
   la.wimg = static_cast<const uint8_t*>(dimg);
   la.status = dstatus;
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
-  if (encode_box_map(&la.tmap_out, c, m, n, 1) != FAV_OK) {
+  if (encode_out_map(&la.tmap_out, c, m, n, 1) != FAV_OK) {
     cudaFree(dimg);
     cudaFree(dstatus);
     return FAV_DEVICE_ERROR;

@@ -55,13 +55,25 @@ struct HistRef {
   int width;   // C (channels per row)
 };
 
+// Epilogue outputs (bit mask). y = accumulator + bias (+ the layer input x for
+// a residual unit). The epilogue also applies the next layer's pointwise
+// prologue, so the next producer only does the work that needs neighbouring rows.
+enum EpilogueFlags : int {
+  kEpiX = 2,       // y (fp32) through tmap_out
+  kEpiS = 4,       // Snake(y) with next_alpha/next_recip (fp32) through tmap_out2
+  kEpiPlanes = 8,  // split-bf16 hi/lo planes of Snake(y * next_scale + next_offset) through tmap_out2
+};
+
 struct LayerArgs {
-  CUtensorMap tmap;       // TMA map of the layer input x [rows][k] fp32 (transposed conv, residual)
-  CUtensorMap tmap_out;   // TMA map of the output, 32 x 32 fp32 boxes, 128-byte swizzle
-                          // (transposed conv: 3-D view [rows][rate][c_out], boxes 32 x 1 x 32)
-  CUtensorMap tmap_skip;  // residual: TMA map of x for the skip add, 32 x 32 boxes, 128-byte swizzle
+  CUtensorMap tmap;       // producer input. Residual: s [rows][k] fp32, boxes of min(k, 64) channels x
+                          // box_rows rows. Transposed conv: planes [2][rows][k] bf16, boxes of 64 x 128 x 1
+                          // in the 128-byte swizzle (the MMA's A layout).
+  CUtensorMap tmap_out;   // y: [rows][c] fp32 (transposed conv: [rows][stride][c]), 16 x 32 boxes, 64-byte swizzle
+  CUtensorMap tmap_out2;  // Snake(y), same shape as tmap_out; or planes [2][rows][c] bf16, 16 x 32 x 1 boxes,
+                          // 32-byte swizzle
   int kind;
   int mode;
+  int epi;              // EpilogueFlags
   int rows;             // GEMM rows: all streams' time steps at this layer's input
   int rows_per_stream;  // time steps per stream at this layer's input
   int k_channels;       // input channels (K of one tap)
@@ -73,23 +85,19 @@ struct LayerArgs {
   int dilation;         // residual depthwise dilation
   int box_rows;         // rows of one TMA input box (tile + causal halo)
   int raw_pitch;        // floats per staged input row (min(k, 64))
-  const float* x;       // input activations [rows][k] fp32 (stem: latents [streams][64][z_stride])
+  const float* x;       // stem: latents [streams][64][z_stride]; residual: layer input x [rows][k] (skip)
   int z_stride;         // stem: frames per stream in the latent buffer
   int z_offset;         // stem: first frame of this step in the latent buffer
-  float* out;           // output activations fp32
   const float* bias;
-  const float* scale;   // stage affine
-  const float* offset;
-  const float* alpha1;  // Snake before the projection (stage) / before the depthwise conv (residual)
-  const float* recip1;
-  const float* alpha2;  // Snake after the depthwise conv (residual)
-  const float* recip2;
-  const float* dw_w;    // depthwise taps: stem [64][7], residual [7][C]
+  const float* dw_w;    // stem depthwise taps [64][7]
   const float* dw_b;
-  // Per-64-channel-block coefficients, packed for one bulk copy per K block:
-  // transposed conv [block][scale, offset, alpha, recip][64]; residual
-  // [block][alpha1, recip1, w0..w6, bias, alpha2, recip2][64] (zero padded).
+  // Residual: per-64-channel-block coefficients packed for one bulk copy per K
+  // block, [block][w0..w6, bias, alpha2, recip2][64] (zero padded).
   const float* coef;
+  const float* next_scale;  // coefficients of the pointwise prologue the epilogue applies
+  const float* next_offset;
+  const float* next_alpha;
+  const float* next_recip;
   const uint8_t* wimg;  // packed weight tiles [n_tile][kblock][term][n_tile rows][128 B]
   StateRef state;
   HistRef hist;
@@ -99,12 +107,10 @@ struct LayerArgs {
 struct FinalArgs {
   int rows;
   int rows_per_stream;
-  const float* x;       // [rows][32]
+  const float* x;       // Snake_final(y) [rows][32]
   float* audio;         // [streams][audio_stride]
   int audio_stride;     // samples per stream in the audio buffer
   int audio_offset;     // first sample of this step in the audio buffer
-  const float* alpha;
-  const float* recip;
   const float* w;       // [32][7]
   const float* b;       // [1]
   StateRef state;
@@ -117,13 +123,12 @@ cudaError_t launch_gemm_layer(const LayerArgs& a, cudaStream_t stream);
 cudaError_t launch_final(const FinalArgs& a, cudaStream_t stream);
 cudaError_t prepare_kernels();
 
-constexpr int kCoefTconv = 4;      // coefficient vectors per channel block
-constexpr int kCoefResidual = 12;
+constexpr int kCoefResidual = 10;  // coefficient vectors per 64-channel block
 
-// Rows of the TMA input box for a layer kind: the 128-row tile plus the
-// causal halo (one row for a transposed conv, 6*dilation for a residual unit).
+// Rows of the TMA input box of a residual unit: the 128-row tile plus the
+// causal halo of 6*dilation rows.
 inline int box_rows_for(int kind, int dilation) {
-  return kind == kTconv ? kTileM + 1 : kind == kResidual ? kTileM + 6 * dilation : 0;
+  return kind == kResidual ? kTileM + 6 * dilation : 0;
 }
 
 }  // namespace fav

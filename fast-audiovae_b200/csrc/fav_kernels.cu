@@ -4,16 +4,26 @@
 // streams (M tile 128), columns = output channels (N tile 32..256), K = input
 // channels. One CTA per SM loops over output tiles; the K-block pipeline runs
 // across tile boundaries and two TMEM accumulators let the epilogue of one tile
-// overlap the mainloop of the next. Warp roles (448 threads):
-//   warps 0-7   A-operand producers: fused prologue (stage affine + Snake, or
-//               Snake -> depthwise k=7 -> Snake, or the stem depthwise conv)
-//               computed from TMA-staged input rows in shared memory and
-//               written straight into the 128-byte-swizzled K-major MMA tile;
-//   warps 8-11  epilogue: TMEM -> registers -> bias / phase interleave /
-//               residual add -> global (each warp owns one TMEM lane quarter);
-//   warp 12     loaders: lane 0 bulk-copies pre-swizzled weight tiles, lane 1
-//               TMA-loads the input rows (tile + causal halo) of each K block;
-//   warp 13     TMEM owner and MMA issuer (tcgen05.mma, one elected lane).
+// overlap the mainloop of the next.
+//
+// Each epilogue also applies the *next* layer's pointwise prologue, so a
+// producer only does the work that needs neighbouring rows:
+//   stem, last residual unit of stages 0-4 -> split-bf16 planes of
+//     Snake(y * scale + offset), which the next transposed conv TMA-loads
+//     straight into its MMA tiles (its producers only patch stream starts);
+//   transposed conv, residual units 0-1 -> y and Snake_pre(y) of the next
+//     residual unit, whose producers then run depthwise k=7 + Snake only;
+//   last residual unit of stage 5 -> Snake_final(y) for the final conv.
+//
+// Warp roles (480 threads):
+//   warps 0-7   A-operand producers (stem depthwise conv; residual depthwise
+//               conv + Snake from a TMA-staged box; transposed-conv patches)
+//   warps 8-11  epilogue: TMEM -> registers -> bias / skip / next prologue ->
+//               swizzled boxes in shared memory -> TMA stores
+//   warp 12     loaders: lane 0 weight tiles (bulk copies), lane 1 producer
+//               inputs (residual boxes + coefficient blocks, transposed-conv planes)
+//   warp 13     TMEM owner and MMA issuer (tcgen05.mma, one elected lane)
+//   warp 14     scheduler: per-tile stream/row tables, one tile ahead
 // Every wait is bounded and records an error code in the caller's status word
 // instead of hanging.
 #include "fav_device.cuh"
@@ -31,22 +41,14 @@ constexpr int kSchedWarp = kMmaWarp + 1;
 constexpr int kSmemBudget = 227 * 1024;
 constexpr int kMaxHalo = 54;                 // 6 * largest dilation
 constexpr int kMaxTileStreams = kTileM + 1;  // streams one 128-row tile can touch
-constexpr uint32_t kEpiBoxBytes = 32 * 32 * 4;
 constexpr int kTableInts = 2 * kMaxTileStreams + 2 * kTileM;  // one tile's stream and row tables
+constexpr int kEpiCols = 16;                 // epilogue chunk: 16 columns x 32 rows per warp
+constexpr int kEpiBox = kEpiCols * 32 * 4;   // one fp32 box; the bf16 hi/lo pair fits in one too
 
-// Input rows of one K block staged by TMA (the box), followed by that block's coefficients.
-template <int KIND>
-__host__ __device__ constexpr int box_bytes() {
-  return KIND == kResidual ? (kTileM + kMaxHalo) * 64 * 4 : KIND == kTconv ? (kTileM + 1) * 64 * 4 : 0;
-}
-template <int KIND>
-__host__ __device__ constexpr int coef_floats() {
-  return KIND == kResidual ? kCoefResidual * 64 : KIND == kTconv ? kCoefTconv * 64 : 0;
-}
-template <int KIND>
-__host__ __device__ constexpr int raw_bytes() {
-  return box_bytes<KIND>() + coef_floats<KIND>() * 4;
-}
+// Residual producer input of one K block: the TMA box (tile + halo rows of 64
+// channels) followed by the block's coefficients.
+constexpr int kResBoxBytes = (kTileM + kMaxHalo) * 64 * 4;
+constexpr int kResCoefBytes = kCoefResidual * 64 * 4;
 
 template <int NT, int MODE, int KIND>
 struct GemmCfg {
@@ -56,14 +58,15 @@ struct GemmCfg {
   static constexpr int kAStage = kTerms * kATile;
   static constexpr int kBStage = kTerms * kBTile;
   static constexpr int kStage = kAStage + kBStage;
-  static constexpr int kRaw = raw_bytes<KIND>();
+  static constexpr int kRaw = KIND == kResidual ? kResBoxBytes + kResCoefBytes : 0;
   static constexpr int kTable = KIND == kTestGemm ? 0 : 2 * ((kTableInts * 4 + 15) / 16) * 16;  // two tiles
   static constexpr int kFixed = 1024 /*align slack*/ + 512 /*barriers*/ + kTable;
-  // Epilogue staging: per epilogue warp, one or two 32 x 32 fp32 boxes.
-  static constexpr int kEpiBox = 32 * 32 * 4;
-  static constexpr int kEpiBufs =
-      (kSmemBudget - 2 * kRaw - kFixed - kEpilogueWarps * 2 * kEpiBox) / kStage >= 2 ? 2 : 1;
-  static constexpr int kEpi = kEpilogueWarps * kEpiBufs * kEpiBox;
+  // Epilogue staging per warp and buffer: an fp32 box for y and one for
+  // Snake(y) (or the bf16 hi/lo plane pair). Two buffers when they still
+  // leave two pipeline stages.
+  static constexpr int kEpiBuf = kEpilogueWarps * 2 * kEpiBox;
+  static constexpr int kEpiBufs = (kSmemBudget - 2 * kRaw - kFixed - 2 * kEpiBuf) / kStage >= 2 ? 2 : 1;
+  static constexpr int kEpi = kEpiBufs * kEpiBuf;
   static constexpr int kStagesFit = (kSmemBudget - 2 * kRaw - kFixed - kEpi) / kStage;
   static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
   static_assert(kStages >= 2, "pipeline needs two stages");
@@ -74,12 +77,16 @@ struct GemmCfg {
 };
 
 __device__ __forceinline__ float2 ldg2(const float* p) { return __ldg(reinterpret_cast<const float2*>(p)); }
-__device__ __forceinline__ float2 lds2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+__device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float4 snake4(float4 v, float4 al, float4 rc) {
+  return make_float4(snake(v.x, al.x, rc.x), snake(v.y, al.y, rc.y), snake(v.z, al.z, rc.z), snake(v.w, al.w, rc.w));
+}
 
 // ----------------------------------------------------------- history rings
-// Per-tile tables, filled once per tile by the producers: for each stream the
-// tile touches, its slot code and window head; for each tile row, its stream
-// (table entry, -1 past the last row) and time within the chunk.
+// Per-tile tables, filled one tile ahead by the scheduler warp: for each stream
+// the tile touches, its slot code and window head; for each tile row, its
+// stream (table entry, -1 past the last row) and time within the chunk.
 struct StreamTable {
   int* code;
   int* head;
@@ -88,6 +95,11 @@ struct StreamTable {
   int s_lo;
 };
 
+__device__ __forceinline__ StreamTable table_at(int* base, int m0, int rows_per_stream) {
+  return StreamTable{base, base + kMaxTileStreams, base + 2 * kMaxTileStreams, base + 2 * kMaxTileStreams + kTileM,
+                     m0 / rows_per_stream};
+}
+
 __device__ __forceinline__ float* slot_base(const StateRef& st, int code) {
   return st.pool + (size_t)(code >> 2) * kSlotStride;
 }
@@ -95,7 +107,6 @@ __device__ __forceinline__ int* head_table(float* slot, int parity) {
   return reinterpret_cast<int*>(slot + kRingFloats) + parity * kHeadInts;
 }
 
-// The scheduler warp fills the tables for the tile starting at m0.
 __device__ void fill_table(const LayerArgs& a, int m0, const StreamTable& tab, int lane) {
   const int N = a.rows_per_stream;
   const int s_hi = (min(m0 + kTileM, a.rows) - 1) / N;
@@ -144,12 +155,6 @@ __device__ __forceinline__ float* hist_new_row(const StateRef& st, const HistRef
 __device__ __forceinline__ void hist_commit_head(const StateRef& st, const HistRef& h, int code, int head, int N) {
   const int H = h.rows;
   head_table(slot_base(st, code), (code & 1) ^ 1)[h.index] = (head + (N < H ? N : H)) % (2 * H);
-}
-
-__device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
-__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
-__device__ __forceinline__ float4 snake4(float4 v, float4 al, float4 rc) {
-  return make_float4(snake(v.x, al.x, rc.x), snake(v.y, al.y, rc.y), snake(v.z, al.z, rc.z), snake(v.w, al.w, rc.w));
 }
 
 // A-operand stores use plain shared-memory stores (no compiler barrier), so
@@ -210,14 +215,10 @@ __device__ __forceinline__ int walk_row(uint32_t lo, uint32_t hi, int u) {
 }
 
 // ------------------------------------------------------------------ producers
-// Transposed-conv and residual producers: lane = (row half rs = lane / 16,
-// channel quad cq = lane % 16), so one warp instruction covers two rows of 64
-// channels; all per-row bookkeeping comes from the per-tile tables.
-
 // Stem: depthwise causal conv k=7 (d=1) on latents [S][64][z_stride]; history =
 // last six raw latent frames [6][64]. Two channels per lane, one row per warp step.
 template <int MODE>
-__device__ void produce_stem(const LayerArgs& a, int m0, uint8_t* a_stage, int warp, int lane, bool write_state,
+__device__ void produce_stem(const LayerArgs& a, uint8_t* a_stage, int warp, int lane, bool write_state,
                              const StreamTable& tab) {
   const int c = 2 * lane;
   const int T = a.rows_per_stream;
@@ -238,8 +239,7 @@ __device__ void produce_stem(const LayerArgs& a, int m0, uint8_t* a_stage, int w
 #pragma unroll
       for (int j = 0; j < 7; ++j) v0[ii][j] = v1[ii][j] = 0.f;
       if (e >= 0) {
-        const int s = tab.s_lo + e;
-        const float* z0 = a.x + ((size_t)s * kLatentChannels + c) * a.z_stride + a.z_offset;
+        const float* z0 = a.x + ((size_t)(tab.s_lo + e) * kLatentChannels + c) * a.z_stride + a.z_offset;
 #pragma unroll
         for (int j = 0; j < 7; ++j) {
           const int tp = t - 6 + j;
@@ -281,7 +281,8 @@ __device__ void produce_stem(const LayerArgs& a, int m0, uint8_t* a_stage, int w
           }
           if ((code & 2) && T < 6) {
             float* ring = slot_base(a.state, code) + a.hist.ring;
-            for (int j = T; j < 6; ++j) *reinterpret_cast<float2*>(ring + j * kLatentChannels + c) = make_float2(0.f, 0.f);
+            for (int j = T; j < 6; ++j)
+              *reinterpret_cast<float2*>(ring + j * kLatentChannels + c) = make_float2(0.f, 0.f);
           }
           if (lane == 0) hist_commit_head(a.state, a.hist, code, head, T);
         }
@@ -291,99 +292,79 @@ __device__ void produce_stem(const LayerArgs& a, int m0, uint8_t* a_stage, int w
   }
 }
 
-// Transposed conv, virtual K block kb: tap 0 reads x[t], tap 1 reads x[t-1];
-// both through affine (x*scale, +offset) and Snake. ``raw`` holds input rows
-// m0-1 .. m0+127 of this K block's 64 channels. History = previous activated
-// input [1][C_in].
-template <int MODE>
-__device__ void produce_tconv(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, const float* raw, int warp,
-                              int lane, bool write_state, const StreamTable& tab) {
-  const int C = a.k_channels;
-  const int kpt = C / kKBlock;
+// Transposed conv, virtual K block kb (tap 0 reads x[t], tap 1 reads x[t-1]):
+// the A stage already holds the split-bf16 planes of the activated input
+// Snake(x * scale + offset), TMA-loaded from rows m0 - tap. Rows whose tap
+// reaches before the chunk (t - tap < 0) take the history instead: the previous
+// activated input, kept as packed (hi << 16 | lo) bf16 bits per channel. Tap-0
+// blocks record that value for each stream's last row as the advanced history.
+// Lane = (row half rs, channel quad cq); lane rows 2*(warp + 8j) + rs.
+__device__ void patch_tconv(const LayerArgs& a, int kb, uint8_t* a_stage, int warp, int lane, bool write_state,
+                            const StreamTable& tab) {
+  const int kpt = a.k_channels / kKBlock;
   const int tap = kb / kpt;
   const int cq = lane & 15, rs = lane >> 4;
   const int kl = 4 * cq;
   const int c = (kb - tap * kpt) * kKBlock + kl;
   const int N = a.rows_per_stream;
-  const float* cf = raw + box_bytes<kTconv>() / 4 + kl;
-  const float4 sc = lds4(cf), of = lds4(cf + 64), al = lds4(cf + 128), rc = lds4(cf + 192);
-  float4 v[8];
-  uint32_t raw_mask = 0;  // bit j: v[j] is a raw input row (needs affine + Snake)
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int r = 2 * (warp + 8 * j) + rs;
-    const int e = tab.row_e[r], t = tab.row_t[r];
-    v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (e >= 0) {
-      if (t - tap >= 0) {
-        v[j] = lds4(raw + (r + 1 - tap) * kKBlock + kl);
-        raw_mask |= 1u << j;
-      } else {
-        const float* h = hist_row(a, tab, e, -1);
-        if (h) v[j] = ldg4(h + c);
-      }
+  uint8_t* lo_tile = a_stage + kTileM * 128;
+  if (tap == 1) {
+#pragma unroll 1
+    for (int j = 0; j < 8; ++j) {
+      const int r = 2 * (warp + 8 * j) + rs;
+      const int e = tab.row_e[r];
+      if (e < 0 || tab.row_t[r] != 0) continue;
+      const float* h = hist_row(a, tab, e, -1);
+      uint4 bits = make_uint4(0u, 0u, 0u, 0u);
+      if (h) bits = __ldg(reinterpret_cast<const uint4*>(h + c));
+      const uint32_t off = sw128_offset(r, kl);
+      *reinterpret_cast<uint2*>(a_stage + off) =
+          make_uint2(__byte_perm(bits.x, bits.y, 0x7632), __byte_perm(bits.z, bits.w, 0x7632));
+      *reinterpret_cast<uint2*>(lo_tile + off) =
+          make_uint2(__byte_perm(bits.x, bits.y, 0x5410), __byte_perm(bits.z, bits.w, 0x5410));
     }
-  }
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int r = 2 * (warp + 8 * j) + rs;
-    float4 y = v[j];
-    if (raw_mask & (1u << j)) {
-      y = make_float4(__fadd_rn(__fmul_rn(y.x, sc.x), of.x), __fadd_rn(__fmul_rn(y.y, sc.y), of.y),
-                      __fadd_rn(__fmul_rn(y.z, sc.z), of.z), __fadd_rn(__fmul_rn(y.w, sc.w), of.w));
-      y = snake4(y, al, rc);
-      if (write_state && tap == 0 && a.state.pool) {
-        const int e = tab.row_e[r];
-        if (tab.row_t[r] == N - 1) {
-          const int code = tab.code[e], head = tab.head[e];
-          *reinterpret_cast<float4*>(hist_new_row(a.state, a.hist, code, head, N - 1, N) + c) = y;
-          if (cq == 0 && kb == 0) hist_commit_head(a.state, a.hist, code, head, N);
-        }
-      }
+  } else if (write_state && a.state.pool) {
+#pragma unroll 1
+    for (int j = 0; j < 8; ++j) {
+      const int r = 2 * (warp + 8 * j) + rs;
+      const int e = tab.row_e[r];
+      if (e < 0 || tab.row_t[r] != N - 1) continue;
+      const uint32_t off = sw128_offset(r, kl);
+      const uint2 hi = *reinterpret_cast<const uint2*>(a_stage + off);
+      const uint2 lo = *reinterpret_cast<const uint2*>(lo_tile + off);
+      const uint4 bits = make_uint4(__byte_perm(lo.x, hi.x, 0x5410), __byte_perm(lo.x, hi.x, 0x7632),
+                                    __byte_perm(lo.y, hi.y, 0x5410), __byte_perm(lo.y, hi.y, 0x7632));
+      const int code = tab.code[e], head = tab.head[e];
+      *reinterpret_cast<uint4*>(hist_new_row(a.state, a.hist, code, head, N - 1, N) + c) = bits;
+      if (cq == 0 && kb == 0) hist_commit_head(a.state, a.hist, code, head, N);
     }
-    put_a4<MODE>(a_stage, r, kl, y);
   }
 }
 
-// Residual unit, K block kb: Snake -> depthwise causal k=7 (dilation d) ->
-// Snake. ``raw`` holds input rows m0-H .. m0+127 of the K block (pitch P);
-// phase 1 applies the first Snake in place; phase 2 walks each half-warp down
-// eight rows in residue-class order (packed in walk_lo/hi) so the seven taps
-// slide through registers, reloading them at stream starts. History = last 6d
-// Snake(x) rows [6d][C]. Depthwise taps come transposed, [7][C].
-// LPR lanes cover one row (16 for 64-channel K blocks, 8 for C = 32), so a
-// warp instruction covers 32/LPR rows and each lane group walks 16*LPR/32 rows.
+// Residual unit, K block kb: depthwise causal k=7 (dilation d) -> Snake on
+// s = Snake_pre(x), which the previous layer's epilogue wrote. ``raw`` holds s
+// rows m0-H .. m0+127 of the K block (pitch P) followed by the block's
+// coefficients [w0..w6, bias, alpha2, recip2][64]. Each lane group walks its
+// rows in residue-class order (packed in walk_lo/hi) so the seven taps slide
+// through registers; a regular chain (one stream, every tap inside the chunk)
+// runs branch-free. History = last 6d rows of s [6d][C]. LPR lanes cover one
+// row (16 for 64-channel K blocks, 8 for C = 32).
 template <int MODE, int LPR>
-__device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, float* raw, int warp,
+__device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, const float* raw, int warp,
                                  int lane, bool write_state, const StreamTable& tab, uint32_t walk_lo,
                                  uint32_t walk_hi, bool regular) {
-  constexpr int kRpi = 32 / LPR;   // rows per warp instruction
-  constexpr int kRpg = 16 / kRpi;  // rows walked per lane group
+  constexpr int kRpg = 16 * LPR / 32;  // rows walked per lane group
   const int C = a.k_channels;
   const int d = a.dilation;
   const int H = 6 * d;
   const int N = a.rows_per_stream;
   const int P = a.raw_pitch;
-  const int cq = lane % LPR, rs = lane / LPR;
+  const int cq = lane % LPR;
   const int kl = 4 * cq;
   const int c = kb * kKBlock + kl;
   const bool valid = kl < P;
   const int tid = warp * 32 + lane;
-  // Phase 1: raw[i] <- Snake(raw[i]) for the box rows i in [0, 128 + H).
-  const float* cf = raw + box_bytes<kResidual>() / 4 + kl;
-  if (valid) {
-    const float4 al = lds4(cf), rc = lds4(cf + 64);
-    const int rows = kTileM + H;
-#pragma unroll
-    for (int j = 0; j < (kTileM + kMaxHalo + 8 * kRpi - 1) / (8 * kRpi); ++j) {
-      const int i = kRpi * (warp + 8 * j) + rs;
-      if (i < rows) {
-        float4* p = reinterpret_cast<float4*>(raw + i * P + kl);
-        *p = snake4(*p, al, rc);
-      }
-    }
-  }
-  named_barrier(1, kProducerThreads);
+  const float* cf = raw + kResBoxBytes / 4 + kl;
   // New window rows of streams whose last row lies in this tile.
   if (write_state && a.state.pool) {
     const int g_end = min(m0 + kTileM, a.rows);
@@ -410,18 +391,13 @@ __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_
       if (tid == 0 && kb == 0) hist_commit_head(a.state, a.hist, code, head, N);
     }
   }
-  // Phase 2.
-  float4 w[7], bias, al2, rc2;
+  const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 w[7];
 #pragma unroll
-  for (int j = 0; j < 7; ++j) w[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-  bias = al2 = rc2 = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (valid) {
-#pragma unroll
-    for (int j = 0; j < 7; ++j) w[j] = lds4(cf + (2 + j) * 64);
-    bias = lds4(cf + 9 * 64);
-    al2 = lds4(cf + 10 * 64);
-    rc2 = lds4(cf + 11 * 64);
-  }
+  for (int j = 0; j < 7; ++j) w[j] = valid ? lds4(cf + j * 64) : zero4;
+  const float4 bias = valid ? lds4(cf + 7 * 64) : zero4;
+  const float4 al2 = valid ? lds4(cf + 8 * 64) : zero4;
+  const float4 rc2 = valid ? lds4(cf + 9 * 64) : zero4;
   float4 win[7];
   if (regular) {
     // The lane group's rows are r0, r0+d, ..., r0+(kRpg-1)d of one stream with
@@ -430,10 +406,10 @@ __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_
     const float* base = raw + (r0 - 6 * d + H) * P + kl;
     const int step = d * P;
 #pragma unroll
-    for (int j = 0; j < 6; ++j) win[j] = valid ? lds4(base + j * step) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < 6; ++j) win[j] = valid ? lds4(base + j * step) : zero4;
 #pragma unroll
     for (int u = 0; u < kRpg; ++u) {
-      win[6] = valid ? lds4(base + (6 + u) * step) : make_float4(0.f, 0.f, 0.f, 0.f);
+      win[6] = valid ? lds4(base + (6 + u) * step) : zero4;
       float4 h;
       h.x = w[0].x * win[0].x;
       h.y = w[0].y * win[0].y;
@@ -447,20 +423,20 @@ __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_
         h.w = fmaf(w[j].w, win[j].w, h.w);
       }
       h = make_float4(h.x + bias.x, h.y + bias.y, h.z + bias.z, h.w + bias.w);
-      put_a4<MODE>(a_stage, r0 + u * d, kl, valid ? snake4(h, al2, rc2) : make_float4(0.f, 0.f, 0.f, 0.f));
+      put_a4<MODE>(a_stage, r0 + u * d, kl, valid ? snake4(h, al2, rc2) : zero4);
 #pragma unroll
       for (int j = 0; j < 6; ++j) win[j] = win[j + 1];
     }
     return;
   }
 #pragma unroll
-  for (int j = 0; j < 7; ++j) win[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = 0; j < 7; ++j) win[j] = zero4;
   int prev_r = -1000000, prev_e = -2;
 #pragma unroll 1
   for (int u = 0; u < kRpg; ++u) {
     const int r = walk_row(walk_lo, walk_hi, u);
     const int e = tab.row_e[r];
-    float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 y = zero4;
     if (valid && e >= 0) {
       if (prev_r == r - d && prev_e == e) {
 #pragma unroll
@@ -474,8 +450,8 @@ __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_
           if (tp >= 0) {
             win[j] = lds4(raw + (r - back + H) * P + kl);
           } else {
-            const float* h = hist_row(a, tab, e, tp);
-            win[j] = h ? ldg4(h + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float* hr = hist_row(a, tab, e, tp);
+            win[j] = hr ? ldg4(hr + c) : zero4;
           }
         }
       }
@@ -517,12 +493,41 @@ __device__ void produce_test(const LayerArgs& a, int m0, int kb, uint8_t* a_stag
   for (int i = 0; i < 16; ++i) put_a<MODE>(a_stage, warp + 8 * i, 2 * lane, v[i].x, v[i].y);
 }
 
+// ------------------------------------------------------------------ epilogue
+// Boxes of one warp (32 rows, one row per lane): fp32 rows of 16 columns (64 B)
+// in the 64-byte swizzle, bf16 rows of 16 columns (32 B) in the 32-byte swizzle.
+__device__ __forceinline__ void box_put_f32(float* box, int row, const float (&v)[16]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    reinterpret_cast<float4*>(box + row * 16)[j ^ ((row >> 1) & 3)] =
+        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+__device__ __forceinline__ void box_put_bf16(uint32_t* box, int row, const uint32_t (&v)[8]) {
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+    reinterpret_cast<uint4*>(box + row * 8)[j ^ ((row >> 2) & 1)] =
+        make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+
+// Skip input of a residual unit: x[g][n .. n+15].
+template <int KIND>
+__device__ __forceinline__ void load_skip(const LayerArgs& a, int g, int n, float4 (&x)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) x[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (KIND == kResidual && g < a.rows) {
+    const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)g * a.c_out + n);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = __ldg(src + j);
+  }
+}
+
 // --------------------------------------------------------------------- engine
 template <int NT, int MODE, int KIND>
 __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_constant__ LayerArgs a) {
   using Cfg = GemmCfg<NT, MODE, KIND>;
   constexpr int S = Cfg::kStages;
-  constexpr bool kStaged = KIND == kTconv || KIND == kResidual;
+  constexpr bool kStaged = KIND == kResidual;
+  constexpr int kLpr = NT == 32 ? 8 : 16;  // residual lanes per row (C = 32 uses eight)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* a_base = smem;
@@ -533,16 +538,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   uint64_t* a_full = bars;
   uint64_t* b_full = bars + S;
   uint64_t* empty = bars + 2 * S;
-  uint64_t* acc_full = bars + 3 * S;       // [2]
-  uint64_t* acc_empty = bars + 3 * S + 2;  // [2]
-  uint64_t* raw_full = bars + 3 * S + 4;   // [2]
-  uint64_t* raw_empty = bars + 3 * S + 6;  // [2]
-  uint64_t* skip_full = bars + 3 * S + 8;     // [epilogue warp][2]
-  uint64_t* table_full = bars + 3 * S + 16;   // [2]
-  uint64_t* table_empty = bars + 3 * S + 18;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 20);
-  int* table = reinterpret_cast<int*>(bars + 3 * S + 22);
-  constexpr int kLpr = NT == 32 ? 8 : 16;  // residual lanes per row (C = 32 uses eight)
+  uint64_t* a_tma = bars + 3 * S;             // [S] transposed-conv A planes landed
+  uint64_t* acc_full = bars + 4 * S;          // [2]
+  uint64_t* acc_empty = bars + 4 * S + 2;     // [2]
+  uint64_t* raw_full = bars + 4 * S + 4;      // [2]
+  uint64_t* raw_empty = bars + 4 * S + 6;     // [2]
+  uint64_t* table_full = bars + 4 * S + 8;    // [2]
+  uint64_t* table_empty = bars + 4 * S + 10;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * S + 12);
+  int* table = reinterpret_cast<int*>(bars + 4 * S + 13);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_kb = a.num_kblocks;
@@ -554,15 +558,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       mbar_init(&a_full[s], kProducerWarps);
       mbar_init(&b_full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&a_tma[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], kEpilogueWarps);
       mbar_init(&raw_full[b], 1);
       mbar_init(&raw_empty[b], kProducerWarps);
-    }
-    for (int b = 0; b < 2 * kEpilogueWarps; ++b) mbar_init(&skip_full[b], 1);
-    for (int b = 0; b < 2; ++b) {
       mbar_init(&table_full[b], 1);
       mbar_init(&table_empty[b], kProducerWarps);
     }
@@ -583,7 +585,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       // C = 32: channels 32-63 of every A stage stay zero.
       for (int s = 0; s < S; ++s)
         for (int r = threadIdx.x; r < kTileM; r += kProducerThreads)
-          for (int k = 32; k < 64; k += 4) put_a4<MODE>(a_base + s * Cfg::kAStage, r, k, make_float4(0.f, 0.f, 0.f, 0.f));
+          for (int k = 32; k < 64; k += 4)
+            put_a4<MODE>(a_base + s * Cfg::kAStage, r, k, make_float4(0.f, 0.f, 0.f, 0.f));
     }
     uint32_t g = 0, ti = 0;
     bool ok = true;
@@ -599,9 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++ti) {
       const int m0 = (t % num_m) * kTileM;
       const bool write_state = t / num_m == 0;
-      int* tb = table + (ti & 1) * kTableInts;
-      StreamTable tab{tb, tb + kMaxTileStreams, tb + 2 * kMaxTileStreams, tb + 2 * kMaxTileStreams + kTileM,
-                      m0 / a.rows_per_stream};
+      const StreamTable tab = table_at(table + (ti & 1) * kTableInts, m0, a.rows_per_stream);
       bool regular = false;
       if (KIND != kTestGemm) {
         ok = named_barrier_and(2, kProducerThreads,
@@ -617,19 +618,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         const uint32_t ph = (g / S) & 1;
         const int rb = g & 1;
         // All producer threads leave together on a timeout, so none is left
-        // waiting at a named barrier inside a producer.
-        bool ready = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer);
+        // waiting at a named barrier inside a producer. A transposed conv waits
+        // for its TMA-loaded planes (issued after the stage was released).
+        bool ready = KIND == kTconv ? mbar_wait(&a_tma[s], ph, a.status, kDevTimeoutProducer)
+                                    : mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer);
         if (kStaged && ready) ready = mbar_wait(&raw_full[rb], (g >> 1) & 1, a.status, kDevTimeoutProducer);
         ok = named_barrier_and(2, kProducerThreads, ready);
         if (!ok) break;
         uint8_t* a_stage = a_base + s * Cfg::kAStage;
-        float* raw = reinterpret_cast<float*>(raw_base + rb * Cfg::kRaw);
-        if (KIND == kStem) produce_stem<MODE>(a, m0, a_stage, warp, lane, write_state, tab);
-        else if (KIND == kTconv) produce_tconv<MODE>(a, m0, kb, a_stage, raw, warp, lane, write_state, tab);
-        else if (KIND == kResidual)
-          produce_residual<MODE, kLpr>(a, m0, kb, a_stage, raw, warp, lane, write_state, tab, walk_lo, walk_hi,
-                                       regular);
-        else produce_test<MODE>(a, m0, kb, a_stage, warp, lane);
+        if (KIND == kStem) {
+          produce_stem<MODE>(a, a_stage, warp, lane, write_state, tab);
+        } else if (KIND == kTconv) {
+          patch_tconv(a, kb, a_stage, warp, lane, write_state, tab);
+        } else if (KIND == kResidual) {
+          produce_residual<MODE, kLpr>(a, m0, kb, a_stage, reinterpret_cast<const float*>(raw_base + rb * Cfg::kRaw),
+                                       warp, lane, write_state, tab, walk_lo, walk_hi, regular);
+        } else {
+          produce_test<MODE>(a, m0, kb, a_stage, warp, lane);
+        }
         fence_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -641,83 +647,104 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       if (KIND != kTestGemm && lane == 0) mbar_arrive(&table_empty[ti & 1]);
     }
   } else if (warp < kLoaderWarp) {
-    // ---- epilogue: per 32-column chunk, TMEM -> registers -> (+ bias, + skip)
-    // -> 128-byte-swizzled box in shared memory -> TMA store. Residual skip
-    // inputs are TMA-loaded into the same box (one chunk ahead when two boxes fit).
-    constexpr int kChunks = NT / 32;
+    // ---- epilogue: per 16-column chunk, TMEM -> registers -> bias (+ skip) ->
+    // next layer's pointwise prologue -> swizzled boxes -> TMA stores.
+    constexpr int kChunks = NT / kEpiCols;
     constexpr int kBufs = Cfg::kEpiBufs;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    float* boxes = reinterpret_cast<float*>(epi_base) + q * kBufs * 1024;
-    uint64_t* sbar = skip_full + 2 * q;
+    uint8_t* boxes = epi_base + q * kBufs * 2 * kEpiBox;
+    const int epi = a.epi;
     uint32_t i = 0, k = 0;  // tile and chunk counters
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
       const int buf = i & 1;
       const int m0 = (t % num_m) * kTileM, n0 = (t / num_m) * NT;
       const int row0 = m0 + q * 32;
-      auto issue_skip = [&](uint32_t kk, int col) {
-        mbar_arrive_expect_tx(&sbar[kk % kBufs], kEpiBoxBytes);
-        tma_load_2d(boxes + (kk % kBufs) * 1024, &a.tmap_skip, n0 + col, row0, &sbar[kk % kBufs]);
-      };
-      if (KIND == kResidual && kBufs == 2 && lane == 0) {
-        bulk_wait_read<0>();
-        issue_skip(k, 0);
-      }
+      const int g = row0 + lane;
+      float4 x[4];
+      load_skip<KIND>(a, g, n0, x);
       if (!mbar_wait(&acc_full[buf], (i >> 1) & 1, a.status, kDevTimeoutEpilogue)) break;
       tc_fence_after();
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * NT);
-      bool ok = true;
 #pragma unroll 1
       for (int c = 0; c < kChunks; ++c, ++k) {
-        float* box = boxes + (k % kBufs) * 1024;
-        if (lane == 0) {
+        const int n = n0 + c * kEpiCols;
+        float4 xn[4];  // next chunk's skip input, loaded while this chunk computes
+        load_skip<KIND>(a, c + 1 < kChunks ? g : a.rows, n + kEpiCols, xn);
+        float v[16];
+        tmem_ld16(base + c * kEpiCols, v);
+        const int p = KIND == kTconv ? n / a.c_out : 0;
+        const int ch = n - p * a.c_out;  // output channel of column n
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (a.bias) b = ldg4(a.bias + ch + 4 * j);
+          v[4 * j] += b.x;
+          v[4 * j + 1] += b.y;
+          v[4 * j + 2] += b.z;
+          v[4 * j + 3] += b.w;
           if (KIND == kResidual) {
-            if (kBufs == 2) {
-              if (c + 1 < kChunks) {
-                bulk_wait_read<0>();
-                issue_skip(k + 1, (c + 1) * 32);
-              }
-            } else {
-              bulk_wait_read<0>();
-              issue_skip(k, c * 32);
-            }
-          } else if (kBufs == 2) {
-            bulk_wait_read<1>();
-          } else {
-            bulk_wait_read<0>();
+            v[4 * j] = x[j].x + v[4 * j];
+            v[4 * j + 1] = x[j].y + v[4 * j + 1];
+            v[4 * j + 2] = x[j].z + v[4 * j + 2];
+            v[4 * j + 3] = x[j].w + v[4 * j + 3];
           }
         }
-        __syncwarp();
-        if (KIND == kResidual && !(ok = mbar_wait(&sbar[k % kBufs], (k / kBufs) & 1, a.status, kDevTimeoutEpilogue)))
-          break;
-        float v[32];
-        tmem_ld32(base + c * 32, v);
-        const int n = n0 + c * 32;
-        const int bias_col = KIND == kTconv ? n % a.c_out : n;
+        float s[16];
+        if (epi & (kEpiS | kEpiPlanes)) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (a.bias) b = ldg4(a.bias + bias_col + 4 * j);
-          float4* p = reinterpret_cast<float4*>(box + lane * 32 + ((j ^ (lane & 7)) << 2));
-          float4 o = make_float4(v[4 * j] + b.x, v[4 * j + 1] + b.y, v[4 * j + 2] + b.z, v[4 * j + 3] + b.w);
-          if (KIND == kResidual) {
-            const float4 x = *p;
-            o = make_float4(x.x + o.x, x.y + o.y, x.z + o.z, x.w + o.w);
+          for (int j = 0; j < 4; ++j) {
+            float4 u = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            if (epi & kEpiPlanes) {
+              const float4 sc = ldg4(a.next_scale + ch + 4 * j), of = ldg4(a.next_offset + ch + 4 * j);
+              u = make_float4(__fadd_rn(__fmul_rn(u.x, sc.x), of.x), __fadd_rn(__fmul_rn(u.y, sc.y), of.y),
+                              __fadd_rn(__fmul_rn(u.z, sc.z), of.z), __fadd_rn(__fmul_rn(u.w, sc.w), of.w));
+            }
+            u = snake4(u, ldg4(a.next_alpha + ch + 4 * j), ldg4(a.next_recip + ch + 4 * j));
+            s[4 * j] = u.x;
+            s[4 * j + 1] = u.y;
+            s[4 * j + 2] = u.z;
+            s[4 * j + 3] = u.w;
           }
-          *p = o;
+        }
+        float* box_x = reinterpret_cast<float*>(boxes + (k % kBufs) * 2 * kEpiBox);
+        float* box_s = box_x + kEpiBox / 4;
+        // The boxes of this buffer are free once the stores issued from them
+        // kBufs chunks ago have read them.
+        if (lane == 0) {
+          if (kBufs == 2) bulk_wait_read<1>();
+          else bulk_wait_read<0>();
+        }
+        __syncwarp();
+        if (epi & kEpiX) box_put_f32(box_x, lane, v);
+        if (epi & kEpiPlanes) {
+          uint32_t hi[8], lo[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) split_bf16(s[2 * j], s[2 * j + 1], hi[j], lo[j]);
+          box_put_bf16(reinterpret_cast<uint32_t*>(box_s), lane, hi);
+          box_put_bf16(reinterpret_cast<uint32_t*>(box_s) + kEpiBox / 8, lane, lo);
+        } else if (epi & kEpiS) {
+          box_put_f32(box_s, lane, s);
         }
         fence_async_smem();
         __syncwarp();
         if (lane == 0) {
           if (KIND == kTconv) {
-            const int ph = n / a.c_out;
-            tma_store_3d(&a.tmap_out, box, n - ph * a.c_out, ph, row0);
+            if (epi & kEpiX) tma_store_3d(&a.tmap_out, box_x, ch, p, row0);
+            if (epi & kEpiS) tma_store_3d(&a.tmap_out2, box_s, ch, p, row0);
           } else {
-            tma_store_2d(&a.tmap_out, box, n, row0);
+            if (epi & kEpiX) tma_store_2d(&a.tmap_out, box_x, n, row0);
+            if (epi & kEpiPlanes) {
+              tma_store_3d(&a.tmap_out2, box_s, n, row0, 0);
+              tma_store_3d(&a.tmap_out2, reinterpret_cast<uint8_t*>(box_s) + kEpiBox / 2, n, row0, 1);
+            } else if (epi & kEpiS) {
+              tma_store_2d(&a.tmap_out2, box_s, n, row0);
+            }
           }
           bulk_commit();
         }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[j] = xn[j];
       }
-      if (!ok) break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
@@ -738,12 +765,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           bulk_g2s(b_base + s * Cfg::kBStage, src + (size_t)kb * Cfg::kBStage, Cfg::kBStage, &b_full[s]);
         }
       }
-    } else if (lane == 1 && kStaged) {
-      // ---- input rows (tile + causal halo) of each K block
+    } else if (lane == 1 && KIND == kResidual) {
+      // ---- residual inputs: tile + causal halo rows of s, then the block's coefficients
       const int halo = a.box_rows - kTileM;
       const uint32_t bytes = (uint32_t)a.box_rows * a.raw_pitch * 4;
-      constexpr uint32_t kCoefBytes = coef_floats<KIND>() * 4;
-      const int kpt = KIND == kTconv ? a.k_channels / kKBlock : 1;
       uint32_t g = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
@@ -751,11 +776,29 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
           const int rb = g & 1;
           if (!(ok = mbar_wait(&raw_empty[rb], ((g >> 1) & 1) ^ 1, a.status, kDevTimeoutLoader))) break;
-          const int blk = KIND == kTconv ? kb % kpt : kb;
           uint8_t* dst = raw_base + rb * Cfg::kRaw;
-          mbar_arrive_expect_tx(&raw_full[rb], bytes + kCoefBytes);
-          tma_load_2d(dst, &a.tmap, blk * kKBlock, m0 - halo, &raw_full[rb]);
-          bulk_g2s(dst + box_bytes<KIND>(), a.coef + (size_t)blk * coef_floats<KIND>(), kCoefBytes, &raw_full[rb]);
+          mbar_arrive_expect_tx(&raw_full[rb], bytes + kResCoefBytes);
+          tma_load_2d(dst, &a.tmap, kb * kKBlock, m0 - halo, &raw_full[rb]);
+          bulk_g2s(dst + kResBoxBytes, a.coef + (size_t)kb * kCoefResidual * 64, kResCoefBytes, &raw_full[rb]);
+        }
+      }
+    } else if (lane == 1 && KIND == kTconv) {
+      // ---- transposed-conv A planes: tap 0 from rows m0, tap 1 from rows m0 - 1
+      // (row -1 reads the zero fill; stream starts are patched by the producers).
+      const int kpt = a.k_channels / kKBlock;
+      uint32_t g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int m0 = (t % num_m) * kTileM;
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader))) break;
+          const int tap = kb / kpt, cb = kb - tap * kpt;
+          uint8_t* dst = a_base + s * Cfg::kAStage;
+          mbar_arrive_expect_tx(&a_tma[s], 2 * kTileM * 128);
+          tma_load_3d(dst, &a.tmap, cb * kKBlock, m0 - tap, 0, &a_tma[s]);
+          tma_load_3d(dst + kTileM * 128, &a.tmap, cb * kKBlock, m0 - tap, 1, &a_tma[s]);
         }
       }
     }
@@ -766,10 +809,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++ti) {
         const int m0 = (t % num_m) * kTileM;
         if (!mbar_wait(&table_empty[ti & 1], ((ti >> 1) & 1) ^ 1, a.status, kDevTimeoutProducer)) break;
-        int* tb = table + (ti & 1) * kTableInts;
-        StreamTable tab{tb, tb + kMaxTileStreams, tb + 2 * kMaxTileStreams, tb + 2 * kMaxTileStreams + kTileM,
-                        m0 / a.rows_per_stream};
-        fill_table(a, m0, tab, lane);
+        fill_table(a, m0, table_at(table + (ti & 1) * kTableInts, m0, a.rows_per_stream), lane);
         __syncwarp();
         if (lane == 0) mbar_arrive(&table_full[ti & 1]);
       }
@@ -835,19 +875,10 @@ static cudaError_t set_smem() {
                               Cfg::kSmem);
 }
 
-// N tiles instantiated per layer kind: the split transposed conv keeps two
-// 64 KB stages next to its double-buffered input rows, so it stops at 128.
-template <int KIND>
-constexpr int max_nt() {
-  return KIND == kTconv ? 128 : 256;
-}
-
 template <int MODE, int KIND>
 static cudaError_t set_smem_all() {
   cudaError_t e;
-  if constexpr (max_nt<KIND>() >= 256) {
-    if ((e = set_smem<256, MODE, KIND>()) != cudaSuccess) return e;
-  }
+  if ((e = set_smem<256, MODE, KIND>()) != cudaSuccess) return e;
   if ((e = set_smem<128, MODE, KIND>()) != cudaSuccess) return e;
   if ((e = set_smem<64, MODE, KIND>()) != cudaSuccess) return e;
   return set_smem<32, MODE, KIND>();
@@ -856,9 +887,7 @@ static cudaError_t set_smem_all() {
 template <int MODE, int KIND>
 static cudaError_t launch_nt(const LayerArgs& a, cudaStream_t stream) {
   switch (a.n_tile) {
-    case 256:
-      if constexpr (max_nt<KIND>() >= 256) return launch_cfg<256, MODE, KIND>(a, stream);
-      return cudaErrorInvalidValue;
+    case 256: return launch_cfg<256, MODE, KIND>(a, stream);
     case 128: return launch_cfg<128, MODE, KIND>(a, stream);
     case 64: return launch_cfg<64, MODE, KIND>(a, stream);
     case 32: return launch_cfg<32, MODE, KIND>(a, stream);
@@ -896,9 +925,10 @@ cudaError_t launch_gemm_layer(const LayerArgs& a, cudaStream_t stream) {
 }
 
 // ------------------------------------------------------------------ final conv
-// Snake(32) -> causal conv 32->1 (k=7) -> tanh on CUDA cores. 256 output rows
-// per block; Snake values for the rows and a 6-row halo staged in shared memory.
-// A stream has at least 1920 rows here, so a block touches at most two streams.
+// Causal conv 32->1 (k=7) -> tanh on CUDA cores over s = Snake_final(y), which
+// the last residual unit's epilogue wrote. 256 output rows per block with a
+// 6-row halo staged in shared memory; a stream has at least 1920 rows here, so
+// a block touches at most two streams. History = last six rows of s [6][32].
 constexpr int kFinalRows = 256;
 constexpr int kFinalPitch = 33;
 constexpr int kFinalLoads = ((kFinalRows + 6) * kFinalChannels + kFinalRows - 1) / kFinalRows;
@@ -914,7 +944,6 @@ __global__ void __launch_bounds__(kFinalRows) final_kernel(const FinalArgs a) {
   const int N = a.rows_per_stream;
   for (int i = threadIdx.x; i < kFinalChannels * 7; i += kFinalRows) wsm[i] = __ldg(a.w + i);
   const int ch = threadIdx.x & (kFinalChannels - 1);
-  const float al = __ldg(a.alpha + ch), rc = __ldg(a.recip + ch);
   {
     float v[kFinalLoads];
 #pragma unroll
@@ -928,13 +957,13 @@ __global__ void __launch_bounds__(kFinalRows) final_kernel(const FinalArgs a) {
 #pragma unroll
     for (int j = 0; j < kFinalLoads; ++j) {
       const int i = threadIdx.x + j * kFinalRows;
-      if (i < (kFinalRows + 6) * kFinalChannels) act[(i / kFinalChannels) * kFinalPitch + ch] = snake(v[j], al, rc);
+      if (i < (kFinalRows + 6) * kFinalChannels) act[(i / kFinalChannels) * kFinalPitch + ch] = v[j];
     }
   }
   __syncthreads();
   const int g_end = min(g0 + kFinalRows, a.rows);
   const HistRef& h = a.hist;
-  // New window (last six activated rows) of streams ending in this block.
+  // New window (last six rows of s) of streams ending in this block.
   if (a.state.pool) {
     const int s_lo = g0 / N, s_hi = (g_end - 1) / N;
     for (int s = s_lo; s <= s_hi; ++s) {

@@ -235,7 +235,10 @@ def test_histories_hold_reference_values(lib, plan, oracle0):
 
     Pool layout: per slot, rings of 2H rows (channels last) for each history at
     twice its reference offset, then two head tables of 32 int32; a step from
-    read table 0 writes its heads to table 1.
+    read table 0 writes its heads to table 1. A transposed conv's one-row
+    history holds its activated input as the split-bf16 pair the MMA consumes,
+    packed per channel as (hi << 16) | lo; hi + lo is the fp32 value to 2^-16
+    relative.
     """
     z = W.seeded_latents(21, 3)
     pool = torch.zeros(lib.fav_state_pool_bytes(2) // 4, device="cuda")
@@ -260,6 +263,9 @@ def test_histories_hold_reference_values(lib, plan, oracle0):
         _, channels, rows = shape
         ring = rings[2 * off:2 * off + 2 * rows * channels].reshape(2 * rows, channels)
         window = ring[(heads[index] + np.arange(rows)) % (2 * rows)]
+        if name.endswith("transpose.history"):
+            bits = window.view(np.uint32)
+            window = (bits & 0xFFFF0000).view(np.float32) + (bits << 16).view(np.float32)
         got = window.T[None]
         ref = states[name].numpy()
         scale = max(1.0, float(np.abs(ref).max()))
