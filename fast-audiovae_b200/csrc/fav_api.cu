@@ -78,30 +78,14 @@ int32_t encode_input_map(CUtensorMap* map, const float* x, int rows, int channel
   return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_NONE, "input");
 }
 
-// Epilogue output y or Snake(y), fp32, viewed as [rows][channels] or, with
-// phases > 1 (a transposed conv's interleaved output), [rows][phases][channels];
-// written in boxes of 16 channels x 32 rows, 64-byte swizzle.
-int32_t encode_out_map(CUtensorMap* map, const float* base, int rows, int channels, int phases) {
-  if (phases > 1) {
-    const cuuint64_t dims[3] = {(cuuint64_t)channels, (cuuint64_t)phases, (cuuint64_t)rows};
-    const cuuint32_t box[3] = {16, 1, 32};
-    return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, 3, dims, box, CU_TENSOR_MAP_SWIZZLE_64B,
-                      "output");
-  }
-  const cuuint64_t dims[2] = {(cuuint64_t)channels, (cuuint64_t)rows};
-  const cuuint32_t box[2] = {16, 32};
-  return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_64B, "output");
-}
-
 // Split-bf16 planes [2][rows][channels] (hi, then lo) of a transposed conv's
-// activated input. The writer stores boxes of 16 channels x 32 rows (32-byte
-// swizzle); the transposed conv loads 64 x 128 boxes in the 128-byte swizzle,
-// which is the MMA's K-major A layout.
-int32_t encode_plane_map(CUtensorMap* map, const void* planes, int rows, int channels, bool load) {
+// activated input, loaded in 64 x 128 x 2 boxes (hi tile, then lo tile) in the
+// 128-byte swizzle, which is the MMA's K-major A layout.
+int32_t encode_plane_map(CUtensorMap* map, const void* planes, int rows, int channels) {
   const cuuint64_t dims[3] = {(cuuint64_t)channels, (cuuint64_t)rows, 2};
-  const cuuint32_t store_box[3] = {16, 32, 1}, load_box[3] = {(cuuint32_t)fav::kKBlock, (cuuint32_t)fav::kTileM, 1};
-  return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, planes, 3, dims, load ? load_box : store_box,
-                    load ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B, "planes");
+  const cuuint32_t box[3] = {(cuuint32_t)fav::kKBlock, (cuuint32_t)fav::kTileM, 2};
+  return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, planes, 3, dims, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                    "planes");
 }
 
 std::once_flag g_prepare_once;
@@ -301,8 +285,8 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
 // Workspace regions of one step, each n_streams * frames * 61440 floats (the
 // largest activation, [rows][channels], of any layer): y and Snake(y) of the
 // residual chain in ping-pong pairs, and the split-bf16 planes a transposed
-// conv reads.
-constexpr int kWorkspaceRegions = 5;
+// conv reads for its two taps (rows as they are, and one time step later).
+constexpr int kWorkspaceRegions = 6;
 constexpr size_t kRegionFloatsPerFrame = 61440;
 
 // Launches the 26 kernels of one decoder step. Layers are numbered 0 (stem),
@@ -321,7 +305,12 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
   const size_t region = (size_t)n_streams * frames * kRegionFloatsPerFrame;
   float* X[2] = {ws, ws + region};
   float* S[2] = {ws + 2 * region, ws + 3 * region};
-  float* planes = ws + 4 * region;
+  uint16_t* planes = reinterpret_cast<uint16_t*>(ws + 4 * region);       // [2][rows][C] bf16
+  uint16_t* planes_prev = reinterpret_cast<uint16_t*>(ws + 5 * region);  // row t holds time step t - 1
+  auto tconv_hist = [p](int i) {
+    const StageDev& st = p->stages[i];
+    return fav::HistRef{1 + 4 * i, 2 * st.state_t, 1, st.c_in};
+  };
   int32_t es = FAV_OK;
   cudaError_t e = cudaSuccess;
   // stem: depthwise k=7 -> 1x1 64->2048; epilogue writes stage 0's activated planes.
@@ -352,9 +341,10 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     a.next_alpha = next.alpha;
     a.next_recip = next.recip;
     a.hist = fav::HistRef{0, 0, 6, fav::kLatentChannels};
-    es = encode_out_map(&a.tmap_out, X[0], a.rows, 2048, 1);
-    if (es == FAV_OK) es = encode_plane_map(&a.tmap_out2, planes, a.rows, 2048, false);
-    if (es != FAV_OK) return es;
+    a.out_x = X[0];
+    a.out_planes = planes;
+    a.out_planes_prev = planes_prev;
+    a.hist_next = tconv_hist(0);
     if ((e = fav::launch_gemm_layer(a, stream)) != cudaSuccess) return cuda_fail(e, "stem launch");
   }
   int layer = 0;
@@ -383,10 +373,10 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     t.next_recip = st.res[0].pre_r;
     t.wimg = st.timg;
     t.hist = fav::HistRef{1 + 4 * i, 2 * st.state_t, 1, st.c_in};
-    es = encode_plane_map(&t.tmap, planes, t.rows, st.c_in, true);
-    if (es == FAV_OK) es = encode_out_map(&t.tmap_out, X[0], t.rows, st.c_out, st.rate);
-    if (es == FAV_OK) es = encode_out_map(&t.tmap_out2, S[0], t.rows, st.c_out, st.rate);
-    if (es != FAV_OK) return es;
+    t.out_x = X[0];
+    t.out_s = S[0];
+    if ((es = encode_plane_map(&t.tmap, planes, t.rows, st.c_in)) != FAV_OK) return es;
+    if ((es = encode_plane_map(&t.tmap2, planes_prev, t.rows, st.c_in)) != FAV_OK) return es;
     if ((e = fav::launch_gemm_layer(t, stream)) != cudaSuccess) return cuda_fail(e, "transpose launch");
     n *= st.rate;
     if (last_out) *last_out = X[0];
@@ -430,17 +420,17 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
         u.next_offset = nx.offset;
         u.next_alpha = nx.alpha;
         u.next_recip = nx.recip;
+        u.hist_next = tconv_hist(i + 1);
       } else {
         u.epi = fav::kEpiS | (debug_y ? fav::kEpiX : 0);
         u.next_alpha = p->fin_a;
         u.next_recip = p->fin_r;
       }
-      es = encode_input_map(&u.tmap, S[in], u.rows, st.c_out, u.box_rows);
-      if (es == FAV_OK) es = encode_out_map(&u.tmap_out, X[out], u.rows, st.c_out, 1);
-      if (es == FAV_OK)
-        es = (u.epi & fav::kEpiPlanes) ? encode_plane_map(&u.tmap_out2, planes, u.rows, st.c_out, false)
-                                       : encode_out_map(&u.tmap_out2, S[out], u.rows, st.c_out, 1);
-      if (es != FAV_OK) return es;
+      u.out_x = X[out];
+      u.out_s = S[out];
+      u.out_planes = planes;
+      u.out_planes_prev = planes_prev;
+      if ((es = encode_input_map(&u.tmap, S[in], u.rows, st.c_out, u.box_rows)) != FAV_OK) return es;
       if ((e = fav::launch_gemm_layer(u, stream)) != cudaSuccess) return cuda_fail(e, "residual launch");
       if (last_out) *last_out = X[out];
       mark(++layer + 1);
@@ -475,7 +465,7 @@ bool overflow_mul(size_t a, size_t b, size_t* out) {
 // Step workspace for fav_step_static, for callers that cannot allocate device
 // memory (a real-time audio callback, a host that forbids cudaMalloc after
 // start-up). It lives in this file-scope device array, so every GPU that loads
-// the library holds FAV_STATIC_MAX_FRAMES * 5 * 61440 floats (18.75 MiB) until
+// the library holds FAV_STATIC_MAX_FRAMES * 6 * 61440 floats (22.5 MiB) until
 // the process exits. Host code must not use the array's name as a device
 // address; fav_step_static looks the address up once per device.
 __device__ __align__(256) float g_static_workspace[(size_t)FAV_STATIC_MAX_FRAMES * kWorkspaceRegions *
@@ -736,11 +726,7 @@ int32_t fav_test_gemm(const float* a, int32_t m, int32_t k, const float* b, int3
   la.wimg = static_cast<const uint8_t*>(dimg);
   la.status = dstatus;
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
-  if (encode_out_map(&la.tmap_out, c, m, n, 1) != FAV_OK) {
-    cudaFree(dimg);
-    cudaFree(dstatus);
-    return FAV_DEVICE_ERROR;
-  }
+  la.out_x = c;
   e = fav::launch_gemm_layer(la, stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
   uint32_t hs = 0;

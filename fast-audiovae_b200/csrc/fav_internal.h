@@ -59,18 +59,25 @@ struct HistRef {
 // a residual unit). The epilogue also applies the next layer's pointwise
 // prologue, so the next producer only does the work that needs neighbouring rows.
 enum EpilogueFlags : int {
-  kEpiX = 2,       // y (fp32) through tmap_out
-  kEpiS = 4,       // Snake(y) with next_alpha/next_recip (fp32) through tmap_out2
-  kEpiPlanes = 8,  // split-bf16 hi/lo planes of Snake(y * next_scale + next_offset) through tmap_out2
+  kEpiX = 2,       // y (fp32) to out_x
+  kEpiS = 4,       // Snake(y) with next_alpha/next_recip (fp32) to out_s
+  kEpiPlanes = 8,  // split-bf16 hi/lo planes of Snake(y * next_scale + next_offset) to out_planes, the
+                   // same planes one row later per stream to out_planes_prev (row t holds t - 1; a
+                   // stream's first row holds the next layer's history), and the next layer's history
 };
 
 struct LayerArgs {
-  CUtensorMap tmap;       // producer input. Residual: s [rows][k] fp32, boxes of min(k, 64) channels x
-                          // box_rows rows. Transposed conv: planes [2][rows][k] bf16, boxes of 64 x 128 x 1
-                          // in the 128-byte swizzle (the MMA's A layout).
-  CUtensorMap tmap_out;   // y: [rows][c] fp32 (transposed conv: [rows][stride][c]), 16 x 32 boxes, 64-byte swizzle
-  CUtensorMap tmap_out2;  // Snake(y), same shape as tmap_out; or planes [2][rows][c] bf16, 16 x 32 x 1 boxes,
-                          // 32-byte swizzle
+  CUtensorMap tmap;   // producer input. Residual: s [rows][k] fp32, boxes of min(k, 64) channels x
+                      // box_rows rows. Transposed conv: tap-0 planes [2][rows][k] bf16, boxes of
+                      // 64 x 128 x 2 in the 128-byte swizzle (the MMA's A layout, hi tile then lo tile).
+  CUtensorMap tmap2;  // transposed conv: tap-1 planes (each row holds the previous time step)
+  // Epilogue outputs: y and Snake(y) as [rows][c] fp32 ([rows][stride][c] for a transposed conv);
+  // planes as [2][rows][c] bf16 (hi, then lo).
+  float* out_x;
+  float* out_s;
+  uint16_t* out_planes;
+  uint16_t* out_planes_prev;
+  HistRef hist_next;  // history of the layer that reads out_planes (its previous activated input)
   int kind;
   int mode;
   int epi;              // EpilogueFlags

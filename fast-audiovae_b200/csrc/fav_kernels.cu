@@ -15,15 +15,17 @@
 //     residual unit, whose producers then run depthwise k=7 + Snake only;
 //   last residual unit of stage 5 -> Snake_final(y) for the final conv.
 //
-// Warp roles (480 threads):
+// Warp roles (512 threads):
 //   warps 0-7   A-operand producers (stem depthwise conv; residual depthwise
 //               conv + Snake from a TMA-staged box; transposed-conv patches)
 //   warps 8-11  epilogue: TMEM -> registers -> bias / skip / next prologue ->
-//               swizzled boxes in shared memory -> TMA stores
-//   warp 12     loaders: lane 0 weight tiles (bulk copies), lane 1 producer
-//               inputs (residual boxes + coefficient blocks, transposed-conv planes)
+//               global stores, one output row per lane
+//   warp 12     loader: weight tiles (bulk copies) and transposed-conv planes
 //   warp 13     TMEM owner and MMA issuer (tcgen05.mma, one elected lane)
 //   warp 14     scheduler: per-tile stream/row tables, one tile ahead
+//   warp 15     residual input loader (TMA boxes + coefficient blocks)
+// Each single-thread role has a warp of its own, so no role's spin-wait
+// delays another's issue.
 // Every wait is bounded and records an error code in the caller's status word
 // instead of hanging.
 #include "fav_device.cuh"
@@ -33,17 +35,17 @@ namespace fav {
 
 constexpr int kProducerWarps = 8;
 constexpr int kEpilogueWarps = 4;
-constexpr int kThreads = (kProducerWarps + kEpilogueWarps + 3) * 32;
+constexpr int kThreads = (kProducerWarps + kEpilogueWarps + 4) * 32;
 constexpr int kProducerThreads = kProducerWarps * 32;
 constexpr int kLoaderWarp = kProducerWarps + kEpilogueWarps;
 constexpr int kMmaWarp = kLoaderWarp + 1;
 constexpr int kSchedWarp = kMmaWarp + 1;
+constexpr int kRawWarp = kSchedWarp + 1;
 constexpr int kSmemBudget = 227 * 1024;
 constexpr int kMaxHalo = 54;                 // 6 * largest dilation
 constexpr int kMaxTileStreams = kTileM + 1;  // streams one 128-row tile can touch
 constexpr int kTableInts = 2 * kMaxTileStreams + 2 * kTileM;  // one tile's stream and row tables
 constexpr int kEpiCols = 16;                 // epilogue chunk: 16 columns x 32 rows per warp
-constexpr int kEpiBox = kEpiCols * 32 * 4;   // one fp32 box; the bf16 hi/lo pair fits in one too
 
 // Residual producer input of one K block: the TMA box (tile + halo rows of 64
 // channels) followed by the block's coefficients.
@@ -61,12 +63,8 @@ struct GemmCfg {
   static constexpr int kRaw = KIND == kResidual ? kResBoxBytes + kResCoefBytes : 0;
   static constexpr int kTable = KIND == kTestGemm ? 0 : 2 * ((kTableInts * 4 + 15) / 16) * 16;  // two tiles
   static constexpr int kFixed = 1024 /*align slack*/ + 512 /*barriers*/ + kTable;
-  // Epilogue staging per warp and buffer: an fp32 box for y and one for
-  // Snake(y) (or the bf16 hi/lo plane pair). Two buffers when they still
-  // leave two pipeline stages.
-  static constexpr int kEpiBuf = kEpilogueWarps * 2 * kEpiBox;
-  static constexpr int kEpiBufs = (kSmemBudget - 2 * kRaw - kFixed - 2 * kEpiBuf) / kStage >= 2 ? 2 : 1;
-  static constexpr int kEpi = kEpiBufs * kEpiBuf;
+  // Epilogue column coefficients, double-buffered per tile.
+  static constexpr int kEpi = 2 * 5 * NT * 4;
   static constexpr int kStagesFit = (kSmemBudget - 2 * kRaw - kFixed - kEpi) / kStage;
   static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
   static_assert(kStages >= 2, "pipeline needs two stages");
@@ -292,55 +290,6 @@ __device__ void produce_stem(const LayerArgs& a, uint8_t* a_stage, int warp, int
   }
 }
 
-// Transposed conv, virtual K block kb (tap 0 reads x[t], tap 1 reads x[t-1]):
-// the A stage already holds the split-bf16 planes of the activated input
-// Snake(x * scale + offset), TMA-loaded from rows m0 - tap. Rows whose tap
-// reaches before the chunk (t - tap < 0) take the history instead: the previous
-// activated input, kept as packed (hi << 16 | lo) bf16 bits per channel. Tap-0
-// blocks record that value for each stream's last row as the advanced history.
-// Lane = (row half rs, channel quad cq); lane rows 2*(warp + 8j) + rs.
-__device__ void patch_tconv(const LayerArgs& a, int kb, uint8_t* a_stage, int warp, int lane, bool write_state,
-                            const StreamTable& tab) {
-  const int kpt = a.k_channels / kKBlock;
-  const int tap = kb / kpt;
-  const int cq = lane & 15, rs = lane >> 4;
-  const int kl = 4 * cq;
-  const int c = (kb - tap * kpt) * kKBlock + kl;
-  const int N = a.rows_per_stream;
-  uint8_t* lo_tile = a_stage + kTileM * 128;
-  if (tap == 1) {
-#pragma unroll 1
-    for (int j = 0; j < 8; ++j) {
-      const int r = 2 * (warp + 8 * j) + rs;
-      const int e = tab.row_e[r];
-      if (e < 0 || tab.row_t[r] != 0) continue;
-      const float* h = hist_row(a, tab, e, -1);
-      uint4 bits = make_uint4(0u, 0u, 0u, 0u);
-      if (h) bits = __ldg(reinterpret_cast<const uint4*>(h + c));
-      const uint32_t off = sw128_offset(r, kl);
-      *reinterpret_cast<uint2*>(a_stage + off) =
-          make_uint2(__byte_perm(bits.x, bits.y, 0x7632), __byte_perm(bits.z, bits.w, 0x7632));
-      *reinterpret_cast<uint2*>(lo_tile + off) =
-          make_uint2(__byte_perm(bits.x, bits.y, 0x5410), __byte_perm(bits.z, bits.w, 0x5410));
-    }
-  } else if (write_state && a.state.pool) {
-#pragma unroll 1
-    for (int j = 0; j < 8; ++j) {
-      const int r = 2 * (warp + 8 * j) + rs;
-      const int e = tab.row_e[r];
-      if (e < 0 || tab.row_t[r] != N - 1) continue;
-      const uint32_t off = sw128_offset(r, kl);
-      const uint2 hi = *reinterpret_cast<const uint2*>(a_stage + off);
-      const uint2 lo = *reinterpret_cast<const uint2*>(lo_tile + off);
-      const uint4 bits = make_uint4(__byte_perm(lo.x, hi.x, 0x5410), __byte_perm(lo.x, hi.x, 0x7632),
-                                    __byte_perm(lo.y, hi.y, 0x5410), __byte_perm(lo.y, hi.y, 0x7632));
-      const int code = tab.code[e], head = tab.head[e];
-      *reinterpret_cast<uint4*>(hist_new_row(a.state, a.hist, code, head, N - 1, N) + c) = bits;
-      if (cq == 0 && kb == 0) hist_commit_head(a.state, a.hist, code, head, N);
-    }
-  }
-}
-
 // Residual unit, K block kb: depthwise causal k=7 (dilation d) -> Snake on
 // s = Snake_pre(x), which the previous layer's epilogue wrote. ``raw`` holds s
 // rows m0-H .. m0+127 of the K block (pitch P) followed by the block's
@@ -494,22 +443,7 @@ __device__ void produce_test(const LayerArgs& a, int m0, int kb, uint8_t* a_stag
 }
 
 // ------------------------------------------------------------------ epilogue
-// Boxes of one warp (32 rows, one row per lane): fp32 rows of 16 columns (64 B)
-// in the 64-byte swizzle, bf16 rows of 16 columns (32 B) in the 32-byte swizzle.
-__device__ __forceinline__ void box_put_f32(float* box, int row, const float (&v)[16]) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-    reinterpret_cast<float4*>(box + row * 16)[j ^ ((row >> 1) & 3)] =
-        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-}
-__device__ __forceinline__ void box_put_bf16(uint32_t* box, int row, const uint32_t (&v)[8]) {
-#pragma unroll
-  for (int j = 0; j < 2; ++j)
-    reinterpret_cast<uint4*>(box + row * 8)[j ^ ((row >> 2) & 1)] =
-        make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-}
-
-// Skip input of a residual unit: x[g][n .. n+15].
+// Skip input of a residual unit: x[g][n .. n+15] (zeros past the last row).
 template <int KIND>
 __device__ __forceinline__ void load_skip(const LayerArgs& a, int g, int n, float4 (&x)[4]) {
 #pragma unroll
@@ -520,6 +454,26 @@ __device__ __forceinline__ void load_skip(const LayerArgs& a, int g, int n, floa
     for (int j = 0; j < 4; ++j) x[j] = __ldg(src + j);
   }
 }
+
+__device__ __forceinline__ void st4(float* dst, const float (&v)[16]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    reinterpret_cast<float4*>(dst)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+
+// 16 bf16 of the hi plane at p and of the lo plane ``plane`` elements later.
+__device__ __forceinline__ void put_planes(uint16_t* p, size_t plane, const uint32_t (&hi)[8], const uint32_t (&lo)[8]) {
+  uint4* ph = reinterpret_cast<uint4*>(p);
+  uint4* pl = reinterpret_cast<uint4*>(p + plane);
+  ph[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  ph[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+  pl[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  pl[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+}
+
+// Per-column epilogue coefficients of one tile, staged in shared memory:
+// [bias, next_alpha, next_recip, next_scale, next_offset][NT].
+constexpr int kEpiCoefVectors = 5;
 
 // --------------------------------------------------------------------- engine
 template <int NT, int MODE, int KIND>
@@ -532,21 +486,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* a_base = smem;
   uint8_t* b_base = a_base + S * Cfg::kAStage;
-  uint8_t* epi_base = b_base + S * Cfg::kBStage;
-  uint8_t* raw_base = epi_base + Cfg::kEpi;
+  float* epi_coef = reinterpret_cast<float*>(b_base + S * Cfg::kBStage);  // [2][kEpiCoefVectors][NT]
+  uint8_t* raw_base = reinterpret_cast<uint8_t*>(epi_coef) + Cfg::kEpi;
   uint64_t* bars = reinterpret_cast<uint64_t*>(raw_base + 2 * Cfg::kRaw);
   uint64_t* a_full = bars;
   uint64_t* b_full = bars + S;
   uint64_t* empty = bars + 2 * S;
-  uint64_t* a_tma = bars + 3 * S;             // [S] transposed-conv A planes landed
-  uint64_t* acc_full = bars + 4 * S;          // [2]
-  uint64_t* acc_empty = bars + 4 * S + 2;     // [2]
-  uint64_t* raw_full = bars + 4 * S + 4;      // [2]
-  uint64_t* raw_empty = bars + 4 * S + 6;     // [2]
-  uint64_t* table_full = bars + 4 * S + 8;    // [2]
-  uint64_t* table_empty = bars + 4 * S + 10;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * S + 12);
-  int* table = reinterpret_cast<int*>(bars + 4 * S + 13);
+  uint64_t* acc_full = bars + 3 * S;          // [2]
+  uint64_t* acc_empty = bars + 3 * S + 2;     // [2]
+  uint64_t* raw_full = bars + 3 * S + 4;      // [2]
+  uint64_t* raw_empty = bars + 3 * S + 6;     // [2]
+  uint64_t* table_full = bars + 3 * S + 8;    // [2]
+  uint64_t* table_empty = bars + 3 * S + 10;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 12);
+  int* table = reinterpret_cast<int*>(bars + 3 * S + 13);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_kb = a.num_kblocks;
@@ -555,10 +508,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&a_full[s], kProducerWarps);
+      // A transposed conv's A operand is one TMA load (transaction count only).
+      mbar_init(&a_full[s], KIND == kTconv ? 1 : kProducerWarps);
       mbar_init(&b_full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&a_tma[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -580,7 +533,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   const uint32_t tmem = *tmem_slot;
 
   if (warp < kProducerWarps) {
-    // ---- A producers
+    // ---- A producers (a transposed conv has none: its A operand is TMA-loaded whole)
+    if (KIND == kTconv) goto done;
     if (KIND == kResidual && kLpr == 8) {
       // C = 32: channels 32-63 of every A stage stay zero.
       for (int s = 0; s < S; ++s)
@@ -618,18 +572,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         const uint32_t ph = (g / S) & 1;
         const int rb = g & 1;
         // All producer threads leave together on a timeout, so none is left
-        // waiting at a named barrier inside a producer. A transposed conv waits
-        // for its TMA-loaded planes (issued after the stage was released).
-        bool ready = KIND == kTconv ? mbar_wait(&a_tma[s], ph, a.status, kDevTimeoutProducer)
-                                    : mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer);
+        // waiting at a named barrier inside a producer.
+        bool ready = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer);
         if (kStaged && ready) ready = mbar_wait(&raw_full[rb], (g >> 1) & 1, a.status, kDevTimeoutProducer);
         ok = named_barrier_and(2, kProducerThreads, ready);
         if (!ok) break;
         uint8_t* a_stage = a_base + s * Cfg::kAStage;
         if (KIND == kStem) {
           produce_stem<MODE>(a, a_stage, warp, lane, write_state, tab);
-        } else if (KIND == kTconv) {
-          patch_tconv(a, kb, a_stage, warp, lane, write_state, tab);
         } else if (KIND == kResidual) {
           produce_residual<MODE, kLpr>(a, m0, kb, a_stage, reinterpret_cast<const float*>(raw_base + rb * Cfg::kRaw),
                                        warp, lane, write_state, tab, walk_lo, walk_hi, regular);
@@ -648,40 +598,94 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
     }
   } else if (warp < kLoaderWarp) {
     // ---- epilogue: per 16-column chunk, TMEM -> registers -> bias (+ skip) ->
-    // next layer's pointwise prologue -> swizzled boxes -> TMA stores.
+    // next layer's pointwise prologue -> global stores (one row per lane). The
+    // next chunk's TMEM load and skip input are in flight while a chunk computes.
     constexpr int kChunks = NT / kEpiCols;
-    constexpr int kBufs = Cfg::kEpiBufs;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    uint8_t* boxes = epi_base + q * kBufs * 2 * kEpiBox;
+    const int etid = threadIdx.x - kProducerThreads;
     const int epi = a.epi;
-    uint32_t i = 0, k = 0;  // tile and chunk counters
+    bool ok = true;
+    uint32_t i = 0;
+    int cbuf = 1, staged_n0 = -1;  // coefficient buffer in use and the N tile it holds
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
       const int buf = i & 1;
       const int m0 = (t % num_m) * kTileM, n0 = (t / num_m) * NT;
+      // Stage the column coefficients when the N tile changes, into the other
+      // buffer (every warp has passed the previous tile's barrier, so no warp
+      // still reads it); the barrier also makes every epilogue warp leave
+      // together after a timeout.
+      const bool restage = n0 != staged_n0;
+      if (restage) {
+        cbuf ^= 1;
+        staged_n0 = n0;
+      }
+      float* cf = epi_coef + cbuf * kEpiCoefVectors * NT;
+      for (int j = etid; restage && j < NT; j += kEpilogueWarps * 32) {
+        const int n = n0 + j;
+        const int ch = KIND == kTconv ? n % a.c_out : n;
+        cf[j] = a.bias ? __ldg(a.bias + ch) : 0.f;
+        if (epi & (kEpiS | kEpiPlanes)) {
+          cf[NT + j] = __ldg(a.next_alpha + ch);
+          cf[2 * NT + j] = __ldg(a.next_recip + ch);
+        }
+        if (epi & kEpiPlanes) {
+          cf[3 * NT + j] = __ldg(a.next_scale + ch);
+          cf[4 * NT + j] = __ldg(a.next_offset + ch);
+        }
+      }
+      if (!named_barrier_and(3, kEpilogueWarps * 32, ok)) break;
       const int row0 = m0 + q * 32;
       const int g = row0 + lane;
+      // Plane writers: this row's time step and, at a stream's first and last
+      // step, the next layer's history (old window row, new ring row).
+      int t_row = -1;
+      const uint32_t* hist_old = nullptr;
+      uint32_t* hist_new = nullptr;
+      int* head_out = nullptr;
+      int head_next = 0;
+      if ((epi & kEpiPlanes) && g < a.rows) {
+        const int N = a.rows_per_stream;
+        const int sid = g / N;
+        t_row = g - sid * N;
+        if (a.state.pool && (t_row == 0 || t_row == N - 1)) {
+          const int code = a.state.slot_codes ? a.state.slot_codes[sid] : ((sid << 2) | a.state.uniform_code);
+          float* slot = slot_base(a.state, code);
+          const HistRef& h = a.hist_next;  // one row (H = 1): window = ring row head
+          const int head = (code & 2) ? 0 : head_table(slot, code & 1)[h.index];
+          if (t_row == 0 && !(code & 2)) hist_old = reinterpret_cast<const uint32_t*>(slot + h.ring + head * h.width);
+          if (t_row == N - 1) {
+            hist_new = reinterpret_cast<uint32_t*>(slot + h.ring + (head ^ 1) * h.width);
+            if (n0 == 0) {
+              head_out = head_table(slot, (code & 1) ^ 1) + h.index;
+              head_next = head ^ 1;
+            }
+          }
+        }
+      }
       float4 x[4];
       load_skip<KIND>(a, g, n0, x);
-      if (!mbar_wait(&acc_full[buf], (i >> 1) & 1, a.status, kDevTimeoutEpilogue)) break;
+      if (!(ok = mbar_wait(&acc_full[buf], (i >> 1) & 1, a.status, kDevTimeoutEpilogue))) continue;
       tc_fence_after();
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * NT);
+      uint32_t r[16];
+      tmem_ld16_async(base, r);
+      tmem_wait_ld(r);
 #pragma unroll 1
-      for (int c = 0; c < kChunks; ++c, ++k) {
+      for (int c = 0; c < kChunks; ++c) {
         const int n = n0 + c * kEpiCols;
-        float4 xn[4];  // next chunk's skip input, loaded while this chunk computes
+        const int j0 = c * kEpiCols;
+        uint32_t rn[16];
+        if (c + 1 < kChunks) tmem_ld16_async(base + (c + 1) * kEpiCols, rn);
+        float4 xn[4];  // next chunk's skip input
         load_skip<KIND>(a, c + 1 < kChunks ? g : a.rows, n + kEpiCols, xn);
         float v[16];
-        tmem_ld16(base + c * kEpiCols, v);
-        const int p = KIND == kTconv ? n / a.c_out : 0;
-        const int ch = n - p * a.c_out;  // output channel of column n
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (a.bias) b = ldg4(a.bias + ch + 4 * j);
-          v[4 * j] += b.x;
-          v[4 * j + 1] += b.y;
-          v[4 * j + 2] += b.z;
-          v[4 * j + 3] += b.w;
+          const float4 b = lds4(cf + j0 + 4 * j);
+          v[4 * j] = __uint_as_float(r[4 * j]) + b.x;
+          v[4 * j + 1] = __uint_as_float(r[4 * j + 1]) + b.y;
+          v[4 * j + 2] = __uint_as_float(r[4 * j + 2]) + b.z;
+          v[4 * j + 3] = __uint_as_float(r[4 * j + 3]) + b.w;
           if (KIND == kResidual) {
             v[4 * j] = x[j].x + v[4 * j];
             v[4 * j + 1] = x[j].y + v[4 * j + 1];
@@ -689,67 +693,89 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
             v[4 * j + 3] = x[j].w + v[4 * j + 3];
           }
         }
-        float s[16];
-        if (epi & (kEpiS | kEpiPlanes)) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float4 u = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            if (epi & kEpiPlanes) {
-              const float4 sc = ldg4(a.next_scale + ch + 4 * j), of = ldg4(a.next_offset + ch + 4 * j);
-              u = make_float4(__fadd_rn(__fmul_rn(u.x, sc.x), of.x), __fadd_rn(__fmul_rn(u.y, sc.y), of.y),
-                              __fadd_rn(__fmul_rn(u.z, sc.z), of.z), __fadd_rn(__fmul_rn(u.w, sc.w), of.w));
-            }
-            u = snake4(u, ldg4(a.next_alpha + ch + 4 * j), ldg4(a.next_recip + ch + 4 * j));
-            s[4 * j] = u.x;
-            s[4 * j + 1] = u.y;
-            s[4 * j + 2] = u.z;
-            s[4 * j + 3] = u.w;
-          }
-        }
-        float* box_x = reinterpret_cast<float*>(boxes + (k % kBufs) * 2 * kEpiBox);
-        float* box_s = box_x + kEpiBox / 4;
-        // The boxes of this buffer are free once the stores issued from them
-        // kBufs chunks ago have read them.
-        if (lane == 0) {
-          if (kBufs == 2) bulk_wait_read<1>();
-          else bulk_wait_read<0>();
-        }
-        __syncwarp();
-        if (epi & kEpiX) box_put_f32(box_x, lane, v);
-        if (epi & kEpiPlanes) {
-          uint32_t hi[8], lo[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) split_bf16(s[2 * j], s[2 * j + 1], hi[j], lo[j]);
-          box_put_bf16(reinterpret_cast<uint32_t*>(box_s), lane, hi);
-          box_put_bf16(reinterpret_cast<uint32_t*>(box_s) + kEpiBox / 8, lane, lo);
-        } else if (epi & kEpiS) {
-          box_put_f32(box_s, lane, s);
-        }
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) {
+        if (g < a.rows) {
+          size_t off;  // element offset of (row g, column n) in the fp32 outputs
           if (KIND == kTconv) {
-            if (epi & kEpiX) tma_store_3d(&a.tmap_out, box_x, ch, p, row0);
-            if (epi & kEpiS) tma_store_3d(&a.tmap_out2, box_s, ch, p, row0);
+            const int p = n / a.c_out;
+            off = ((size_t)g * a.stride + p) * a.c_out + (n - p * a.c_out);
           } else {
-            if (epi & kEpiX) tma_store_2d(&a.tmap_out, box_x, n, row0);
+            off = (size_t)g * a.c_out + n;
+          }
+          if (epi & kEpiX) st4(a.out_x + off, v);
+          if (epi & (kEpiS | kEpiPlanes)) {
+            float s[16];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float4 u = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+              if (epi & kEpiPlanes) {
+                const float4 sc = lds4(cf + 3 * NT + j0 + 4 * j), of = lds4(cf + 4 * NT + j0 + 4 * j);
+                u = make_float4(__fadd_rn(__fmul_rn(u.x, sc.x), of.x), __fadd_rn(__fmul_rn(u.y, sc.y), of.y),
+                                __fadd_rn(__fmul_rn(u.z, sc.z), of.z), __fadd_rn(__fmul_rn(u.w, sc.w), of.w));
+              }
+              u = snake4(u, lds4(cf + NT + j0 + 4 * j), lds4(cf + 2 * NT + j0 + 4 * j));
+              s[4 * j] = u.x;
+              s[4 * j + 1] = u.y;
+              s[4 * j + 2] = u.z;
+              s[4 * j + 3] = u.w;
+            }
             if (epi & kEpiPlanes) {
-              tma_store_3d(&a.tmap_out2, box_s, n, row0, 0);
-              tma_store_3d(&a.tmap_out2, reinterpret_cast<uint8_t*>(box_s) + kEpiBox / 2, n, row0, 1);
-            } else if (epi & kEpiS) {
-              tma_store_2d(&a.tmap_out2, box_s, n, row0);
+              uint32_t hi[8], lo[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) split_bf16(s[2 * j], s[2 * j + 1], hi[j], lo[j]);
+              const size_t plane = (size_t)a.rows * a.c_out;
+              put_planes(a.out_planes + (size_t)g * a.c_out + n, plane, hi, lo);
+              if (t_row + 1 < a.rows_per_stream) {
+                put_planes(a.out_planes_prev + (size_t)(g + 1) * a.c_out + n, plane, hi, lo);
+              } else if (hist_new) {
+                // New history row, packed per channel as (hi << 16) | lo.
+                uint4* dst = reinterpret_cast<uint4*>(hist_new + n);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  dst[j] = make_uint4(__byte_perm(lo[2 * j], hi[2 * j], 0x5410), __byte_perm(lo[2 * j], hi[2 * j], 0x7632),
+                                      __byte_perm(lo[2 * j + 1], hi[2 * j + 1], 0x5410),
+                                      __byte_perm(lo[2 * j + 1], hi[2 * j + 1], 0x7632));
+              }
+              if (t_row == 0) {
+                // A stream's first row of the shifted planes: the previous activated input.
+                uint32_t w[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) w[j] = 0u;
+                if (hist_old) {
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    const uint4 u = __ldg(reinterpret_cast<const uint4*>(hist_old + n) + j);
+                    w[4 * j] = u.x;
+                    w[4 * j + 1] = u.y;
+                    w[4 * j + 2] = u.z;
+                    w[4 * j + 3] = u.w;
+                  }
+                }
+                uint32_t ho[8], lw[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  ho[j] = __byte_perm(w[2 * j], w[2 * j + 1], 0x7632);
+                  lw[j] = __byte_perm(w[2 * j], w[2 * j + 1], 0x5410);
+                }
+                put_planes(a.out_planes_prev + (size_t)g * a.c_out + n, plane, ho, lw);
+              }
+            } else {
+              st4(a.out_s + off, s);
             }
           }
-          bulk_commit();
+        }
+        if (c + 1 < kChunks) {
+          tmem_wait_ld(rn);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) r[j] = rn[j];
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) x[j] = xn[j];
       }
+      if (head_out) *head_out = head_next;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
-    if (lane == 0) bulk_wait<0>();
   } else if (warp == kLoaderWarp) {
     if (lane == 0) {
       // ---- weight tiles
@@ -765,7 +791,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           bulk_g2s(b_base + s * Cfg::kBStage, src + (size_t)kb * Cfg::kBStage, Cfg::kBStage, &b_full[s]);
         }
       }
-    } else if (lane == 1 && KIND == kResidual) {
+    }
+  } else if (warp == kRawWarp) {
+    if (lane == 0 && KIND == kTconv) {
+      // ---- transposed-conv A operand: tap 0 from the planes, tap 1 from the
+      // shifted planes, hi and lo tiles in one 3-D box
+      const int kpt = a.k_channels / kKBlock;
+      uint32_t g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int m0 = (t % num_m) * kTileM;
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader))) break;
+          const int tap = kb / kpt, cb = kb - tap * kpt;
+          mbar_arrive_expect_tx(&a_full[s], Cfg::kAStage);
+          tma_load_3d(a_base + s * Cfg::kAStage, tap ? &a.tmap2 : &a.tmap, cb * kKBlock, m0, 0, &a_full[s]);
+        }
+      }
+    } else if (lane == 0 && KIND == kResidual) {
       // ---- residual inputs: tile + causal halo rows of s, then the block's coefficients
       const int halo = a.box_rows - kTileM;
       const uint32_t bytes = (uint32_t)a.box_rows * a.raw_pitch * 4;
@@ -782,29 +827,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           bulk_g2s(dst + kResBoxBytes, a.coef + (size_t)kb * kCoefResidual * 64, kResCoefBytes, &raw_full[rb]);
         }
       }
-    } else if (lane == 1 && KIND == kTconv) {
-      // ---- transposed-conv A planes: tap 0 from rows m0, tap 1 from rows m0 - 1
-      // (row -1 reads the zero fill; stream starts are patched by the producers).
-      const int kpt = a.k_channels / kKBlock;
-      uint32_t g = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int m0 = (t % num_m) * kTileM;
-        for (int kb = 0; kb < num_kb; ++kb, ++g) {
-          const int s = g % S;
-          const uint32_t ph = (g / S) & 1;
-          if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader))) break;
-          const int tap = kb / kpt, cb = kb - tap * kpt;
-          uint8_t* dst = a_base + s * Cfg::kAStage;
-          mbar_arrive_expect_tx(&a_tma[s], 2 * kTileM * 128);
-          tma_load_3d(dst, &a.tmap, cb * kKBlock, m0 - tap, 0, &a_tma[s]);
-          tma_load_3d(dst + kTileM * 128, &a.tmap, cb * kKBlock, m0 - tap, 1, &a_tma[s]);
-        }
-      }
     }
   } else if (warp == kSchedWarp) {
     // ---- scheduler: per-tile stream/row tables, one tile ahead of the producers
-    if (KIND != kTestGemm) {
+    if (KIND == kStem || KIND == kResidual) {
       uint32_t ti = 0;
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++ti) {
         const int m0 = (t % num_m) * kTileM;
@@ -849,6 +875,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       }
     }
   }
+done:
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {

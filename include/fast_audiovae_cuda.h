@@ -137,7 +137,7 @@ FAV_API int32_t fav_step(const fav_plan *plan, float *state_pool, int32_t num_sl
  * hosts own all device memory and forbid allocation after start-up. The caller
  * still passes the plan, history pool, slot codes, latents and audio.
  * The step's scratch is a library-owned, file-scope device array sized for
- * n_streams * frames <= FAV_STATIC_MAX_FRAMES (18.75 MiB, held on every GPU
+ * n_streams * frames <= FAV_STATIC_MAX_FRAMES (22.5 MiB, held on every GPU
  * that loads the library until the process exits); larger calls are rejected
  * with FAV_SIZE_OVERFLOW. The first call on a device looks up that array's
  * device address (cudaGetSymbolAddress) with the device current; make that

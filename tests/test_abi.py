@@ -46,9 +46,9 @@ def test_abi_version_and_sizes(lib):
     assert lib.fav_abi_version() == 1
     assert lib.fav_state_pool_bytes(3) == 3 * (2 * 647424 + 256)
     assert lib.fav_state_pool_bytes(0) == 0
-    assert lib.fav_step_workspace_bytes(2, 3) == 2 * 3 * 5 * 61440 * 4
+    assert lib.fav_step_workspace_bytes(2, 3) == 2 * 3 * 6 * 61440 * 4
     assert lib.fav_step_workspace_bytes(0, 3) == 0
-    assert lib.fav_batch_workspace_bytes(2, 4) == 2 * 4 * 5 * 61440 * 4 + 2 * (2 * 647424 + 256)
+    assert lib.fav_batch_workspace_bytes(2, 4) == 2 * 4 * 6 * 61440 * 4 + 2 * (2 * 647424 + 256)
     assert lib.fav_status_string(6) == b"device wait timed out"
 
 
