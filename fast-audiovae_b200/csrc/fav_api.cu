@@ -366,6 +366,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     t.num_kblocks = 2 * st.c_in / fav::kKBlock;
     t.n_total = st.c_out * st.rate;
     t.n_tile = st.n_tile_t;
+    t.n_major = t.rows > t.n_total;  // A (both taps' planes) outweighs the weights
     t.c_out = st.c_out;
     t.stride = st.rate;
     t.bias = st.tbias;
@@ -399,6 +400,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       u.num_kblocks = st.c_out < fav::kKBlock ? 1 : st.c_out / fav::kKBlock;
       u.n_total = st.c_out;
       u.n_tile = r.n_tile;
+      u.n_major = 1;  // N tiles of one M tile share its input box in L2
       u.c_out = st.c_out;
       u.dilation = r.dilation;
       u.x = X[in];

@@ -87,6 +87,7 @@ struct LayerArgs {
   int num_kblocks;      // K blocks of the whole reduction (both taps for a transposed conv)
   int n_total;          // GEMM N
   int n_tile;           // GEMM N per CTA
+  int n_major;          // tile order: 0 = M tiles fastest (share weights), 1 = N tiles fastest (share A)
   int c_out;            // output channels
   int stride;           // transposed-conv rate
   int dilation;         // residual depthwise dilation

@@ -504,7 +504,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_kb = a.num_kblocks;
   const int num_m = (a.rows + kTileM - 1) / kTileM;
-  const int num_tiles = num_m * (a.n_total / NT);
+  const int num_n = a.n_total / NT;
+  const int num_tiles = num_m * num_n;
+  // Tile t -> (M tile, N tile): M fastest by default, so concurrently running
+  // CTAs share weight tiles in L2; N fastest when the A operand is the larger
+  // one, so they share A instead.
+  auto tile_m = [&](int t) { return a.n_major ? t / num_n : t % num_m; };
+  auto tile_n = [&](int t) { return a.n_major ? t % num_n : t / num_m; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -547,15 +553,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
     uint32_t walk_lo = 0, walk_hi = 0;
     constexpr int kRpg = 16 * kLpr / 32;
     bool chain = false;  // this lane group's rows form one arithmetic chain of step d
+    // A tile with empty rows (the last M tile, e.g. one stream) walks rows
+    // interleaved across the lane groups instead, so the valid rows spread
+    // over every warp.
+    uint32_t iwalk_lo = 0, iwalk_hi = 0;
     if (KIND == kResidual) {
+      constexpr int kGroups = kProducerThreads / kLpr;
+      const int grp = (warp * 32 + lane) / kLpr;
+      for (int u = 0; u < kRpg; ++u) {
+        const uint32_t r = grp + kGroups * u;
+        if (u < 4) iwalk_lo |= r << (8 * u);
+        else iwalk_hi |= r << (8 * (u - 4));
+      }
       class_rows(a.dilation, warp, lane / kLpr, kRpg, walk_lo, walk_hi);
       chain = true;
       for (int u = 1; u < kRpg; ++u)
         chain = chain && walk_row(walk_lo, walk_hi, u) == (int)(walk_lo & 255) + u * a.dilation;
     }
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++ti) {
-      const int m0 = (t % num_m) * kTileM;
-      const bool write_state = t / num_m == 0;
+      const int m0 = tile_m(t) * kTileM;
+      const bool write_state = tile_n(t) == 0;
       const StreamTable tab = table_at(table + (ti & 1) * kTableInts, m0, a.rows_per_stream);
       bool regular = false;
       if (KIND != kTestGemm) {
@@ -566,6 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           const int r0 = walk_lo & 255, rl = walk_row(walk_lo, walk_hi, kRpg - 1), e0 = tab.row_e[r0];
           regular = e0 >= 0 && e0 == tab.row_e[rl] && tab.row_t[r0] >= 6 * a.dilation;
         }
+        if (KIND == kResidual && a.rows - m0 < kTileM) regular = false;
       }
       for (int kb = 0; kb < num_kb; ++kb, ++g) {
         const int s = g % S;
@@ -581,8 +599,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         if (KIND == kStem) {
           produce_stem<MODE>(a, a_stage, warp, lane, write_state, tab);
         } else if (KIND == kResidual) {
+          const bool partial = a.rows - m0 < kTileM;
           produce_residual<MODE, kLpr>(a, m0, kb, a_stage, reinterpret_cast<const float*>(raw_base + rb * Cfg::kRaw),
-                                       warp, lane, write_state, tab, walk_lo, walk_hi, regular);
+                                       warp, lane, write_state, tab, partial ? iwalk_lo : walk_lo,
+                                       partial ? iwalk_hi : walk_hi, regular);
         } else {
           produce_test<MODE>(a, m0, kb, a_stage, warp, lane);
         }
@@ -609,7 +629,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
     int cbuf = 1, staged_n0 = -1;  // coefficient buffer in use and the N tile it holds
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
       const int buf = i & 1;
-      const int m0 = (t % num_m) * kTileM, n0 = (t / num_m) * NT;
+      const int m0 = tile_m(t) * kTileM, n0 = tile_n(t) * NT;
       // Stage the column coefficients when the N tile changes, into the other
       // buffer (every warp has passed the previous tile's barrier, so no warp
       // still reads it); the barrier also makes every epilogue warp leave
@@ -664,6 +684,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       }
       float4 x[4];
       load_skip<KIND>(a, g, n0, x);
+      uint4 hw[4];  // history bits of this chunk (zero without a history row)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        hw[j] = hist_old ? __ldg(reinterpret_cast<const uint4*>(hist_old + n0) + j) : make_uint4(0u, 0u, 0u, 0u);
       if (!(ok = mbar_wait(&acc_full[buf], (i >> 1) & 1, a.status, kDevTimeoutEpilogue))) continue;
       tc_fence_after();
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * NT);
@@ -678,6 +702,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         if (c + 1 < kChunks) tmem_ld16_async(base + (c + 1) * kEpiCols, rn);
         float4 xn[4];  // next chunk's skip input
         load_skip<KIND>(a, c + 1 < kChunks ? g : a.rows, n + kEpiCols, xn);
+        uint4 wn[4];  // next chunk's history bits (a plane writer's stream-start rows)
+        if (hist_old && c + 1 < kChunks) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) wn[j] = __ldg(reinterpret_cast<const uint4*>(hist_old + n + kEpiCols) + j);
+        }
         float v[16];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -739,16 +768,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
                 // A stream's first row of the shifted planes: the previous activated input.
                 uint32_t w[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) w[j] = 0u;
-                if (hist_old) {
-#pragma unroll
-                  for (int j = 0; j < 4; ++j) {
-                    const uint4 u = __ldg(reinterpret_cast<const uint4*>(hist_old + n) + j);
-                    w[4 * j] = u.x;
-                    w[4 * j + 1] = u.y;
-                    w[4 * j + 2] = u.z;
-                    w[4 * j + 3] = u.w;
-                  }
+                for (int j = 0; j < 4; ++j) {
+                  w[4 * j] = hw[j].x;
+                  w[4 * j + 1] = hw[j].y;
+                  w[4 * j + 2] = hw[j].z;
+                  w[4 * j + 3] = hw[j].w;
                 }
                 uint32_t ho[8], lw[8];
 #pragma unroll
@@ -770,6 +794,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) x[j] = xn[j];
+        if (hist_old && c + 1 < kChunks) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) hw[j] = wn[j];
+        }
       }
       if (head_out) *head_out = head_next;
       tc_fence_before();
@@ -782,7 +810,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       uint32_t g = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const uint8_t* src = a.wimg + (size_t)(t / num_m) * num_kb * Cfg::kBStage;
+        const uint8_t* src = a.wimg + (size_t)tile_n(t) * num_kb * Cfg::kBStage;
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
@@ -800,7 +828,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       uint32_t g = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int m0 = (t % num_m) * kTileM;
+        const int m0 = tile_m(t) * kTileM;
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
@@ -817,7 +845,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       uint32_t g = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int m0 = (t % num_m) * kTileM;
+        const int m0 = tile_m(t) * kTileM;
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
           const int rb = g & 1;
           if (!(ok = mbar_wait(&raw_empty[rb], ((g >> 1) & 1) ^ 1, a.status, kDevTimeoutLoader))) break;
@@ -833,7 +861,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
     if (KIND == kStem || KIND == kResidual) {
       uint32_t ti = 0;
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++ti) {
-        const int m0 = (t % num_m) * kTileM;
+        const int m0 = tile_m(t) * kTileM;
         if (!mbar_wait(&table_empty[ti & 1], ((ti >> 1) & 1) ^ 1, a.status, kDevTimeoutProducer)) break;
         fill_table(a, m0, table_at(table + (ti & 1) * kTableInts, m0, a.rows_per_stream), lane);
         __syncwarp();
