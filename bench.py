@@ -70,26 +70,47 @@ def peaks():
 # ------------------------------------------------------------------ algorithmic cost
 def layer_costs():
     """Per latent frame: algorithmic FLOPs (2*MAC of the layer's contraction) and
-    HBM bytes (fp32 activations in/out once), plus per-launch weight bytes and
-    per-stream history bytes (read + write)."""
+    HBM bytes of this design's data layout (each activation read and written
+    once), plus per-launch weight bytes and per-stream history bytes (read +
+    write). Activations: fp32 y and Snake(y) between residual units; the
+    split-bf16 planes a transposed conv reads, written twice (as they are, and
+    one time step later for the second tap)."""
     out = []
     n = 1  # rows per frame at the current layer input
-    out.append(dict(flops=2 * 2048 * 64, act=(64 + 2048) * 4, weights=2048 * 64 * 4, hist=6 * 64 * 4 * 2))
+    out.append(dict(flops=2 * 2048 * 64, act=64 * 4 + 2048 * 8, weights=2048 * 64 * 4,
+                    hist=6 * 64 * 4 * 2 + 2048 * 4 * 2))
     cin = 2048
     for i, s in enumerate(RATES):
         cout = cin // 2
-        out.append(dict(flops=2 * cin * cout * 2 * s * n, act=(n * cin + n * s * cout) * 4,
-                        weights=cin * cout * 2 * s * 4, hist=cin * 4 * 2))
+        out.append(dict(flops=2 * cin * cout * 2 * s * n, act=n * cin * 8 + n * s * cout * 8,
+                        weights=cin * cout * 2 * s * 4, hist=0))
         n *= s
-        for d in (1, 3, 9):
-            out.append(dict(flops=2 * cout * cout * n, act=2 * n * cout * 4, weights=cout * cout * 2,
-                            hist=6 * d * cout * 4 * 2))
+        for j, d in enumerate((1, 3, 9)):
+            last_out = 4 if (i == 5 and j == 2) else 8
+            nxt = 0 if (j < 2 or i == 5) else cout * 4 * 2  # next transposed conv's history row
+            out.append(dict(flops=2 * cout * cout * n, act=n * cout * 8 + n * cout * last_out, weights=cout * cout * 2,
+                            hist=6 * d * cout * 4 * 2 + nxt))
         cin = cout
     out.append(dict(flops=2 * 32 * 7 * n, act=(n * 32 + n) * 4, weights=0, hist=6 * 32 * 4 * 2))
     return out
 
 
-def roofline(layer_ms, frames_per_launch, streams, pk):
+def measured_traffic(layer, streams, frames):
+    """DRAM bytes (read + write) of one launch of ``layer`` from the committed
+    ncu launch list, which was captured on this workload (512 streams x 1 frame)."""
+    path = ROOT / "profiles" / "step_launches_stream40ms_512.md"
+    if streams != 512 or frames != 1 or not path.is_file():
+        return None
+    text = path.read_text()
+    block = text.split("```csv", 1)[-1].split("```", 1)[0]
+    for line in block.strip().splitlines()[1:]:
+        name, _, rd, wr = line.split(",")
+        if name == layer:
+            return int(rd) + int(wr)
+    return None
+
+
+def roofline(layer_ms, frames_per_launch, streams, pk, frames=1):
     costs = layer_costs()
     dom = int(np.argmax(layer_ms))
     c = costs[dom]
@@ -103,8 +124,12 @@ def roofline(layer_ms, frames_per_launch, streams, pk):
     else:
         achieved, peak, unit, bound = bytes_ / sec / 1e9, pk["hbm_gbs"], "GB/s", "hbm"
     share = float(layer_ms[dom] / np.sum(layer_ms))
+    traffic = measured_traffic(LAYER_NAMES[dom], streams, frames)
     return {"kernel": LAYER_NAMES[dom], "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
-            "frac": round(achieved / peak, 4), "traffic": None, "share_of_step": round(share, 4),
+            "frac": round(achieved / peak, 4), "traffic": traffic,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, "
+                              "profiles/step_launches_stream40ms_512.md" if traffic else None,
+            "share_of_step": round(share, 4),
             "algorithmic_per_launch": {"flops": flops, "bytes": bytes_}, "peak_source": pk["source"],
             "layer_ms": {LAYER_NAMES[i]: round(float(v), 4) for i, v in enumerate(layer_ms)}}
 
@@ -332,7 +357,7 @@ def run_ours(args, world, rank, local):
     result = None
     if rank == 0:
         pk = peaks()
-        rl = roofline(layer_ms, S * F, S, pk)
+        rl = roofline(layer_ms, S * F, S, pk, F)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cores = host_cores()
