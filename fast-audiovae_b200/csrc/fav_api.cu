@@ -4,6 +4,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -129,6 +130,51 @@ std::vector<uint16_t> pack_operand(int n_total, int k_total, int nt, int mode,
   return img;
 }
 
+// The reference's int8 weight quantisation (precision.cpp:82-92, ip_create
+// :370-376): one scale per matrix row, scale = max|w| / 127 (1 for a zero row,
+// max|w| when the quotient underflows), q = clamp(w / scale, -127, 127)
+// rounded half to even.
+float quant_scale_host(float mx) {
+  if (mx == 0.f) return 1.f;
+  const float s = mx / 127.f;
+  return s > 0.f ? s : mx;
+}
+int8_t quant_host(float v, float scale) {
+  float q = v / scale;
+  q = q < -127.f ? -127.f : (q > 127.f ? 127.f : q);
+  return static_cast<int8_t>(std::nearbyint(q));  // default rounding: half to even
+}
+
+// int8 weight operand: rows n of ``terms`` matrices value(term, n, k), each row
+// quantised with its own scale (scales[term * n_total + n]), packed as
+// [n_tile][kblock][term][NT rows][128 B] in the 128-byte swizzle (16-byte chunk
+// j of row r at chunk j ^ (r % 8)); K padded with zeros to a multiple of 128.
+std::vector<int8_t> pack_operand_i8(int n_total, int k_total, int nt, int terms,
+                                    const std::function<float(int, int, int)>& value, std::vector<float>& scales) {
+  const int kblocks = (k_total + fav::kKBlockI8 - 1) / fav::kKBlockI8;
+  const int ntiles = n_total / nt;
+  std::vector<int8_t> img((size_t)ntiles * kblocks * terms * nt * 128, 0);
+  scales.assign((size_t)terms * n_total, 1.f);
+  std::vector<float> row(k_total);
+  for (int term = 0; term < terms; ++term)
+    for (int n = 0; n < n_total; ++n) {
+      float mx = 0.f;
+      for (int k = 0; k < k_total; ++k) {
+        row[k] = value(term, n, k);
+        mx = std::fmax(mx, std::fabs(row[k]));
+      }
+      const float sc = quant_scale_host(mx);
+      scales[(size_t)term * n_total + n] = sc;
+      const int tile = n / nt, r = n % nt;
+      for (int k = 0; k < k_total; ++k) {
+        const int kb = k / fav::kKBlockI8, kk = k % fav::kKBlockI8;
+        const size_t base = (((size_t)tile * kblocks + kb) * terms + term) * nt * 128;
+        img[base + (size_t)r * 128 + ((((kk >> 4) ^ (r & 7)) << 4) | (kk & 15))] = quant_host(row[k], sc);
+      }
+    }
+  return img;
+}
+
 struct DeviceArrays {
   std::vector<void*> owned;
   size_t bytes = 0;
@@ -152,11 +198,15 @@ struct StageDev {
   const float *scale, *offset, *alpha, *recip, *tbias;
   const uint8_t* timg;
   int state_t;
+  bool int8 = false;                    // int8 plan and a selected transposed conv (W8A8)
+  const float *tsw = nullptr;           // int8: row scales [2][n_total] (current tap, previous tap)
   struct Res {
     int dilation, n_tile;
     const float *pre_a, *pre_r, *pw_b, *coef;
     const uint8_t* img;
     int state_off;
+    bool int8 = false;                  // int8 plan and a selected residual 1x1 (W8A8)
+    const float* sw = nullptr;          // int8: row scales [C]
   } res[3];
 };
 
@@ -167,9 +217,11 @@ struct fav_plan {
   DeviceArrays mem;
   const float *stem_w = nullptr, *stem_b = nullptr, *pw_b = nullptr;
   const uint8_t* stem_img = nullptr;
+  const float* stem_pw = nullptr;  // int8 plan: fp32 stem 1x1 weights [2048][64] for the CUDA-core stem
   StageDev stages[fav::kStages];
   const float *fin_a = nullptr, *fin_r = nullptr, *fin_w = nullptr, *fin_b = nullptr;
   int state_final = 0;
+  int precision = FAV_PRECISION_BF16;
 };
 
 namespace {
@@ -193,7 +245,17 @@ size_t expected_count(int index) {
   return sizes[r];
 }
 
+// The int8 recipe's selection (tools/rewrite.py:19-30): matrices with
+// min(rows, cols) >= 128. Transposed conv of stage i: rows C_out * rate per tap,
+// cols C_in; residual 1x1: C x C.
+bool int8_transpose(int i) {
+  const int cin = 2048 >> i, cout = cin / 2;
+  return std::min(cout * fav::kRates[i], cin) >= 128;
+}
+bool int8_residual(int i) { return (1024 >> i) >= 128; }
+
 int32_t build_plan(fav_plan* plan, const float* const* w) {
+  const bool i8 = plan->precision == FAV_PRECISION_INT8;
   cudaError_t e = cudaSuccess;
   auto up = [&](int index) -> const float* {
     return plan->mem.upload(w[index], expected_count(index), &e);
@@ -210,6 +272,7 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
                                          [pw](int n, int k) { return pw[(size_t)n * 64 + k]; }));
   }
   plan->pw_b = up(3);
+  if (i8) plan->stem_pw = up(2);
   if (e != cudaSuccess) return cuda_fail(e, "plan upload");
   int off = 6 * fav::kLatentChannels;
   for (int i = 0; i < fav::kStages; ++i) {
@@ -227,13 +290,28 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
     {
       const float* tw = w[base + 4];
       const int cin = st.c_in, cout = st.c_out, s = st.rate;
-      // n = phase * C_out + o; k < C_in: current tap W[k][o][p], else previous tap W[k-C_in][o][p+s].
-      st.timg = up_img(pack_operand(n_total, 2 * cin, st.n_tile_t, fav::kModeSplit, [=](int n, int k) {
-        const int p = n / cout, o = n % cout;
-        const int i_ch = k < cin ? k : k - cin;
-        const int tap = k < cin ? p : p + s;
-        return tw[((size_t)i_ch * cout + o) * 2 * s + tap];
-      }));
+      st.int8 = i8 && int8_transpose(i);
+      if (st.int8) {
+        // Two matrices (current tap p, previous tap p + s), each [C_out * s][C_in], row
+        // n = phase * C_out + o, quantised per row like the reference's split projections
+        // (graph/upsampling.py:122-127).
+        std::vector<float> scales;
+        auto img = pack_operand_i8(n_total, cin, 128, 2, [=](int term, int n, int k) {
+          const int p = n / cout, o = n % cout;
+          return tw[((size_t)k * cout + o) * 2 * s + p + term * s];
+        }, scales);
+        st.n_tile_t = 128;
+        st.timg = reinterpret_cast<const uint8_t*>(plan->mem.upload(img.data(), img.size(), &e));
+        st.tsw = plan->mem.upload(scales.data(), scales.size(), &e);
+      } else {
+        // n = phase * C_out + o; k < C_in: current tap W[k][o][p], else previous tap W[k-C_in][o][p+s].
+        st.timg = up_img(pack_operand(n_total, 2 * cin, st.n_tile_t, fav::kModeSplit, [=](int n, int k) {
+          const int p = n / cout, o = n % cout;
+          const int i_ch = k < cin ? k : k - cin;
+          const int tap = k < cin ? p : p + s;
+          return tw[((size_t)i_ch * cout + o) * 2 * s + tap];
+        }));
+      }
     }
     st.tbias = up(base + 5);
     st.state_t = off;
@@ -247,8 +325,17 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
       r.pre_r = up(rb + 1);
       const float* pw = w[rb + 6];
       const int c = st.c_out;
-      r.img = up_img(pack_operand(c, c, r.n_tile, fav::kModeF16,
-                                  [pw, c](int n, int k) { return pw[(size_t)n * c + k]; }));
+      r.int8 = i8 && int8_residual(i);
+      if (r.int8) {
+        std::vector<float> scales;
+        auto img = pack_operand_i8(c, c, r.n_tile, 1, [pw, c](int, int n, int k) { return pw[(size_t)n * c + k]; },
+                                   scales);
+        r.img = reinterpret_cast<const uint8_t*>(plan->mem.upload(img.data(), img.size(), &e));
+        r.sw = plan->mem.upload(scales.data(), scales.size(), &e);
+      } else {
+        r.img = up_img(pack_operand(c, c, r.n_tile, fav::kModeF16,
+                                    [pw, c](int n, int k) { return pw[(size_t)n * c + k]; }));
+      }
       r.pw_b = up(rb + 7);
       {
         // [block][w0..w6, bias, alpha2, recip2][64], zero padded past C. The
@@ -311,6 +398,33 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     const StageDev& st = p->stages[i];
     return fav::HistRef{1 + 4 * i, 2 * st.state_t, 1, st.c_in};
   };
+  // int8 plans: the activated input of an int8 transposed conv (fp32) takes
+  // the planes' region, its per-row partial maxima the shifted planes' region,
+  // and the residual units' scratch follows the six regions.
+  float* act = reinterpret_cast<float*>(planes);
+  float* rowmax = reinterpret_cast<float*>(planes_prev);
+  float* scratch = ws + kWorkspaceRegions * region;
+  int act_parts = 0;  // partial row maxima per row of the activation feeding the next int8 conv
+  // Sets the epilogue of a layer whose output feeds stage ``i``'s transposed
+  // conv: split-bf16 planes, or (int8 conv) the fp32 activation and row maxima.
+  auto feed_tconv = [&](fav::LayerArgs& l, int i, bool debug_y) {
+    const StageDev& nx = p->stages[i];
+    l.next_scale = nx.scale;
+    l.next_offset = nx.offset;
+    l.next_alpha = nx.alpha;
+    l.next_recip = nx.recip;
+    l.hist_next = tconv_hist(i);
+    if (nx.int8) {
+      l.epi = fav::kEpiAct | (debug_y ? fav::kEpiX : 0);
+      l.out_s = act;
+      l.rowmax_out = rowmax;
+      l.rowmax_parts = l.n_total / l.n_tile;
+    } else {
+      l.epi = fav::kEpiPlanes | (debug_y ? fav::kEpiX : 0);
+      l.out_planes = planes;
+      l.out_planes_prev = planes_prev;
+    }
+  };
   int32_t es = FAV_OK;
   cudaError_t e = cudaSuccess;
   // stem: depthwise k=7 -> 1x1 64->2048; epilogue writes stage 0's activated planes.
@@ -319,8 +433,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     a.state = state;
     a.status = status;
     a.kind = fav::kStem;
-    a.mode = fav::kModeSplit;
-    a.epi = fav::kEpiPlanes | (last_layer == 0 ? fav::kEpiX : 0);
+    a.mode = fav::kModeSplit4;
     a.rows = n_streams * frames;
     a.rows_per_stream = frames;
     a.k_channels = 64;
@@ -335,17 +448,19 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     a.dw_w = p->stem_w;
     a.dw_b = p->stem_b;
     a.wimg = p->stem_img;
-    const StageDev& next = p->stages[0];
-    a.next_scale = next.scale;
-    a.next_offset = next.offset;
-    a.next_alpha = next.alpha;
-    a.next_recip = next.recip;
     a.hist = fav::HistRef{0, 0, 6, fav::kLatentChannels};
     a.out_x = X[0];
-    a.out_planes = planes;
-    a.out_planes_prev = planes_prev;
-    a.hist_next = tconv_hist(0);
-    if ((e = fav::launch_gemm_layer(a, stream)) != cudaSuccess) return cuda_fail(e, "stem launch");
+    feed_tconv(a, 0, last_layer == 0);
+    if (p->precision == FAV_PRECISION_INT8) {
+      // The int8 recipe's cascade starts here: the stem runs in the oracle's operation order.
+      a.dense_w = p->stem_pw;
+      a.rowmax_parts = 1;
+      e = fav::launch_stem_exact(a, stream);
+    } else {
+      e = fav::launch_gemm_layer(a, stream);
+    }
+    act_parts = a.rowmax_parts;
+    if (e != cudaSuccess) return cuda_fail(e, "stem launch");
   }
   int layer = 0;
   mark(1);
@@ -376,8 +491,20 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     t.hist = fav::HistRef{1 + 4 * i, 2 * st.state_t, 1, st.c_in};
     t.out_x = X[0];
     t.out_s = S[0];
-    if ((es = encode_plane_map(&t.tmap, planes, t.rows, st.c_in)) != FAV_OK) return es;
-    if ((es = encode_plane_map(&t.tmap2, planes_prev, t.rows, st.c_in)) != FAV_OK) return es;
+    if (st.int8) {
+      // W8A8: producers quantise the fp32 activation (row m0 - 1 .. m0 + 127 boxes of 64 channels).
+      t.mode = fav::kModeI8;
+      t.num_kblocks = st.c_in / fav::kKBlockI8;
+      t.rowmax_in = rowmax;
+      t.rowmax_in_parts = act_parts;
+      t.w_scale = st.tsw;
+      t.w_scale2 = st.tsw + t.n_total;
+      t.hist_max_slot = fav::kNumHistories + i;
+      if ((es = encode_input_map(&t.tmap, act, t.rows, st.c_in, fav::kTileM + 1)) != FAV_OK) return es;
+    } else {
+      if ((es = encode_plane_map(&t.tmap, planes, t.rows, st.c_in)) != FAV_OK) return es;
+      if ((es = encode_plane_map(&t.tmap2, planes_prev, t.rows, st.c_in)) != FAV_OK) return es;
+    }
     if ((e = fav::launch_gemm_layer(t, stream)) != cudaSuccess) return cuda_fail(e, "transpose launch");
     n *= st.rate;
     if (last_out) *last_out = X[0];
@@ -410,28 +537,28 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       u.hist = fav::HistRef{2 + 4 * i + j, 2 * r.state_off, 6 * r.dilation, st.c_out};
       u.box_rows = fav::box_rows_for(fav::kResidual, r.dilation);
       u.raw_pitch = st.c_out < fav::kKBlock ? st.c_out : fav::kKBlock;
+      if (r.int8) {
+        // W8A8: two-pass producers (depthwise + Snake to scratch, then quantise per row).
+        u.mode = fav::kModeI8;
+        u.num_kblocks = st.c_out / fav::kKBlockI8;
+        u.w_scale = r.sw;
+        u.scratch = scratch;
+      }
       const bool debug_y = layer + 1 == last_layer;
+      u.out_x = X[out];
+      u.out_s = S[out];
       if (j < 2) {
         u.epi = fav::kEpiX | fav::kEpiS;
         u.next_alpha = st.res[j + 1].pre_a;
         u.next_recip = st.res[j + 1].pre_r;
       } else if (i + 1 < fav::kStages) {
-        const StageDev& nx = p->stages[i + 1];
-        u.epi = fav::kEpiPlanes | (debug_y ? fav::kEpiX : 0);
-        u.next_scale = nx.scale;
-        u.next_offset = nx.offset;
-        u.next_alpha = nx.alpha;
-        u.next_recip = nx.recip;
-        u.hist_next = tconv_hist(i + 1);
+        feed_tconv(u, i + 1, debug_y);
+        act_parts = u.rowmax_parts;
       } else {
         u.epi = fav::kEpiS | (debug_y ? fav::kEpiX : 0);
         u.next_alpha = p->fin_a;
         u.next_recip = p->fin_r;
       }
-      u.out_x = X[out];
-      u.out_s = S[out];
-      u.out_planes = planes;
-      u.out_planes_prev = planes_prev;
       if ((es = encode_input_map(&u.tmap, S[in], u.rows, st.c_out, u.box_rows)) != FAV_OK) return es;
       if ((e = fav::launch_gemm_layer(u, stream)) != cudaSuccess) return cuda_fail(e, "residual launch");
       if (last_out) *last_out = X[out];
@@ -530,7 +657,8 @@ int32_t fav_plan_create(const float* const* coefficients, int32_t count, int32_t
   *plan_out = nullptr;
   if (!coefficients || count != FAV_NUM_COEFFICIENTS)
     return fail(FAV_INVALID_ARGUMENT, "expected %d coefficient arrays", FAV_NUM_COEFFICIENTS);
-  if (precision != FAV_PRECISION_BF16) return fail(FAV_UNSUPPORTED, "unsupported precision %d", precision);
+  if (precision != FAV_PRECISION_BF16 && precision != FAV_PRECISION_INT8)
+    return fail(FAV_UNSUPPORTED, "unsupported precision %d", precision);
   for (int i = 0; i < count; ++i) {
     if (!coefficients[i]) return fail(FAV_INVALID_ARGUMENT, "coefficient %d is NULL", i);
     const size_t nvals = expected_count(i);
@@ -543,6 +671,7 @@ int32_t fav_plan_create(const float* const* coefficients, int32_t count, int32_t
   fav_plan* plan = new (std::nothrow) fav_plan();
   if (!plan) return fail(FAV_DEVICE_ERROR, "out of host memory");
   cudaGetDevice(&plan->device);
+  plan->precision = precision;
   const int32_t st = build_plan(plan, coefficients);
   if (st != FAV_OK) {
     delete plan;
@@ -581,7 +710,7 @@ int32_t fav_step(const fav_plan* plan, float* state_pool, int32_t num_slots, con
   if (!latents || !audio || !workspace) return fail(FAV_INVALID_ARGUMENT, "NULL latents, audio or workspace");
   if (!state_pool || !slot_codes || num_slots < n_streams)
     return fail(FAV_INVALID_ARGUMENT, "state pool, slot codes and num_slots >= n_streams are required");
-  const size_t need = fav_step_workspace_bytes(n_streams, frames);
+  const size_t need = fav_plan_workspace_bytes(plan, n_streams, frames);
   if (!need) return fail(FAV_SIZE_OVERFLOW, "workspace size overflow");
   if (workspace_bytes < need)
     return fail(FAV_INVALID_ARGUMENT, "workspace too small: %zu < %zu bytes", workspace_bytes, need);
@@ -603,6 +732,8 @@ int32_t fav_step_static(const fav_plan* plan, float* state_pool, int32_t num_slo
   if (!latents || !audio) return fail(FAV_INVALID_ARGUMENT, "NULL latents or audio");
   if (!state_pool || !slot_codes || num_slots < n_streams)
     return fail(FAV_INVALID_ARGUMENT, "state pool, slot codes and num_slots >= n_streams are required");
+  if (plan->precision != FAV_PRECISION_BF16)
+    return fail(FAV_UNSUPPORTED, "the allocation-free step supports FAV_PRECISION_BF16 plans only");
   float* ws = nullptr;
   const int32_t st = static_workspace(&ws);
   if (st != FAV_OK) return st;
@@ -617,6 +748,20 @@ size_t fav_batch_workspace_bytes(int32_t n_clips, int32_t chunk_frames) {
   return act + fav_state_pool_bytes(n_clips);
 }
 
+size_t fav_plan_workspace_bytes(const fav_plan* plan, int32_t n_streams, int32_t frames) {
+  const size_t act = fav_step_workspace_bytes(n_streams, frames);
+  if (!plan || !act) return 0;
+  return act + (plan->precision == FAV_PRECISION_INT8 ? fav::kScratchFloats * sizeof(float) : 0);
+}
+
+size_t fav_plan_batch_workspace_bytes(const fav_plan* plan, int32_t n_clips, int32_t chunk_frames) {
+  const size_t act = fav_plan_workspace_bytes(plan, n_clips, chunk_frames);
+  if (!act) return 0;
+  return act + fav_state_pool_bytes(n_clips);
+}
+
+int32_t fav_plan_precision(const fav_plan* plan) { return plan ? plan->precision : -1; }
+
 int32_t fav_decode_batch(const fav_plan* plan, const float* latents, int32_t n_clips, int32_t frames,
                          int32_t chunk_frames, float* audio, void* workspace, size_t workspace_bytes,
                          uint32_t* status, void* cuda_stream) {
@@ -628,11 +773,11 @@ int32_t fav_decode_batch(const fav_plan* plan, const float* latents, int32_t n_c
   if ((int64_t)frames * fav::kHop > INT32_MAX || (int64_t)n_clips * chunk_frames * fav::kHop > INT32_MAX)
     return fail(FAV_SIZE_OVERFLOW, "clip too large");
   if (chunk_frames > frames) chunk_frames = frames;
-  const size_t need = fav_batch_workspace_bytes(n_clips, chunk_frames);
+  const size_t need = fav_plan_batch_workspace_bytes(plan, n_clips, chunk_frames);
   if (!need || workspace_bytes < need)
     return fail(FAV_INVALID_ARGUMENT, "workspace too small: %zu < %zu bytes", workspace_bytes, need);
   float* ws = static_cast<float*>(workspace);
-  float* pool = ws + fav_step_workspace_bytes(n_clips, chunk_frames) / sizeof(float);
+  float* pool = ws + fav_plan_workspace_bytes(plan, n_clips, chunk_frames) / sizeof(float);
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
   for (int t0 = 0, c = 0; t0 < frames; t0 += chunk_frames, ++c) {
     const int tc = frames - t0 < chunk_frames ? frames - t0 : chunk_frames;
@@ -653,7 +798,7 @@ int32_t fav_step_profile(const fav_plan* plan, float* state_pool, int32_t num_sl
   if (!plan || n_streams <= 0 || frames <= 0 || !latents || !audio || !workspace || !state_pool || !slot_codes ||
       num_slots < n_streams)
     return fail(FAV_INVALID_ARGUMENT, "bad profile step arguments");
-  if (workspace_bytes < fav_step_workspace_bytes(n_streams, frames))
+  if (workspace_bytes < fav_plan_workspace_bytes(plan, n_streams, frames))
     return fail(FAV_INVALID_ARGUMENT, "workspace too small");
   cudaEvent_t ev[27];
   for (int i = 0; i < 27; ++i) {
@@ -684,7 +829,7 @@ int32_t fav_debug_step_layers(const fav_plan* plan, float* state_pool, int32_t n
   if (!plan || !layer_out || last_layer < 0 || last_layer > 24 || n_streams <= 0 || frames <= 0 || !latents ||
       !workspace)
     return fail(FAV_INVALID_ARGUMENT, "bad debug step arguments");
-  if (workspace_bytes < fav_step_workspace_bytes(n_streams, frames))
+  if (workspace_bytes < fav_plan_workspace_bytes(plan, n_streams, frames))
     return fail(FAV_INVALID_ARGUMENT, "workspace too small");
   if (state_pool && (!slot_codes || num_slots < n_streams))
     return fail(FAV_INVALID_ARGUMENT, "slot codes and num_slots >= n_streams are required with a state pool");
@@ -702,16 +847,34 @@ int32_t fav_test_gemm(const float* a, int32_t m, int32_t k, const float* b, int3
   if (!nt) return fail(FAV_INVALID_ARGUMENT, "N must be a multiple of 32");
   cudaError_t e = prepare_once();
   if (e != cudaSuccess) return cuda_fail(e, "kernel attributes");
-  const int md = mode ? fav::kModeSplit : fav::kModeF16;
-  auto img = pack_operand(n, k, nt, md, [b, k](int row, int col) { return b[(size_t)row * k + col]; });
+  if (mode < 0 || mode > 2) return fail(FAV_INVALID_ARGUMENT, "mode must be 0, 1 or 2");
+  const int md = mode == 2 ? fav::kModeI8 : mode ? fav::kModeSplit : fav::kModeF16;
+  std::vector<uint8_t> img;
+  if (md == fav::kModeI8) {
+    // Operands hold integers in [-127, 127]; B is packed as it is (no scales).
+    const int kb = (k + fav::kKBlockI8 - 1) / fav::kKBlockI8;
+    img.assign((size_t)(n / nt) * kb * nt * 128, 0);
+    for (int row = 0; row < n; ++row)
+      for (int col = 0; col < k; ++col) {
+        const int tile = row / nt, r = row % nt, blk = col / fav::kKBlockI8, kk = col % fav::kKBlockI8;
+        const long q = std::lround(b[(size_t)row * k + col]);
+        if (q < -127 || q > 127) return fail(FAV_INVALID_ARGUMENT, "int8 test operands must be integers in [-127, 127]");
+        img[((size_t)tile * kb + blk) * nt * 128 + (size_t)r * 128 + ((((kk >> 4) ^ (r & 7)) << 4) | (kk & 15))] =
+            static_cast<uint8_t>(static_cast<int8_t>(q));
+      }
+  } else {
+    auto h = pack_operand(n, k, nt, md, [b, k](int row, int col) { return b[(size_t)row * k + col]; });
+    img.resize(h.size() * 2);
+    std::memcpy(img.data(), h.data(), img.size());
+  }
   void* dimg = nullptr;
   uint32_t* dstatus = nullptr;
-  if ((e = cudaMalloc(&dimg, img.size() * 2)) != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+  if ((e = cudaMalloc(&dimg, img.size())) != cudaSuccess) return cuda_fail(e, "cudaMalloc");
   if ((e = cudaMalloc(&dstatus, 4)) != cudaSuccess) {
     cudaFree(dimg);
     return cuda_fail(e, "cudaMalloc");
   }
-  cudaMemcpy(dimg, img.data(), img.size() * 2, cudaMemcpyHostToDevice);
+  cudaMemcpy(dimg, img.data(), img.size(), cudaMemcpyHostToDevice);
   cudaMemset(dstatus, 0, 4);
   fav::LayerArgs la{};
   la.kind = fav::kTestGemm;
@@ -719,7 +882,7 @@ int32_t fav_test_gemm(const float* a, int32_t m, int32_t k, const float* b, int3
   la.rows = m;
   la.rows_per_stream = m;
   la.k_channels = k;
-  la.num_kblocks = (k + fav::kKBlock - 1) / fav::kKBlock;
+  la.num_kblocks = md == fav::kModeI8 ? (k + fav::kKBlockI8 - 1) / fav::kKBlockI8 : (k + fav::kKBlock - 1) / fav::kKBlock;
   la.n_total = n;
   la.n_tile = nt;
   la.c_out = n;
@@ -738,6 +901,13 @@ int32_t fav_test_gemm(const float* a, int32_t m, int32_t k, const float* b, int3
   if (e != cudaSuccess) return cuda_fail(e, "test GEMM");
   if (hs) return fail(FAV_TIMEOUT, "test GEMM kernel status 0x%x", hs);
   return FAV_OK;
+}
+
+int32_t fav_test_sine(const float* x, int32_t n, float* out, void* cuda_stream) {
+  g_error[0] = 0;
+  if (!x || !out || n < 0) return fail(FAV_INVALID_ARGUMENT, "bad sine test arguments");
+  const cudaError_t e = fav::launch_sine_test(x, n, out, static_cast<cudaStream_t>(cuda_stream));
+  return e == cudaSuccess ? FAV_OK : cuda_fail(e, "sine test launch");
 }
 
 }  // extern "C"

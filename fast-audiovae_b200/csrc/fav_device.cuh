@@ -170,6 +170,15 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::i8 (signed 8-bit operands, s32 accumulate).
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Arrive once on ``bar`` when all previously issued MMAs of this thread finish.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -222,6 +231,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // ------------------------------------------------------------ descriptors
 // Instruction descriptor, kind::f16: fp32 accumulator, K-major A and B.
 // fmt: 0 = f16, 1 = bf16. M = 128.
+// Instruction descriptor, kind::i8: s32 accumulator, signed 8-bit K-major A and B. M = 128.
+__host__ __device__ constexpr uint32_t instr_desc_i8(uint32_t n) {
+  return (2u << 4)              // D format s32
+         | (1u << 7)            // A format s8
+         | (1u << 10)           // B format s8
+         | ((n >> 3) << 17)     // N / 8
+         | ((128u >> 4) << 24); // M / 16
+}
 __host__ __device__ constexpr uint32_t instr_desc_f16(uint32_t fmt, uint32_t n) {
   return (1u << 4)              // D format f32
          | (fmt << 7)           // A format
@@ -250,6 +267,62 @@ __host__ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t
 __device__ __forceinline__ float snake(float x, float a, float r) {
   const float s = __sinf(a * x);
   return fmaf(r, s * s, x);
+}
+// Sine in a fixed sequence of IEEE fp32 operations (no fused multiply-add),
+// the same sequence as the int8 oracle's ``sin_cw``: Cody-Waite argument
+// reduction (Cody & Waite, Software Manual for the Elementary Functions, 1980)
+// with pi/2 = P1 + P2 + P3 (P1, P2 of 15 significant bits, so k*P1 and k*P2 are
+// exact for |k| < 2^9), then Taylor polynomials of degree 11 (sine) and 12
+// (cosine) on [-pi/4, pi/4] by Horner's rule. The constants are 2/pi, the
+// parts of pi/2 and +-1/n! rounded to fp32. Within ~1.3 ulp of sin for the
+// arguments Snake sees.
+__device__ __forceinline__ float sin_cw(float x) {
+  const float k = rintf(__fmul_rn(x, 0x1.45f306p-1f));
+  const float r = __fsub_rn(__fsub_rn(__fsub_rn(x, __fmul_rn(k, 0x1.921cp+0f)), __fmul_rn(k, 0x1.daap-15f)),
+                            __fmul_rn(k, 0x1.10b46p-30f));
+  const float r2 = __fmul_rn(r, r);
+  float ps = __fmul_rn(r2, -0x1.ae6456p-26f);  // -1/11!
+  ps = __fmul_rn(r2, __fadd_rn(ps, 0x1.71de3ap-19f));   // 1/9!
+  ps = __fmul_rn(r2, __fadd_rn(ps, -0x1.a01a02p-13f));  // -1/7!
+  ps = __fmul_rn(r2, __fadd_rn(ps, 0x1.111112p-7f));    // 1/5!
+  ps = __fmul_rn(r2, __fadd_rn(ps, -0x1.555556p-3f));   // -1/3!
+  const float sin_r = __fadd_rn(r, __fmul_rn(r, ps));
+  float pc = __fmul_rn(r2, 0x1.1eed8ep-29f);   // 1/12!
+  pc = __fmul_rn(r2, __fadd_rn(pc, -0x1.27e4fcp-22f));  // -1/10!
+  pc = __fmul_rn(r2, __fadd_rn(pc, 0x1.a01a02p-16f));   // 1/8!
+  pc = __fmul_rn(r2, __fadd_rn(pc, -0x1.6c16c2p-10f));  // -1/6!
+  pc = __fmul_rn(r2, __fadd_rn(pc, 0x1.555556p-5f));    // 1/4!
+  pc = __fmul_rn(r2, __fadd_rn(pc, -0x1p-1f));          // -1/2!
+  const float cos_r = __fadd_rn(1.f, pc);
+  const int q = static_cast<int>(k) & 3;
+  return q == 0 ? sin_r : q == 1 ? cos_r : q == 2 ? -sin_r : -cos_r;
+}
+// Snake in the int8 path's fixed operation order (mps_decoder.py:44-50:
+// scaled = alpha*x; s = sin(scaled); y = x + r*(s*s), each step rounded). A
+// quantised cascade turns any difference before a quantisation step into
+// whole-step rounding flips downstream, so the int8 path and its oracle share it.
+__device__ __forceinline__ float snake_exact(float x, float a, float r) {
+  const float s = sin_cw(__fmul_rn(a, x));
+  return __fadd_rn(x, __fmul_rn(r, __fmul_rn(s, s)));
+}
+
+// The W8A8 recipe's symmetric quantisation (precision.cpp:82-92 of the
+// reference): scale = max|v| / 127 in fp32 (1 for an all-zero vector, max|v|
+// itself when the quotient underflows to zero); q = clamp(v / scale, -127, 127)
+// rounded half to even. Both divisions are IEEE round-to-nearest.
+__device__ __forceinline__ float quant_scale(float mx) {
+  if (mx == 0.f) return 1.f;
+  const float s = __fdiv_rn(mx, 127.f);
+  return s > 0.f ? s : mx;
+}
+__device__ __forceinline__ uint32_t quant_byte(float v, float scale) {
+  const float q = fminf(fmaxf(__fdiv_rn(v, scale), -127.f), 127.f);
+  return static_cast<uint32_t>(__float2int_rn(q)) & 0xffu;
+}
+// Four quantised values packed little-endian (v.x in the lowest byte).
+__device__ __forceinline__ uint32_t quant4(float4 v, float scale) {
+  return quant_byte(v.x, scale) | (quant_byte(v.y, scale) << 8) | (quant_byte(v.z, scale) << 16) |
+         (quant_byte(v.w, scale) << 24);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo_elem, float hi_elem) {

@@ -36,7 +36,17 @@ enum LayerKind : int { kStem = 0, kTconv = 1, kResidual = 2, kTestGemm = 3 };
 enum GemmMode : int {
   kModeF16 = 0,    // one f16 x f16 MMA, fp32 accumulate
   kModeSplit = 1,  // three bf16 MMAs (hi*hi + hi*lo + lo*hi), fp32 accumulate
+  kModeI8 = 2,     // W8A8: s8 x s8 MMAs (kind::i8), s32 accumulate, per-row weight and activation scales
+  kModeSplit4 = 3, // four bf16 MMAs (adds lo*lo): the fp32 product to ~2^-24 relative
 };
+
+// K elements of one int8 pipeline stage (128 bytes per operand row).
+constexpr int kKBlockI8 = 128;
+// int8 residual units stage their depthwise + Snake result per CTA in a global
+// scratch of [CTA][128 rows][up to 1024 channels] fp32; the launch caps the grid
+// at kScratchCtas.
+constexpr int kScratchCtas = 148;
+constexpr size_t kScratchFloats = (size_t)kScratchCtas * 128 * 1024;
 
 // Stream slot codes passed to a step: (slot << 2) | (fresh << 1) | read_parity.
 // ``fresh`` starts the stream from an all-zero history.
@@ -64,6 +74,8 @@ enum EpilogueFlags : int {
   kEpiPlanes = 8,  // split-bf16 hi/lo planes of Snake(y * next_scale + next_offset) to out_planes, the
                    // same planes one row later per stream to out_planes_prev (row t holds t - 1; a
                    // stream's first row holds the next layer's history), and the next layer's history
+  kEpiAct = 16,    // int8 path: Snake(y * next_scale + next_offset) fp32 to out_s, this tile's per-row max of
+                   // its magnitude to rowmax_out[row * rowmax_parts + n_tile], and the next layer's history
 };
 
 struct LayerArgs {
@@ -78,6 +90,16 @@ struct LayerArgs {
   uint16_t* out_planes;
   uint16_t* out_planes_prev;
   HistRef hist_next;  // history of the layer that reads out_planes (its previous activated input)
+  // int8 path (kModeI8 and kEpiAct):
+  float* rowmax_out;         // [rows][rowmax_parts] partial row maxima of |out_s|
+  int rowmax_parts;
+  const float* rowmax_in;    // the same, written by the previous layer, for this layer's input rows
+  int rowmax_in_parts;
+  const float* w_scale;      // per-GEMM-column weight scale (transposed conv: current tap)
+  const float* w_scale2;     // transposed conv: previous tap
+  float* scratch;            // residual: per-CTA [128][k] fp32 of the depthwise + Snake result
+  int hist_max_slot;         // transposed conv: head-table entry holding the history row's max |x|
+  const float* dense_w;      // int8 plan's stem on CUDA cores: 1x1 weights [n_total][k] fp32
   int kind;
   int mode;
   int epi;              // EpilogueFlags
@@ -128,6 +150,11 @@ struct FinalArgs {
 
 // Kernel launchers (fav_kernels.cu). Return cudaError_t of the launch.
 cudaError_t launch_gemm_layer(const LayerArgs& a, cudaStream_t stream);
+// The int8 plan's stem (depthwise k=7 -> 1x1 -> stage 0's affine + Snake, row
+// maxima and history) on CUDA cores, every sum in the int8 oracle's order.
+cudaError_t launch_stem_exact(const LayerArgs& a, cudaStream_t stream);
+// Diagnostic: out[i] = the int8 path's fixed-order sine of x[i] (device arrays).
+cudaError_t launch_sine_test(const float* x, int n, float* out, cudaStream_t stream);
 cudaError_t launch_final(const FinalArgs& a, cudaStream_t stream);
 cudaError_t prepare_kernels();
 

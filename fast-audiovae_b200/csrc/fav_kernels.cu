@@ -52,33 +52,80 @@ constexpr int kEpiCols = 16;                 // epilogue chunk: 16 columns x 32 
 constexpr int kResBoxBytes = (kTileM + kMaxHalo) * 64 * 4;
 constexpr int kResCoefBytes = kCoefResidual * 64 * 4;
 
+// Split-bf16 operand modes store hi and lo tiles.
+template <int MODE>
+constexpr bool kSplitOperands = MODE == kModeSplit || MODE == kModeSplit4;
+
 template <int NT, int MODE, int KIND>
 struct GemmCfg {
-  static constexpr int kTerms = MODE == kModeSplit ? 2 : 1;
+  static constexpr bool kI8 = MODE == kModeI8;
+  static constexpr bool kI8Tconv = kI8 && KIND == kTconv;
+  // Operand tiles per stage: split-bf16 hi and lo, or the int8 transposed
+  // conv's two taps (separately scaled, separate accumulators).
+  static constexpr int kTerms = (kSplitOperands<MODE> || kI8Tconv) ? 2 : 1;
   static constexpr int kATile = kTileM * 128;
   static constexpr int kBTile = NT * 128;
   static constexpr int kAStage = kTerms * kATile;
   static constexpr int kBStage = kTerms * kBTile;
   static constexpr int kStage = kAStage + kBStage;
-  static constexpr int kRaw = KIND == kResidual ? kResBoxBytes + kResCoefBytes : 0;
-  static constexpr int kTable = KIND == kTestGemm ? 0 : 2 * ((kTableInts * 4 + 15) / 16) * 16;  // two tiles
-  static constexpr int kFixed = 1024 /*align slack*/ + 512 /*barriers*/ + kTable;
+  static constexpr int kRaw = KIND == kResidual ? kResBoxBytes + kResCoefBytes : kI8Tconv ? (kTileM + 1) * 64 * 4 : 0;
+  // Per-tile tables: streams and rows, plus the int8 transposed conv's row scales.
+  static constexpr int kTableI = kTableInts + (kI8Tconv ? 2 * kTileM : 0);
+  static constexpr int kTable = KIND == kTestGemm ? 0 : 2 * ((kTableI * 4 + 15) / 16) * 16;  // two tiles
+  // int8: row scales for the epilogue [2 buffers][current, previous tap][128], and pass-1 row maxima [128].
+  static constexpr int kScales = kI8 ? (2 * 2 * kTileM + kTileM) * 4 : 0;
+  static constexpr int kFixed = 1024 /*align slack*/ + 512 /*barriers*/ + kTable + kScales;
   // Epilogue column coefficients, double-buffered per tile.
-  static constexpr int kEpi = 2 * 5 * NT * 4;
+  static constexpr int kEpi = 2 * 7 * NT * 4;
   static constexpr int kStagesFit = (kSmemBudget - 2 * kRaw - kFixed - kEpi) / kStage;
   static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
   static_assert(kStages >= 2, "pipeline needs two stages");
   static constexpr int kSmem = kFixed + kStages * kStage + kEpi + 2 * kRaw;
-  // Two accumulators of NT fp32 columns each.
-  static constexpr uint32_t kTmemCols = 2 * NT < 32 ? 32 : 2 * NT;
-  static constexpr uint32_t kIdesc = instr_desc_f16(MODE == kModeSplit ? 1u : 0u, NT);
+  // Two accumulator buffers; one buffer holds NT fp32/s32 columns per accumulator.
+  static constexpr int kAccCols = kI8Tconv ? 2 * NT : NT;
+  static constexpr uint32_t kTmemCols = 2 * kAccCols < 32 ? 32 : 2 * kAccCols;
+  static_assert(kTmemCols <= 512, "TMEM holds 512 columns");
+  static constexpr uint32_t kIdesc = kI8 ? instr_desc_i8(NT) : instr_desc_f16(kSplitOperands<MODE> ? 1u : 0u, NT);
 };
 
 __device__ __forceinline__ float2 ldg2(const float* p) { return __ldg(reinterpret_cast<const float2*>(p)); }
 __device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+template <bool EXACT = false>
 __device__ __forceinline__ float4 snake4(float4 v, float4 al, float4 rc) {
+  if constexpr (EXACT)
+    return make_float4(snake_exact(v.x, al.x, rc.x), snake_exact(v.y, al.y, rc.y), snake_exact(v.z, al.z, rc.z),
+                       snake_exact(v.w, al.w, rc.w));
   return make_float4(snake(v.x, al.x, rc.x), snake(v.y, al.y, rc.y), snake(v.z, al.z, rc.z), snake(v.w, al.w, rc.w));
+}
+
+// Depthwise k=7 tap sum of four channels, oldest tap first, plus bias. The
+// int8 path (EXACT) rounds every product and sum (the oracle's order); the
+// bf16 path chains fused multiply-adds.
+template <bool EXACT>
+__device__ __forceinline__ float4 dw7(const float4 (&w)[7], const float4 (&win)[7], float4 bias) {
+  float4 h;
+  if constexpr (EXACT) {
+    h = make_float4(__fmul_rn(w[0].x, win[0].x), __fmul_rn(w[0].y, win[0].y), __fmul_rn(w[0].z, win[0].z),
+                    __fmul_rn(w[0].w, win[0].w));
+#pragma unroll
+    for (int j = 1; j < 7; ++j) {
+      h.x = __fadd_rn(h.x, __fmul_rn(w[j].x, win[j].x));
+      h.y = __fadd_rn(h.y, __fmul_rn(w[j].y, win[j].y));
+      h.z = __fadd_rn(h.z, __fmul_rn(w[j].z, win[j].z));
+      h.w = __fadd_rn(h.w, __fmul_rn(w[j].w, win[j].w));
+    }
+    return make_float4(__fadd_rn(h.x, bias.x), __fadd_rn(h.y, bias.y), __fadd_rn(h.z, bias.z), __fadd_rn(h.w, bias.w));
+  }
+  h = make_float4(w[0].x * win[0].x, w[0].y * win[0].y, w[0].z * win[0].z, w[0].w * win[0].w);
+#pragma unroll
+  for (int j = 1; j < 7; ++j) {
+    h.x = fmaf(w[j].x, win[j].x, h.x);
+    h.y = fmaf(w[j].y, win[j].y, h.y);
+    h.z = fmaf(w[j].z, win[j].z, h.z);
+    h.w = fmaf(w[j].w, win[j].w, h.w);
+  }
+  return make_float4(h.x + bias.x, h.y + bias.y, h.z + bias.z, h.w + bias.w);
 }
 
 // ----------------------------------------------------------- history rings
@@ -162,7 +209,7 @@ __device__ __forceinline__ void hist_commit_head(const StateRef& st, const HistR
 template <int MODE>
 __device__ __forceinline__ void put_a(uint8_t* a_stage, int r, int k, float v0, float v1) {
   const uint32_t off = sw128_offset(r, k);
-  if (MODE == kModeSplit) {
+  if (kSplitOperands<MODE>) {
     uint32_t hi, lo;
     split_bf16(v0, v1, hi, lo);
     *reinterpret_cast<uint32_t*>(a_stage + off) = hi;
@@ -176,7 +223,7 @@ __device__ __forceinline__ void put_a(uint8_t* a_stage, int r, int k, float v0, 
 template <int MODE>
 __device__ __forceinline__ void put_a4(uint8_t* a_stage, int r, int k, float4 v) {
   const uint32_t off = sw128_offset(r, k);
-  if (MODE == kModeSplit) {
+  if (kSplitOperands<MODE>) {
     uint32_t h0, l0, h1, l1;
     split_bf16(v.x, v.y, h0, l0);
     split_bf16(v.z, v.w, h1, l1);
@@ -298,10 +345,28 @@ __device__ void produce_stem(const LayerArgs& a, uint8_t* a_stage, int warp, int
 // through registers; a regular chain (one stream, every tap inside the chunk)
 // runs branch-free. History = last 6d rows of s [6d][C]. LPR lanes cover one
 // row (16 for 64-channel K blocks, 8 for C = 32).
+// Output of a residual producer for row r, channels kl..kl+3 of K block kb:
+// into the A tile, or (int8 pass 1) into the CTA's fp32 scratch with the row's
+// max |value| folded into rowmax. All 16 lanes of a row group call it together.
+template <int MODE>
+__device__ __forceinline__ void residual_out(const LayerArgs& a, uint8_t* a_stage, uint32_t* rowmax, int kb, int r,
+                                             int kl, int lane, float4 y) {
+  if constexpr (MODE == kModeI8) {
+    *reinterpret_cast<float4*>(a.scratch + ((size_t)blockIdx.x * kTileM + r) * a.k_channels + kb * kKBlock + kl) = y;
+    float m = fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w)));
+    const unsigned group = 0xffffu << (lane & 16);
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(group, m, o));
+    if ((lane & 15) == 0) atomicMax(rowmax + r, __float_as_uint(m));
+  } else {
+    put_a4<MODE>(a_stage, r, kl, y);
+  }
+}
+
 template <int MODE, int LPR>
 __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, const float* raw, int warp,
                                  int lane, bool write_state, const StreamTable& tab, uint32_t walk_lo,
-                                 uint32_t walk_hi, bool regular) {
+                                 uint32_t walk_hi, bool regular, uint32_t* rowmax) {
   constexpr int kRpg = 16 * LPR / 32;  // rows walked per lane group
   const int C = a.k_channels;
   const int d = a.dilation;
@@ -359,20 +424,8 @@ __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_
 #pragma unroll
     for (int u = 0; u < kRpg; ++u) {
       win[6] = valid ? lds4(base + (6 + u) * step) : zero4;
-      float4 h;
-      h.x = w[0].x * win[0].x;
-      h.y = w[0].y * win[0].y;
-      h.z = w[0].z * win[0].z;
-      h.w = w[0].w * win[0].w;
-#pragma unroll
-      for (int j = 1; j < 7; ++j) {
-        h.x = fmaf(w[j].x, win[j].x, h.x);
-        h.y = fmaf(w[j].y, win[j].y, h.y);
-        h.z = fmaf(w[j].z, win[j].z, h.z);
-        h.w = fmaf(w[j].w, win[j].w, h.w);
-      }
-      h = make_float4(h.x + bias.x, h.y + bias.y, h.z + bias.z, h.w + bias.w);
-      put_a4<MODE>(a_stage, r0 + u * d, kl, valid ? snake4(h, al2, rc2) : zero4);
+      const float4 h = dw7<MODE == kModeI8>(w, win, bias);
+      residual_out<MODE>(a, a_stage, rowmax, kb, r0 + u * d, kl, lane, valid ? snake4<MODE == kModeI8>(h, al2, rc2) : zero4);
 #pragma unroll
       for (int j = 0; j < 6; ++j) win[j] = win[j + 1];
     }
@@ -405,32 +458,84 @@ __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_
         }
       }
       win[6] = lds4(raw + (r + H) * P + kl);
-      float4 h;
-      h.x = w[0].x * win[0].x;
-      h.y = w[0].y * win[0].y;
-      h.z = w[0].z * win[0].z;
-      h.w = w[0].w * win[0].w;
-#pragma unroll
-      for (int j = 1; j < 7; ++j) {
-        h.x = fmaf(w[j].x, win[j].x, h.x);
-        h.y = fmaf(w[j].y, win[j].y, h.y);
-        h.z = fmaf(w[j].z, win[j].z, h.z);
-        h.w = fmaf(w[j].w, win[j].w, h.w);
-      }
-      h = make_float4(h.x + bias.x, h.y + bias.y, h.z + bias.z, h.w + bias.w);
-      y = snake4(h, al2, rc2);
+      const float4 h = dw7<MODE == kModeI8>(w, win, bias);
+      y = snake4<MODE == kModeI8>(h, al2, rc2);
       prev_r = r;
       prev_e = e;
     } else {
       prev_e = -2;
     }
-    put_a4<MODE>(a_stage, r, kl, y);
+    residual_out<MODE>(a, a_stage, rowmax, kb, r, kl, lane, y);
   }
 }
 
-// Plain GEMM operand for the engine self-test: A [rows][K] fp32 row-major.
+// Residual unit, int8 pass 2, K block kb8 (128 channels): the depthwise +
+// Snake result staged by pass 1 in the CTA's scratch, quantised with each
+// row's scale into the s8 A tile. Warp w covers rows w, w + 8, ...; a lane
+// covers 4 channels.
+__device__ void quantize_residual_i8(const LayerArgs& a, int kb8, uint8_t* a_stage, const float* row_scale,
+                                     int warp, int lane) {
+  const float* src = a.scratch + (size_t)blockIdx.x * kTileM * a.k_channels + kb8 * kKBlockI8 + 4 * lane;
+#pragma unroll 4
+  for (int j = 0; j < 16; ++j) {
+    const int r = warp + 8 * j;
+    const float4 v = *reinterpret_cast<const float4*>(src + (size_t)r * a.k_channels);
+    *reinterpret_cast<uint32_t*>(a_stage + sw128_offset(r, 2 * lane)) = quant4(v, row_scale[r]);
+  }
+}
+
+// Transposed conv, int8, half h (64 channels) of K block kb8: ``raw`` holds the
+// activated input rows m0-1 .. m0+127 (fp32, 64 channels). Each box row is
+// quantised once with its own scale and written to both taps: row r of the
+// current-tap tile holds input row m0+r, row r of the previous-tap tile input
+// row m0+r-1, or, at a stream's first step, the history (previous activated
+// input) quantised with its own scale. scale[r] is the scale of input row
+// m0+r; scale_prev[r] the previous-tap scale of tile row r.
+__device__ void produce_tconv_i8(const LayerArgs& a, int kb8, int h, uint8_t* a_stage, const float* raw,
+                                 const float* scale, const float* scale_prev, int warp, int lane,
+                                 const StreamTable& tab) {
+  constexpr int kATile = kTileM * 128;
+  const int cq = lane & 15, rs = lane >> 4;
+  const int kl = 4 * cq;
+  const int byte = h * 64 + kl;  // byte within the 128-byte operand row
+  const int c = kb8 * kKBlockI8 + byte;
+#pragma unroll 1
+  for (int j = 0; j < 9; ++j) {
+    const int i = 2 * (warp + 8 * j) + rs;  // box row: input row m0 - 1 + i
+    if (i > kTileM) break;
+    const float4 v = lds4(raw + i * 64 + kl);
+    if (i >= 1)
+      *reinterpret_cast<uint32_t*>(a_stage + sw128_offset(i - 1, byte >> 1)) = quant4(v, scale[i - 1]);
+    if (i < kTileM) {
+      const int e = tab.row_e[i];
+      float4 pv = v;
+      if (e >= 0 && tab.row_t[i] == 0) {
+        const float* hr = hist_row(a, tab, e, -1);
+        pv = hr ? ldg4(hr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      *reinterpret_cast<uint32_t*>(a_stage + kATile + sw128_offset(i, byte >> 1)) = quant4(pv, scale_prev[i]);
+    }
+  }
+}
+
+// Plain GEMM operand for the engine self-test: A [rows][K] fp32 row-major
+// (int8 mode: integer values in [-127, 127], taken as they are).
 template <int MODE>
 __device__ void produce_test(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, int warp, int lane) {
+  if constexpr (MODE == kModeI8) {
+#pragma unroll 1
+    for (int j = 0; j < 16; ++j) {
+      const int r = warp + 8 * j, g = m0 + r, c = kb * kKBlockI8 + 4 * lane;
+      uint32_t word = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float v = (g < a.rows && c + e < a.k_channels) ? __ldg(a.x + (size_t)g * a.k_channels + c + e) : 0.f;
+        word |= (static_cast<uint32_t>(__float2int_rn(v)) & 0xffu) << (8 * e);
+      }
+      *reinterpret_cast<uint32_t*>(a_stage + sw128_offset(r, 2 * lane)) = word;
+    }
+    return;
+  }
   const int c = kb * kKBlock + 2 * lane;
   float2 v[16];
 #pragma unroll
@@ -472,15 +577,24 @@ __device__ __forceinline__ void put_planes(uint16_t* p, size_t plane, const uint
 }
 
 // Per-column epilogue coefficients of one tile, staged in shared memory:
-// [bias, next_alpha, next_recip, next_scale, next_offset][NT].
-constexpr int kEpiCoefVectors = 5;
+// [bias, next_alpha, next_recip, next_scale, next_offset, w_scale, w_scale2][NT].
+constexpr int kEpiCoefVectors = 7;
 
 // --------------------------------------------------------------------- engine
-template <int NT, int MODE, int KIND>
+// Epilogue output class (besides y, written when the layer's kEpiX flag is set).
+enum EpilogueOut : int { kOutNone = 0, kOutS = 1, kOutPlanes = 2, kOutAct = 3 };
+
+template <int NT, int MODE, int KIND, int OUT>
 __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_constant__ LayerArgs a) {
   using Cfg = GemmCfg<NT, MODE, KIND>;
+  constexpr bool kOutSnake = OUT == kOutS;
+  constexpr bool kOutPl = OUT == kOutPlanes;
+  constexpr bool kOutA = OUT == kOutAct;
   constexpr int S = Cfg::kStages;
-  constexpr bool kStaged = KIND == kResidual;
+  constexpr bool kI8 = Cfg::kI8;
+  constexpr bool kI8Tconv = Cfg::kI8Tconv;
+  constexpr bool kI8Res = kI8 && KIND == kResidual;
+  constexpr bool kStaged = KIND == kResidual || kI8Tconv;  // producers read TMA-staged input boxes
   constexpr int kLpr = NT == 32 ? 8 : 16;  // residual lanes per row (C = 32 uses eight)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -498,8 +612,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   uint64_t* raw_empty = bars + 3 * S + 6;     // [2]
   uint64_t* table_full = bars + 3 * S + 8;    // [2]
   uint64_t* table_empty = bars + 3 * S + 10;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 12);
-  int* table = reinterpret_cast<int*>(bars + 3 * S + 13);
+  uint64_t* scale_full = bars + 3 * S + 12;   // [2] int8: a tile's row scales are written
+  uint64_t* scale_empty = bars + 3 * S + 14;  // [2] int8: the epilogue has read them
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 16);
+  int* table = reinterpret_cast<int*>(bars + 3 * S + 17);
+  float* scales = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 512 + Cfg::kTable);  // [2][2][128]
+  uint32_t* rowmax = reinterpret_cast<uint32_t*>(scales + 4 * kTileM);                            // [128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_kb = a.num_kblocks;
@@ -514,8 +632,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      // A transposed conv's A operand is one TMA load (transaction count only).
-      mbar_init(&a_full[s], KIND == kTconv ? 1 : kProducerWarps);
+      // A bf16 transposed conv's A operand is one TMA load (transaction count only).
+      mbar_init(&a_full[s], (KIND == kTconv && !kI8) ? 1 : kProducerWarps);
       mbar_init(&b_full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -526,9 +644,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       mbar_init(&raw_empty[b], kProducerWarps);
       mbar_init(&table_full[b], 1);
       mbar_init(&table_empty[b], kProducerWarps);
+      mbar_init(&scale_full[b], kI8Res ? kProducerWarps : 1);
+      mbar_init(&scale_empty[b], kEpilogueWarps);
     }
     fence_mbar_init();
   }
+  if (kI8Res && threadIdx.x < kTileM) rowmax[threadIdx.x] = 0u;
   if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
@@ -539,8 +660,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   const uint32_t tmem = *tmem_slot;
 
   if (warp < kProducerWarps) {
-    // ---- A producers (a transposed conv has none: its A operand is TMA-loaded whole)
-    if (KIND == kTconv) goto done;
+    // ---- A producers (a bf16 transposed conv has none: its A operand is TMA-loaded whole)
+    if (KIND == kTconv && !kI8) goto done;
     if (KIND == kResidual && kLpr == 8) {
       // C = 32: channels 32-63 of every A stage stay zero.
       for (int s = 0; s < S; ++s)
@@ -548,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           for (int k = 32; k < 64; k += 4)
             put_a4<MODE>(a_base + s * Cfg::kAStage, r, k, make_float4(0.f, 0.f, 0.f, 0.f));
     }
-    uint32_t g = 0, ti = 0;
+    uint32_t g = 0, g2 = 0, ti = 0;  // stage, staged-box and tile counters
     bool ok = true;
     uint32_t walk_lo = 0, walk_hi = 0;
     constexpr int kRpg = 16 * kLpr / 32;
@@ -570,10 +691,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       for (int u = 1; u < kRpg; ++u)
         chain = chain && walk_row(walk_lo, walk_hi, u) == (int)(walk_lo & 255) + u * a.dilation;
     }
+    const int res_boxes = a.k_channels < kKBlock ? 1 : a.k_channels / kKBlock;  // residual boxes per tile
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++ti) {
       const int m0 = tile_m(t) * kTileM;
       const bool write_state = tile_n(t) == 0;
-      const StreamTable tab = table_at(table + (ti & 1) * kTableInts, m0, a.rows_per_stream);
+      int* tbase = table + (ti & 1) * Cfg::kTableI;
+      const StreamTable tab = table_at(tbase, m0, a.rows_per_stream);
       bool regular = false;
       if (KIND != kTestGemm) {
         ok = named_barrier_and(2, kProducerThreads,
@@ -585,41 +708,108 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         }
         if (KIND == kResidual && a.rows - m0 < kTileM) regular = false;
       }
-      for (int kb = 0; kb < num_kb; ++kb, ++g) {
-        const int s = g % S;
-        const uint32_t ph = (g / S) & 1;
-        const int rb = g & 1;
-        // All producer threads leave together on a timeout, so none is left
-        // waiting at a named barrier inside a producer.
-        bool ready = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer);
-        if (kStaged && ready) ready = mbar_wait(&raw_full[rb], (g >> 1) & 1, a.status, kDevTimeoutProducer);
+      const bool partial = a.rows - m0 < kTileM;
+      if constexpr (kI8Res) {
+        // Pass 1: depthwise + Snake of every 64-channel block into the CTA's
+        // scratch, with each row's max |value| (reference ip_prepare: one
+        // activation scale per time step over all input channels).
+        for (int kb = 0; kb < res_boxes && ok; ++kb, ++g2) {
+          const int rb = g2 & 1;
+          ok = named_barrier_and(2, kProducerThreads,
+                                 mbar_wait(&raw_full[rb], (g2 >> 1) & 1, a.status, kDevTimeoutProducer));
+          if (!ok) break;
+          produce_residual<MODE, kLpr>(a, m0, kb, nullptr, reinterpret_cast<const float*>(raw_base + rb * Cfg::kRaw),
+                                       warp, lane, write_state, tab, partial ? iwalk_lo : walk_lo,
+                                       partial ? iwalk_hi : walk_hi, regular, rowmax);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&raw_empty[rb]);
+        }
+        if (!ok) break;
+        // Row scales into this tile's buffer, once the epilogue has read the
+        // buffer's previous tile.
+        bool ready = true;
+        if (threadIdx.x == 0) ready = mbar_wait(&scale_empty[ti & 1], ((ti >> 1) & 1) ^ 1, a.status, kDevTimeoutProducer);
         ok = named_barrier_and(2, kProducerThreads, ready);
         if (!ok) break;
-        uint8_t* a_stage = a_base + s * Cfg::kAStage;
-        if (KIND == kStem) {
-          produce_stem<MODE>(a, a_stage, warp, lane, write_state, tab);
-        } else if (KIND == kResidual) {
-          const bool partial = a.rows - m0 < kTileM;
-          produce_residual<MODE, kLpr>(a, m0, kb, a_stage, reinterpret_cast<const float*>(raw_base + rb * Cfg::kRaw),
-                                       warp, lane, write_state, tab, partial ? iwalk_lo : walk_lo,
-                                       partial ? iwalk_hi : walk_hi, regular);
-        } else {
-          produce_test<MODE>(a, m0, kb, a_stage, warp, lane);
+        float* sx = scales + (ti & 1) * 2 * kTileM;
+        if (threadIdx.x < kTileM) {
+          sx[threadIdx.x] = quant_scale(__uint_as_float(rowmax[threadIdx.x]));
+          rowmax[threadIdx.x] = 0u;
         }
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          if (kStaged) mbar_arrive(&raw_empty[rb]);
-          mbar_arrive(&a_full[s]);
+        named_barrier(2, kProducerThreads);
+        if (lane == 0) mbar_arrive(&scale_full[ti & 1]);
+        // Pass 2: quantise 128-channel blocks into the s8 A tiles.
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          ok = named_barrier_and(2, kProducerThreads, mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer));
+          if (!ok) break;
+          quantize_residual_i8(a, kb, a_base + s * Cfg::kAStage, sx, warp, lane);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[s]);
+        }
+      } else if constexpr (kI8Tconv) {
+        const float* sc = reinterpret_cast<const float*>(tbase + kTableInts);
+        for (int kb = 0; kb < num_kb && ok; ++kb, ++g) {
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          ok = named_barrier_and(2, kProducerThreads, mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer));
+          if (!ok) break;
+          uint8_t* a_stage = a_base + s * Cfg::kAStage;
+          for (int h = 0; h < 2 && ok; ++h, ++g2) {
+            const int rb = g2 & 1;
+            ok = named_barrier_and(2, kProducerThreads,
+                                   mbar_wait(&raw_full[rb], (g2 >> 1) & 1, a.status, kDevTimeoutProducer));
+            if (!ok) break;
+            produce_tconv_i8(a, kb, h, a_stage, reinterpret_cast<const float*>(raw_base + rb * Cfg::kRaw), sc,
+                             sc + kTileM, warp, lane, tab);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[rb]);
+          }
+          if (!ok) break;
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[s]);
+        }
+      } else {
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          const int rb = g & 1;
+          // All producer threads leave together on a timeout, so none is left
+          // waiting at a named barrier inside a producer.
+          bool ready = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer);
+          if (kStaged && ready) ready = mbar_wait(&raw_full[rb], (g >> 1) & 1, a.status, kDevTimeoutProducer);
+          ok = named_barrier_and(2, kProducerThreads, ready);
+          if (!ok) break;
+          uint8_t* a_stage = a_base + s * Cfg::kAStage;
+          if (KIND == kStem) {
+            produce_stem<MODE>(a, a_stage, warp, lane, write_state, tab);
+          } else if (KIND == kResidual) {
+            produce_residual<MODE, kLpr>(a, m0, kb, a_stage, reinterpret_cast<const float*>(raw_base + rb * Cfg::kRaw),
+                                         warp, lane, write_state, tab, partial ? iwalk_lo : walk_lo,
+                                         partial ? iwalk_hi : walk_hi, regular, nullptr);
+          } else {
+            produce_test<MODE>(a, m0, kb, a_stage, warp, lane);
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (kStaged) mbar_arrive(&raw_empty[rb]);
+            mbar_arrive(&a_full[s]);
+          }
         }
       }
       __syncwarp();
       if (KIND != kTestGemm && lane == 0) mbar_arrive(&table_empty[ti & 1]);
     }
   } else if (warp < kLoaderWarp) {
-    // ---- epilogue: per 16-column chunk, TMEM -> registers -> bias (+ skip) ->
-    // next layer's pointwise prologue -> global stores (one row per lane). The
-    // next chunk's TMEM load and skip input are in flight while a chunk computes.
+    // ---- epilogue: per 16-column chunk, TMEM -> registers -> (int8: integer
+    // accumulators rescaled by weight-row and activation-row scales) + bias
+    // (+ skip) -> next layer's pointwise prologue -> global stores (one row per
+    // lane). The next chunk's TMEM load and skip input are in flight while a
+    // chunk computes (bf16 paths).
     constexpr int kChunks = NT / kEpiCols;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int etid = threadIdx.x - kProducerThreads;
@@ -644,27 +834,29 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         const int n = n0 + j;
         const int ch = KIND == kTconv ? n % a.c_out : n;
         cf[j] = a.bias ? __ldg(a.bias + ch) : 0.f;
-        if (epi & (kEpiS | kEpiPlanes)) {
+        if (OUT != kOutNone) {
           cf[NT + j] = __ldg(a.next_alpha + ch);
           cf[2 * NT + j] = __ldg(a.next_recip + ch);
         }
-        if (epi & kEpiPlanes) {
+        if (kOutPl || kOutA) {
           cf[3 * NT + j] = __ldg(a.next_scale + ch);
           cf[4 * NT + j] = __ldg(a.next_offset + ch);
         }
+        if (kI8 && a.w_scale) cf[5 * NT + j] = __ldg(a.w_scale + n);
+        if (kI8Tconv) cf[6 * NT + j] = __ldg(a.w_scale2 + n);
       }
       if (!named_barrier_and(3, kEpilogueWarps * 32, ok)) break;
       const int row0 = m0 + q * 32;
       const int g = row0 + lane;
-      // Plane writers: this row's time step and, at a stream's first and last
-      // step, the next layer's history (old window row, new ring row).
+      const int N = a.rows_per_stream;
+      // Plane / activation writers: this row's time step and, at a stream's
+      // first and last step, the next layer's history (old window row, new ring row).
       int t_row = -1;
       const uint32_t* hist_old = nullptr;
       uint32_t* hist_new = nullptr;
       int* head_out = nullptr;
       int head_next = 0;
-      if ((epi & kEpiPlanes) && g < a.rows) {
-        const int N = a.rows_per_stream;
+      if ((kOutPl || kOutA) && g < a.rows) {
         const int sid = g / N;
         t_row = g - sid * N;
         if (a.state.pool && (t_row == 0 || t_row == N - 1)) {
@@ -672,7 +864,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           float* slot = slot_base(a.state, code);
           const HistRef& h = a.hist_next;  // one row (H = 1): window = ring row head
           const int head = (code & 2) ? 0 : head_table(slot, code & 1)[h.index];
-          if (t_row == 0 && !(code & 2)) hist_old = reinterpret_cast<const uint32_t*>(slot + h.ring + head * h.width);
+          if (t_row == 0 && !(code & 2) && kOutPl)
+            hist_old = reinterpret_cast<const uint32_t*>(slot + h.ring + head * h.width);
           if (t_row == N - 1) {
             hist_new = reinterpret_cast<uint32_t*>(slot + h.ring + (head ^ 1) * h.width);
             if (n0 == 0) {
@@ -690,7 +883,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         hw[j] = hist_old ? __ldg(reinterpret_cast<const uint4*>(hist_old + n0) + j) : make_uint4(0u, 0u, 0u, 0u);
       if (!(ok = mbar_wait(&acc_full[buf], (i >> 1) & 1, a.status, kDevTimeoutEpilogue))) continue;
       tc_fence_after();
-      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * NT);
+      // int8: this row's activation scales (current and previous tap).
+      float sx = 1.f, sxp = 1.f;
+      if constexpr (kI8 && KIND != kTestGemm) {
+        if (!(ok = mbar_wait(&scale_full[buf], (i >> 1) & 1, a.status, kDevTimeoutEpilogue))) continue;
+        const float* sb = scales + buf * 2 * kTileM;
+        sx = sb[q * 32 + lane];
+        if (kI8Tconv) sxp = sb[kTileM + q * 32 + lane];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&scale_empty[buf]);
+      }
+      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * Cfg::kAccCols);
+      float rmax = 0.f;  // kEpiAct: max |output| of this row over the tile's columns
       uint32_t r[16];
       tmem_ld16_async(base, r);
       tmem_wait_ld(r);
@@ -699,6 +903,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         const int n = n0 + c * kEpiCols;
         const int j0 = c * kEpiCols;
         uint32_t rn[16];
+        uint32_t rp[16];  // int8 transposed conv: previous-tap accumulator
+        if constexpr (kI8Tconv) {
+          tmem_ld16_async(base + NT + c * kEpiCols, rp);
+          tmem_wait_ld(rp);
+        }
         if (c + 1 < kChunks) tmem_ld16_async(base + (c + 1) * kEpiCols, rn);
         float4 xn[4];  // next chunk's skip input
         load_skip<KIND>(a, c + 1 < kChunks ? g : a.rows, n + kEpiCols, xn);
@@ -711,10 +920,34 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float4 b = lds4(cf + j0 + 4 * j);
-          v[4 * j] = __uint_as_float(r[4 * j]) + b.x;
-          v[4 * j + 1] = __uint_as_float(r[4 * j + 1]) + b.y;
-          v[4 * j + 2] = __uint_as_float(r[4 * j + 2]) + b.z;
-          v[4 * j + 3] = __uint_as_float(r[4 * j + 3]) + b.w;
+          float4 acc;
+          if constexpr (kI8) {
+            // Reference ip_run_rows: float(dot) * (s_w * s_x); transposed conv:
+            // (current + previous) + bias; residual: x + (product + bias).
+            const float4 sw = lds4(cf + 5 * NT + j0 + 4 * j);
+            acc.x = __fmul_rn(__int2float_rn((int)r[4 * j]), __fmul_rn(sw.x, sx));
+            acc.y = __fmul_rn(__int2float_rn((int)r[4 * j + 1]), __fmul_rn(sw.y, sx));
+            acc.z = __fmul_rn(__int2float_rn((int)r[4 * j + 2]), __fmul_rn(sw.z, sx));
+            acc.w = __fmul_rn(__int2float_rn((int)r[4 * j + 3]), __fmul_rn(sw.w, sx));
+            if constexpr (kI8Tconv) {
+              const float4 sw2 = lds4(cf + 6 * NT + j0 + 4 * j);
+              acc.x = __fadd_rn(acc.x, __fmul_rn(__int2float_rn((int)rp[4 * j]), __fmul_rn(sw2.x, sxp)));
+              acc.y = __fadd_rn(acc.y, __fmul_rn(__int2float_rn((int)rp[4 * j + 1]), __fmul_rn(sw2.y, sxp)));
+              acc.z = __fadd_rn(acc.z, __fmul_rn(__int2float_rn((int)rp[4 * j + 2]), __fmul_rn(sw2.z, sxp)));
+              acc.w = __fadd_rn(acc.w, __fmul_rn(__int2float_rn((int)rp[4 * j + 3]), __fmul_rn(sw2.w, sxp)));
+            }
+            if (KIND == kTestGemm) {
+              acc = make_float4(__int2float_rn((int)r[4 * j]), __int2float_rn((int)r[4 * j + 1]),
+                                __int2float_rn((int)r[4 * j + 2]), __int2float_rn((int)r[4 * j + 3]));
+            }
+          } else {
+            acc = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
+                              __uint_as_float(r[4 * j + 3]));
+          }
+          v[4 * j] = acc.x + b.x;
+          v[4 * j + 1] = acc.y + b.y;
+          v[4 * j + 2] = acc.z + b.z;
+          v[4 * j + 3] = acc.w + b.w;
           if (KIND == kResidual) {
             v[4 * j] = x[j].x + v[4 * j];
             v[4 * j + 1] = x[j].y + v[4 * j + 1];
@@ -731,29 +964,29 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
             off = (size_t)g * a.c_out + n;
           }
           if (epi & kEpiX) st4(a.out_x + off, v);
-          if (epi & (kEpiS | kEpiPlanes)) {
+          if constexpr (OUT != kOutNone) {
             float s[16];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               float4 u = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-              if (epi & kEpiPlanes) {
+              if (kOutPl || kOutA) {
                 const float4 sc = lds4(cf + 3 * NT + j0 + 4 * j), of = lds4(cf + 4 * NT + j0 + 4 * j);
                 u = make_float4(__fadd_rn(__fmul_rn(u.x, sc.x), of.x), __fadd_rn(__fmul_rn(u.y, sc.y), of.y),
                                 __fadd_rn(__fmul_rn(u.z, sc.z), of.z), __fadd_rn(__fmul_rn(u.w, sc.w), of.w));
               }
-              u = snake4(u, lds4(cf + NT + j0 + 4 * j), lds4(cf + 2 * NT + j0 + 4 * j));
+              u = snake4<kI8 || kOutA>(u, lds4(cf + NT + j0 + 4 * j), lds4(cf + 2 * NT + j0 + 4 * j));
               s[4 * j] = u.x;
               s[4 * j + 1] = u.y;
               s[4 * j + 2] = u.z;
               s[4 * j + 3] = u.w;
             }
-            if (epi & kEpiPlanes) {
+            if constexpr (kOutPl) {
               uint32_t hi[8], lo[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) split_bf16(s[2 * j], s[2 * j + 1], hi[j], lo[j]);
               const size_t plane = (size_t)a.rows * a.c_out;
               put_planes(a.out_planes + (size_t)g * a.c_out + n, plane, hi, lo);
-              if (t_row + 1 < a.rows_per_stream) {
+              if (t_row + 1 < N) {
                 put_planes(a.out_planes_prev + (size_t)(g + 1) * a.c_out + n, plane, hi, lo);
               } else if (hist_new) {
                 // New history row, packed per channel as (hi << 16) | lo.
@@ -784,6 +1017,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
               }
             } else {
               st4(a.out_s + off, s);
+              if constexpr (kOutA) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) rmax = fmaxf(rmax, fabsf(s[j]));
+                if (hist_new) st4(reinterpret_cast<float*>(hist_new) + n, s);
+              }
             }
           }
         }
@@ -799,6 +1037,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           for (int j = 0; j < 4; ++j) hw[j] = wn[j];
         }
       }
+      if (kOutA && g < a.rows) a.rowmax_out[(size_t)g * a.rowmax_parts + n0 / NT] = rmax;
       if (head_out) *head_out = head_next;
       tc_fence_before();
       __syncwarp();
@@ -821,7 +1060,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       }
     }
   } else if (warp == kRawWarp) {
-    if (lane == 0 && KIND == kTconv) {
+    if (lane == 0 && KIND == kTconv && !kI8) {
       // ---- transposed-conv A operand: tap 0 from the planes, tap 1 from the
       // shifted planes, hi and lo tiles in one 3-D box
       const int kpt = a.k_channels / kKBlock;
@@ -838,33 +1077,75 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           tma_load_3d(a_base + s * Cfg::kAStage, tap ? &a.tmap2 : &a.tmap, cb * kKBlock, m0, 0, &a_full[s]);
         }
       }
-    } else if (lane == 0 && KIND == kResidual) {
-      // ---- residual inputs: tile + causal halo rows of s, then the block's coefficients
-      const int halo = a.box_rows - kTileM;
-      const uint32_t bytes = (uint32_t)a.box_rows * a.raw_pitch * 4;
+    } else if (lane == 0 && (KIND == kResidual || kI8Tconv)) {
+      // ---- staged producer inputs. Residual: per 64-channel block the tile +
+      // causal halo rows of s and the block's coefficients. int8 transposed
+      // conv: per 64-channel half of a K block, input rows m0-1 .. m0+127.
+      const int halo = KIND == kResidual ? a.box_rows - kTileM : 1;
+      const uint32_t bytes = KIND == kResidual ? (uint32_t)a.box_rows * a.raw_pitch * 4 + kResCoefBytes
+                                               : (uint32_t)(kTileM + 1) * 64 * 4;
+      const int boxes = KIND == kResidual ? (a.k_channels < kKBlock ? 1 : a.k_channels / kKBlock) : 2 * num_kb;
       uint32_t g = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         const int m0 = tile_m(t) * kTileM;
-        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+        for (int kb = 0; kb < boxes; ++kb, ++g) {
           const int rb = g & 1;
           if (!(ok = mbar_wait(&raw_empty[rb], ((g >> 1) & 1) ^ 1, a.status, kDevTimeoutLoader))) break;
           uint8_t* dst = raw_base + rb * Cfg::kRaw;
-          mbar_arrive_expect_tx(&raw_full[rb], bytes + kResCoefBytes);
+          mbar_arrive_expect_tx(&raw_full[rb], bytes);
           tma_load_2d(dst, &a.tmap, kb * kKBlock, m0 - halo, &raw_full[rb]);
-          bulk_g2s(dst + kResBoxBytes, a.coef + (size_t)kb * kCoefResidual * 64, kResCoefBytes, &raw_full[rb]);
+          if (KIND == kResidual)
+            bulk_g2s(dst + kResBoxBytes, a.coef + (size_t)kb * kCoefResidual * 64, kResCoefBytes, &raw_full[rb]);
         }
       }
     }
   } else if (warp == kSchedWarp) {
-    // ---- scheduler: per-tile stream/row tables, one tile ahead of the producers
-    if (KIND == kStem || KIND == kResidual) {
+    // ---- scheduler: per-tile stream/row tables (and the int8 transposed
+    // conv's row scales), one tile ahead of the producers
+    if (KIND == kStem || KIND == kResidual || kI8Tconv) {
       uint32_t ti = 0;
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++ti) {
         const int m0 = tile_m(t) * kTileM;
         if (!mbar_wait(&table_empty[ti & 1], ((ti >> 1) & 1) ^ 1, a.status, kDevTimeoutProducer)) break;
-        fill_table(a, m0, table_at(table + (ti & 1) * kTableInts, m0, a.rows_per_stream), lane);
+        int* tbase = table + (ti & 1) * Cfg::kTableI;
+        const StreamTable tab = table_at(tbase, m0, a.rows_per_stream);
+        fill_table(a, m0, tab, lane);
         __syncwarp();
+        if constexpr (kI8Tconv) {
+          // Row scales of the input rows (max over the previous layer's N tiles).
+          float* sc = reinterpret_cast<float*>(tbase + kTableInts);
+          auto row_max = [&](int gr) {
+            float m = 0.f;
+            for (int p = 0; p < a.rowmax_in_parts; ++p) m = fmaxf(m, __ldg(a.rowmax_in + (size_t)gr * a.rowmax_in_parts + p));
+            return m;
+          };
+          const bool write_state = tile_n(t) == 0;
+          for (int r = lane; r < kTileM; r += 32) {
+            const int gr = m0 + r;
+            const int e = tab.row_e[r];
+            const float mx = e >= 0 ? row_max(gr) : 0.f;
+            sc[r] = quant_scale(mx);
+            float prev = 0.f;  // max |x| of the previous time step
+            if (e >= 0) {
+              if (tab.row_t[r] > 0) {
+                prev = row_max(gr - 1);
+              } else if (a.state.pool && !(tab.code[e] & 2)) {
+                prev = __int_as_float(head_table(slot_base(a.state, tab.code[e]), tab.code[e] & 1)[a.hist_max_slot]);
+              }
+              // The history of the next step: this stream's last step's max.
+              if (write_state && a.state.pool && tab.row_t[r] == a.rows_per_stream - 1)
+                head_table(slot_base(a.state, tab.code[e]), (tab.code[e] & 1) ^ 1)[a.hist_max_slot] = __float_as_int(mx);
+            }
+            sc[kTileM + r] = quant_scale(prev);
+          }
+          __syncwarp();
+          if (!mbar_wait(&scale_empty[ti & 1], ((ti >> 1) & 1) ^ 1, a.status, kDevTimeoutProducer)) break;
+          float* sb = scales + (ti & 1) * 2 * kTileM;
+          for (int r = lane; r < 2 * kTileM; r += 32) sb[r] = sc[r];
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&scale_full[ti & 1]);
+        }
         if (lane == 0) mbar_arrive(&table_full[ti & 1]);
       }
     }
@@ -877,7 +1158,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         const int buf = i & 1;
         if (!(ok = mbar_wait(&acc_empty[buf], ((i >> 1) & 1) ^ 1, a.status, kDevTimeoutMma))) break;
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(buf * NT);
+        const uint32_t d = tmem + (uint32_t)(buf * Cfg::kAccCols);
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
@@ -888,13 +1169,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           const uint32_t a0 = smem_u32(a_base + s * Cfg::kAStage);
           const uint32_t b0 = smem_u32(b_base + s * Cfg::kBStage);
 #pragma unroll
-          for (int k = 0; k < kKBlock / 16; ++k) {
-            const uint32_t ko = k * 32;
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t ko = k * 32;  // 32 bytes of K per MMA (16 f16/bf16 or 32 s8)
             const uint32_t acc = (kb | k) ? 1u : 0u;
-            mma_f16(d, smem_desc_sw128(a0 + ko), smem_desc_sw128(b0 + ko), Cfg::kIdesc, acc);
-            if (MODE == kModeSplit) {
-              mma_f16(d, smem_desc_sw128(a0 + ko), smem_desc_sw128(b0 + Cfg::kBTile + ko), Cfg::kIdesc, 1u);
-              mma_f16(d, smem_desc_sw128(a0 + Cfg::kATile + ko), smem_desc_sw128(b0 + ko), Cfg::kIdesc, 1u);
+            if constexpr (kI8) {
+              mma_i8(d, smem_desc_sw128(a0 + ko), smem_desc_sw128(b0 + ko), Cfg::kIdesc, acc);
+              if (kI8Tconv)
+                mma_i8(d + NT, smem_desc_sw128(a0 + Cfg::kATile + ko), smem_desc_sw128(b0 + Cfg::kBTile + ko),
+                       Cfg::kIdesc, acc);
+            } else {
+              mma_f16(d, smem_desc_sw128(a0 + ko), smem_desc_sw128(b0 + ko), Cfg::kIdesc, acc);
+              if (kSplitOperands<MODE>) {
+                mma_f16(d, smem_desc_sw128(a0 + ko), smem_desc_sw128(b0 + Cfg::kBTile + ko), Cfg::kIdesc, 1u);
+                mma_f16(d, smem_desc_sw128(a0 + Cfg::kATile + ko), smem_desc_sw128(b0 + ko), Cfg::kIdesc, 1u);
+              }
+              if (MODE == kModeSplit4)
+                mma_f16(d, smem_desc_sw128(a0 + Cfg::kATile + ko), smem_desc_sw128(b0 + Cfg::kBTile + ko),
+                        Cfg::kIdesc, 1u);
             }
           }
           mma_commit(&empty[s]);
@@ -914,69 +1205,61 @@ done:
 
 static int g_sm_count = 0;
 
-template <int NT, int MODE, int KIND>
+template <int NT, int MODE, int KIND, int OUT>
 static cudaError_t launch_cfg(const LayerArgs& a, cudaStream_t stream) {
   using Cfg = GemmCfg<NT, MODE, KIND>;
   const int tiles = ((a.rows + kTileM - 1) / kTileM) * (a.n_total / NT);
-  const int grid = tiles < g_sm_count ? tiles : g_sm_count;
-  gemm_layer_kernel<NT, MODE, KIND><<<grid, kThreads, Cfg::kSmem, stream>>>(a);
+  int grid = tiles < g_sm_count ? tiles : g_sm_count;
+  if (MODE == kModeI8 && KIND == kResidual && grid > kScratchCtas) grid = kScratchCtas;
+  gemm_layer_kernel<NT, MODE, KIND, OUT><<<grid, kThreads, Cfg::kSmem, stream>>>(a);
   return cudaGetLastError();
 }
 
-template <int NT, int MODE, int KIND>
+template <int NT, int MODE, int KIND, int OUT>
 static cudaError_t set_smem() {
   using Cfg = GemmCfg<NT, MODE, KIND>;
-  return cudaFuncSetAttribute(gemm_layer_kernel<NT, MODE, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  return cudaFuncSetAttribute(gemm_layer_kernel<NT, MODE, KIND, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               Cfg::kSmem);
 }
 
-template <int MODE, int KIND>
-static cudaError_t set_smem_all() {
-  cudaError_t e;
-  if ((e = set_smem<256, MODE, KIND>()) != cudaSuccess) return e;
-  if ((e = set_smem<128, MODE, KIND>()) != cudaSuccess) return e;
-  if ((e = set_smem<64, MODE, KIND>()) != cudaSuccess) return e;
-  return set_smem<32, MODE, KIND>();
-}
-
-template <int MODE, int KIND>
-static cudaError_t launch_nt(const LayerArgs& a, cudaStream_t stream) {
-  switch (a.n_tile) {
-    case 256: return launch_cfg<256, MODE, KIND>(a, stream);
-    case 128: return launch_cfg<128, MODE, KIND>(a, stream);
-    case 64: return launch_cfg<64, MODE, KIND>(a, stream);
-    case 32: return launch_cfg<32, MODE, KIND>(a, stream);
-    default: return cudaErrorInvalidValue;
-  }
-}
+// The (N tile, operand mode, layer kind, epilogue output) combinations the
+// step schedules use; anything else is rejected at launch.
+#define FAV_CONFIGS(X)                                                                                      \
+  X(256, kModeSplit4, kStem, kOutPlanes) X(256, kModeSplit4, kStem, kOutAct)                                \
+  X(128, kModeSplit, kTconv, kOutS) X(64, kModeSplit, kTconv, kOutS) X(128, kModeI8, kTconv, kOutS)         \
+  X(256, kModeF16, kResidual, kOutS) X(128, kModeF16, kResidual, kOutS) X(64, kModeF16, kResidual, kOutS)  \
+  X(32, kModeF16, kResidual, kOutS) X(256, kModeF16, kResidual, kOutPlanes)                                \
+  X(128, kModeF16, kResidual, kOutPlanes) X(64, kModeF16, kResidual, kOutPlanes)                           \
+  X(256, kModeI8, kResidual, kOutS) X(128, kModeI8, kResidual, kOutS) X(256, kModeI8, kResidual, kOutAct)  \
+  X(128, kModeI8, kResidual, kOutAct)                                                                       \
+  X(256, kModeF16, kTestGemm, kOutNone) X(128, kModeF16, kTestGemm, kOutNone)                              \
+  X(64, kModeF16, kTestGemm, kOutNone) X(32, kModeF16, kTestGemm, kOutNone)                                \
+  X(256, kModeSplit, kTestGemm, kOutNone) X(128, kModeSplit, kTestGemm, kOutNone)                          \
+  X(64, kModeSplit, kTestGemm, kOutNone) X(32, kModeSplit, kTestGemm, kOutNone)                            \
+  X(256, kModeI8, kTestGemm, kOutNone) X(128, kModeI8, kTestGemm, kOutNone)                                \
+  X(64, kModeI8, kTestGemm, kOutNone) X(32, kModeI8, kTestGemm, kOutNone)
 
 cudaError_t prepare_kernels() {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
-  if ((e = set_smem_all<kModeSplit, kStem>()) != cudaSuccess) return e;
-  if ((e = set_smem_all<kModeSplit, kTconv>()) != cudaSuccess) return e;
-  if ((e = set_smem_all<kModeF16, kResidual>()) != cudaSuccess) return e;
-  if ((e = set_smem_all<kModeSplit, kTestGemm>()) != cudaSuccess) return e;
-  return set_smem_all<kModeF16, kTestGemm>();
+#define FAV_SET(NT, MODE, KIND, OUT) \
+  if ((e = set_smem<NT, MODE, KIND, OUT>()) != cudaSuccess) return e;
+  FAV_CONFIGS(FAV_SET)
+#undef FAV_SET
+  return cudaSuccess;
 }
 
 cudaError_t launch_gemm_layer(const LayerArgs& a, cudaStream_t stream) {
   if (a.rows <= 0) return cudaSuccess;
   if (a.n_total % a.n_tile) return cudaErrorInvalidValue;
-  switch (a.kind) {
-    case kStem:
-      return a.mode == kModeSplit ? launch_nt<kModeSplit, kStem>(a, stream) : cudaErrorInvalidValue;
-    case kTconv:
-      return a.mode == kModeSplit ? launch_nt<kModeSplit, kTconv>(a, stream) : cudaErrorInvalidValue;
-    case kResidual:
-      return a.mode == kModeF16 ? launch_nt<kModeF16, kResidual>(a, stream) : cudaErrorInvalidValue;
-    case kTestGemm:
-      return a.mode == kModeSplit ? launch_nt<kModeSplit, kTestGemm>(a, stream)
-                                  : launch_nt<kModeF16, kTestGemm>(a, stream);
-    default: return cudaErrorInvalidValue;
-  }
+  const int out = (a.epi & kEpiPlanes) ? kOutPlanes : (a.epi & kEpiAct) ? kOutAct : (a.epi & kEpiS) ? kOutS : kOutNone;
+#define FAV_LAUNCH(NT, MODE, KIND, OUT) \
+  if (a.n_tile == NT && a.mode == MODE && a.kind == KIND && out == OUT) return launch_cfg<NT, MODE, KIND, OUT>(a, stream);
+  FAV_CONFIGS(FAV_LAUNCH)
+#undef FAV_LAUNCH
+  return cudaErrorInvalidValue;
 }
 
 // ------------------------------------------------------------------ final conv
@@ -1065,6 +1348,154 @@ __global__ void __launch_bounds__(kFinalRows) final_kernel(const FinalArgs a) {
 cudaError_t launch_final(const FinalArgs& a, cudaStream_t stream) {
   if (a.rows <= 0) return cudaSuccess;
   final_kernel<<<(a.rows + kFinalRows - 1) / kFinalRows, kFinalRows, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace fav
+
+namespace fav {
+
+// ------------------------------------------------------------- int8 stem
+// The int8 plan's stem on CUDA cores: a quantised cascade follows, so every
+// sum runs in the int8 oracle's order (oracle/exact.py): depthwise taps oldest
+// first then the bias, the 1x1 over input channels in order then the bias,
+// then stage 0's affine and Snake (kEpiAct). Eight rows per block of 256
+// threads; a thread owns 8 output channels.
+constexpr int kStemRows = 8;
+
+__global__ void __launch_bounds__(256) stem_exact_kernel(const __grid_constant__ LayerArgs a) {
+  __shared__ float dwc[kStemRows][kLatentChannels];
+  __shared__ float wmax[kStemRows][8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g0 = blockIdx.x * kStemRows;
+  const int T = a.rows_per_stream;
+  // Depthwise conv (history = last six latent frames) for this block's rows.
+  for (int i = tid; i < kStemRows * kLatentChannels; i += 256) {
+    const int r = i / kLatentChannels, c = i - r * kLatentChannels;
+    const int g = g0 + r;
+    float y = 0.f;
+    if (g < a.rows) {
+      const int s = g / T, t = g - s * T;
+      const float* z0 = a.x + ((size_t)s * kLatentChannels + c) * a.z_stride + a.z_offset;
+      int code = 0, head = 0;
+      const float* ring = nullptr;
+      if (a.state.pool) {
+        code = a.state.slot_codes ? a.state.slot_codes[s] : ((s << 2) | a.state.uniform_code);
+        if (!(code & 2)) {
+          head = head_table(slot_base(a.state, code), code & 1)[a.hist.index];
+          ring = slot_base(a.state, code) + a.hist.ring;
+        }
+      }
+      for (int j = 0; j < 7; ++j) {
+        const int tp = t - 6 + j;
+        float v = 0.f;
+        if (tp >= 0) v = __ldg(z0 + tp);
+        else if (ring) v = ring[((head + 6 + tp) % 12) * kLatentChannels + c];
+        const float p = __fmul_rn(__ldg(a.dw_w + c * 7 + j), v);
+        y = j ? __fadd_rn(y, p) : p;
+      }
+      y = __fadd_rn(y, __ldg(a.dw_b + c));
+      // The stem history of the next step: the last min(T, 6) frames (zeros
+      // before a fresh stream's first frame), written at the stream's last row.
+      if (t == T - 1 && a.state.pool) {
+        for (int tp = T > 6 ? T - 6 : 0; tp < T; ++tp)
+          hist_new_row(a.state, a.hist, code, head, tp, T)[c] = __ldg(z0 + tp);
+        if ((code & 2) && T < 6) {
+          float* fresh = slot_base(a.state, code) + a.hist.ring;
+          for (int j = T; j < 6; ++j) fresh[j * kLatentChannels + c] = 0.f;
+        }
+        if (c == 0) hist_commit_head(a.state, a.hist, code, head, T);
+      }
+    }
+    dwc[r][c] = y;
+  }
+  __syncthreads();
+  // 1x1 64 -> 2048: channels n = 8*tid .. 8*tid+7 for all eight rows.
+  const int n0 = 8 * tid;
+  float acc[8][kStemRows];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int r = 0; r < kStemRows; ++r) acc[i][r] = 0.f;
+  for (int k = 0; k < kLatentChannels; ++k) {
+    float wk[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) wk[i] = __ldg(a.dense_w + (size_t)(n0 + i) * kLatentChannels + k);
+#pragma unroll
+    for (int r = 0; r < kStemRows; ++r) {
+      const float x = dwc[r][k];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float p = __fmul_rn(wk[i], x);
+        acc[i][r] = k ? __fadd_rn(acc[i][r], p) : p;
+      }
+    }
+  }
+  // Epilogue: y = sum + bias; activation Snake(y * scale + offset); per-row max.
+  float rmax[kStemRows];
+#pragma unroll
+  for (int r = 0; r < kStemRows; ++r) {
+    const int g = g0 + r;
+    rmax[r] = 0.f;
+    float act[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int n = n0 + i;
+      const float y = __fadd_rn(acc[i][r], __ldg(a.bias + n));
+      if ((a.epi & kEpiX) && g < a.rows) a.out_x[(size_t)g * a.c_out + n] = y;
+      const float u = __fadd_rn(__fmul_rn(y, __ldg(a.next_scale + n)), __ldg(a.next_offset + n));
+      act[i] = snake_exact(u, __ldg(a.next_alpha + n), __ldg(a.next_recip + n));
+      rmax[r] = fmaxf(rmax[r], fabsf(act[i]));
+    }
+    if (g < a.rows) {
+      float4* dst = reinterpret_cast<float4*>(a.out_s + (size_t)g * a.c_out + n0);
+      dst[0] = make_float4(act[0], act[1], act[2], act[3]);
+      dst[1] = make_float4(act[4], act[5], act[6], act[7]);
+      const int s = g / T, t = g - s * T;
+      if (t == T - 1 && a.state.pool) {
+        // The next layer's (stage 0 transposed conv's) one-row history.
+        const int code = a.state.slot_codes ? a.state.slot_codes[s] : ((s << 2) | a.state.uniform_code);
+        float* slot = slot_base(a.state, code);
+        const HistRef& h = a.hist_next;
+        const int head = (code & 2) ? 0 : head_table(slot, code & 1)[h.index];
+        float4* hn = reinterpret_cast<float4*>(slot + h.ring + (head ^ 1) * h.width + n0);
+        hn[0] = dst[0];
+        hn[1] = dst[1];
+        if (tid == 0) head_table(slot, (code & 1) ^ 1)[h.index] = head ^ 1;
+      }
+    }
+  }
+  // Row maxima over all 2048 channels (rowmax_parts = 1).
+#pragma unroll
+  for (int r = 0; r < kStemRows; ++r) {
+    float m = rmax[r];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) wmax[r][warp] = m;
+  }
+  __syncthreads();
+  if (tid < kStemRows && g0 + tid < a.rows) {
+    float m = 0.f;
+    for (int w = 0; w < 8; ++w) m = fmaxf(m, wmax[tid][w]);
+    a.rowmax_out[(size_t)(g0 + tid) * a.rowmax_parts] = m;
+  }
+}
+
+__global__ void sine_test_kernel(const float* x, int n, float* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = sin_cw(x[i]);
+}
+
+cudaError_t launch_sine_test(const float* x, int n, float* out, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  sine_test_kernel<<<(n + 255) / 256, 256, 0, stream>>>(x, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_stem_exact(const LayerArgs& a, cudaStream_t stream) {
+  if (a.rows <= 0) return cudaSuccess;
+  if (a.n_total != 256 * 8 || a.k_channels != kLatentChannels || a.rowmax_parts != 1) return cudaErrorInvalidValue;
+  stem_exact_kernel<<<(a.rows + kStemRows - 1) / kStemRows, 256, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

@@ -36,6 +36,14 @@ def _options(mode, threads, device):
     return _MODES[mode]
 
 
+# Precisions (values of the C ABI's fav_precision).
+PRECISIONS = {
+    "bf16": (0, "split-bf16 transposed/stem projections, f16 residual projections, fp32 accumulate"),
+    "int8": (1, "W8A8 int8 recipe on the projections with min(rows, cols) >= 128 (s8 tensor cores, per-row weight "
+                "and per-time-step activation scales, s32 accumulate); other layers as bf16"),
+}
+
+
 def _coefficients(weights_arg, source, weight_seed):
     if weights_arg is not None and source is not None:
         raise ValueError("Pass weights or source, not both")
@@ -54,7 +62,7 @@ def _coefficients(weights_arg, source, weight_seed):
 
 
 def setup(*, mode="streaming", threads=1, device="cuda", cache_dir=None, source=None, offline=False,
-          prefer_custom=True, weights=None, weight_seed=0, **_ignored):
+          prefer_custom=True, weights=None, weight_seed=0, precision="bf16", **_ignored):
     """Validate options and describe the selected route, without building a decoder.
 
     Mirrors ``gpu.setup_gpu`` (``gpu.py:55-95``): no decoder is instantiated and
@@ -62,8 +70,10 @@ def setup(*, mode="streaming", threads=1, device="cuda", cache_dir=None, source=
     recipe options of the reference and have no effect on the CUDA route.
     """
     selected = _options(mode, threads, device)
+    if precision not in PRECISIONS:
+        raise ValueError("precision must be bf16 or int8")
     return {"device": "cuda", "backend": "cuda", "selected": "b200_tcgen05", "recipe": "b200_sm100a_v1",
-            "precision": "split-bf16 transposed/stem projections, f16 residual projections, fp32 accumulate",
+            "precision": precision, "precision_detail": PRECISIONS[precision][1],
             "mode": selected, "threads": 1, "cpu_only": False, "fallback": False,
             "reason": "Explicit CUDA request", "sample_rate": _coeffs.SAMPLE_RATE,
             "latent_rate": 25, "latent_channels": 64, "samples_per_latent": _coeffs.HOP_SAMPLES,
@@ -71,14 +81,18 @@ def setup(*, mode="streaming", threads=1, device="cuda", cache_dir=None, source=
 
 
 def load(*, mode="streaming", threads=1, device="cuda", cache_dir=None, source=None, offline=False,
-         prefer_custom=True, weights=None, weight_seed=0, max_streams=256, device_index=0):
-    """Load the CUDA decoder; ``mode="stream"`` is accepted as an alias of ``"streaming"``."""
+         prefer_custom=True, weights=None, weight_seed=0, max_streams=256, device_index=0, precision="bf16"):
+    """Load the CUDA decoder; ``mode="stream"`` is accepted as an alias of ``"streaming"``.
+
+    ``precision="int8"`` runs the reference's W8A8 int8 recipe on its selected
+    projections (experiments/intel-precision), the rest as ``"bf16"``.
+    """
     info = setup(mode=mode, threads=threads, device=device, cache_dir=cache_dir, source=source,
-                 offline=offline, prefer_custom=prefer_custom, weight_seed=weight_seed)
+                 offline=offline, prefer_custom=prefer_custom, weight_seed=weight_seed, precision=precision)
     coeffs, origin = _coefficients(weights, source, weight_seed)
     from .cuda import CUDADecoder
     decoder = CUDADecoder(coeffs, {**info, "coefficient_source": origin}, info["mode"],
-                          max_streams=max_streams, device=device_index)
+                          max_streams=max_streams, device=device_index, precision=PRECISIONS[precision][0])
     import torch
     props = torch.cuda.get_device_properties(decoder._backend.device)
     decoder.info.update(device_name=props.name, sm_count=props.multi_processor_count)

@@ -36,12 +36,16 @@ SIGNATURES = {
     "fav_step": ([_P, _P, ct.c_int32, _P, ct.c_int32, ct.c_int32, _P, _P, _P, ct.c_size_t, _P, _P], ct.c_int32),
     "fav_step_static": ([_P, _P, ct.c_int32, _P, ct.c_int32, ct.c_int32, _P, _P, _P, _P], ct.c_int32),
     "fav_batch_workspace_bytes": ([ct.c_int32, ct.c_int32], ct.c_size_t),
+    "fav_plan_workspace_bytes": ([_P, ct.c_int32, ct.c_int32], ct.c_size_t),
+    "fav_plan_batch_workspace_bytes": ([_P, ct.c_int32, ct.c_int32], ct.c_size_t),
+    "fav_plan_precision": ([_P], ct.c_int32),
     "fav_decode_batch": ([_P, _P, ct.c_int32, ct.c_int32, ct.c_int32, _P, _P, ct.c_size_t, _P, _P], ct.c_int32),
     "fav_step_profile": ([_P, _P, ct.c_int32, _P, ct.c_int32, ct.c_int32, _P, _P, _P, ct.c_size_t, _P,
                           ct.POINTER(ct.c_float), _P], ct.c_int32),
     "fav_debug_step_layers": ([_P, _P, ct.c_int32, _P, ct.c_int32, ct.c_int32, _P, _P, ct.c_size_t, _P,
                                ct.c_int32, ct.POINTER(ct.c_void_p), _P], ct.c_int32),
     "fav_test_gemm": ([_P, ct.c_int32, ct.c_int32, _P, ct.c_int32, ct.c_int32, _P, _P], ct.c_int32),
+    "fav_test_sine": ([_P, ct.c_int32, _P, _P], ct.c_int32),
 }
 
 _lock = threading.Lock()

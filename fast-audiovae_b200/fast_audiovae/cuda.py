@@ -65,7 +65,7 @@ class DeviceBackend:
     failed step may have written the *unread* half of a history slot only.
     """
 
-    def __init__(self, weights, *, max_streams, device=0, batch_chunk_frames=128):
+    def __init__(self, weights, *, max_streams, device=0, batch_chunk_frames=128, precision=0):
         torch = _torch()
         from ._native import Plan, load_library
         self.torch = torch
@@ -76,7 +76,7 @@ class DeviceBackend:
             self.lib = load_library()
             if not self.lib.fav_device_supported():
                 raise RuntimeError("CUDA decoding requires an sm_100 (B200) GPU; no fallback is permitted")
-            self.plan = Plan(weights)
+            self.plan = Plan(weights, precision)
             self.pool = torch.zeros(self.lib.fav_state_pool_bytes(max_streams) // 4, dtype=torch.float32,
                                     device=self.device)
             self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
@@ -139,7 +139,7 @@ class DeviceBackend:
             codes_host.numpy()[:] = codes
             codes_dev = self._buffer("codes_dev", (n,), torch.int32)
             codes_dev.copy_(codes_host, non_blocking=True)
-            ws_bytes = int(lib.fav_step_workspace_bytes(n, frames))
+            ws_bytes = int(lib.fav_plan_workspace_bytes(self.plan.handle, n, frames))
             ws = self._buffer("workspace", (ws_bytes,), torch.uint8)
             check(lib, lib.fav_step(self.plan.handle, self._ptr(self.pool), self.max_streams, self._ptr(codes_dev),
                                     n, frames, self._ptr(z), self._ptr(audio), self._ptr(ws), ws_bytes,
@@ -155,7 +155,7 @@ class DeviceBackend:
             z = self._upload(arrays, frames)
             audio = self._buffer("batch_audio", (n, HOP * frames), torch.float32)
             chunk = min(self.chunk, frames)
-            ws_bytes = int(lib.fav_batch_workspace_bytes(n, chunk))
+            ws_bytes = int(lib.fav_plan_batch_workspace_bytes(self.plan.handle, n, chunk))
             ws = self._buffer("batch_ws", (ws_bytes,), torch.uint8)
             check(lib, lib.fav_decode_batch(self.plan.handle, self._ptr(z), n, frames, chunk, self._ptr(audio),
                                             self._ptr(ws), ws_bytes, self._ptr(self.status), self._stream()))
@@ -169,7 +169,8 @@ class DeviceBackend:
 class CUDADecoder:
     """Immutable CUDA weights shared by independent, serialised streams."""
 
-    def __init__(self, weights, info, mode, *, max_streams=256, device=0, batch_chunk_frames=128, backend=None):
+    def __init__(self, weights, info, mode, *, max_streams=256, device=0, batch_chunk_frames=128, backend=None,
+                 precision=0):
         if mode not in ("batch", "streaming"):
             raise ValueError("mode must be batch or streaming")
         if type(max_streams) is not int or max_streams < 1:
@@ -177,7 +178,8 @@ class CUDADecoder:
         self.mode = mode
         self._max_streams = max_streams if mode == "streaming" else 1
         self._backend = backend if backend is not None else DeviceBackend(
-            weights, max_streams=self._max_streams, device=device, batch_chunk_frames=batch_chunk_frames)
+            weights, max_streams=self._max_streams, device=device, batch_chunk_frames=batch_chunk_frames,
+            precision=precision)
         self._lock = threading.Lock()
         self._free_slots = list(range(self._max_streams - 1, -1, -1))
         self.state_bytes = STATE_BYTES

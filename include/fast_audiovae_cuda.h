@@ -69,7 +69,15 @@ typedef enum fav_precision {
   /* Stem 1x1 and transposed convs: split-bf16 operands (three bf16 MMAs,
    * hi*hi + hi*lo + lo*hi) with fp32 accumulation; residual 1x1s: f16
    * operands, fp32 accumulation; everything else fp32. */
-  FAV_PRECISION_BF16 = 0
+  FAV_PRECISION_BF16 = 0,
+  /* The reference's int8 recipe (experiments/intel-precision: precision.cpp
+   * ip_create / ip_prepare / ip_run_rows, selection tools/rewrite.py:19-30):
+   * every projection with min(rows, cols) >= 128 (transposed convs of stages
+   * 0-4, one matrix per tap; residual 1x1s of stages 0-3) runs W8A8 on s8
+   * tensor cores: per-row weight scales, per-time-step activation scales over
+   * all input channels, round half to even, exact s32 dot, fp32 rescale. The
+   * other layers run as FAV_PRECISION_BF16. */
+  FAV_PRECISION_INT8 = 1
 } fav_precision;
 
 typedef struct fav_plan fav_plan;
@@ -110,6 +118,11 @@ FAV_API size_t fav_plan_bytes(const fav_plan *plan);
 FAV_API size_t fav_state_pool_bytes(int32_t num_slots);
 /* Workspace bytes one fav_step with n_streams x frames needs. */
 FAV_API size_t fav_step_workspace_bytes(int32_t n_streams, int32_t frames);
+/* Workspace bytes one fav_step with this plan needs: fav_step_workspace_bytes
+ * plus, for a FAV_PRECISION_INT8 plan, the int8 residual units' scratch. */
+FAV_API size_t fav_plan_workspace_bytes(const fav_plan *plan, int32_t n_streams, int32_t frames);
+/* The plan's precision (fav_precision), -1 for NULL. */
+FAV_API int32_t fav_plan_precision(const fav_plan *plan);
 
 /* One decoder step for n_streams independent streams, each decoding `frames`
  * new latent frames (the reference's MPSModel.decode(z, states) for a batch of
@@ -118,7 +131,7 @@ FAV_API size_t fav_step_workspace_bytes(int32_t n_streams, int32_t frames);
  *     fresh=1 starts the stream from zero history (reference decode(z, {})).
  *     The advanced heads are written to head table (read_table ^ 1) of `slot`.
  *   latents [n_streams][64][frames], audio [n_streams][1920*frames] (device).
- *   workspace: >= fav_step_workspace_bytes(n_streams, frames) device bytes.
+ *   workspace: >= fav_plan_workspace_bytes(plan, n_streams, frames) device bytes.
  *   status: device uint32 word, 0 on entry; nonzero after the step means a
  *     kernel gave up a bounded wait (FAV_TIMEOUT class failure). May be NULL.
  * Slots in one call must be distinct. */
@@ -152,6 +165,8 @@ FAV_API int32_t fav_step_static(const fav_plan *plan, float *state_pool, int32_t
 /* Workspace bytes fav_decode_batch needs for n_clips clips decoded in chunks
  * of chunk_frames frames (activations plus a temporary history pool). */
 FAV_API size_t fav_batch_workspace_bytes(int32_t n_clips, int32_t chunk_frames);
+/* fav_decode_batch workspace for this plan (see fav_plan_workspace_bytes). */
+FAV_API size_t fav_plan_batch_workspace_bytes(const fav_plan *plan, int32_t n_clips, int32_t chunk_frames);
 /* Batch decode of n_clips independent clips [n_clips][64][frames] from zero
  * history (reference GPUDecoder.decode, gpu.py:187-194). Long clips are
  * decoded in chunks of chunk_frames with carried history, which gives the same
@@ -182,9 +197,16 @@ FAV_API int32_t fav_debug_step_layers(const fav_plan *plan, float *state_pool, i
 
 /* Engine self-test (diagnostic, no reference counterpart): C[M][N] = A[M][K] * B[N][K]^T
  * through the tcgen05 GEMM engine. a, c device fp32; b host fp32.
- * mode 0 = f16 operands, 1 = split-bf16. Synchronises. */
+ * mode 0 = f16 operands, 1 = split-bf16, 2 = s8 (A and B hold integers in
+ * [-127, 127]; C is the exact integer product). Synchronises. */
 FAV_API int32_t fav_test_gemm(const float *a, int32_t m, int32_t k, const float *b, int32_t n, int32_t mode,
                               float *c, void *cuda_stream);
+
+/* Diagnostic (no reference counterpart): out[i] = the fixed-order sine the
+ * int8 path's Snake uses (Cody-Waite reduction, Taylor polynomials; the int8
+ * oracle's oracle/exact.py sin_cw), for device arrays x and out of n floats.
+ * Asynchronous on cuda_stream. */
+FAV_API int32_t fav_test_sine(const float *x, int32_t n, float *out, void *cuda_stream);
 
 #ifdef __cplusplus
 }

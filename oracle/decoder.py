@@ -125,6 +125,13 @@ class Decoder:
         p = f"stage{i}.residual{j}.pointwise."
         return pointwise(h, self.w[p + "weight"], self.w[p + "bias"])
 
+    # Elementwise and depthwise hooks (the int8 recipe oracle fixes their fp32 operation order).
+    def snake(self, x, alpha, reciprocal):
+        return snake(x, alpha, reciprocal)
+
+    def depthwise(self, x, history, weight, bias, dilation):
+        return causal_conv(x, history, weight, bias, dilation, x.shape[1])
+
     @torch.inference_mode()
     def decode(self, z, states=None, trace=None):
         """One step: ``z`` [1,64,T] (numpy or tensor) -> (audio [1,1,1920T], states).
@@ -144,26 +151,25 @@ class Decoder:
         if z.shape[-1] == 0:
             return z.new_empty((1, 1, 0)), {k: v.clone() for k, v in history.items()}
         out = {}
-        x, out["stem.history"] = causal_conv(z, history["stem.history"], w["stem.weight"],
-                                             w["stem.bias"], 1, 64)
+        x, out["stem.history"] = self.depthwise(z, history["stem.history"], w["stem.weight"], w["stem.bias"], 1)
         x = keep(self.stem_pointwise(x))
         for i in range(len(RATES)):
             p = f"stage{i}."
             x = x * w[p + "scale"].reshape(1, -1, 1)
             x = x + w[p + "offset"].reshape(1, -1, 1)
             key = p + "transpose.history"
-            x, out[key] = self.transpose(i, snake(x, w[p + "snake.alpha"], w[p + "snake.reciprocal"]),
+            x, out[key] = self.transpose(i, self.snake(x, w[p + "snake.alpha"], w[p + "snake.reciprocal"]),
                                          history[key])
             keep(x)
             for j, d in enumerate(DILATIONS):
                 r = f"{p}residual{j}."
                 key = r[:-1] + ".history"
-                before = snake(x, w[r + "pre.alpha"], w[r + "pre.reciprocal"])
-                branch, out[key] = causal_conv(before, history[key], w[r + "depthwise.weight"],
-                                               w[r + "depthwise.bias"], d, before.shape[1])
-                branch = snake(branch, w[r + "post.alpha"], w[r + "post.reciprocal"])
+                before = self.snake(x, w[r + "pre.alpha"], w[r + "pre.reciprocal"])
+                branch, out[key] = self.depthwise(before, history[key], w[r + "depthwise.weight"],
+                                                  w[r + "depthwise.bias"], d)
+                branch = self.snake(branch, w[r + "post.alpha"], w[r + "post.reciprocal"])
                 x = keep(x + self.residual_pointwise(i, j, branch))
-        before = snake(x, w["final.snake.alpha"], w["final.snake.reciprocal"])
+        before = self.snake(x, w["final.snake.alpha"], w["final.snake.reciprocal"])
         x, out["final.history"] = causal_conv(before, history["final.history"], w["final.weight"],
                                               w["final.bias"], 1, 1)
         return torch.tanh(x), out

@@ -25,6 +25,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
+from . import exact
 from .decoder import Decoder, RATES
 
 INT8_MIN_DIM = 128
@@ -93,6 +94,17 @@ class Int8RecipeDecoder(Decoder):
     def __init__(self, weights):
         super().__init__(weights)
         self.selected = set(selected_matrices())
+
+    # The fp32 layers around the quantised projections run in one fixed
+    # operation order (``oracle.exact``), the order the CUDA int8 path uses.
+    def snake(self, x, alpha, reciprocal):
+        return exact.snake_exact(x, alpha, reciprocal)
+
+    def depthwise(self, x, history, weight, bias, dilation):
+        return exact.depthwise_exact(x, history, weight, bias, dilation)
+
+    def stem_pointwise(self, x):
+        return exact.pointwise_exact(x, self.w["pointwise.weight"], self.w["pointwise.bias"])
 
     def transpose(self, i, x, history):
         if f"stage{i}.transpose" not in self.selected:

@@ -18,7 +18,8 @@ Outputs (small ``.npz`` files next to this script):
   own check (``experiments/intel-precision/native/check_micro.py:80-87``), the
   full-range signedness cases and the exact-zero case (``:108-114``).
 * ``int8_decoder_seed0.npz``: the int8-recipe decoder with every W8A8 product
-  computed by the compiled reference core, latents seed 0, 3 frames.
+  computed by the compiled reference core, latents seed 0, 3 frames (the fp32
+  layers around the products in ``oracle.exact``'s operation order).
 * ``elementwise.npz``: the reference x86 C kernels (``native_kernels.c``,
   scalar libm sine) for fused Snake -> DW7 -> Snake at dilations 1/3/9 and
   ``skip + (product + bias)``.

@@ -1,0 +1,171 @@
+"""The int8 (W8A8) path on a B200 against the reference's int8 recipe (``-m gpu``).
+
+The recipe (experiments/intel-precision: precision.cpp backend 0, selection
+tools/rewrite.py:19-30) quantises every projection with min(rows, cols) >= 128:
+per-row weight scales, per-time-step activation scales over all input
+channels, round half to even, exact integer dot, fp32 rescale. The oracle
+(``oracle.int8_recipe``) restates it bit-exactly against the compiled reference
+core (tests/test_int8_recipe.py). Gate: SNR >= 35 dB against the recipe's
+output. The recipe itself is only ~26-27 dB from the fp32 decoder, so the test
+also checks that the int8 arithmetic is really in use (the output sits far
+from fp32 and close to the recipe).
+
+A quantised cascade amplifies any difference before a quantisation step into
+whole-step rounding flips (one ulp at the stem output moves the recipe's own
+output to ~38 dB), so the int8 path runs the fp32 layers up to its last
+quantised projection in the oracle's operation order (``oracle.exact``) and
+matches the oracle bit for bit there; the layers after it (stage 4 residual
+units, stage 5) run the bf16 path's operands.
+"""
+import ctypes as ct
+
+import numpy as np
+import pytest
+import torch
+
+from fast_audiovae import _native, build
+from fast_audiovae import weights as W
+from oracle.decoder import Decoder, discrepancy
+from oracle.int8_recipe import Int8RecipeDecoder
+
+pytestmark = pytest.mark.gpu
+
+SNR_VS_RECIPE_DB = 35.0
+INT8 = 1
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    if not build.LIBRARY.exists():
+        build.build()
+    lib = _native.load_library()
+    assert lib.fav_device_supported(), "not an sm_100 GPU"
+    return lib
+
+
+@pytest.fixture(scope="module")
+def weights0():
+    return W.seeded_weights(0)
+
+
+@pytest.fixture(scope="module")
+def int8_batch(lib, weights0):
+    from fast_audiovae.cuda import CUDADecoder
+    return CUDADecoder(weights0, {}, "batch", precision=INT8)
+
+
+@pytest.fixture(scope="module")
+def int8_stream(lib, weights0):
+    from fast_audiovae.cuda import CUDADecoder
+    return CUDADecoder(weights0, {}, "streaming", max_streams=16, precision=INT8)
+
+
+def test_engine_s8_gemm_is_exact(lib):
+    """tcgen05 kind::i8 through the engine: integer operands, exact s32 result."""
+    rng = np.random.default_rng(3)
+    for m, k, n in [(200, 320, 128), (64, 128, 256), (300, 256, 64)]:
+        a = rng.integers(-127, 128, (m, k)).astype(np.float32)
+        b = rng.integers(-127, 128, (n, k)).astype(np.float32)
+        c = torch.full((m, n), float("nan"), device="cuda")
+        ad = torch.from_numpy(a).cuda()
+        _native.check(lib, lib.fav_test_gemm(ct.c_void_p(ad.data_ptr()), m, k, b.ctypes.data_as(ct.c_void_p), n, 2,
+                                             ct.c_void_p(c.data_ptr()),
+                                             ct.c_void_p(torch.cuda.current_stream().cuda_stream)))
+        want = (a.astype(np.int64) @ b.astype(np.int64).T).astype(np.float32)
+        assert np.array_equal(c.cpu().numpy(), want), (m, k, n)
+
+
+def test_fixed_order_sine_matches_oracle_bitwise(lib):
+    """The int8 path's Snake sine equals the oracle's ``sin_cw`` bit for bit."""
+    from oracle import exact
+    x = torch.cat([torch.linspace(-40, 40, 400001), torch.randn(100000) * 8]).to(torch.float32)
+    xd = x.cuda()
+    out = torch.empty_like(xd)
+    _native.check(lib, lib.fav_test_sine(ct.c_void_p(xd.data_ptr()), x.numel(), ct.c_void_p(out.data_ptr()),
+                                         ct.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    want = exact.sin_cw(x)
+    assert torch.equal(out.cpu().view(torch.int32), want.view(torch.int32))
+
+
+LAST_QUANTISED_LAYER = 17  # stage 4's transposed conv (layers: stem 0, stage i conv 1 + 4i, units 2 + 4i + j)
+
+
+@pytest.mark.parametrize("streams,frames", [(1, 6), (3, 2)])
+def test_layers_bitwise_to_the_last_quantised_projection(lib, weights0, streams, frames):
+    """Every layer up to stage 4's transposed conv equals the recipe oracle bit for bit."""
+    plan = _native.Plan(weights0, INT8)
+    zs = [W.seeded_latents(200 + s, frames) for s in range(streams)]
+    traces = []
+    for z in zs:
+        trace = []
+        Int8RecipeDecoder(weights0).decode(z, trace=trace)
+        traces.append(trace)
+    z = torch.from_numpy(np.concatenate(zs, 0)).cuda()
+    ws_bytes = lib.fav_plan_workspace_bytes(plan.handle, streams, frames)
+    ws = torch.empty(ws_bytes // 4, dtype=torch.float32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for layer in range(LAST_QUANTISED_LAYER + 1):
+        out = ct.c_void_p()
+        _native.check(lib, lib.fav_debug_step_layers(plan.handle, None, 0, None, streams, frames,
+                                                     ct.c_void_p(z.data_ptr()), ct.c_void_p(ws.data_ptr()), ws_bytes,
+                                                     ct.c_void_p(status.data_ptr()), layer, ct.byref(out), stream))
+        torch.cuda.synchronize()
+        assert status.item() == 0
+        ref = torch.cat([t[layer][0].T for t in traces], 0).contiguous()
+        off = (out.value - ws.data_ptr()) // 4
+        got = ws[off:off + ref.numel()].view(ref.shape).cpu()
+        assert torch.equal(got.view(torch.int32), ref.view(torch.int32)), layer
+    plan.close()
+
+
+def test_plan_reports_int8(lib, int8_batch):
+    assert lib.fav_plan_precision(int8_batch._backend.plan.handle) == INT8
+
+
+def test_int8_decode_matches_recipe(weights0, int8_batch):
+    z = W.seeded_latents(0, 25)
+    got = int8_batch.decode(z)
+    recipe = Int8RecipeDecoder(weights0).decode_numpy(z)
+    fp32 = Decoder(weights0).decode_numpy(z)
+    vs_recipe = discrepancy(recipe, got)
+    vs_fp32 = discrepancy(fp32, got)
+    assert vs_recipe["snr_db"] >= SNR_VS_RECIPE_DB, vs_recipe
+    # The int8 arithmetic is in use: far closer to the recipe than to fp32.
+    assert vs_fp32["snr_db"] < vs_recipe["snr_db"] - 10, (vs_fp32, vs_recipe)
+
+
+def test_int8_decode_matches_reference_core_golden(golden, int8_batch):
+    """Golden audio made with every W8A8 product computed by the compiled reference core."""
+    g = golden("int8_decoder_seed0.npz")
+    got = int8_batch.decode(g["z"])
+    d = discrepancy(g["audio"], got)
+    assert d["snr_db"] >= SNR_VS_RECIPE_DB, d
+
+
+def test_int8_streaming_is_bitwise_batch(weights0, int8_batch, int8_stream):
+    z = W.seeded_latents(7, 24)
+    batch = int8_batch.decode(z)
+    with int8_stream.stream() as s:
+        parts = [s.decode_chunk(z[..., t:t + c]) for t, c in zip((0, 1, 3, 10, 11), (1, 2, 7, 1, 13))]
+    got = np.concatenate(parts, axis=-1)
+    assert got.shape == batch.shape
+    assert np.array_equal(got.view(np.uint32), batch.view(np.uint32))
+
+
+def test_int8_many_streams_equal_single_streams(int8_stream):
+    zs = [W.seeded_latents(100 + i, 4) for i in range(6)]
+    streams = [int8_stream.stream() for _ in zs]
+    many = []
+    for t in range(0, 4, 2):
+        many.append(int8_stream.decode_streams(streams, [z[..., t:t + 2] for z in zs]))
+    for s in streams:
+        s.close()
+    for i, z in enumerate(zs):
+        with int8_stream.stream() as one:
+            alone = np.concatenate([one.decode_chunk(z[..., t:t + 2]) for t in range(0, 4, 2)], axis=-1)
+        joined = np.concatenate([many[0][i], many[1][i]], axis=-1)
+        assert np.array_equal(joined.view(np.uint32), alone.view(np.uint32)), i
