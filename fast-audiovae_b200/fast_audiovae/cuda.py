@@ -65,7 +65,7 @@ class DeviceBackend:
     failed step may have written the *unread* half of a history slot only.
     """
 
-    def __init__(self, weights, *, max_streams, device=0, batch_chunk_frames=128, precision=0):
+    def __init__(self, weights, *, max_streams, device=0, batch_chunk_frames=128, precision=0, graphs=True):
         torch = _torch()
         from ._native import Plan, load_library
         self.torch = torch
@@ -82,6 +82,12 @@ class DeviceBackend:
             self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
             self.status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         self.cache = {}
+        # Streaming steps replay a CUDA graph of the step's 26 launches per
+        # (streams, frames, buffers): the first step of a shape runs eagerly,
+        # the second captures, later ones replay (one launch call per step).
+        self.graphs_enabled = graphs
+        self.graphs = {}
+        self.graph_seen = set()
 
     @property
     def plan_bytes(self):
@@ -141,9 +147,23 @@ class DeviceBackend:
             codes_dev.copy_(codes_host, non_blocking=True)
             ws_bytes = int(lib.fav_plan_workspace_bytes(self.plan.handle, n, frames))
             ws = self._buffer("workspace", (ws_bytes,), torch.uint8)
-            check(lib, lib.fav_step(self.plan.handle, self._ptr(self.pool), self.max_streams, self._ptr(codes_dev),
-                                    n, frames, self._ptr(z), self._ptr(audio), self._ptr(ws), ws_bytes,
-                                    self._ptr(self.status), self._stream()))
+            args = (self.plan.handle, self._ptr(self.pool), self.max_streams, self._ptr(codes_dev), n, frames,
+                    self._ptr(z), self._ptr(audio), self._ptr(ws), ws_bytes, self._ptr(self.status))
+            key = (n, frames, z.data_ptr(), audio.data_ptr(), codes_dev.data_ptr(), ws.data_ptr())
+            graph = self.graphs.get(key) if self.graphs_enabled else None
+            if graph is None and self.graphs_enabled and key in self.graph_seen:
+                side = torch.cuda.Stream(self.device)
+                side.wait_stream(torch.cuda.current_stream(self.device))
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=side):
+                    check(lib, lib.fav_step(*args, ct.c_void_p(side.cuda_stream)))
+                torch.cuda.current_stream(self.device).wait_stream(side)
+                self.graphs[key] = graph
+            if graph is not None:
+                graph.replay()
+            else:
+                self.graph_seen.add(key)
+                check(lib, lib.fav_step(*args, self._stream()))
             return self._download(audio)
 
     def decode_many(self, arrays, frames):
@@ -162,6 +182,7 @@ class DeviceBackend:
             return self._download(audio)
 
     def close(self):
+        self.graphs = {}
         if getattr(self, "plan", None) is not None:
             self.plan.close()
 
