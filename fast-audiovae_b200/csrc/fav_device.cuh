@@ -18,6 +18,7 @@ enum DeviceError : uint32_t {
   kDevTimeoutMma = 0x103,
   kDevTimeoutEpilogue = 0x104,
   kDevBadLaunch = 0x105,
+  kDevNonFinite = 0x106,  // the step produced a non-finite audio sample
 };
 
 // A wait that has not completed after this many polls is a bug; the kernel

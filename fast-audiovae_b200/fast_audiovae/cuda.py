@@ -46,6 +46,29 @@ def _latents(value):
     return np.array(value, copy=True, order="C") if value.shape[2] else value
 
 
+def _latents_step(chunks):
+    """``gpu.py:115-122`` for one step of many streams: every chunk a float32
+    ``[1,64,L]`` array of one common L, all finite. Returns the chunks stacked
+    as an owned ``[n,64,L]`` array (one copy, one vectorised finiteness check)."""
+    for value in chunks:
+        if (not isinstance(value, np.ndarray) or value.dtype != np.float32
+                or value.ndim != 3 or value.shape[:2] != (1, 64)):
+            raise ValueError("Latents must be a float32 NumPy array with shape [1,64,L]")
+    if not chunks:
+        return np.empty((0, 64, 0), dtype=np.float32)
+    frames = chunks[0].shape[2]
+    if any(c.shape[2] != frames for c in chunks):
+        raise ValueError("decode_streams requires chunks of equal length")
+    stacked = np.concatenate(chunks, axis=0)
+    if not np.isfinite(stacked).all():
+        raise ValueError("Latents must contain only finite values")
+    return stacked
+
+
+# Kernel status of a step whose audio was not finite (the final kernel's check).
+NONFINITE_STATUS = 0x106
+
+
 def _torch():
     try:
         import torch
@@ -114,8 +137,11 @@ class DeviceBackend:
         n = len(arrays)
         host = self._buffer("z_host", (n, 64, frames), self.torch.float32, pinned=True)
         hn = host.numpy()
-        for i, a in enumerate(arrays):
-            hn[i] = a[0]
+        if isinstance(arrays, np.ndarray):
+            hn[...] = arrays  # already stacked [n, 64, frames]
+        else:
+            for i, a in enumerate(arrays):
+                hn[i] = a[0]
         dev = self._buffer("z_dev", (n, 64, frames), self.torch.float32)
         dev.copy_(host, non_blocking=True)
         return dev
@@ -126,12 +152,11 @@ class DeviceBackend:
         self.status_host.copy_(self.status, non_blocking=True)
         self.torch.cuda.current_stream(self.device).synchronize()
         status = int(self.status_host.item())
+        if status == NONFINITE_STATUS:
+            raise RuntimeError("CUDA model returned nonfinite audio")
         if status:
             raise RuntimeError("CUDA decoder kernel reported status 0x%x" % status)
-        result = host.numpy().copy()
-        if not np.isfinite(result).all():
-            raise RuntimeError("CUDA model returned nonfinite audio")
-        return result
+        return host.numpy().copy()
 
     def step(self, codes, arrays, frames):
         from ._native import check
@@ -283,14 +308,12 @@ class CUDADecoder:
             raise RuntimeError("Load mode='streaming' to create an audio stream")
         if len(streams) != len(chunks):
             raise ValueError("One chunk per stream required")
-        chunks = [_latents(c) for c in chunks]
+        chunks = _latents_step(chunks)
         if not streams:
             return []
         if len({id(s) for s in streams}) != len(streams):
             raise ValueError("A stream may appear only once per step")
-        frames = chunks[0].shape[2]
-        if any(c.shape[2] != frames for c in chunks):
-            raise ValueError("decode_streams requires chunks of equal length")
+        frames = chunks.shape[2]
         if any(s._decoder is not self for s in streams):
             raise ValueError("Stream belongs to another decoder")
         ordered = sorted(streams, key=id)

@@ -38,6 +38,7 @@ class FakeBackend:
             time.sleep(0.001)
             out = []
             for code, z in zip(codes, arrays):
+                z = z if z.ndim == 3 else z[None]  # a stacked [n, 64, L] step yields [64, L] rows
                 slot, fresh, half = code >> 2, bool(code & 2), code & 1
                 states = None if fresh else self.pool.get((slot, half))
                 audio, new = self.oracle.decode(z, states)
