@@ -365,7 +365,7 @@ __device__ __forceinline__ void residual_out(const LayerArgs& a, uint8_t* a_stag
 
 template <int MODE, int LPR>
 __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, const float* raw, int warp,
-                                 int lane, bool write_state, const StreamTable& tab, uint32_t walk_lo,
+                                 int lane, bool hist_writer, const StreamTable& tab, uint32_t walk_lo,
                                  uint32_t walk_hi, bool regular, uint32_t* rowmax) {
   constexpr int kRpg = 16 * LPR / 32;  // rows walked per lane group
   const int C = a.k_channels;
@@ -379,31 +379,37 @@ __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_
   const bool valid = kl < P;
   const int tid = warp * 32 + lane;
   const float* cf = raw + kResBoxBytes / 4 + kl;
-  // New window rows of streams whose last row lies in this tile.
-  if (write_state && a.state.pool) {
+  // New window rows of the streams whose last row lies in this tile (table
+  // entries 0 .. ns-1): one flat loop over (stream, row, quad) so every
+  // producer thread stores independent items.
+  if (hist_writer && a.state.pool) {
     const int g_end = min(m0 + kTileM, a.rows);
+    const int ns = g_end / N - tab.s_lo;
     const int n_new = N < H ? N : H;
     const int quads = P / 4;
-    for (int e = 0; tab.s_lo + e <= (g_end - 1) / N; ++e) {
-      const int s = tab.s_lo + e;
-      const int last = s * N + N - 1;
-      if (last < m0 || last >= g_end) continue;
-      const int code = tab.code[e], head = tab.head[e];
-      for (int it = tid; it < n_new * quads; it += kProducerThreads) {
-        const int q = it / quads, k4 = 4 * (it - q * quads);
-        const int tp = N - n_new + q;
-        *reinterpret_cast<float4*>(hist_new_row(a.state, a.hist, code, head, tp, N) + kb * kKBlock + k4) =
-            lds4(raw + (s * N + tp - m0 + H) * P + k4);
-      }
-      if ((code & 2) && N < H) {
-        float* ring = slot_base(a.state, code) + a.hist.ring;
-        for (int it = tid; it < (H - N) * quads; it += kProducerThreads) {
-          const int q = it / quads, k4 = 4 * (it - q * quads);
-          *reinterpret_cast<float4*>(ring + (N + q) * C + kb * kKBlock + k4) = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      }
-      if (tid == 0 && kb == 0) hist_commit_head(a.state, a.hist, code, head, N);
+    const int per = n_new * quads;
+#pragma unroll 2
+    for (int it = tid; it < ns * per; it += kProducerThreads) {
+      const int e = it / per, rem = it - e * per;
+      const int q = rem / quads, k4 = 4 * (rem - q * quads);
+      const int tp = N - n_new + q;
+      *reinterpret_cast<float4*>(hist_new_row(a.state, a.hist, tab.code[e], tab.head[e], tp, N) + kb * kKBlock + k4) =
+          lds4(raw + ((tab.s_lo + e) * N + tp - m0 + H) * P + k4);
     }
+    if (N < H) {
+      // A fresh stream's window starts as H - N zero rows before its N new ones.
+      const int zper = (H - N) * quads;
+      for (int it = tid; it < ns * zper; it += kProducerThreads) {
+        const int e = it / zper, rem = it - e * zper;
+        const int code = tab.code[e];
+        if (!(code & 2)) continue;
+        const int q = rem / quads, k4 = 4 * (rem - q * quads);
+        *reinterpret_cast<float4*>(slot_base(a.state, code) + a.hist.ring + (N + q) * C + kb * kKBlock + k4) =
+            make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    if (kb == 0)
+      for (int e = tid; e < ns; e += kProducerThreads) hist_commit_head(a.state, a.hist, tab.code[e], tab.head[e], N);
   }
   const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
   float4 w[7];
@@ -719,7 +725,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
                                  mbar_wait(&raw_full[rb], (g2 >> 1) & 1, a.status, kDevTimeoutProducer));
           if (!ok) break;
           produce_residual<MODE, kLpr>(a, m0, kb, nullptr, reinterpret_cast<const float*>(raw_base + rb * Cfg::kRaw),
-                                       warp, lane, write_state, tab, partial ? iwalk_lo : walk_lo,
+                                       warp, lane, kb % num_n == tile_n(t), tab, partial ? iwalk_lo : walk_lo,
                                        partial ? iwalk_hi : walk_hi, regular, rowmax);
           __syncwarp();
           if (lane == 0) mbar_arrive(&raw_empty[rb]);
@@ -788,7 +794,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
             produce_stem<MODE>(a, a_stage, warp, lane, write_state, tab);
           } else if (KIND == kResidual) {
             produce_residual<MODE, kLpr>(a, m0, kb, a_stage, reinterpret_cast<const float*>(raw_base + rb * Cfg::kRaw),
-                                         warp, lane, write_state, tab, partial ? iwalk_lo : walk_lo,
+                                         warp, lane, kb % num_n == tile_n(t), tab, partial ? iwalk_lo : walk_lo,
                                          partial ? iwalk_hi : walk_hi, regular, nullptr);
           } else {
             produce_test<MODE>(a, m0, kb, a_stage, warp, lane);
