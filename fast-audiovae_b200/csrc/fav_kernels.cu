@@ -77,10 +77,12 @@ struct GemmCfg {
   static constexpr int kFixed = 1024 /*align slack*/ + 512 /*barriers*/ + kTable + kScales;
   // Epilogue column coefficients, double-buffered per tile.
   static constexpr int kEpi = 2 * 7 * NT * 4;
-  static constexpr int kStagesFit = (kSmemBudget - 2 * kRaw - kFixed - kEpi) / kStage;
+  // Per epilogue warp: one 32-row x 16-column fp32 chunk staged for coalesced stores.
+  static constexpr int kEpiStage = kEpilogueWarps * 32 * kEpiCols * 4;
+  static constexpr int kStagesFit = (kSmemBudget - 2 * kRaw - kFixed - kEpi - kEpiStage) / kStage;
   static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
   static_assert(kStages >= 2, "pipeline needs two stages");
-  static constexpr int kSmem = kFixed + kStages * kStage + kEpi + 2 * kRaw;
+  static constexpr int kSmem = kFixed + kStages * kStage + kEpi + 2 * kRaw + kEpiStage;
   // Two accumulator buffers; one buffer holds NT fp32/s32 columns per accumulator.
   static constexpr int kAccCols = kI8Tconv ? 2 * NT : NT;
   static constexpr uint32_t kTmemCols = 2 * kAccCols < 32 ? 32 : 2 * kAccCols;
@@ -173,6 +175,35 @@ __device__ void fill_table(const LayerArgs& a, int m0, const StreamTable& tab, i
     }
     tab.row_e[r] = e;
     tab.row_t[r] = t;
+  }
+}
+
+// Each stage's last residual unit (a plane writer): the shifted planes' first
+// row of every stream starting in tile m0, columns n0 .. n0+nt-1, is the
+// stream's previous activated row, kept packed as (hi << 16) | lo in the next
+// layer's one-row history (zero for a fresh stream or without a state pool).
+// The epilogue writes every other row of both planes. (The stem, whose tiles
+// start a stream at nearly every row, copies these rows in its epilogue.)
+__device__ void first_rows_prev_planes(const LayerArgs& a, int m0, int n0, int nt, const StreamTable& tab, int lane) {
+  const int N = a.rows_per_stream;
+  const int g_end = min(m0 + kTileM, a.rows);
+  const int s_first = (m0 + N - 1) / N;
+  const int nf = (g_end - 1) / N - s_first + 1;
+  const int quads = nt / 4;
+  const size_t plane = (size_t)a.rows * a.c_out;
+  for (int it = lane; it < nf * quads; it += 32) {
+    const int e = it / quads, c4 = n0 + 4 * (it - e * quads);
+    const int s = s_first + e;
+    const int code = tab.code[s - tab.s_lo];
+    uint4 w = make_uint4(0u, 0u, 0u, 0u);
+    if (a.state.pool && !(code & 2)) {
+      float* slot = slot_base(a.state, code);
+      const int head = head_table(slot, code & 1)[a.hist_next.index];
+      w = __ldg(reinterpret_cast<const uint4*>(slot + a.hist_next.ring + head * a.hist_next.width + c4));
+    }
+    uint16_t* dst = a.out_planes_prev + (size_t)s * N * a.c_out + c4;
+    *reinterpret_cast<uint2*>(dst) = make_uint2(__byte_perm(w.x, w.y, 0x7632), __byte_perm(w.z, w.w, 0x7632));
+    *reinterpret_cast<uint2*>(dst + plane) = make_uint2(__byte_perm(w.x, w.y, 0x5410), __byte_perm(w.z, w.w, 0x5410));
   }
 }
 
@@ -554,15 +585,82 @@ __device__ void produce_test(const LayerArgs& a, int m0, int kb, uint8_t* a_stag
 }
 
 // ------------------------------------------------------------------ epilogue
-// Skip input of a residual unit: x[g][n .. n+15] (zeros past the last row).
+// Epilogue chunks move between registers (one row per lane) and global memory
+// (eight rows of 64 bytes per instruction) through the warp's 32-row x
+// 64-byte staging buffer. The 16-byte granule j of row r sits at granule
+// j ^ ((r >> 1) & 3), so both the row-wise and the column-wise accesses touch
+// each bank group four times (four wavefronts per 512-byte access).
+__device__ __forceinline__ int stage_granule(int r, int j) { return r * 4 + (j ^ ((r >> 1) & 3)); }
+
+// Skip input of a residual unit, rows row0 .. row0+31, columns n .. n+15, in
+// the coalesced order: xr[k] = granule (lane & 3) of row 8k + lane/4 (zeros
+// past the last row).
 template <int KIND>
-__device__ __forceinline__ void load_skip(const LayerArgs& a, int g, int n, float4 (&x)[4]) {
+__device__ __forceinline__ void load_skip(const LayerArgs& a, int row0, int n, int lane, float4 (&xr)[4]) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) x[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (KIND == kResidual && g < a.rows) {
-    const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)g * a.c_out + n);
+  for (int k = 0; k < 4; ++k) {
+    const int g = row0 + 8 * k + (lane >> 2);
+    xr[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (KIND == kResidual && g < a.rows) xr[k] = __ldg(reinterpret_cast<const float4*>(a.x + (size_t)g * a.c_out + n) + (lane & 3));
+  }
+}
+
+// The coalesced skip chunk xr, transposed to this lane's row. Warp-collective.
+__device__ __forceinline__ void transpose_skip(float* stage, int lane, const float4 (&xr)[4], float4 (&x)[4]) {
+  float4* sg = reinterpret_cast<float4*>(stage);
+  __syncwarp();  // the previous chunk's reads of the buffer are done
 #pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] = __ldg(src + j);
+  for (int k = 0; k < 4; ++k) sg[stage_granule(8 * k + (lane >> 2), lane & 3)] = xr[k];
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 4; ++j) x[j] = sg[stage_granule(lane, j)];
+}
+
+// Coalesced store of a warp's 32-row x 16-column fp32 chunk (this lane's row
+// in v): row r to dst0 + r * pitch, rows r >= valid skipped. Warp-collective.
+__device__ __forceinline__ void store_chunk(float* stage, int lane, const float (&v)[16], float* dst0, size_t pitch,
+                                            int valid) {
+  float4* sg = reinterpret_cast<float4*>(stage);
+  __syncwarp();  // the previous reads of the buffer are done
+#pragma unroll
+  for (int j = 0; j < 4; ++j) sg[stage_granule(lane, j)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  __syncwarp();
+  const int gq = lane & 3;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = 8 * k + (lane >> 2);
+    const float4 u = sg[stage_granule(r, gq)];
+    if (r < valid) *reinterpret_cast<float4*>(dst0 + r * pitch + 4 * gq) = u;
+  }
+}
+
+// Coalesced store of a warp's 32-row x 16-column chunk of split-bf16 planes
+// (this lane's row in hi/lo): row r's 32-byte hi and lo segments go to the
+// current planes at cur + off0 + r * c_out (lo one plane later) and, unless
+// the row is its stream's last step, one row later in the shifted planes.
+// tq[k]: time step of row 8k + lane/4 within its stream, -1 past the last row.
+// Warp-collective.
+__device__ __forceinline__ void store_planes_chunk(float* stage, int lane, const uint32_t (&hi)[8],
+                                                   const uint32_t (&lo)[8], uint16_t* cur, uint16_t* prev,
+                                                   size_t plane, size_t off0, int c_out, int N, const int (&tq)[4]) {
+  uint4* sg = reinterpret_cast<uint4*>(stage);
+  __syncwarp();  // the previous reads of the buffer are done
+  sg[stage_granule(lane, 0)] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  sg[stage_granule(lane, 1)] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+  sg[stage_granule(lane, 2)] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  sg[stage_granule(lane, 3)] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+  __syncwarp();
+  const int gq = lane & 3;
+  const size_t part = (gq >> 1) * plane + (gq & 1) * 8;  // hi or lo plane, first or second 8 columns
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = 8 * k + (lane >> 2);
+    const uint4 u = sg[stage_granule(r, gq)];
+    if (tq[k] >= 0) {
+      const size_t o = off0 + (size_t)r * c_out + part;
+      *reinterpret_cast<uint4*>(cur + o) = u;
+      if (tq[k] + 1 < N) *reinterpret_cast<uint4*>(prev + o + c_out) = u;
+    }
   }
 }
 
@@ -570,16 +668,6 @@ __device__ __forceinline__ void st4(float* dst, const float (&v)[16]) {
 #pragma unroll
   for (int j = 0; j < 4; ++j)
     reinterpret_cast<float4*>(dst)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-}
-
-// 16 bf16 of the hi plane at p and of the lo plane ``plane`` elements later.
-__device__ __forceinline__ void put_planes(uint16_t* p, size_t plane, const uint32_t (&hi)[8], const uint32_t (&lo)[8]) {
-  uint4* ph = reinterpret_cast<uint4*>(p);
-  uint4* pl = reinterpret_cast<uint4*>(p + plane);
-  ph[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-  ph[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-  pl[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-  pl[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
 }
 
 // Per-column epilogue coefficients of one tile, staged in shared memory:
@@ -608,7 +696,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   uint8_t* b_base = a_base + S * Cfg::kAStage;
   float* epi_coef = reinterpret_cast<float*>(b_base + S * Cfg::kBStage);  // [2][kEpiCoefVectors][NT]
   uint8_t* raw_base = reinterpret_cast<uint8_t*>(epi_coef) + Cfg::kEpi;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(raw_base + 2 * Cfg::kRaw);
+  float* epi_stage = reinterpret_cast<float*>(raw_base + 2 * Cfg::kRaw);  // [kEpilogueWarps][32][kEpiCols]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(epi_stage) + Cfg::kEpiStage);
   uint64_t* a_full = bars;
   uint64_t* b_full = bars + S;
   uint64_t* empty = bars + 2 * S;
@@ -819,6 +908,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
     constexpr int kChunks = NT / kEpiCols;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int etid = threadIdx.x - kProducerThreads;
+    float* stage = epi_stage + (warp - kProducerWarps) * 32 * kEpiCols;
     const int epi = a.epi;
     bool ok = true;
     uint32_t i = 0;
@@ -856,7 +946,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       const int g = row0 + lane;
       const int N = a.rows_per_stream;
       // Plane / activation writers: this row's time step and, at a stream's
-      // first and last step, the next layer's history (old window row, new ring row).
+      // last step, the next layer's new history row; the stem also reads the
+      // old one at a stream's first step.
+      constexpr bool kStemPl = kOutPl && KIND == kStem;
       int t_row = -1;
       const uint32_t* hist_old = nullptr;
       uint32_t* hist_new = nullptr;
@@ -865,12 +957,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       if ((kOutPl || kOutA) && g < a.rows) {
         const int sid = g / N;
         t_row = g - sid * N;
-        if (a.state.pool && (t_row == 0 || t_row == N - 1)) {
+        if (a.state.pool && (t_row == N - 1 || (kStemPl && t_row == 0))) {
           const int code = a.state.slot_codes ? a.state.slot_codes[sid] : ((sid << 2) | a.state.uniform_code);
           float* slot = slot_base(a.state, code);
           const HistRef& h = a.hist_next;  // one row (H = 1): window = ring row head
           const int head = (code & 2) ? 0 : head_table(slot, code & 1)[h.index];
-          if (t_row == 0 && !(code & 2) && kOutPl)
+          if (kStemPl && t_row == 0 && !(code & 2))
             hist_old = reinterpret_cast<const uint32_t*>(slot + h.ring + head * h.width);
           if (t_row == N - 1) {
             hist_new = reinterpret_cast<uint32_t*>(slot + h.ring + (head ^ 1) * h.width);
@@ -881,12 +973,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           }
         }
       }
-      float4 x[4];
-      load_skip<KIND>(a, g, n0, x);
-      uint4 hw[4];  // history bits of this chunk (zero without a history row)
+      int tq[4];  // plane writers: time step of row 8k + lane/4 (-1 past the last row)
+      if constexpr (kOutPl) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        hw[j] = hist_old ? __ldg(reinterpret_cast<const uint4*>(hist_old + n0) + j) : make_uint4(0u, 0u, 0u, 0u);
+        for (int k = 0; k < 4; ++k) {
+          const int gr = row0 + 8 * k + (lane >> 2);
+          tq[k] = gr < a.rows ? gr - (gr / N) * N : -1;
+        }
+      }
+      float4 xr[4];  // skip input of the current chunk, coalesced order
+      load_skip<KIND>(a, row0, n0, lane, xr);
+      uint4 hw[4];  // stem: history bits of this chunk (zero without a history row)
+      if constexpr (kStemPl) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          hw[j] = hist_old ? __ldg(reinterpret_cast<const uint4*>(hist_old + n0) + j) : make_uint4(0u, 0u, 0u, 0u);
+      }
       if (!(ok = mbar_wait(&acc_full[buf], (i >> 1) & 1, a.status, kDevTimeoutEpilogue))) continue;
       tc_fence_after();
       // int8: this row's activation scales (current and previous tap).
@@ -914,14 +1016,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           tmem_ld16_async(base + NT + c * kEpiCols, rp);
           tmem_wait_ld(rp);
         }
-        if (c + 1 < kChunks) tmem_ld16_async(base + (c + 1) * kEpiCols, rn);
-        float4 xn[4];  // next chunk's skip input
-        load_skip<KIND>(a, c + 1 < kChunks ? g : a.rows, n + kEpiCols, xn);
-        uint4 wn[4];  // next chunk's history bits (a plane writer's stream-start rows)
-        if (hist_old && c + 1 < kChunks) {
+        // Next chunk's accumulator columns (the last chunk reloads its own):
+        // issued and waited for unconditionally, so the registers the load
+        // writes asynchronously never meet a control-flow merge before the wait.
+        tmem_ld16_async(base + (c + 1 < kChunks ? c + 1 : c) * kEpiCols, rn);
+        float4 x[4];  // this lane's row of the skip input
+        if (KIND == kResidual) transpose_skip(stage, lane, xr, x);
+        uint4 wn[4];  // stem: next chunk's history bits
+        if (kStemPl && hist_old && c + 1 < kChunks) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) wn[j] = __ldg(reinterpret_cast<const uint4*>(hist_old + n + kEpiCols) + j);
         }
+        float4 xn[4];  // next chunk's skip input
+        load_skip<KIND>(a, c + 1 < kChunks ? row0 : a.rows, n + kEpiCols, lane, xn);
         float v[16];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -961,15 +1068,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
             v[4 * j + 3] = x[j].w + v[4 * j + 3];
           }
         }
-        if (g < a.rows) {
-          size_t off;  // element offset of (row g, column n) in the fp32 outputs
-          if (KIND == kTconv) {
-            const int p = n / a.c_out;
-            off = ((size_t)g * a.stride + p) * a.c_out + (n - p * a.c_out);
-          } else {
-            off = (size_t)g * a.c_out + n;
-          }
-          if (epi & kEpiX) st4(a.out_x + off, v);
+        {
+          // fp32 outputs: row g, column n at g * pitch + n (a transposed conv's
+          // output row g * stride + p holds GEMM columns p * c_out ..).
+          const size_t pitch = KIND == kTconv ? (size_t)a.stride * a.c_out : (size_t)a.c_out;
+          const size_t off0 = (size_t)row0 * pitch + n;
+          if (epi & kEpiX) store_chunk(stage, lane, v, a.out_x + off0, pitch, a.rows - row0);
           if constexpr (OUT != kOutNone) {
             float s[16];
 #pragma unroll
@@ -991,10 +1095,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
 #pragma unroll
               for (int j = 0; j < 8; ++j) split_bf16(s[2 * j], s[2 * j + 1], hi[j], lo[j]);
               const size_t plane = (size_t)a.rows * a.c_out;
-              put_planes(a.out_planes + (size_t)g * a.c_out + n, plane, hi, lo);
-              if (t_row + 1 < N) {
-                put_planes(a.out_planes_prev + (size_t)(g + 1) * a.c_out + n, plane, hi, lo);
-              } else if (hist_new) {
+              store_planes_chunk(stage, lane, hi, lo, a.out_planes, a.out_planes_prev, plane,
+                                 (size_t)row0 * a.c_out + n, a.c_out, N, tq);
+              if (g < a.rows) {
+              if (t_row + 1 >= N && hist_new) {
                 // New history row, packed per channel as (hi << 16) | lo.
                 uint4* dst = reinterpret_cast<uint4*>(hist_new + n);
 #pragma unroll
@@ -1003,42 +1107,39 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
                                       __byte_perm(lo[2 * j + 1], hi[2 * j + 1], 0x5410),
                                       __byte_perm(lo[2 * j + 1], hi[2 * j + 1], 0x7632));
               }
-              if (t_row == 0) {
+              if (kStemPl && t_row == 0) {
                 // A stream's first row of the shifted planes: the previous activated input.
-                uint32_t w[16];
+                uint4* ph = reinterpret_cast<uint4*>(a.out_planes_prev + (size_t)g * a.c_out + n);
+                uint4* pl = reinterpret_cast<uint4*>(a.out_planes_prev + (size_t)g * a.c_out + n + plane);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  w[4 * j] = hw[j].x;
-                  w[4 * j + 1] = hw[j].y;
-                  w[4 * j + 2] = hw[j].z;
-                  w[4 * j + 3] = hw[j].w;
+                for (int j = 0; j < 2; ++j) {
+                  ph[j] = make_uint4(__byte_perm(hw[2 * j].x, hw[2 * j].y, 0x7632), __byte_perm(hw[2 * j].z, hw[2 * j].w, 0x7632),
+                                     __byte_perm(hw[2 * j + 1].x, hw[2 * j + 1].y, 0x7632),
+                                     __byte_perm(hw[2 * j + 1].z, hw[2 * j + 1].w, 0x7632));
+                  pl[j] = make_uint4(__byte_perm(hw[2 * j].x, hw[2 * j].y, 0x5410), __byte_perm(hw[2 * j].z, hw[2 * j].w, 0x5410),
+                                     __byte_perm(hw[2 * j + 1].x, hw[2 * j + 1].y, 0x5410),
+                                     __byte_perm(hw[2 * j + 1].z, hw[2 * j + 1].w, 0x5410));
                 }
-                uint32_t ho[8], lw[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  ho[j] = __byte_perm(w[2 * j], w[2 * j + 1], 0x7632);
-                  lw[j] = __byte_perm(w[2 * j], w[2 * j + 1], 0x5410);
-                }
-                put_planes(a.out_planes_prev + (size_t)g * a.c_out + n, plane, ho, lw);
+              }
               }
             } else {
-              st4(a.out_s + off, s);
+              store_chunk(stage, lane, s, a.out_s + off0, pitch, a.rows - row0);
               if constexpr (kOutA) {
+                if (g < a.rows) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j) rmax = fmaxf(rmax, fabsf(s[j]));
-                if (hist_new) st4(reinterpret_cast<float*>(hist_new) + n, s);
+                  for (int j = 0; j < 16; ++j) rmax = fmaxf(rmax, fabsf(s[j]));
+                  if (hist_new) st4(reinterpret_cast<float*>(hist_new) + n, s);
+                }
               }
             }
           }
         }
-        if (c + 1 < kChunks) {
-          tmem_wait_ld(rn);
+        tmem_wait_ld(rn);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) r[j] = rn[j];
-        }
+        for (int j = 0; j < 16; ++j) r[j] = rn[j];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) x[j] = xn[j];
-        if (hist_old && c + 1 < kChunks) {
+        for (int j = 0; j < 4; ++j) xr[j] = xn[j];
+        if (kStemPl && hist_old && c + 1 < kChunks) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) hw[j] = wn[j];
         }
@@ -1153,6 +1254,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           if (lane == 0) mbar_arrive(&scale_full[ti & 1]);
         }
         if (lane == 0) mbar_arrive(&table_full[ti & 1]);
+        // After publishing the table: nothing in this kernel reads these rows.
+        if (KIND == kResidual && (a.epi & kEpiPlanes)) first_rows_prev_planes(a, m0, tile_n(t) * NT, NT, tab, lane);
       }
     }
   } else {
