@@ -89,6 +89,14 @@ int32_t encode_plane_map(CUtensorMap* map, const void* planes, int rows, int cha
                     "planes");
 }
 
+// Stage-5 input y [rows][32] fp32 for the fused tail: boxes of 32 channels x
+// (128 + 84) rows in the 128-byte swizzle.
+int32_t encode_tail_map(CUtensorMap* map, const float* x, int rows) {
+  const cuuint64_t dims[2] = {(cuuint64_t)fav::kTailC, (cuuint64_t)rows};
+  const cuuint32_t box[2] = {(cuuint32_t)fav::kTailC, (cuuint32_t)(fav::kTileM + 84)};
+  return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_128B, "tail");
+}
+
 std::once_flag g_prepare_once;
 cudaError_t g_prepare_error = cudaSuccess;
 
@@ -394,6 +402,10 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
   float* S[2] = {ws + 2 * region, ws + 3 * region};
   uint16_t* planes = reinterpret_cast<uint16_t*>(ws + 4 * region);       // [2][rows][C] bf16
   uint16_t* planes_prev = reinterpret_cast<uint16_t*>(ws + 5 * region);  // row t holds time step t - 1
+  // A whole step runs stage 5's residual units and the final conv as one fused
+  // kernel; a step stopped inside stage 5 (layer checks) runs them one by one.
+  bool tail = last_layer >= 25 && p->stages[fav::kStages - 1].c_out == fav::kTailC;
+  for (int j = 0; j < 3; ++j) tail = tail && !p->stages[fav::kStages - 1].res[j].int8;
   auto tconv_hist = [p](int i) {
     const StageDev& st = p->stages[i];
     return fav::HistRef{1 + 4 * i, 2 * st.state_t, 1, st.c_in};
@@ -474,7 +486,8 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     t.status = status;
     t.kind = fav::kTconv;
     t.mode = fav::kModeSplit;
-    t.epi = fav::kEpiX | fav::kEpiS;
+    const bool into_tail = tail && i + 1 == fav::kStages;
+    t.epi = fav::kEpiX | (into_tail ? 0 : fav::kEpiS);
     t.rows = n_streams * n;
     t.rows_per_stream = n;
     t.k_channels = st.c_in;
@@ -510,6 +523,32 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     if (last_out) *last_out = X[0];
     mark(++layer + 1);
     if (layer == last_layer) return FAV_OK;
+    if (into_tail) {
+      fav::TailArgs ta{};
+      ta.rows = n_streams * n;
+      ta.rows_per_stream = n;
+      for (int j = 0; j < 3; ++j) {
+        const auto& r = st.res[j];
+        ta.unit[j] = fav::TailUnitArgs{r.pre_a, r.pre_r, r.coef, r.pw_b, r.img,
+                                       fav::HistRef{2 + 4 * i + j, 2 * r.state_off, 6 * r.dilation, st.c_out}};
+      }
+      ta.fin_a = p->fin_a;
+      ta.fin_r = p->fin_r;
+      ta.fin_w = p->fin_w;
+      ta.fin_b = p->fin_b;
+      ta.fin_hist = fav::HistRef{25, 2 * p->state_final, 6, fav::kFinalChannels};
+      ta.audio = audio;
+      ta.audio_stride = audio_stride;
+      ta.audio_offset = audio_offset;
+      ta.state = state;
+      ta.status = status;
+      if ((es = encode_tail_map(&ta.xmap, X[0], ta.rows)) != FAV_OK) return es;
+      if ((e = fav::launch_tail(ta, stream)) != cudaSuccess) return cuda_fail(e, "tail launch");
+      // The fused kernel's time counts as stage 5's first residual unit.
+      for (int l = 23; l <= 26; ++l) mark(l);
+      if (last_out) *last_out = audio;
+      return FAV_OK;
+    }
     // Residual unit j reads y and Snake_pre(y) from pair j % 2 and writes pair
     // (j + 1) % 2; the last unit writes the next stage's planes instead (stage 5:
     // Snake_final(y) for the final conv).

@@ -148,6 +148,35 @@ struct FinalArgs {
   uint32_t* status;
 };
 
+// Fused stage-5 tail (fav_tail.cu): the three residual units and the final conv.
+constexpr int kTailC = 32;  // stage-5 channels
+struct TailUnitArgs {
+  const float* pre_a;    // Snake before the depthwise conv [32]
+  const float* pre_r;
+  const float* coef;     // depthwise block [w0..w6, bias, alpha2, recip2][64] (zero padded)
+  const float* bias;     // 1x1 bias [32]
+  const uint8_t* wimg;   // 1x1 weights, 32 rows x 128 B (f16, K-major, 128-byte swizzle)
+  HistRef hist;          // window of Snake_pre(input), 6 * dilation rows
+};
+struct TailArgs {
+  CUtensorMap xmap;      // stage input y [rows][32] fp32: boxes of 32 x 212 rows, 128-byte swizzle
+  int rows;              // all streams' rows (multiple of 128)
+  int rows_per_stream;   // multiple of 128
+  TailUnitArgs unit[3];
+  const float* fin_a;    // final Snake [32]
+  const float* fin_r;
+  const float* fin_w;    // final conv [32][7]
+  const float* fin_b;    // [1]
+  HistRef fin_hist;      // window of Snake_final(y3), 6 rows
+  float* audio;
+  int audio_stride;
+  int audio_offset;
+  StateRef state;
+  uint32_t* status;
+};
+cudaError_t launch_tail(const TailArgs& a, cudaStream_t stream);
+cudaError_t prepare_tail();
+
 // Kernel launchers (fav_kernels.cu). Return cudaError_t of the launch.
 cudaError_t launch_gemm_layer(const LayerArgs& a, cudaStream_t stream);
 // The int8 plan's stem (depthwise k=7 -> 1x1 -> stage 0's affine + Snake, row

@@ -28,8 +28,7 @@
 // delays another's issue.
 // Every wait is bounded and records an error code in the caller's status word
 // instead of hanging.
-#include "fav_device.cuh"
-#include "fav_internal.h"
+#include "fav_common.cuh"
 
 namespace fav {
 
@@ -90,45 +89,6 @@ struct GemmCfg {
   static constexpr uint32_t kIdesc = kI8 ? instr_desc_i8(NT) : instr_desc_f16(kSplitOperands<MODE> ? 1u : 0u, NT);
 };
 
-__device__ __forceinline__ float2 ldg2(const float* p) { return __ldg(reinterpret_cast<const float2*>(p)); }
-__device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
-__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
-template <bool EXACT = false>
-__device__ __forceinline__ float4 snake4(float4 v, float4 al, float4 rc) {
-  if constexpr (EXACT)
-    return make_float4(snake_exact(v.x, al.x, rc.x), snake_exact(v.y, al.y, rc.y), snake_exact(v.z, al.z, rc.z),
-                       snake_exact(v.w, al.w, rc.w));
-  return make_float4(snake(v.x, al.x, rc.x), snake(v.y, al.y, rc.y), snake(v.z, al.z, rc.z), snake(v.w, al.w, rc.w));
-}
-
-// Depthwise k=7 tap sum of four channels, oldest tap first, plus bias. The
-// int8 path (EXACT) rounds every product and sum (the oracle's order); the
-// bf16 path chains fused multiply-adds.
-template <bool EXACT>
-__device__ __forceinline__ float4 dw7(const float4 (&w)[7], const float4 (&win)[7], float4 bias) {
-  float4 h;
-  if constexpr (EXACT) {
-    h = make_float4(__fmul_rn(w[0].x, win[0].x), __fmul_rn(w[0].y, win[0].y), __fmul_rn(w[0].z, win[0].z),
-                    __fmul_rn(w[0].w, win[0].w));
-#pragma unroll
-    for (int j = 1; j < 7; ++j) {
-      h.x = __fadd_rn(h.x, __fmul_rn(w[j].x, win[j].x));
-      h.y = __fadd_rn(h.y, __fmul_rn(w[j].y, win[j].y));
-      h.z = __fadd_rn(h.z, __fmul_rn(w[j].z, win[j].z));
-      h.w = __fadd_rn(h.w, __fmul_rn(w[j].w, win[j].w));
-    }
-    return make_float4(__fadd_rn(h.x, bias.x), __fadd_rn(h.y, bias.y), __fadd_rn(h.z, bias.z), __fadd_rn(h.w, bias.w));
-  }
-  h = make_float4(w[0].x * win[0].x, w[0].y * win[0].y, w[0].z * win[0].z, w[0].w * win[0].w);
-#pragma unroll
-  for (int j = 1; j < 7; ++j) {
-    h.x = fmaf(w[j].x, win[j].x, h.x);
-    h.y = fmaf(w[j].y, win[j].y, h.y);
-    h.z = fmaf(w[j].z, win[j].z, h.z);
-    h.w = fmaf(w[j].w, win[j].w, h.w);
-  }
-  return make_float4(h.x + bias.x, h.y + bias.y, h.z + bias.z, h.w + bias.w);
-}
 
 // ----------------------------------------------------------- history rings
 // Per-tile tables, filled one tile ahead by the scheduler warp: for each stream
@@ -147,12 +107,6 @@ __device__ __forceinline__ StreamTable table_at(int* base, int m0, int rows_per_
                      m0 / rows_per_stream};
 }
 
-__device__ __forceinline__ float* slot_base(const StateRef& st, int code) {
-  return st.pool + (size_t)(code >> 2) * kSlotStride;
-}
-__device__ __forceinline__ int* head_table(float* slot, int parity) {
-  return reinterpret_cast<int*>(slot + kRingFloats) + parity * kHeadInts;
-}
 
 __device__ void fill_table(const LayerArgs& a, int m0, const StreamTable& tab, int lane) {
   const int N = a.rows_per_stream;
@@ -218,20 +172,7 @@ __device__ __forceinline__ const float* hist_row(const LayerArgs& a, const Strea
   return slot_base(a.state, code) + a.hist.ring + row * a.hist.width;
 }
 
-// Ring row that receives chunk row tp (tp >= max(0, N - H)).
-__device__ __forceinline__ float* hist_new_row(const StateRef& st, const HistRef& h, int code, int head, int tp,
-                                               int N) {
-  const int H = h.rows;
-  int row = head + H + tp - (N > H ? N - H : 0);
-  row %= 2 * H;
-  return slot_base(st, code) + h.ring + row * h.width;
-}
 
-// Advanced head of the history, written to the other head table.
-__device__ __forceinline__ void hist_commit_head(const StateRef& st, const HistRef& h, int code, int head, int N) {
-  const int H = h.rows;
-  head_table(slot_base(st, code), (code & 1) ^ 1)[h.index] = (head + (N < H ? N : H)) % (2 * H);
-}
 
 // A-operand stores use plain shared-memory stores (no compiler barrier), so
 // loads for later rows can be scheduled ahead of them; fence.proxy.async before
@@ -1336,6 +1277,7 @@ static cudaError_t set_smem() {
 #define FAV_CONFIGS(X)                                                                                      \
   X(256, kModeSplit4, kStem, kOutPlanes) X(256, kModeSplit4, kStem, kOutAct)                                \
   X(128, kModeSplit, kTconv, kOutS) X(64, kModeSplit, kTconv, kOutS) X(128, kModeI8, kTconv, kOutS)         \
+  X(64, kModeSplit, kTconv, kOutNone)                                                                      \
   X(256, kModeF16, kResidual, kOutS) X(128, kModeF16, kResidual, kOutS) X(64, kModeF16, kResidual, kOutS)  \
   X(32, kModeF16, kResidual, kOutS) X(256, kModeF16, kResidual, kOutPlanes)                                \
   X(128, kModeF16, kResidual, kOutPlanes) X(64, kModeF16, kResidual, kOutPlanes)                           \
@@ -1357,7 +1299,7 @@ cudaError_t prepare_kernels() {
   if ((e = set_smem<NT, MODE, KIND, OUT>()) != cudaSuccess) return e;
   FAV_CONFIGS(FAV_SET)
 #undef FAV_SET
-  return cudaSuccess;
+  return prepare_tail();
 }
 
 cudaError_t launch_gemm_layer(const LayerArgs& a, cudaStream_t stream) {
