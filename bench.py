@@ -4,7 +4,9 @@ Workload ("stream40ms"): every GPU decodes S independent streams (default 512,
 the per-GPU shard of 4096 streams on 8 GPUs) that each receive one-frame
 (40 ms, 1920-sample) latent chunks ~N(0,1) with per-stream seeds, carrying
 causal history across steps; decoder coefficients are the seeded random init.
-One step = one chunk for all S streams (26 kernel launches). Weak scaling:
+One step = one chunk for all S streams (23 kernel launches: stem, then per
+stage a transposed conv and three residual units, with stage 5's units and the
+final conv fused into one kernel). Weak scaling:
 each rank owns S streams, no collective on the data path.
 
 Reported (one JSON line, rank 0):
@@ -41,8 +43,19 @@ sys.path.insert(0, str(ROOT))
 FRAME_SECONDS = 1920 / 48000
 RATES = (8, 6, 5, 2, 2, 2)
 METRIC = "aggregate audio-s/s (RTF^-1), 40 ms streaming chunks"
-LAYER_NAMES = ["stem"] + [f"stage{i}.{k}" for i in range(6) for k in ("transpose", "res0", "res1", "res2")] + \
-    ["final"]
+# Kernels of one step, in launch order: the stem, per stage a transposed conv
+# and three residual units (stage 5: its transposed conv and the fused tail =
+# three residual units + final conv).
+LAYER_NAMES = ["stem"] + [f"stage{i}.{k}" for i in range(5) for k in ("transpose", "res0", "res1", "res2")] + \
+    ["stage5.transpose", "stage5.tail"]
+LAUNCHES_PER_STEP = len(LAYER_NAMES)
+
+
+def kernel_ms(layer_ms26):
+    """Per-kernel durations from the 26 per-layer event intervals of
+    ``fav_step_profile`` (the fused tail spans layers 22-25)."""
+    v = np.asarray(layer_ms26, dtype=np.float64)
+    return np.concatenate([v[:22], [v[22:].sum()]])
 
 
 def parse():
@@ -69,12 +82,14 @@ def peaks():
 
 # ------------------------------------------------------------------ algorithmic cost
 def layer_costs():
-    """Per latent frame: algorithmic FLOPs (2*MAC of the layer's contraction) and
-    HBM bytes of this design's data layout (each activation read and written
-    once), plus per-launch weight bytes and per-stream history bytes (read +
-    write). Activations: fp32 y and Snake(y) between residual units; the
-    split-bf16 planes a transposed conv reads, written twice (as they are, and
-    one time step later for the second tap)."""
+    """Per kernel of ``LAYER_NAMES``, per latent frame: algorithmic FLOPs (2*MAC
+    of the contractions) and HBM bytes of this design's data layout (each
+    activation read and written once), plus per-launch weight bytes and
+    per-stream history bytes (read + write). Activations: fp32 y and Snake(y)
+    between residual units; the split-bf16 planes a transposed conv reads,
+    written twice (as they are, and one time step later for the second tap).
+    The fused stage-5 tail reads its input y once and writes audio; its
+    intermediates stay on chip."""
     out = []
     n = 1  # rows per frame at the current layer input
     out.append(dict(flops=2 * 2048 * 64, act=64 * 4 + 2048 * 8, weights=2048 * 64 * 4,
@@ -82,16 +97,20 @@ def layer_costs():
     cin = 2048
     for i, s in enumerate(RATES):
         cout = cin // 2
-        out.append(dict(flops=2 * cin * cout * 2 * s * n, act=n * cin * 8 + n * s * cout * 8,
+        y_bytes = 4 if i == 5 else 8  # stage 5's transposed conv writes y only (the tail applies Snake_pre)
+        out.append(dict(flops=2 * cin * cout * 2 * s * n, act=n * cin * 8 + n * s * cout * y_bytes,
                         weights=cin * cout * 2 * s * 4, hist=0))
         n *= s
+        if i == 5:
+            out.append(dict(flops=n * (3 * 2 * cout * cout + 2 * cout * 7), act=n * cout * 4 + n * 4,
+                            weights=3 * cout * cout * 2, hist=(6 + 18 + 54 + 6) * cout * 4 * 2))
+            break
         for j, d in enumerate((1, 3, 9)):
-            last_out = 4 if (i == 5 and j == 2) else 8
-            nxt = 0 if (j < 2 or i == 5) else cout * 4 * 2  # next transposed conv's history row
-            out.append(dict(flops=2 * cout * cout * n, act=n * cout * 8 + n * cout * last_out, weights=cout * cout * 2,
+            nxt = 0 if j < 2 else cout * 4 * 2  # next transposed conv's history row
+            out.append(dict(flops=2 * cout * cout * n, act=n * cout * 16, weights=cout * cout * 2,
                             hist=6 * d * cout * 4 * 2 + nxt))
         cin = cout
-    out.append(dict(flops=2 * 32 * 7 * n, act=(n * 32 + n) * 4, weights=0, hist=6 * 32 * 4 * 2))
+    assert len(out) == LAUNCHES_PER_STEP
     return out
 
 
@@ -119,7 +138,7 @@ def roofline(layer_ms, frames_per_launch, streams, pk, frames=1):
     t_tensor = flops / (pk["tflops"] * 1e12)
     t_hbm = bytes_ / (pk["hbm_gbs"] * 1e9)
     sec = layer_ms[dom] / 1e3
-    if t_tensor >= t_hbm and dom not in (25,):
+    if t_tensor >= t_hbm:
         achieved, peak, unit, bound = flops / sec / 1e12, pk["tflops"], "TFLOP/s", "tensor"
     else:
         achieved, peak, unit, bound = bytes_ / sec / 1e9, pk["hbm_gbs"], "GB/s", "hbm"
@@ -322,7 +341,7 @@ def run_ours(args, world, rank, local):
         _native.check(lib, lib.fav_step_profile(be.plan.handle, P(pool), S, P(codes[i % 2]), S, F, P(z_dev[i]),
                                                 P(audio), P(ws), ws_bytes, P(status), buf, stream))
         layer_ms += np.array(buf[:])
-    layer_ms /= reps
+    layer_ms = kernel_ms(layer_ms / reps)
 
     # end to end through the public API: host chunks in, host audio out
     streams = [dec.stream() for _ in range(S)]
@@ -383,7 +402,7 @@ def run_ours(args, world, rank, local):
                            "streams_per_step": S},
             "latency_1stream_ms": {"p50": round(float(np.percentile(single, 50)), 3),
                                    "p99": round(float(np.percentile(single, 99)), 3)},
-            "gpu_launches": 26 * K,
+            "gpu_launches": LAUNCHES_PER_STEP * K,
             "roofline": rl,
             "cpu_baseline": cpu,
             "clocks": clock_info,

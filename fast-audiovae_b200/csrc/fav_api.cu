@@ -391,7 +391,7 @@ constexpr size_t kRegionFloatsPerFrame = 61440;
 int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, int frames, const float* z,
                  int z_stride, int z_offset, float* audio, int audio_stride, int audio_offset, float* ws,
                  uint32_t* status, cudaStream_t stream, int last_layer = 25, float** last_out = nullptr,
-                 cudaEvent_t* events = nullptr) {
+                 cudaEvent_t* events = nullptr, bool fuse_tail = true) {
   // events (optional, 27): recorded before the stem and after each layer.
   auto mark = [&](int i) {
     if (events) cudaEventRecord(events[i], stream);
@@ -404,7 +404,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
   uint16_t* planes_prev = reinterpret_cast<uint16_t*>(ws + 5 * region);  // row t holds time step t - 1
   // A whole step runs stage 5's residual units and the final conv as one fused
   // kernel; a step stopped inside stage 5 (layer checks) runs them one by one.
-  bool tail = last_layer >= 25 && p->stages[fav::kStages - 1].c_out == fav::kTailC;
+  bool tail = fuse_tail && last_layer >= 25 && p->stages[fav::kStages - 1].c_out == fav::kTailC;
   for (int j = 0; j < 3; ++j) tail = tail && !p->stages[fav::kStages - 1].res[j].int8;
   auto tconv_hist = [p](int i) {
     const StageDev& st = p->stages[i];
@@ -756,6 +756,24 @@ int32_t fav_step(const fav_plan* plan, float* state_pool, int32_t num_slots, con
   fav::StateRef st{state_pool, slot_codes, num_slots, 0};
   return run_step(plan, st, n_streams, frames, latents, frames, 0, audio, frames * fav::kHop, 0,
                   static_cast<float*>(workspace), status, static_cast<cudaStream_t>(cuda_stream));
+}
+
+int32_t fav_debug_step_unfused(const fav_plan* plan, float* state_pool, int32_t num_slots, const int32_t* slot_codes,
+                               int32_t n_streams, int32_t frames, const float* latents, float* audio, void* workspace,
+                               size_t workspace_bytes, uint32_t* status, void* cuda_stream) {
+  g_error[0] = 0;
+  if (!plan || n_streams <= 0 || frames <= 0 || !latents || !audio || !workspace)
+    return fail(FAV_INVALID_ARGUMENT, "bad debug step arguments");
+  if ((int64_t)n_streams * frames * fav::kHop > INT32_MAX)
+    return fail(FAV_SIZE_OVERFLOW, "step too large: %d streams x %d frames", n_streams, frames);
+  if (!state_pool || !slot_codes || num_slots < n_streams)
+    return fail(FAV_INVALID_ARGUMENT, "state pool, slot codes and num_slots >= n_streams are required");
+  if (workspace_bytes < fav_plan_workspace_bytes(plan, n_streams, frames))
+    return fail(FAV_INVALID_ARGUMENT, "workspace too small");
+  fav::StateRef st{state_pool, slot_codes, num_slots, 0};
+  return run_step(plan, st, n_streams, frames, latents, frames, 0, audio, frames * fav::kHop, 0,
+                  static_cast<float*>(workspace), status, static_cast<cudaStream_t>(cuda_stream), 25, nullptr,
+                  nullptr, false);
 }
 
 int32_t fav_step_static(const fav_plan* plan, float* state_pool, int32_t num_slots, const int32_t* slot_codes,

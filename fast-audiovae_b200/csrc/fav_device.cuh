@@ -98,32 +98,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
-// TMA tile stores (shared -> global, bulk-group completion). Coordinates past
-// the tensor's extent are clipped; coordinates must not be negative.
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(smem_u32(src)), "r"(x), "r"(y)
-               : "memory");
-}
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
-  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// Wait until at most N committed store groups still read shared memory.
-template <int N>
-__device__ __forceinline__ void bulk_wait_read() {
-  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-// Wait until at most N committed store groups are incomplete.
-template <int N>
-__device__ __forceinline__ void bulk_wait() {
-  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // Make generic-proxy shared-memory writes visible to the async proxy (MMA).
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -206,32 +180,8 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
                :
                : "memory");
 }
-// Load and wait: the values are complete when it returns.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  tmem_ld16_async(taddr, r);
-  tmem_wait_ld(r);
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// 32 lanes x 32 consecutive fp32 columns of the accumulator (load and wait in
-// one statement, so the values are complete when it returns).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
-      : "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
 
 // ------------------------------------------------------------ descriptors
-// Instruction descriptor, kind::f16: fp32 accumulator, K-major A and B.
-// fmt: 0 = f16, 1 = bf16. M = 128.
 // Instruction descriptor, kind::i8: s32 accumulator, signed 8-bit K-major A and B. M = 128.
 __host__ __device__ constexpr uint32_t instr_desc_i8(uint32_t n) {
   return (2u << 4)              // D format s32
@@ -240,6 +190,8 @@ __host__ __device__ constexpr uint32_t instr_desc_i8(uint32_t n) {
          | ((n >> 3) << 17)     // N / 8
          | ((128u >> 4) << 24); // M / 16
 }
+// Instruction descriptor, kind::f16: fp32 accumulator, K-major A and B.
+// fmt: 0 = f16, 1 = bf16. M = 128.
 __host__ __device__ constexpr uint32_t instr_desc_f16(uint32_t fmt, uint32_t n) {
   return (1u << 4)              // D format f32
          | (fmt << 7)           // A format
@@ -339,14 +291,6 @@ __device__ __forceinline__ void split_bf16(float v0, float v1, uint32_t& hi, uin
   hi = pack_bf16(v0, v1);
   const float h0 = __uint_as_float(hi << 16), h1 = __uint_as_float(hi & 0xffff0000u);
   lo = pack_bf16(v0 - h0, v1 - h1);
-}
-
-__device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t v0, uint32_t v1) {
-  asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(v0), "r"(v1) : "memory");
-}
-
-__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
-  asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
 
 }  // namespace fav

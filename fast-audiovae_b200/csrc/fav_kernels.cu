@@ -89,7 +89,6 @@ struct GemmCfg {
   static constexpr uint32_t kIdesc = kI8 ? instr_desc_i8(NT) : instr_desc_f16(kSplitOperands<MODE> ? 1u : 0u, NT);
 };
 
-
 // ----------------------------------------------------------- history rings
 // Per-tile tables, filled one tile ahead by the scheduler warp: for each stream
 // the tile touches, its slot code and window head; for each tile row, its
@@ -106,7 +105,6 @@ __device__ __forceinline__ StreamTable table_at(int* base, int m0, int rows_per_
   return StreamTable{base, base + kMaxTileStreams, base + 2 * kMaxTileStreams, base + 2 * kMaxTileStreams + kTileM,
                      m0 / rows_per_stream};
 }
-
 
 __device__ void fill_table(const LayerArgs& a, int m0, const StreamTable& tab, int lane) {
   const int N = a.rows_per_stream;
@@ -171,8 +169,6 @@ __device__ __forceinline__ const float* hist_row(const LayerArgs& a, const Strea
   if (row >= 2 * H) row -= 2 * H;
   return slot_base(a.state, code) + a.hist.ring + row * a.hist.width;
 }
-
-
 
 // A-operand stores use plain shared-memory stores (no compiler barrier), so
 // loads for later rows can be scheduled ahead of them; fence.proxy.async before
@@ -622,7 +618,6 @@ enum EpilogueOut : int { kOutNone = 0, kOutS = 1, kOutPlanes = 2, kOutAct = 3 };
 template <int NT, int MODE, int KIND, int OUT>
 __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_constant__ LayerArgs a) {
   using Cfg = GemmCfg<NT, MODE, KIND>;
-  constexpr bool kOutSnake = OUT == kOutS;
   constexpr bool kOutPl = OUT == kOutPlanes;
   constexpr bool kOutA = OUT == kOutAct;
   constexpr int S = Cfg::kStages;

@@ -59,7 +59,7 @@ struct TailSmem {
   static constexpr int kPreR = kPreA + 3 * kTailC;               // [3][32]
   static constexpr int kFinA = kPreR + 3 * kTailC;               // [32]
   static constexpr int kFinR = kFinA + kTailC;                   // [32]
-  static constexpr int kFinW = kFinR + kTailC;                   // [32][7]
+  static constexpr int kFinW = kFinR + kTailC;                   // [7][32] (tap-major)
   static constexpr int kFinB = kFinW + kTailC * 7;               // [4]
   static constexpr int kCoefFloats = kFinB + 4;
   static constexpr int kMisc = kCoefs + kCoefFloats * 4;         // ints: heads[4], code, pad
@@ -85,6 +85,31 @@ __device__ __forceinline__ float4 hist_quad(const StateRef& st, const HistRef& h
   int row = head + h.rows + tp;
   if (row >= 2 * h.rows) row -= 2 * h.rows;
   return ldg4(slot_base(st, code) + h.ring + row * h.width + 4 * q);
+}
+
+// Depthwise k=7 (dilation d) + Snake_post of rows [0, n_out) into the f16 A
+// operand, for this thread's chain of L rows in channel quad q.
+template <int L>
+__device__ __forceinline__ void depthwise_chains(const float* uc, const float* pbuf, uint8_t* aop, int rg, int q, int d,
+                                                 int n_out) {
+  const int i0 = (rg / d) * L * d + rg % d;
+  if (i0 >= n_out) return;
+  float4 w[7], win[7];
+#pragma unroll
+  for (int j = 0; j < 7; ++j) w[j] = lds4(uc + j * 64 + 4 * q);
+  const float4 bias = lds4(uc + 7 * 64 + 4 * q), al2 = lds4(uc + 8 * 64 + 4 * q), rc2 = lds4(uc + 9 * 64 + 4 * q);
+#pragma unroll
+  for (int j = 0; j < 6; ++j) win[j] = lds4(pbuf + swq(i0 + j * d, q));
+#pragma unroll
+  for (int c = 0; c < L; ++c) {
+    const int i = i0 + c * d;
+    if (i >= n_out) break;
+    win[6] = lds4(pbuf + swq(i + 6 * d, q));
+    const float4 y = snake4(dw7<false>(w, win, bias), al2, rc2);
+    *reinterpret_cast<uint2*>(aop + sw128_offset(i, 4 * q)) = make_uint2(pack_f16(y.x, y.y), pack_f16(y.z, y.w));
+#pragma unroll
+    for (int j = 0; j < 6; ++j) win[j] = win[j + 1];
+  }
 }
 
 __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_constant__ TailArgs a) {
@@ -133,7 +158,7 @@ __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_cons
     cf[TailSmem::kFinA + i] = __ldg(a.fin_a + i);
     cf[TailSmem::kFinR + i] = __ldg(a.fin_r + i);
   }
-  for (int i = tid; i < kTailC * 7; i += kTailThreads) cf[TailSmem::kFinW + i] = __ldg(a.fin_w + i);
+  for (int i = tid; i < kTailC * 7; i += kTailThreads) cf[TailSmem::kFinW + (i % 7) * kTailC + i / 7] = __ldg(a.fin_w + i);
   if (tid == 0) cf[TailSmem::kFinB] = __ldg(a.fin_b);
   fence_async_smem();  // weights written by the generic proxy, read by the tensor core
   tc_fence_before();
@@ -173,6 +198,7 @@ __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_cons
     const int code = misc[4];
     float* xb = xbuf[buf];
 
+#pragma unroll
     for (int u = 0; u < 3; ++u) {
       const int d = u == 0 ? 1 : u == 1 ? 3 : 9, H = 6 * d;
       const int in_off = u == 0 ? 84 : u == 1 ? 78 : 60;  // input buffer row of relative row 0
@@ -182,50 +208,32 @@ __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_cons
       float* out = u == 0 ? qbuf : u == 1 ? xb : qbuf;  // y1 -> q, y2 -> x buffer, Snake_f(y3) -> q
       const HistRef& hist = a.unit[u].hist;
       const float* uc = cf + TailSmem::kUnitCoef + u * kTailCoef;
-      // (a) p = Snake_pre(input); a stream's first tile takes the rows before
-      // the stream from the history window.
-      // Each thread keeps one channel quad (q = tid % 8) throughout.
+      // (a) p = Snake_pre(input) (units 1 and 2: written by the previous
+      // unit's epilogue); a stream's first tile takes the rows before the
+      // stream from the history window.
+      // Each thread keeps one channel quad (q = tid % 8) in (a) and (b).
       const int q = tid & 7, rg = tid >> 3;
-      {
-        const float4 pa = lds4(cf + TailSmem::kPreA + u * kTailC + 4 * q);
-        const float4 pr = lds4(cf + TailSmem::kPreR + u * kTailC + 4 * q);
-        for (int i = rg; i < n_in; i += kTailThreads / 8) {
-          const int rel = i - in_off;
-          float4 v;
-          if (first && rel < 0 && rel >= -H) {
-            v = hist_quad(a.state, hist, code, misc[u], rel, q);
-          } else {
-            v = snake4(lds4(in + swq(i, q)), pa, pr);
-          }
-          *reinterpret_cast<float4*>(pbuf + swq(i, q)) = v;
-        }
+      if (u == 0) {
+        const float4 pa = lds4(cf + TailSmem::kPreA + 4 * q);
+        const float4 pr = lds4(cf + TailSmem::kPreR + 4 * q);
+        for (int i = rg; i < n_in; i += kTailThreads / 8)
+          *reinterpret_cast<float4*>(pbuf + swq(i, q)) = snake4(lds4(in + swq(i, q)), pa, pr);
       }
-      __syncthreads();
+      if (first) {
+        if (u == 0) __syncthreads();
+        for (int i = in_off - H + rg; i < in_off; i += kTailThreads / 8)
+          *reinterpret_cast<float4*>(pbuf + swq(i, q)) = hist_quad(a.state, hist, code, misc[u], i - in_off, q);
+      }
+      if (u == 0 || first) __syncthreads();
       // (b) A = Snake_post(depthwise(p)) in f16; the stream's last tile also
       // writes the new window (the last H rows of p).
-      // A thread's rows form a chain i0, i0 + d, ..., i0 + 3d (blocks of 4d rows
-      // split into d chains), so the seven taps slide through registers.
-      {
-        float4 w[7], win[7];
-#pragma unroll
-        for (int j = 0; j < 7; ++j) w[j] = lds4(uc + j * 64 + 4 * q);
-        const float4 bias = lds4(uc + 7 * 64 + 4 * q), al2 = lds4(uc + 8 * 64 + 4 * q), rc2 = lds4(uc + 9 * 64 + 4 * q);
-        const int i0 = (rg / d) * 4 * d + rg % d;
-        if (i0 < n_out) {
-#pragma unroll
-          for (int j = 0; j < 6; ++j) win[j] = lds4(pbuf + swq(i0 + j * d, q));
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int i = i0 + c * d;
-            if (i >= n_out) break;
-            win[6] = lds4(pbuf + swq(i + 6 * d, q));
-            const float4 y = snake4(dw7<false>(w, win, bias), al2, rc2);
-            *reinterpret_cast<uint2*>(aop + sw128_offset(i, 4 * q)) =
-                make_uint2(pack_f16(y.x, y.y), pack_f16(y.z, y.w));
-#pragma unroll
-            for (int j = 0; j < 6; ++j) win[j] = win[j + 1];
-          }
-        }
+      // A thread's rows form a chain i0, i0 + d, ... (blocks of L*d rows split
+      // into d chains of L), so the seven taps slide through registers: L = 4
+      // covers unit 0's 206 rows with 64 row groups, L = 3 the others'.
+      if (u == 0) {
+        depthwise_chains<4>(uc, pbuf, aop, rg, q, 1, n_out);
+      } else {
+        depthwise_chains<3>(uc, pbuf, aop, rg, q, d, n_out);
       }
       if (last && a.state.pool && tid < H * 8) {
         const int m = tid >> 3, q = tid & 7;  // window row m = time N - H + m
@@ -252,7 +260,8 @@ __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_cons
       ++n_mma;
       tc_fence_after();
       if (!ok) break;
-      // (d) y = input + (D + b) for rows [0, n_out); unit 2 keeps Snake_final(y).
+      // (d) y = input + (D + b) for rows [0, n_out), with Snake_pre of the next
+      // unit into p (the next unit's input rows); unit 2 keeps Snake_final(y).
       {
         const int lq = warp & 3, mt = (warp >> 2) & 1, half = warp >> 3;
         const int i = mt * kTileM + lq * 32 + lane;
@@ -268,7 +277,13 @@ __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_cons
             const float4 x = lds4(in + swq(i + H, q));
             float4 y = make_float4(x.x + (__uint_as_float(r[4 * j]) + b.x), x.y + (__uint_as_float(r[4 * j + 1]) + b.y),
                                    x.z + (__uint_as_float(r[4 * j + 2]) + b.z), x.w + (__uint_as_float(r[4 * j + 3]) + b.w));
-            if (u == 2) y = snake4(y, lds4(cf + TailSmem::kFinA + 4 * q), lds4(cf + TailSmem::kFinR + 4 * q));
+            if (u == 2) {
+              y = snake4(y, lds4(cf + TailSmem::kFinA + 4 * q), lds4(cf + TailSmem::kFinR + 4 * q));
+            } else {
+              *reinterpret_cast<float4*>(pbuf + swq(i, q)) =
+                  snake4(y, lds4(cf + TailSmem::kPreA + (u + 1) * kTailC + 4 * q),
+                         lds4(cf + TailSmem::kPreR + (u + 1) * kTailC + 4 * q));
+            }
             *reinterpret_cast<float4*>(out + swq(i, q)) = y;
           }
         }
@@ -295,23 +310,25 @@ __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_cons
     }
     __syncthreads();
     {
-      // Four lanes per output row, eight channels each (taps oldest first,
-      // channels in order), summed pairwise.
+      // Four lanes per output row, eight channels each: one accumulator per
+      // channel of a quad (taps oldest first), summed in a fixed tree.
       const int o = tid >> 2, grp = tid & 3;
       const float* fw = cf + TailSmem::kFinW;
-      float acc = 0.f;
+      float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int j = 0; j < 7; ++j) {
 #pragma unroll
         for (int qq = 0; qq < 2; ++qq) {
           const int q = 2 * grp + qq;
           const float4 v = lds4(qbuf + swq(o + j, q));
-          acc = fmaf(fw[(4 * q) * 7 + j], v.x, acc);
-          acc = fmaf(fw[(4 * q + 1) * 7 + j], v.y, acc);
-          acc = fmaf(fw[(4 * q + 2) * 7 + j], v.z, acc);
-          acc = fmaf(fw[(4 * q + 3) * 7 + j], v.w, acc);
+          const float4 wj = lds4(fw + j * kTailC + 4 * q);
+          acc4.x = fmaf(wj.x, v.x, acc4.x);
+          acc4.y = fmaf(wj.y, v.y, acc4.y);
+          acc4.z = fmaf(wj.z, v.z, acc4.z);
+          acc4.w = fmaf(wj.w, v.w, acc4.w);
         }
       }
+      float acc = (acc4.x + acc4.y) + (acc4.z + acc4.w);
       acc += __shfl_xor_sync(0xffffffffu, acc, 1);
       acc += __shfl_xor_sync(0xffffffffu, acc, 2);
       if (grp == 0) {

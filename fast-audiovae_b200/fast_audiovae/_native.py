@@ -34,6 +34,8 @@ SIGNATURES = {
     "fav_state_pool_bytes": ([ct.c_int32], ct.c_size_t),
     "fav_step_workspace_bytes": ([ct.c_int32, ct.c_int32], ct.c_size_t),
     "fav_step": ([_P, _P, ct.c_int32, _P, ct.c_int32, ct.c_int32, _P, _P, _P, ct.c_size_t, _P, _P], ct.c_int32),
+    "fav_debug_step_unfused": ([_P, _P, ct.c_int32, _P, ct.c_int32, ct.c_int32, _P, _P, _P, ct.c_size_t, _P, _P],
+                               ct.c_int32),
     "fav_step_static": ([_P, _P, ct.c_int32, _P, ct.c_int32, ct.c_int32, _P, _P, _P, _P], ct.c_int32),
     "fav_batch_workspace_bytes": ([ct.c_int32, ct.c_int32], ct.c_size_t),
     "fav_plan_workspace_bytes": ([_P, ct.c_int32, ct.c_int32], ct.c_size_t),

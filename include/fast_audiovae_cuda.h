@@ -195,6 +195,15 @@ FAV_API int32_t fav_debug_step_layers(const fav_plan *plan, float *state_pool, i
                                       const float *latents, void *workspace, size_t workspace_bytes,
                                       uint32_t *status, int32_t last_layer, float **layer_out, void *cuda_stream);
 
+/* Diagnostic (no reference counterpart): fav_step with every layer as its own
+ * kernel (stage 5's residual units and the final conv unfused), for checking
+ * the fused stage-5 kernel against the per-layer kernels. Same arguments and
+ * contract as fav_step. */
+FAV_API int32_t fav_debug_step_unfused(const fav_plan *plan, float *state_pool, int32_t num_slots,
+                                       const int32_t *slot_codes, int32_t n_streams, int32_t frames,
+                                       const float *latents, float *audio, void *workspace, size_t workspace_bytes,
+                                       uint32_t *status, void *cuda_stream);
+
 /* Engine self-test (diagnostic, no reference counterpart): C[M][N] = A[M][K] * B[N][K]^T
  * through the tcgen05 GEMM engine. a, c device fp32; b host fp32.
  * mode 0 = f16 operands, 1 = split-bf16, 2 = s8 (A and B hold integers in
