@@ -50,15 +50,23 @@ def _latents_step(chunks):
     """``gpu.py:115-122`` for one step of many streams: every chunk a float32
     ``[1,64,L]`` array of one common L, all finite. Returns the chunks stacked
     as an owned ``[n,64,L]`` array (one copy, one vectorised finiteness check)."""
-    for value in chunks:
-        if (not isinstance(value, np.ndarray) or value.dtype != np.float32
-                or value.ndim != 3 or value.shape[:2] != (1, 64)):
-            raise ValueError("Latents must be a float32 NumPy array with shape [1,64,L]")
     if not chunks:
         return np.empty((0, 64, 0), dtype=np.float32)
-    frames = chunks[0].shape[2]
-    if any(c.shape[2] != frames for c in chunks):
-        raise ValueError("decode_streams requires chunks of equal length")
+    # One pass each over types, dtypes and shapes (a server step carries
+    # hundreds of chunks); the per-chunk loop below only names the failure.
+    if (all(type(c) is np.ndarray for c in chunks) and {c.dtype for c in chunks} == {np.dtype(np.float32)}
+            and len(shapes := {c.shape for c in chunks}) == 1):
+        (shape,) = shapes
+        if len(shape) != 3 or shape[:2] != (1, 64):
+            raise ValueError("Latents must be a float32 NumPy array with shape [1,64,L]")
+    else:
+        for value in chunks:
+            if (not isinstance(value, np.ndarray) or value.dtype != np.float32
+                    or value.ndim != 3 or value.shape[:2] != (1, 64)):
+                raise ValueError("Latents must be a float32 NumPy array with shape [1,64,L]")
+        frames = chunks[0].shape[2]
+        if any(c.shape[2] != frames for c in chunks):
+            raise ValueError("decode_streams requires chunks of equal length")
     stacked = np.concatenate(chunks, axis=0)
     if not np.isfinite(stacked).all():
         raise ValueError("Latents must contain only finite values")
@@ -237,13 +245,16 @@ class CUDADecoder:
     # ------------------------------------------------------------ internals
     def _step(self, streams, arrays, frames):
         """One device step for ``streams``; commits their histories only on success."""
-        audio = self._backend.step([s._code() for s in streams], arrays, frames)
+        codes = [(s._slot << 2) | (_FRESH if s._fresh else 0) | s._parity for s in streams]  # CUDAStream._code
+        audio = self._backend.step(codes, arrays, frames)
         if (not isinstance(audio, np.ndarray) or audio.dtype != np.float32
                 or audio.shape != (len(streams), HOP * frames)):
             raise RuntimeError("CUDA model returned invalid audio")
-        for s in streams:
-            s._commit(frames)
-        return [audio[i].reshape(1, 1, HOP * frames) for i in range(len(streams))]
+        for s in streams:  # CUDAStream._commit
+            s._parity ^= 1
+            s._fresh = False
+            s.frames_decoded += frames
+        return list(audio.reshape(len(streams), 1, 1, HOP * frames))
 
     def _acquire_slot(self):
         with self._lock:
@@ -320,8 +331,8 @@ class CUDADecoder:
         for s in ordered:
             s._lock.acquire()
         try:
-            for s in streams:
-                s._check_open()
+            if any(s._closed for s in streams):
+                next(s for s in streams if s._closed)._check_open()
             if not frames:
                 return [np.empty((1, 1, 0), dtype=np.float32) for _ in streams]
             with self._lock:
