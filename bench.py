@@ -4,9 +4,10 @@ Workload ("stream40ms"): every GPU decodes S independent streams (default 512,
 the per-GPU shard of 4096 streams on 8 GPUs) that each receive one-frame
 (40 ms, 1920-sample) latent chunks ~N(0,1) with per-stream seeds, carrying
 causal history across steps; decoder coefficients are the seeded random init.
-One step = one chunk for all S streams (23 kernel launches: stem, then per
-stage a transposed conv and three residual units, with stage 5's units and the
-final conv fused into one kernel). Weak scaling:
+One step = one chunk for all S streams (29 kernel launches: stem, then per
+stage a transposed conv and three residual units, stages 0-1's units as a
+depthwise pre-pass plus the GEMM, stage 5's units and the final conv fused into
+one kernel). Weak scaling:
 each rank owns S streams, no collective on the data path.
 
 Reported (one JSON line, rank 0):
@@ -48,7 +49,8 @@ METRIC = "aggregate audio-s/s (RTF^-1), 40 ms streaming chunks"
 # three residual units + final conv).
 LAYER_NAMES = ["stem"] + [f"stage{i}.{k}" for i in range(5) for k in ("transpose", "res0", "res1", "res2")] + \
     ["stage5.transpose", "stage5.tail"]
-LAUNCHES_PER_STEP = len(LAYER_NAMES)
+# The residual units of stages 0-1 are two launches each (depthwise pre-pass, then the GEMM).
+LAUNCHES_PER_STEP = len(LAYER_NAMES) + 6
 
 
 def kernel_ms(layer_ms26):
@@ -107,7 +109,8 @@ def layer_costs():
             break
         for j, d in enumerate((1, 3, 9)):
             nxt = 0 if j < 2 else cout * 4 * 2  # next transposed conv's history row
-            out.append(dict(flops=2 * cout * cout * n, act=n * cout * 16, weights=cout * cout * 2,
+            pre = n * cout * 4 if i <= 1 else 0  # stages 0-1: the f16 A operand written and read once
+            out.append(dict(flops=2 * cout * cout * n, act=n * cout * 16 + pre, weights=cout * cout * 2,
                             hist=6 * d * cout * 4 * 2 + nxt))
         cin = cout
     assert len(out) == LAUNCHES_PER_STEP

@@ -89,6 +89,14 @@ int32_t encode_plane_map(CUtensorMap* map, const void* planes, int rows, int cha
                     "planes");
 }
 
+// Preformed residual A operand [rows][channels] f16: boxes of 64 channels x
+// 128 rows in the 128-byte swizzle (the MMA's K-major layout).
+int32_t encode_operand_map(CUtensorMap* map, const uint16_t* a, int rows, int channels) {
+  const cuuint64_t dims[2] = {(cuuint64_t)channels, (cuuint64_t)rows};
+  const cuuint32_t box[2] = {(cuuint32_t)fav::kKBlock, (cuuint32_t)fav::kTileM};
+  return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_128B, "operand");
+}
+
 // Stage-5 input y [rows][32] fp32 for the fused tail: boxes of 32 channels x
 // (128 + 84) rows in the 128-byte swizzle.
 int32_t encode_tail_map(CUtensorMap* map, const float* x, int rows) {
@@ -384,7 +392,7 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
 constexpr int kWorkspaceRegions = 6;
 constexpr size_t kRegionFloatsPerFrame = 61440;
 
-// Launches the 26 kernels of one decoder step. Layers are numbered 0 (stem),
+// Launches the kernels of one decoder step. Layers are numbered 0 (stem),
 // 1 + 4i (stage i transposed conv), 2 + 4i + j (stage i residual j) and 25
 // (final conv); the schedule stops after ``last_layer`` and reports the buffer
 // holding that layer's output y (a layer whose y nothing reads writes it only then).
@@ -598,7 +606,19 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
         u.next_alpha = p->fin_a;
         u.next_recip = p->fin_r;
       }
-      if ((es = encode_input_map(&u.tmap, S[in], u.rows, st.c_out, u.box_rows)) != FAV_OK) return es;
+      if (!r.int8 && i <= 1) {
+        // Stages 0-1 (8 and 48 rows per stream and frame, mostly history taps,
+        // N split over 4 and 2 tiles): the depthwise pre-pass writes the f16 A
+        // operand once, behind this layer's Snake output in S[out] (both fit:
+        // 1.5 * rows * C <= the region), and the engine TMA-loads it.
+        uint16_t* a_op = reinterpret_cast<uint16_t*>(S[out] + (size_t)u.rows * st.c_out);
+        const fav::DepthwiseArgs dw{S[in], a_op, r.coef, u.rows, n, st.c_out, r.dilation, state, u.hist};
+        if ((e = fav::launch_depthwise(dw, stream)) != cudaSuccess) return cuda_fail(e, "depthwise launch");
+        u.kind = fav::kResidualPre;
+        if ((es = encode_operand_map(&u.tmap, a_op, u.rows, st.c_out)) != FAV_OK) return es;
+      } else if ((es = encode_input_map(&u.tmap, S[in], u.rows, st.c_out, u.box_rows)) != FAV_OK) {
+        return es;
+      }
       if ((e = fav::launch_gemm_layer(u, stream)) != cudaSuccess) return cuda_fail(e, "residual launch");
       if (last_out) *last_out = X[out];
       mark(++layer + 1);

@@ -30,7 +30,9 @@ constexpr int kRingFloats = 2 * kSlotFloats;              // ring rows of all hi
 constexpr int kHeadInts = 32;                             // per head table (26 used)
 constexpr int kSlotStride = kRingFloats + 2 * kHeadInts;  // floats per slot
 
-enum LayerKind : int { kStem = 0, kTconv = 1, kResidual = 2, kTestGemm = 3 };
+// kResidualPre: a residual unit whose A operand (depthwise + Snake_post, f16
+// [rows][C]) was written by launch_depthwise; the engine TMA-loads it.
+enum LayerKind : int { kStem = 0, kTconv = 1, kResidual = 2, kTestGemm = 3, kResidualPre = 4 };
 
 // Operand precision of a GEMM layer.
 enum GemmMode : int {
@@ -175,6 +177,22 @@ struct TailArgs {
   uint32_t* status;
 };
 cudaError_t launch_tail(const TailArgs& a, cudaStream_t stream);
+
+// Depthwise pre-pass of a residual unit (fav_prepass.cu): A = Snake_post(
+// depthwise_k7(s)) as f16 [rows][channels] for a kResidualPre GEMM, plus the
+// layer's new history window.
+struct DepthwiseArgs {
+  const float* s;        // Snake_pre(x) [rows][channels] fp32
+  uint16_t* a;           // A operand [rows][channels] f16
+  const float* coef;     // [channels / 64][w0..w6, bias, alpha2, recip2][64]
+  int rows;
+  int rows_per_stream;
+  int channels;          // multiple of 4, at most 1024
+  int dilation;
+  StateRef state;
+  HistRef hist;
+};
+cudaError_t launch_depthwise(const DepthwiseArgs& a, cudaStream_t stream);
 cudaError_t prepare_tail();
 
 // Kernel launchers (fav_kernels.cu). Return cudaError_t of the launch.

@@ -538,7 +538,7 @@ __device__ __forceinline__ void load_skip(const LayerArgs& a, int row0, int n, i
   for (int k = 0; k < 4; ++k) {
     const int g = row0 + 8 * k + (lane >> 2);
     xr[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (KIND == kResidual && g < a.rows) xr[k] = __ldg(reinterpret_cast<const float4*>(a.x + (size_t)g * a.c_out + n) + (lane & 3));
+    if ((KIND == kResidual || KIND == kResidualPre) && g < a.rows) xr[k] = __ldg(reinterpret_cast<const float4*>(a.x + (size_t)g * a.c_out + n) + (lane & 3));
   }
 }
 
@@ -625,6 +625,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   constexpr bool kI8Tconv = Cfg::kI8Tconv;
   constexpr bool kI8Res = kI8 && KIND == kResidual;
   constexpr bool kStaged = KIND == kResidual || kI8Tconv;  // producers read TMA-staged input boxes
+  constexpr bool kSkipAdd = KIND == kResidual || KIND == kResidualPre;  // y = x + (D + b)
+  // The A operand is TMA-loaded whole (no producer work): a bf16 transposed
+  // conv's planes, or a residual unit's preformed depthwise output.
+  constexpr bool kTmaA = (KIND == kTconv && !kI8) || KIND == kResidualPre;
   constexpr int kLpr = NT == 32 ? 8 : 16;  // residual lanes per row (C = 32 uses eight)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -664,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       // A bf16 transposed conv's A operand is one TMA load (transaction count only).
-      mbar_init(&a_full[s], (KIND == kTconv && !kI8) ? 1 : kProducerWarps);
+      mbar_init(&a_full[s], kTmaA ? 1 : kProducerWarps);
       mbar_init(&b_full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -692,7 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
 
   if (warp < kProducerWarps) {
     // ---- A producers (a bf16 transposed conv has none: its A operand is TMA-loaded whole)
-    if (KIND == kTconv && !kI8) goto done;
+    if (kTmaA) goto done;
     if (KIND == kResidual && kLpr == 8) {
       // C = 32: channels 32-63 of every A stage stay zero.
       for (int s = 0; s < S; ++s)
@@ -957,7 +961,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         // writes asynchronously never meet a control-flow merge before the wait.
         tmem_ld16_async(base + (c + 1 < kChunks ? c + 1 : c) * kEpiCols, rn);
         float4 x[4];  // this lane's row of the skip input
-        if (KIND == kResidual) transpose_skip(stage, lane, xr, x);
+        if (kSkipAdd) transpose_skip(stage, lane, xr, x);
         uint4 wn[4];  // stem: next chunk's history bits
         if (kStemPl && hist_old && c + 1 < kChunks) {
 #pragma unroll
@@ -997,7 +1001,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           v[4 * j + 1] = acc.y + b.y;
           v[4 * j + 2] = acc.z + b.z;
           v[4 * j + 3] = acc.w + b.w;
-          if (KIND == kResidual) {
+          if (kSkipAdd) {
             v[4 * j] = x[j].x + v[4 * j];
             v[4 * j + 1] = x[j].y + v[4 * j + 1];
             v[4 * j + 2] = x[j].z + v[4 * j + 2];
@@ -1103,7 +1107,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       }
     }
   } else if (warp == kRawWarp) {
-    if (lane == 0 && KIND == kTconv && !kI8) {
+    if (lane == 0 && KIND == kResidualPre) {
+      // ---- preformed residual A operand: one 64-channel x 128-row f16 box per K block
+      uint32_t g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int m0 = tile_m(t) * kTileM;
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader))) break;
+          mbar_arrive_expect_tx(&a_full[s], Cfg::kAStage);
+          tma_load_2d(a_base + s * Cfg::kAStage, &a.tmap, kb * kKBlock, m0, &a_full[s]);
+        }
+      }
+    } else if (lane == 0 && KIND == kTconv && !kI8) {
       // ---- transposed-conv A operand: tap 0 from the planes, tap 1 from the
       // shifted planes, hi and lo tiles in one 3-D box
       const int kpt = a.k_channels / kKBlock;
@@ -1146,7 +1164,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   } else if (warp == kSchedWarp) {
     // ---- scheduler: per-tile stream/row tables (and the int8 transposed
     // conv's row scales), one tile ahead of the producers
-    if (KIND == kStem || KIND == kResidual || kI8Tconv) {
+    if (KIND == kResidualPre && (a.epi & kEpiPlanes)) {
+      // No producers: the table only serves the stream-start plane rows.
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        const int m0 = tile_m(t) * kTileM;
+        const StreamTable tab = table_at(table, m0, a.rows_per_stream);
+        fill_table(a, m0, tab, lane);
+        __syncwarp();
+        first_rows_prev_planes(a, m0, tile_n(t) * NT, NT, tab, lane);
+        __syncwarp();
+      }
+    } else if (KIND == kStem || KIND == kResidual || kI8Tconv) {
       uint32_t ti = 0;
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++ti) {
         const int m0 = tile_m(t) * kTileM;
@@ -1274,6 +1302,7 @@ static cudaError_t set_smem() {
   X(128, kModeSplit, kTconv, kOutS) X(64, kModeSplit, kTconv, kOutS) X(128, kModeI8, kTconv, kOutS)         \
   X(64, kModeSplit, kTconv, kOutNone)                                                                      \
   X(256, kModeF16, kResidual, kOutS) X(128, kModeF16, kResidual, kOutS) X(64, kModeF16, kResidual, kOutS)  \
+  X(256, kModeF16, kResidualPre, kOutS) X(256, kModeF16, kResidualPre, kOutPlanes)                          \
   X(32, kModeF16, kResidual, kOutS) X(256, kModeF16, kResidual, kOutPlanes)                                \
   X(128, kModeF16, kResidual, kOutPlanes) X(64, kModeF16, kResidual, kOutPlanes)                           \
   X(256, kModeI8, kResidual, kOutS) X(128, kModeI8, kResidual, kOutS) X(256, kModeI8, kResidual, kOutAct)  \

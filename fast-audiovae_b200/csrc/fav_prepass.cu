@@ -1,0 +1,83 @@
+// Depthwise pre-pass of a residual unit (stages 0 and 1): the A operand of the
+// unit's 1x1 projection, Snake_post(depthwise_k7(s)) in f16, written once to
+// HBM so the GEMM engine TMA-loads it (LayerKind kResidualPre) instead of
+// rebuilding it in every N tile's producers. The reference computes the unit
+// as snake -> causal depthwise conv (with the stream's history) -> snake ->
+// 1x1 conv (mps_decoder.py residual blocks, restated at oracle/decoder.py:165-171).
+//
+// At these stages a stream has 8 or 48 rows per frame, fewer than the 6d rows
+// of history a dilated tap reaches back, so most taps come from the history
+// ring. One thread per (row, channel quad) gives the gathers the whole GPU's
+// memory-level parallelism; the arithmetic (fused multiply-add chain, Snake)
+// is the producers' own, so the result is the same bit for bit.
+//
+// Each thread also writes its row of the layer's new history window (the
+// input rows s that the next step's taps reach), zero rows for a fresh stream
+// whose window is longer than the chunk, and the stream's advanced head.
+#include "fav_common.cuh"
+
+namespace fav {
+namespace {
+
+constexpr int kDwThreads = 256;
+
+__global__ void __launch_bounds__(kDwThreads) depthwise_kernel(const __grid_constant__ DepthwiseArgs a) {
+  const int C = a.channels, quads = C / 4;
+  const long long idx = (long long)blockIdx.x * kDwThreads + threadIdx.x;
+  if (idx >= (long long)a.rows * quads) return;
+  const int g = (int)(idx / quads), q = (int)(idx - (long long)g * quads);
+  const int N = a.rows_per_stream, d = a.dilation, H = 6 * d;
+  const int s = g / N, t = g - s * N;
+  const int n_new = N < H ? N : H;
+  const bool pool = a.state.pool != nullptr;
+  int code = 0, head = 0;
+  float* slot = nullptr;
+  if (pool) {
+    code = a.state.slot_codes ? a.state.slot_codes[s] : ((s << 2) | a.state.uniform_code);
+    slot = slot_base(a.state, code);
+    if (!(code & 2)) head = head_table(slot, code & 1)[a.hist.index];
+  }
+  const int kl = (4 * q) & (kKBlock - 1);
+  const float* cf = a.coef + (size_t)(4 * q / kKBlock) * kCoefResidual * 64 + kl;
+  float4 w[7], win[7];
+#pragma unroll
+  for (int j = 0; j < 7; ++j) w[j] = ldg4(cf + j * 64);
+  const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 7; ++j) {
+    const int back = (6 - j) * d;
+    const int tp = t - back;
+    if (tp >= 0) {
+      win[j] = ldg4(a.s + (size_t)(g - back) * C + 4 * q);
+    } else if (pool && !(code & 2)) {
+      int row = head + H + tp;  // window [head, head + H)
+      if (row >= 2 * H) row -= 2 * H;
+      win[j] = ldg4(slot + a.hist.ring + row * a.hist.width + 4 * q);
+    } else {
+      win[j] = zero4;
+    }
+  }
+  const float4 y = snake4(dw7<false>(w, win, ldg4(cf + 7 * 64)), ldg4(cf + 8 * 64), ldg4(cf + 9 * 64));
+  *reinterpret_cast<uint2*>(a.a + (size_t)g * C + 4 * q) = make_uint2(pack_f16(y.x, y.y), pack_f16(y.z, y.w));
+  if (!pool) return;
+  if (t >= N - n_new)
+    *reinterpret_cast<float4*>(hist_new_row(a.state, a.hist, code, head, t, N) + 4 * q) = win[6];
+  if ((code & 2) && N < H) {
+    // A fresh stream's window starts as H - N zero rows before its N new ones.
+    for (int r = N + t; r < H; r += N)
+      *reinterpret_cast<float4*>(slot + a.hist.ring + r * a.hist.width + 4 * q) = zero4;
+  }
+  if (t == 0 && q == 0) hist_commit_head(a.state, a.hist, code, head, N);
+}
+
+}  // namespace
+
+cudaError_t launch_depthwise(const DepthwiseArgs& a, cudaStream_t stream) {
+  if (a.rows <= 0) return cudaSuccess;
+  if (a.channels % 4 || a.channels > 1024) return cudaErrorInvalidValue;
+  const long long items = (long long)a.rows * (a.channels / 4);
+  depthwise_kernel<<<(unsigned)((items + kDwThreads - 1) / kDwThreads), kDwThreads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace fav
