@@ -113,7 +113,7 @@ def layer_costs():
             out.append(dict(flops=2 * cout * cout * n, act=n * cout * 16 + pre, weights=cout * cout * 2,
                             hist=6 * d * cout * 4 * 2 + nxt))
         cin = cout
-    assert len(out) == LAUNCHES_PER_STEP
+    assert len(out) == len(LAYER_NAMES)
     return out
 
 

@@ -26,6 +26,7 @@ from __future__ import annotations
 
 import ctypes as ct
 import threading
+import weakref
 
 import numpy as np
 
@@ -87,6 +88,52 @@ def _torch():
     return torch
 
 
+class LentBuffers:
+    """Host output buffers lent to returned audio arrays.
+
+    A step's audio is copied from the device straight into a pinned buffer,
+    and the caller receives NumPy arrays over that buffer; the buffer returns
+    to the pool only when the last of those arrays is gone (a weakref
+    finalizer), so no live result is ever overwritten. While more than
+    ``limit`` results are held, ``acquire`` returns None and the caller copies
+    into an ordinary owned array instead, so keeping results never pins more
+    than ``limit`` buffers. ``alloc(numel)`` makes a buffer (a pinned fp32
+    tensor in DeviceBackend).
+    """
+
+    def __init__(self, alloc, limit=4):
+        self._alloc = alloc
+        self._limit = limit
+        self._free = []
+        self._lent = 0
+        self._lock = threading.Lock()
+
+    def acquire(self, numel):
+        with self._lock:
+            for i, buf in enumerate(self._free):
+                if buf.numel() >= numel:
+                    self._lent += 1
+                    return self._free.pop(i)
+            if self._lent >= self._limit:
+                return None
+            self._lent += 1
+        return self._alloc(numel)
+
+    def release(self, buf):
+        with self._lock:
+            self._lent -= 1
+            self._free.append(buf)
+
+    def lend(self, buf, array):
+        """Return ``buf`` to the pool once ``array`` and every view of it are gone."""
+        weakref.finalize(array, self.release, buf)
+        return array
+
+    @property
+    def lent(self):
+        return self._lent
+
+
 class DeviceBackend:
     """Device memory and C-ABI calls for one decoder (one plan, one history pool).
 
@@ -113,6 +160,7 @@ class DeviceBackend:
             self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
             self.status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         self.cache = {}
+        self.out_buffers = LentBuffers(lambda numel: torch.empty(numel, dtype=torch.float32, pin_memory=True))
         # Streaming steps replay a CUDA graph of the step's 26 launches per
         # (streams, frames, buffers): the first step of a shape runs eagerly,
         # the second captures, later ones replay (one launch call per step).
@@ -155,16 +203,25 @@ class DeviceBackend:
         return dev
 
     def _download(self, audio_dev):
-        host = self._buffer("a_host", tuple(audio_dev.shape), self.torch.float32, pinned=True)
+        """The step's audio as host fp32: in a lent pinned buffer (no host copy),
+        or, while too many earlier results are still held, an owned copy."""
+        shape = tuple(audio_dev.shape)
+        lent = self.out_buffers.acquire(audio_dev.numel())
+        host = (lent[:audio_dev.numel()].view(*shape) if lent is not None
+                else self._buffer("a_host", shape, self.torch.float32, pinned=True))
         host.copy_(audio_dev, non_blocking=True)
         self.status_host.copy_(self.status, non_blocking=True)
         self.torch.cuda.current_stream(self.device).synchronize()
         status = int(self.status_host.item())
-        if status == NONFINITE_STATUS:
-            raise RuntimeError("CUDA model returned nonfinite audio")
         if status:
+            if lent is not None:
+                self.out_buffers.release(lent)
+            if status == NONFINITE_STATUS:
+                raise RuntimeError("CUDA model returned nonfinite audio")
             raise RuntimeError("CUDA decoder kernel reported status 0x%x" % status)
-        return host.numpy().copy()
+        if lent is None:
+            return host.numpy().copy()
+        return self.out_buffers.lend(lent, host.numpy())
 
     def step(self, codes, arrays, frames):
         from ._native import check

@@ -219,3 +219,32 @@ def test_load_without_gpu_never_falls_back():
     import fast_audiovae
     with pytest.raises(RuntimeError, match="CUDA"):
         fast_audiovae.load(mode="batch")
+
+
+def test_lent_output_buffers_are_reused_only_after_release():
+    """Returned audio lives in a pooled host buffer until its last view is gone."""
+    import gc
+
+    import torch
+
+    from fast_audiovae.cuda import LentBuffers
+
+    made = []
+
+    def alloc(numel):
+        made.append(torch.zeros(numel))
+        return made[-1]
+
+    pool = LentBuffers(alloc, limit=2)
+    a = pool.lend(buf := pool.acquire(8), buf[:8].numpy())
+    views = list(a.reshape(2, 1, 1, 4))
+    del a, buf
+    gc.collect()
+    assert pool.lent == 1  # the views keep the buffer lent
+    b_buf = pool.acquire(8)
+    assert len(made) == 2 and b_buf is made[1]
+    assert pool.acquire(8) is None  # limit reached: caller copies instead
+    del views
+    gc.collect()
+    assert pool.lent == 1
+    assert pool.acquire(8) is made[0]  # released buffer comes back
