@@ -298,7 +298,10 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
     st.c_out = st.c_in / 2;
     st.rate = fav::kRates[i];
     const int n_total = st.c_out * st.rate;
-    st.n_tile_t = n_total % 128 == 0 ? 128 : n_total;
+    // Wide layers (N >= 1024, stages 0-2) take N tiles of 256 columns (two
+    // 256-column accumulators fill TMEM), halving the A operand's re-reads;
+    // measured slower at stage 3 (N = 256, one tile), which keeps 128.
+    st.n_tile_t = n_total % 256 == 0 && n_total >= 1024 ? 256 : n_total % 128 == 0 ? 128 : n_total;
     st.scale = up(base + 0);
     st.offset = up(base + 1);
     st.alpha = up(base + 2);

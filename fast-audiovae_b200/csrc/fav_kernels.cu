@@ -1299,7 +1299,8 @@ static cudaError_t set_smem() {
 // step schedules use; anything else is rejected at launch.
 #define FAV_CONFIGS(X)                                                                                      \
   X(256, kModeSplit4, kStem, kOutPlanes) X(256, kModeSplit4, kStem, kOutAct)                                \
-  X(128, kModeSplit, kTconv, kOutS) X(64, kModeSplit, kTconv, kOutS) X(128, kModeI8, kTconv, kOutS)         \
+  X(256, kModeSplit, kTconv, kOutS) X(128, kModeSplit, kTconv, kOutS) X(64, kModeSplit, kTconv, kOutS)      \
+  X(128, kModeI8, kTconv, kOutS)                                                                           \
   X(64, kModeSplit, kTconv, kOutNone)                                                                      \
   X(256, kModeF16, kResidual, kOutS) X(128, kModeF16, kResidual, kOutS) X(64, kModeF16, kResidual, kOutS)  \
   X(256, kModeF16, kResidualPre, kOutS) X(256, kModeF16, kResidualPre, kOutPlanes)                          \
