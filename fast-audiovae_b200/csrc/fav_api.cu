@@ -232,7 +232,8 @@ struct fav_plan {
   int device = 0;
   DeviceArrays mem;
   const float *stem_w = nullptr, *stem_b = nullptr, *pw_b = nullptr;
-  const uint8_t* stem_img = nullptr;
+  const uint8_t* stem_img = nullptr;    // stem 1x1 weights for 256-column N tiles
+  const uint8_t* stem_img64 = nullptr;  // the same for 64-column N tiles (steps of few rows)
   const float* stem_pw = nullptr;  // int8 plan: fp32 stem 1x1 weights [2048][64] for the CUDA-core stem
   StageDev stages[fav::kStages];
   const float *fin_a = nullptr, *fin_r = nullptr, *fin_w = nullptr, *fin_b = nullptr;
@@ -286,6 +287,8 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
     const float* pw = w[2];
     plan->stem_img = up_img(pack_operand(2048, 64, 256, fav::kModeSplit,
                                          [pw](int n, int k) { return pw[(size_t)n * 64 + k]; }));
+    plan->stem_img64 = up_img(pack_operand(2048, 64, 64, fav::kModeSplit,
+                                           [pw](int n, int k) { return pw[(size_t)n * 64 + k]; }));
   }
   plan->pw_b = up(3);
   if (i8) plan->stem_pw = up(2);
@@ -462,7 +465,9 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     a.k_channels = 64;
     a.num_kblocks = 1;
     a.n_total = 2048;
-    a.n_tile = 256;
+    // A step of few rows (a server's one-frame chunks, one stream's latency)
+    // spreads the stem over 64-column N tiles so more SMs share its epilogue.
+    a.n_tile = a.rows <= 1024 ? 64 : 256;
     a.c_out = 2048;
     a.x = z;
     a.z_stride = z_stride;
@@ -470,7 +475,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     a.bias = p->pw_b;
     a.dw_w = p->stem_w;
     a.dw_b = p->stem_b;
-    a.wimg = p->stem_img;
+    a.wimg = a.n_tile == 64 ? p->stem_img64 : p->stem_img;
     a.hist = fav::HistRef{0, 0, 6, fav::kLatentChannels};
     a.out_x = X[0];
     feed_tconv(a, 0, last_layer == 0);

@@ -1298,7 +1298,8 @@ static cudaError_t set_smem() {
 // The (N tile, operand mode, layer kind, epilogue output) combinations the
 // step schedules use; anything else is rejected at launch.
 #define FAV_CONFIGS(X)                                                                                      \
-  X(256, kModeSplit4, kStem, kOutPlanes) X(256, kModeSplit4, kStem, kOutAct)                                \
+  X(256, kModeSplit4, kStem, kOutPlanes) X(64, kModeSplit4, kStem, kOutPlanes)                            \
+  X(256, kModeSplit4, kStem, kOutAct)                                                                      \
   X(256, kModeSplit, kTconv, kOutS) X(128, kModeSplit, kTconv, kOutS) X(64, kModeSplit, kTconv, kOutS)      \
   X(128, kModeI8, kTconv, kOutS)                                                                           \
   X(64, kModeSplit, kTconv, kOutNone)                                                                      \
