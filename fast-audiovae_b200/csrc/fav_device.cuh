@@ -98,6 +98,18 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// Programmatic dependent launch. A kernel launched with the programmatic
+// stream serialization attribute may start while the previous kernel in the
+// stream is still draining: it waits here, before touching any memory an
+// earlier kernel writes or reads, until that kernel has completed and its
+// writes are visible, then lets the next kernel in the stream launch (whose
+// blocks take SMs only as this kernel's blocks finish). Both are no-ops in a
+// kernel launched the ordinary way.
+__device__ __forceinline__ void grid_dependency_sync() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Make generic-proxy shared-memory writes visible to the async proxy (MMA).
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -150,6 +150,25 @@ struct FinalArgs {
   uint32_t* status;
 };
 
+// Launches ``kernel`` so that it may start while the previous kernel in the
+// stream drains (programmatic dependent launch); the kernel must call
+// grid_dependency_sync() before its first access to memory earlier kernels use.
+template <typename Args>
+inline cudaError_t launch_overlapped(void (*kernel)(Args), unsigned grid, unsigned block, size_t smem,
+                                     cudaStream_t stream, const Args& a) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, a);
+}
+
 // Fused stage-5 tail (fav_tail.cu): the three residual units and the final conv.
 constexpr int kTailC = 32;  // stage-5 channels
 struct TailUnitArgs {

@@ -693,6 +693,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dependency_sync();
 
   if (warp < kProducerWarps) {
     // ---- A producers (a bf16 transposed conv has none: its A operand is TMA-loaded whole)
@@ -1284,8 +1285,7 @@ static cudaError_t launch_cfg(const LayerArgs& a, cudaStream_t stream) {
   const int tiles = ((a.rows + kTileM - 1) / kTileM) * (a.n_total / NT);
   int grid = tiles < g_sm_count ? tiles : g_sm_count;
   if (MODE == kModeI8 && KIND == kResidual && grid > kScratchCtas) grid = kScratchCtas;
-  gemm_layer_kernel<NT, MODE, KIND, OUT><<<grid, kThreads, Cfg::kSmem, stream>>>(a);
-  return cudaGetLastError();
+  return launch_overlapped(gemm_layer_kernel<NT, MODE, KIND, OUT>, grid, kThreads, Cfg::kSmem, stream, a);
 }
 
 template <int NT, int MODE, int KIND, int OUT>

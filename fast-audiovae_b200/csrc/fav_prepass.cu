@@ -24,6 +24,7 @@ constexpr int kDwThreads = 256;
 // Four blocks per SM (64 registers) keep more gathers in flight than the
 // unconstrained 80-register build; measured faster at stages 0-1.
 __global__ void __launch_bounds__(kDwThreads, 4) depthwise_kernel(const __grid_constant__ DepthwiseArgs a) {
+  grid_dependency_sync();
   const int C = a.channels, quads = C / 4;
   const long long idx = (long long)blockIdx.x * kDwThreads + threadIdx.x;
   if (idx >= (long long)a.rows * quads) return;
@@ -78,8 +79,8 @@ cudaError_t launch_depthwise(const DepthwiseArgs& a, cudaStream_t stream) {
   if (a.rows <= 0) return cudaSuccess;
   if (a.channels % 4 || a.channels > 1024) return cudaErrorInvalidValue;
   const long long items = (long long)a.rows * (a.channels / 4);
-  depthwise_kernel<<<(unsigned)((items + kDwThreads - 1) / kDwThreads), kDwThreads, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_overlapped(depthwise_kernel, (unsigned)((items + kDwThreads - 1) / kDwThreads), kDwThreads, 0,
+                           stream, a);
 }
 
 }  // namespace fav

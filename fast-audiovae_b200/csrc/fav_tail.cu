@@ -165,6 +165,7 @@ __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dependency_sync();  // plan constants above; the stage input and histories below
 
   if (tid == 0 && blockIdx.x < num_tiles) {
     mbar_arrive_expect_tx(&xfull[0], kBoxBytes);
@@ -370,8 +371,7 @@ cudaError_t launch_tail(const TailArgs& a, cudaStream_t stream) {
   if (a.rows % kTailRows || a.rows_per_stream % kTailRows) return cudaErrorInvalidValue;
   const int tiles = a.rows / kTailRows;
   const int grid = tiles < g_tail_sms ? tiles : g_tail_sms;
-  tail_kernel<<<grid, kTailThreads, TailSmem::kAlloc, stream>>>(a);
-  return cudaGetLastError();
+  return launch_overlapped(tail_kernel, grid, kTailThreads, TailSmem::kAlloc, stream, a);
 }
 
 }  // namespace fav
