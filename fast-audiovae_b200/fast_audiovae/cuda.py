@@ -161,7 +161,7 @@ class DeviceBackend:
             self.status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         self.cache = {}
         self.out_buffers = LentBuffers(lambda numel: torch.empty(numel, dtype=torch.float32, pin_memory=True))
-        # Streaming steps replay a CUDA graph of the step's 26 launches per
+        # Streaming steps replay a CUDA graph of the step's kernel launches per
         # (streams, frames, buffers): the first step of a shape runs eagerly,
         # the second captures, later ones replay (one launch call per step).
         self.graphs_enabled = graphs

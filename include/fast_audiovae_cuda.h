@@ -177,9 +177,12 @@ FAV_API int32_t fav_decode_batch(const fav_plan *plan, const float *latents, int
 
 /* fav_step with per-layer timing (no reference counterpart; the reference
  * profiles ORT operators instead, benchmarks/profile_candidate.py:37-60):
- * CUDA events recorded on cuda_stream around each of the 26 kernel launches;
+ * CUDA events recorded on cuda_stream around each of the 26 layers;
  * layer_ms[26] receives their durations (0 = stem, 1+4i = stage i transposed
- * conv, 2+4i+j = stage i residual j, 25 = final conv). Synchronises. */
+ * conv, 2+4i+j = stage i residual j, 25 = final conv). A stage 0-1 residual
+ * unit's interval covers its depthwise pre-pass and its GEMM; stage 5's fused
+ * kernel (three residual units and the final conv) counts as layer 22, and
+ * layers 23-25 then read zero. Synchronises. */
 FAV_API int32_t fav_step_profile(const fav_plan *plan, float *state_pool, int32_t num_slots,
                                  const int32_t *slot_codes, int32_t n_streams, int32_t frames,
                                  const float *latents, float *audio, void *workspace, size_t workspace_bytes,
