@@ -97,6 +97,14 @@ int32_t encode_operand_map(CUtensorMap* map, const uint16_t* a, int rows, int ch
   return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_128B, "operand");
 }
 
+// Preformed int8 transposed-conv tap [rows][channels] s8: boxes of 128
+// channels x 128 rows in the 128-byte swizzle.
+int32_t encode_s8_map(CUtensorMap* map, const uint8_t* q, int rows, int channels) {
+  const cuuint64_t dims[2] = {(cuuint64_t)channels, (cuuint64_t)rows};
+  const cuuint32_t box[2] = {(cuuint32_t)fav::kKBlockI8, (cuuint32_t)fav::kTileM};
+  return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_128B, "s8 taps");
+}
+
 // Stage-5 input y [rows][32] fp32 for the fused tail: boxes of 32 channels x
 // (128 + 84) rows in the 128-byte swizzle.
 int32_t encode_tail_map(CUtensorMap* map, const float* x, int rows) {
@@ -521,7 +529,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     t.out_x = X[0];
     t.out_s = S[0];
     if (st.int8) {
-      // W8A8: producers quantise the fp32 activation (row m0 - 1 .. m0 + 127 boxes of 64 channels).
+      // W8A8: s8 taps of the fp32 activation, per-row scales from the row maxima, one accumulator per tap.
       t.mode = fav::kModeI8;
       t.num_kblocks = st.c_in / fav::kKBlockI8;
       t.rowmax_in = rowmax;
@@ -529,7 +537,21 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       t.w_scale = st.tsw;
       t.w_scale2 = st.tsw + t.n_total;
       t.hist_max_slot = fav::kNumHistories + i;
+    }
+    if (st.int8 && t.n_total / t.n_tile < 4) {
+      // Few N tiles (stages 3-4): the producers quantise staged fp32 rows.
       if ((es = encode_input_map(&t.tmap, act, t.rows, st.c_in, fav::kTileM + 1)) != FAV_OK) return es;
+    } else if (st.int8) {
+      // Many N tiles (stages 0-2) would each quantise the same rows: quantise
+      // each input row once into both s8 taps (in S[1], unused while the conv
+      // runs: 2 * rows * C bytes fit the region); the engine TMA-loads them.
+      uint8_t* q0 = reinterpret_cast<uint8_t*>(S[1]);
+      uint8_t* q1 = q0 + (size_t)t.rows * st.c_in;
+      const fav::QuantizeArgs qa{act, rowmax, act_parts, q0, q1, t.rows, n, st.c_in, state, t.hist, t.hist_max_slot};
+      if ((e = fav::launch_quantize(qa, stream)) != cudaSuccess) return cuda_fail(e, "quantize launch");
+      t.kind = fav::kTconvPre;
+      if ((es = encode_s8_map(&t.tmap, q0, t.rows, st.c_in)) != FAV_OK) return es;
+      if ((es = encode_s8_map(&t.tmap2, q1, t.rows, st.c_in)) != FAV_OK) return es;
     } else {
       if ((es = encode_plane_map(&t.tmap, planes, t.rows, st.c_in)) != FAV_OK) return es;
       if ((es = encode_plane_map(&t.tmap2, planes_prev, t.rows, st.c_in)) != FAV_OK) return es;

@@ -32,7 +32,9 @@ constexpr int kSlotStride = kRingFloats + 2 * kHeadInts;  // floats per slot
 
 // kResidualPre: a residual unit whose A operand (depthwise + Snake_post, f16
 // [rows][C]) was written by launch_depthwise; the engine TMA-loads it.
-enum LayerKind : int { kStem = 0, kTconv = 1, kResidual = 2, kTestGemm = 3, kResidualPre = 4 };
+// kTconvPre: an int8 transposed conv whose two s8 taps were written by
+// launch_quantize; the engine TMA-loads them.
+enum LayerKind : int { kStem = 0, kTconv = 1, kResidual = 2, kTestGemm = 3, kResidualPre = 4, kTconvPre = 5 };
 
 // Operand precision of a GEMM layer.
 enum GemmMode : int {
@@ -212,6 +214,24 @@ struct DepthwiseArgs {
   HistRef hist;
 };
 cudaError_t launch_depthwise(const DepthwiseArgs& a, cudaStream_t stream);
+
+// Quantise-once pre-pass of an int8 transposed conv (fav_prepass.cu): the
+// conv's two s8 taps, each row quantised with its time step's scale (the
+// reference's per-time-step activation scale over all input channels).
+struct QuantizeArgs {
+  const float* act;      // [rows][channels] fp32 activation written by the previous epilogue
+  const float* rowmax;   // [rows][parts] partial maxima of |act| (one per N tile of that epilogue)
+  int parts;
+  uint8_t* q0;           // [rows][channels] s8: row t
+  uint8_t* q1;           // [rows][channels] s8: row t - 1 (a stream's first row: its history row)
+  int rows;
+  int rows_per_stream;
+  int channels;          // multiple of 4
+  StateRef state;
+  HistRef hist;          // the conv's one-row fp32 history
+  int hist_max_slot;     // head-table entry holding the history row's max |x|
+};
+cudaError_t launch_quantize(const QuantizeArgs& a, cudaStream_t stream);
 cudaError_t prepare_tail();
 
 // Kernel launchers (fav_kernels.cu). Return cudaError_t of the launch.

@@ -58,7 +58,7 @@ constexpr bool kSplitOperands = MODE == kModeSplit || MODE == kModeSplit4;
 template <int NT, int MODE, int KIND>
 struct GemmCfg {
   static constexpr bool kI8 = MODE == kModeI8;
-  static constexpr bool kI8Tconv = kI8 && KIND == kTconv;
+  static constexpr bool kI8Tconv = kI8 && (KIND == kTconv || KIND == kTconvPre);
   // Operand tiles per stage: split-bf16 hi and lo, or the int8 transposed
   // conv's two taps (separately scaled, separate accumulators).
   static constexpr int kTerms = (kSplitOperands<MODE> || kI8Tconv) ? 2 : 1;
@@ -67,7 +67,8 @@ struct GemmCfg {
   static constexpr int kAStage = kTerms * kATile;
   static constexpr int kBStage = kTerms * kBTile;
   static constexpr int kStage = kAStage + kBStage;
-  static constexpr int kRaw = KIND == kResidual ? kResBoxBytes + kResCoefBytes : kI8Tconv ? (kTileM + 1) * 64 * 4 : 0;
+  static constexpr int kRaw =
+      KIND == kResidual ? kResBoxBytes + kResCoefBytes : (kI8 && KIND == kTconv) ? (kTileM + 1) * 64 * 4 : 0;
   // Per-tile tables: streams and rows, plus the int8 transposed conv's row scales.
   static constexpr int kTableI = kTableInts + (kI8Tconv ? 2 * kTileM : 0);
   static constexpr int kTable = KIND == kTestGemm ? 0 : 2 * ((kTableI * 4 + 15) / 16) * 16;  // two tiles
@@ -624,11 +625,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   constexpr bool kI8 = Cfg::kI8;
   constexpr bool kI8Tconv = Cfg::kI8Tconv;
   constexpr bool kI8Res = kI8 && KIND == kResidual;
-  constexpr bool kStaged = KIND == kResidual || kI8Tconv;  // producers read TMA-staged input boxes
+  constexpr bool kStaged = KIND == kResidual || (kI8 && KIND == kTconv);  // producers read TMA-staged boxes
+  constexpr bool kConv = KIND == kTconv || KIND == kTconvPre;
   constexpr bool kSkipAdd = KIND == kResidual || KIND == kResidualPre;  // y = x + (D + b)
   // The A operand is TMA-loaded whole (no producer work): a bf16 transposed
   // conv's planes, or a residual unit's preformed depthwise output.
-  constexpr bool kTmaA = (KIND == kTconv && !kI8) || KIND == kResidualPre;
+  constexpr bool kTmaA = (KIND == kTconv && !kI8) || KIND == kResidualPre || KIND == kTconvPre;
   constexpr int kLpr = NT == 32 ? 8 : 16;  // residual lanes per row (C = 32 uses eight)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -869,7 +871,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       float* cf = epi_coef + cbuf * kEpiCoefVectors * NT;
       for (int j = etid; restage && j < NT; j += kEpilogueWarps * 32) {
         const int n = n0 + j;
-        const int ch = KIND == kTconv ? n % a.c_out : n;
+        const int ch = kConv ? n % a.c_out : n;
         cf[j] = a.bias ? __ldg(a.bias + ch) : 0.f;
         if (OUT != kOutNone) {
           cf[NT + j] = __ldg(a.next_alpha + ch);
@@ -1012,7 +1014,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         {
           // fp32 outputs: row g, column n at g * pitch + n (a transposed conv's
           // output row g * stride + p holds GEMM columns p * c_out ..).
-          const size_t pitch = KIND == kTconv ? (size_t)a.stride * a.c_out : (size_t)a.c_out;
+          const size_t pitch = kConv ? (size_t)a.stride * a.c_out : (size_t)a.c_out;
           const size_t off0 = (size_t)row0 * pitch + n;
           if (epi & kEpiX) store_chunk(stage, lane, v, a.out_x + off0, pitch, a.rows - row0);
           if constexpr (OUT != kOutNone) {
@@ -1122,6 +1124,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           tma_load_2d(a_base + s * Cfg::kAStage, &a.tmap, kb * kKBlock, m0, &a_full[s]);
         }
       }
+    } else if (lane == 0 && KIND == kTconvPre) {
+      // ---- preformed int8 transposed-conv taps: one 128-channel x 128-row s8
+      // box per tap per K block
+      uint32_t g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int m0 = tile_m(t) * kTileM;
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader))) break;
+          mbar_arrive_expect_tx(&a_full[s], Cfg::kAStage);
+          tma_load_2d(a_base + s * Cfg::kAStage, &a.tmap, kb * kKBlockI8, m0, &a_full[s]);
+          tma_load_2d(a_base + s * Cfg::kAStage + Cfg::kATile, &a.tmap2, kb * kKBlockI8, m0, &a_full[s]);
+        }
+      }
     } else if (lane == 0 && KIND == kTconv && !kI8) {
       // ---- transposed-conv A operand: tap 0 from the planes, tap 1 from the
       // shifted planes, hi and lo tiles in one 3-D box
@@ -1179,7 +1197,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       uint32_t ti = 0;
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++ti) {
         const int m0 = tile_m(t) * kTileM;
-        if (!mbar_wait(&table_empty[ti & 1], ((ti >> 1) & 1) ^ 1, a.status, kDevTimeoutProducer)) break;
+        // (A TMA-fed int8 conv has no producers to hand the table to.)
+        if (!kTmaA && !mbar_wait(&table_empty[ti & 1], ((ti >> 1) & 1) ^ 1, a.status, kDevTimeoutProducer)) break;
         int* tbase = table + (ti & 1) * Cfg::kTableI;
         const StreamTable tab = table_at(tbase, m0, a.rows_per_stream);
         fill_table(a, m0, tab, lane);
@@ -1218,7 +1237,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           __syncwarp();
           if (lane == 0) mbar_arrive(&scale_full[ti & 1]);
         }
-        if (lane == 0) mbar_arrive(&table_full[ti & 1]);
+        if (lane == 0 && !kTmaA) mbar_arrive(&table_full[ti & 1]);
         // After publishing the table: nothing in this kernel reads these rows.
         if (KIND == kResidual && (a.epi & kEpiPlanes)) first_rows_prev_planes(a, m0, tile_n(t) * NT, NT, tab, lane);
       }
@@ -1301,7 +1320,7 @@ static cudaError_t set_smem() {
   X(256, kModeSplit4, kStem, kOutPlanes) X(64, kModeSplit4, kStem, kOutPlanes)                            \
   X(256, kModeSplit4, kStem, kOutAct)                                                                      \
   X(256, kModeSplit, kTconv, kOutS) X(128, kModeSplit, kTconv, kOutS) X(64, kModeSplit, kTconv, kOutS)      \
-  X(128, kModeI8, kTconv, kOutS)                                                                           \
+  X(128, kModeI8, kTconv, kOutS) X(128, kModeI8, kTconvPre, kOutS)                                        \
   X(64, kModeSplit, kTconv, kOutNone)                                                                      \
   X(256, kModeF16, kResidual, kOutS) X(128, kModeF16, kResidual, kOutS) X(64, kModeF16, kResidual, kOutS)  \
   X(256, kModeF16, kResidualPre, kOutS) X(256, kModeF16, kResidualPre, kOutPlanes)                          \

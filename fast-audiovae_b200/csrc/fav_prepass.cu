@@ -1,3 +1,6 @@
+// Pre-passes that write a GEMM's A operand once to HBM for the engine to
+// TMA-load.
+//
 // Depthwise pre-pass of a residual unit (stages 0 and 1): the A operand of the
 // unit's 1x1 projection, Snake_post(depthwise_k7(s)) in f16, written once to
 // HBM so the GEMM engine TMA-loads it (LayerKind kResidualPre) instead of
@@ -73,7 +76,55 @@ __global__ void __launch_bounds__(kDwThreads, 4) depthwise_kernel(const __grid_c
   if (t == 0 && q == 0) hist_commit_head(a.state, a.hist, code, head, N);
 }
 
+// Quantise-once pre-pass of an int8 transposed conv (int8 plans): the recipe
+// quantises each time step of the conv's input with its own scale, max|x|/127
+// over all input channels (precision.cpp ip_prepare, restated in
+// oracle/int8_recipe.py). Each row is quantised once here into both taps:
+// tap 0 at its own row, tap 1 one row later in the same stream; a stream's
+// first tap-1 row is its history row (the previous step's last input row,
+// kept in fp32 with its max in a spare head-table entry), zero for a fresh
+// stream. The scale and rounding are the engine's producers' own, so the s8
+// operands are the same bit for bit; one thread per (row, channel quad).
+__global__ void __launch_bounds__(kDwThreads) quantize_kernel(const __grid_constant__ QuantizeArgs a) {
+  grid_dependency_sync();
+  const int C = a.channels, quads = C / 4;
+  const long long idx = (long long)blockIdx.x * kDwThreads + threadIdx.x;
+  if (idx >= (long long)a.rows * quads) return;
+  const int g = (int)(idx / quads), q = (int)(idx - (long long)g * quads);
+  const int N = a.rows_per_stream;
+  const int s = g / N, t = g - s * N;
+  float m = 0.f;
+  for (int p = 0; p < a.parts; ++p) m = fmaxf(m, __ldg(a.rowmax + (size_t)g * a.parts + p));
+  const uint32_t v = quant4(ldg4(a.act + (size_t)g * C + 4 * q), quant_scale(m));
+  *reinterpret_cast<uint32_t*>(a.q0 + (size_t)g * C + 4 * q) = v;
+  if (t + 1 < N) *reinterpret_cast<uint32_t*>(a.q1 + (size_t)(g + 1) * C + 4 * q) = v;
+  if (t == 0) {
+    float4 hv = make_float4(0.f, 0.f, 0.f, 0.f);
+    float hm = 0.f;
+    if (a.state.pool) {
+      const int code = a.state.slot_codes ? a.state.slot_codes[s] : ((s << 2) | a.state.uniform_code);
+      if (!(code & 2)) {
+        float* slot = slot_base(a.state, code);
+        const int* heads = head_table(slot, code & 1);
+        int row = heads[a.hist.index] + a.hist.rows - 1;  // window row of time -1
+        if (row >= 2 * a.hist.rows) row -= 2 * a.hist.rows;
+        hv = ldg4(slot + a.hist.ring + row * a.hist.width + 4 * q);
+        hm = __int_as_float(heads[a.hist_max_slot]);
+      }
+    }
+    *reinterpret_cast<uint32_t*>(a.q1 + (size_t)g * C + 4 * q) = quant4(hv, quant_scale(hm));
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_quantize(const QuantizeArgs& a, cudaStream_t stream) {
+  if (a.rows <= 0) return cudaSuccess;
+  if (a.channels % 4) return cudaErrorInvalidValue;
+  const long long items = (long long)a.rows * (a.channels / 4);
+  return launch_overlapped(quantize_kernel, (unsigned)((items + kDwThreads - 1) / kDwThreads), kDwThreads, 0,
+                           stream, a);
+}
 
 cudaError_t launch_depthwise(const DepthwiseArgs& a, cudaStream_t stream) {
   if (a.rows <= 0) return cudaSuccess;
