@@ -24,9 +24,11 @@ and ``decode_many`` batch-decodes several equal-length clips at once.
 """
 from __future__ import annotations
 
+import collections
 import ctypes as ct
 import threading
 import weakref
+from operator import attrgetter
 
 import numpy as np
 
@@ -35,6 +37,16 @@ from . import weights as W
 HOP = W.HOP_SAMPLES
 STATE_BYTES = W.STATE_BYTES_FP32
 _FRESH = 2
+
+# Per-stream fields read with ``map`` so a step over hundreds of streams loops in C.
+_DTYPE, _SHAPE = attrgetter("dtype"), attrgetter("shape")
+_DECODER, _LOCK, _CLOSED = attrgetter("_decoder"), attrgetter("_lock"), attrgetter("_closed")
+_SLOT, _FRESH_FLAG, _PARITY = attrgetter("_slot"), attrgetter("_fresh"), attrgetter("_parity")
+_LOCK_ACQUIRE, _LOCK_RELEASE = type(threading.Lock()).acquire, type(threading.Lock()).release
+
+
+def _drain(iterator):
+    collections.deque(iterator, maxlen=0)
 
 
 def _latents(value):
@@ -55,8 +67,8 @@ def _latents_step(chunks):
         return np.empty((0, 64, 0), dtype=np.float32)
     # One pass each over types, dtypes and shapes (a server step carries
     # hundreds of chunks); the per-chunk loop below only names the failure.
-    if (all(type(c) is np.ndarray for c in chunks) and {c.dtype for c in chunks} == {np.dtype(np.float32)}
-            and len(shapes := {c.shape for c in chunks}) == 1):
+    if (set(map(type, chunks)) == {np.ndarray} and set(map(_DTYPE, chunks)) == {np.dtype(np.float32)}
+            and len(shapes := set(map(_SHAPE, chunks))) == 1):
         (shape,) = shapes
         if len(shape) != 3 or shape[:2] != (1, 64):
             raise ValueError("Latents must be a float32 NumPy array with shape [1,64,L]")
@@ -302,7 +314,10 @@ class CUDADecoder:
     # ------------------------------------------------------------ internals
     def _step(self, streams, arrays, frames):
         """One device step for ``streams``; commits their histories only on success."""
-        codes = [(s._slot << 2) | (_FRESH if s._fresh else 0) | s._parity for s in streams]  # CUDAStream._code
+        n = len(streams)  # CUDAStream._code, over all streams at once
+        codes = ((np.fromiter(map(_SLOT, streams), np.int32, n) << 2)
+                 | np.fromiter(map(_FRESH_FLAG, streams), np.bool_, n).astype(np.int32) * _FRESH
+                 | np.fromiter(map(_PARITY, streams), np.int32, n))
         audio = self._backend.step(codes, arrays, frames)
         if (not isinstance(audio, np.ndarray) or audio.dtype != np.float32
                 or audio.shape != (len(streams), HOP * frames)):
@@ -379,24 +394,24 @@ class CUDADecoder:
         chunks = _latents_step(chunks)
         if not streams:
             return []
-        if len({id(s) for s in streams}) != len(streams):
+        if len(set(map(id, streams))) != len(streams):
             raise ValueError("A stream may appear only once per step")
         frames = chunks.shape[2]
-        if any(s._decoder is not self for s in streams):
+        if any(d is not self for d in set(map(_DECODER, streams))):
             raise ValueError("Stream belongs to another decoder")
-        ordered = sorted(streams, key=id)
-        for s in ordered:
-            s._lock.acquire()
+        # Stream locks in one global (address) order, so concurrent steps over
+        # overlapping streams cannot deadlock.
+        locks = list(map(_LOCK, sorted(streams, key=id)))
+        _drain(map(_LOCK_ACQUIRE, locks))
         try:
-            if any(s._closed for s in streams):
+            if any(map(_CLOSED, streams)):
                 next(s for s in streams if s._closed)._check_open()
             if not frames:
                 return [np.empty((1, 1, 0), dtype=np.float32) for _ in streams]
             with self._lock:
                 return self._step(streams, chunks, frames)
         finally:
-            for s in reversed(ordered):
-                s._lock.release()
+            _drain(map(_LOCK_RELEASE, reversed(locks)))
 
     def close(self):
         close = getattr(self._backend, "close", None)
