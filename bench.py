@@ -14,7 +14,8 @@ Reported (one JSON line, rank 0):
   value   aggregate audio-s/s, inputs resident in HBM, device time (CUDA events,
           max over ranks);
   e2e     the same metric through the public API (``CUDADecoder.decode_streams``
-          with host numpy chunks: validation, pinned H2D, step, D2H, finite
+          with host numpy chunks: validation, pinned H2D, step (audio written
+          device-to-host into mapped pinned memory by the final kernel), finite
           check), host wall time, max over ranks; plus p50/p99 chunk latency;
   roofline  the dominant kernel's algorithmic FLOPs or bytes per launch over its
           CUDA-event duration, against MEASURED_PEAKS.json;

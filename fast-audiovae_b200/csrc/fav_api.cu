@@ -732,6 +732,16 @@ const char* fav_status_string(int32_t s) {
   }
 }
 
+int32_t fav_host_device_pointer(void* host, void** device) {
+  if (!host || !device) return fail(FAV_INVALID_ARGUMENT, "host and device must be non-null");
+  const cudaError_t e = cudaHostGetDevicePointer(device, host, 0);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // not sticky: clear it for the caller's next call
+    return cuda_fail(e, "not mapped page-locked host memory");
+  }
+  return FAV_OK;
+}
+
 int32_t fav_device_supported(void) {
   int dev = 0, major = 0, minor = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;

@@ -64,7 +64,8 @@ struct TailSmem {
   static constexpr int kCoefFloats = kFinB + 4;
   static constexpr int kMisc = kCoefs + kCoefFloats * 4;         // ints: heads[4], code, pad
   static constexpr int kBars = ((kMisc + 8 * 4 + 7) / 8) * 8;    // xfull[2], mma_done, tmem slot
-  static constexpr int kBytes = kBars + 4 * 8;
+  static constexpr int kOut = ((kBars + 4 * 8 + 15) / 16) * 16;   // float[128]: one tile's audio
+  static constexpr int kBytes = kOut + kTailRows * 4;
   static constexpr int kAlloc = kBytes + 1024;
 };
 static_assert(TailSmem::kAlloc <= 227 * 1024, "tail kernel shared memory");
@@ -122,6 +123,7 @@ __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_cons
   uint8_t* wop = sm + TailSmem::kW;
   float* cf = reinterpret_cast<float*>(sm + TailSmem::kCoefs);
   int* misc = reinterpret_cast<int*>(sm + TailSmem::kMisc);
+  float* obuf = reinterpret_cast<float*>(sm + TailSmem::kOut);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + TailSmem::kBars);
   uint64_t* xfull = bars;         // [2]
   uint64_t* mma_done = bars + 2;  // [1]
@@ -336,11 +338,23 @@ __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_cons
         const float y = tanhf(acc + cf[TailSmem::kFinB]);
         // The reference checks the audio is finite (gpu.py:182-184).
         if (!(fabsf(y) <= 1.f)) record_error(a.status, kDevNonFinite);
-        a.audio[(size_t)s * a.audio_stride + a.audio_offset + t0 + o] = y;
+        obuf[o] = y;
       }
     }
     fence_async_smem();  // this tile's generic writes to the x buffer precede the next TMA into it
     __syncthreads();
+    if (tid < 32) {
+      // One warp stores the tile's 128 samples as 512 contiguous bytes, whole
+      // 128-byte lines whether the audio is device memory or mapped host
+      // memory. (obuf is rewritten only after the next tile's barriers.)
+      float* dst = a.audio + (size_t)s * a.audio_stride + a.audio_offset + t0;
+      if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        reinterpret_cast<float4*>(dst)[tid] = lds4(obuf + 4 * tid);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[tid + 32 * k] = obuf[tid + 32 * k];
+      }
+    }
   }
   // After a timeout: let x loads still in flight land before the CTA exits
   // (a wait on a load that has landed returns at once).

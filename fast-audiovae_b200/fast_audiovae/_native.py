@@ -28,6 +28,7 @@ SIGNATURES = {
     "fav_last_error": ([], ct.c_char_p),
     "fav_status_string": ([ct.c_int32], ct.c_char_p),
     "fav_device_supported": ([], ct.c_int32),
+    "fav_host_device_pointer": ([ct.c_void_p, ct.POINTER(ct.c_void_p)], ct.c_int32),
     "fav_plan_create": ([ct.POINTER(ct.POINTER(ct.c_float)), ct.c_int32, ct.c_int32, ct.POINTER(_P)], ct.c_int32),
     "fav_plan_destroy": ([_P], None),
     "fav_plan_bytes": ([_P], ct.c_size_t),

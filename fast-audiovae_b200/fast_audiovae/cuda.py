@@ -103,8 +103,9 @@ def _torch():
 class LentBuffers:
     """Host output buffers lent to returned audio arrays.
 
-    A step's audio is copied from the device straight into a pinned buffer,
-    and the caller receives NumPy arrays over that buffer; the buffer returns
+    A step's audio lands in a pinned buffer (written there by the kernels
+    through its mapped device address, or copied from the device), and the
+    caller receives NumPy arrays over that buffer; the buffer returns
     to the pool only when the last of those arrays is gone (a weakref
     finalizer), so no live result is ever overwritten. While more than
     ``limit`` results are held, ``acquire`` returns None and the caller copies
@@ -173,6 +174,7 @@ class DeviceBackend:
             self.status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         self.cache = {}
         self.out_buffers = LentBuffers(lambda numel: torch.empty(numel, dtype=torch.float32, pin_memory=True))
+        self.mapped = {}  # lent buffer host address -> its device address (None: not mapped)
         # Streaming steps replay a CUDA graph of the step's kernel launches per
         # (streams, frames, buffers): the first step of a shape runs eagerly,
         # the second captures, later ones replay (one launch call per step).
@@ -214,14 +216,18 @@ class DeviceBackend:
         dev.copy_(host, non_blocking=True)
         return dev
 
-    def _download(self, audio_dev):
-        """The step's audio as host fp32: in a lent pinned buffer (no host copy),
-        or, while too many earlier results are still held, an owned copy."""
-        shape = tuple(audio_dev.shape)
-        lent = self.out_buffers.acquire(audio_dev.numel())
-        host = (lent[:audio_dev.numel()].view(*shape) if lent is not None
-                else self._buffer("a_host", shape, self.torch.float32, pinned=True))
-        host.copy_(audio_dev, non_blocking=True)
+    def _mapped(self, buf):
+        """Device address of pinned buffer ``buf``, or None when it is not mapped."""
+        key = buf.data_ptr()
+        if key not in self.mapped:
+            dev = ct.c_void_p()
+            ok = self.lib.fav_host_device_pointer(ct.c_void_p(key), ct.byref(dev)) == 0
+            self.mapped[key] = dev.value if ok else None
+        return self.mapped[key]
+
+    def _finish(self, lent):
+        """Synchronise and read the kernels' status; on failure the lent buffer
+        goes back to the pool and the step raises."""
         self.status_host.copy_(self.status, non_blocking=True)
         self.torch.cuda.current_stream(self.device).synchronize()
         status = int(self.status_host.item())
@@ -231,6 +237,16 @@ class DeviceBackend:
             if status == NONFINITE_STATUS:
                 raise RuntimeError("CUDA model returned nonfinite audio")
             raise RuntimeError("CUDA decoder kernel reported status 0x%x" % status)
+
+    def _download(self, audio_dev):
+        """The step's audio as host fp32: in a lent pinned buffer (no host copy),
+        or, while too many earlier results are still held, an owned copy."""
+        shape = tuple(audio_dev.shape)
+        lent = self.out_buffers.acquire(audio_dev.numel())
+        host = (lent[:audio_dev.numel()].view(*shape) if lent is not None
+                else self._buffer("a_host", shape, self.torch.float32, pinned=True))
+        host.copy_(audio_dev, non_blocking=True)
+        self._finish(lent)
         if lent is None:
             return host.numpy().copy()
         return self.out_buffers.lend(lent, host.numpy())
@@ -242,7 +258,18 @@ class DeviceBackend:
         with torch.cuda.device(self.device):
             self.status.zero_()
             z = self._upload(arrays, frames)
-            audio = self._buffer("audio_dev", (n, HOP * frames), torch.float32)
+            # The kernels write the audio straight into a lent pinned buffer
+            # when it has a device address (no device-to-host copy after the
+            # step); otherwise into device memory, downloaded afterwards.
+            shape = (n, HOP * frames)
+            lent = self.out_buffers.acquire(n * HOP * frames)
+            target = self._mapped(lent) if lent is not None else None
+            if target is None:
+                if lent is not None:
+                    self.out_buffers.release(lent)
+                    lent = None
+                audio = self._buffer("audio_dev", shape, torch.float32)
+                target = audio.data_ptr()
             codes_host = self._buffer("codes_host", (n,), torch.int32, pinned=True)
             codes_host.numpy()[:] = codes
             codes_dev = self._buffer("codes_dev", (n,), torch.int32)
@@ -250,23 +277,31 @@ class DeviceBackend:
             ws_bytes = int(lib.fav_plan_workspace_bytes(self.plan.handle, n, frames))
             ws = self._buffer("workspace", (ws_bytes,), torch.uint8)
             args = (self.plan.handle, self._ptr(self.pool), self.max_streams, self._ptr(codes_dev), n, frames,
-                    self._ptr(z), self._ptr(audio), self._ptr(ws), ws_bytes, self._ptr(self.status))
-            key = (n, frames, z.data_ptr(), audio.data_ptr(), codes_dev.data_ptr(), ws.data_ptr())
-            graph = self.graphs.get(key) if self.graphs_enabled else None
-            if graph is None and self.graphs_enabled and key in self.graph_seen:
-                side = torch.cuda.Stream(self.device)
-                side.wait_stream(torch.cuda.current_stream(self.device))
-                graph = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(graph, stream=side):
-                    check(lib, lib.fav_step(*args, ct.c_void_p(side.cuda_stream)))
-                torch.cuda.current_stream(self.device).wait_stream(side)
-                self.graphs[key] = graph
-            if graph is not None:
-                graph.replay()
-            else:
-                self.graph_seen.add(key)
-                check(lib, lib.fav_step(*args, self._stream()))
-            return self._download(audio)
+                    self._ptr(z), ct.c_void_p(target), self._ptr(ws), ws_bytes, self._ptr(self.status))
+            key = (n, frames, z.data_ptr(), target, codes_dev.data_ptr(), ws.data_ptr())
+            try:
+                graph = self.graphs.get(key) if self.graphs_enabled else None
+                if graph is None and self.graphs_enabled and key in self.graph_seen:
+                    side = torch.cuda.Stream(self.device)
+                    side.wait_stream(torch.cuda.current_stream(self.device))
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph, stream=side):
+                        check(lib, lib.fav_step(*args, ct.c_void_p(side.cuda_stream)))
+                    torch.cuda.current_stream(self.device).wait_stream(side)
+                    self.graphs[key] = graph
+                if graph is not None:
+                    graph.replay()
+                else:
+                    self.graph_seen.add(key)
+                    check(lib, lib.fav_step(*args, self._stream()))
+            except BaseException:
+                if lent is not None:
+                    self.out_buffers.release(lent)
+                raise
+            if lent is None:
+                return self._download(audio)
+            self._finish(lent)
+            return self.out_buffers.lend(lent, lent[:n * HOP * frames].view(*shape).numpy())
 
     def decode_many(self, arrays, frames):
         from ._native import check

@@ -91,6 +91,13 @@ FAV_API const char *fav_last_error(void);
 FAV_API const char *fav_status_string(int32_t status);
 /* 1 when the current CUDA device is a B200-class sm_100 part. */
 FAV_API int32_t fav_device_supported(void);
+/* Device address (cudaHostGetDevicePointer) of page-locked, mapped host
+ * memory, so that a step's audio can be that host buffer: the kernels then
+ * write the samples to the host as they finish and no device-to-host copy
+ * follows. FAV_DEVICE_ERROR when `host` is not such memory. No counterpart in
+ * the reference, whose GPU route copies its output tensor to the host
+ * (gpu.py:177-185). */
+FAV_API int32_t fav_host_device_pointer(void *host, void **device);
 
 /* Immutable weight plan on the current device from FAV_NUM_COEFFICIENTS host
  * fp32 arrays, replacing MPSModel.from_onnx's coefficient load

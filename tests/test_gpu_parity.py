@@ -223,6 +223,39 @@ def test_many_streams_per_step_bitwise(batch_dec, stream_dec):
         assert np.array_equal(np.concatenate(got[i], -1), refs[i]), i
 
 
+def test_step_into_mapped_host_memory(lib, plan, stream_dec):
+    """fav_step writing its audio through a pinned buffer's mapped address
+    equals the same step into device memory, bit for bit; pageable memory has
+    no device address; the streaming facade takes the mapped path."""
+    S, F = 5, 2
+    pinned = torch.empty(S * 1920 * F, dtype=torch.float32, pin_memory=True)
+    dev_ptr = ct.c_void_p()
+    assert lib.fav_host_device_pointer(ct.c_void_p(pinned.data_ptr()), ct.byref(dev_ptr)) == 0
+    pageable = np.zeros(64, np.float32)
+    assert lib.fav_host_device_pointer(ct.c_void_p(pageable.ctypes.data), ct.byref(ct.c_void_p())) != 0
+    lat = torch.from_numpy(np.concatenate([W.seeded_latents(70 + s, F) for s in range(S)], 0)).cuda()
+    ws_bytes = lib.fav_plan_workspace_bytes(plan.handle, S, F)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    codes = torch.tensor([(s << 2) | 2 for s in range(S)], dtype=torch.int32, device="cuda")
+    stream = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
+    outs = []
+    for target in (None, dev_ptr):
+        pool = torch.zeros(lib.fav_state_pool_bytes(S) // 4, device="cuda")
+        dev_audio = torch.empty(S, 1920 * F, device="cuda")
+        audio = target if target is not None else ct.c_void_p(dev_audio.data_ptr())
+        _native.check(lib, lib.fav_step(plan.handle, ct.c_void_p(pool.data_ptr()), S, ct.c_void_p(codes.data_ptr()),
+                                        S, F, ct.c_void_p(lat.data_ptr()), audio, ct.c_void_p(ws.data_ptr()),
+                                        ws_bytes, ct.c_void_p(status.data_ptr()), stream))
+        torch.cuda.synchronize()
+        assert status.item() == 0
+        outs.append(dev_audio.cpu().numpy() if target is None else pinned.numpy().reshape(S, -1).copy())
+    assert np.array_equal(outs[0], outs[1])
+    with stream_dec.stream() as s:
+        s.decode_chunk(W.seeded_latents(3, 1))
+    assert any(v is not None for v in stream_dec._backend.mapped.values())
+
+
 def test_decode_many_equals_single_decodes(batch_dec):
     zs = [W.seeded_latents(40 + i, 9) for i in range(5)]
     many = batch_dec.decode_many(zs)
