@@ -406,6 +406,13 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
 constexpr int kWorkspaceRegions = 6;
 constexpr size_t kRegionFloatsPerFrame = 61440;
 
+// Diagnostic settings for one engine launch of a step (fav_debug_step_gated).
+struct StepDiag {
+  int layer;                // 0 = stem, 1 + 4i = stage i transposed conv, 2 + 4i + j = residual unit
+  uint32_t wait_limit;      // polls before a wait of that launch gives up
+  const uint32_t* gate;     // device flag its MMA issuer waits for first
+};
+
 // Launches the kernels of one decoder step. Layers are numbered 0 (stem),
 // 1 + 4i (stage i transposed conv), 2 + 4i + j (stage i residual j) and 25
 // (final conv); the schedule stops after ``last_layer`` and reports the buffer
@@ -413,10 +420,16 @@ constexpr size_t kRegionFloatsPerFrame = 61440;
 int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, int frames, const float* z,
                  int z_stride, int z_offset, float* audio, int audio_stride, int audio_offset, float* ws,
                  uint32_t* status, cudaStream_t stream, int last_layer = 25, float** last_out = nullptr,
-                 cudaEvent_t* events = nullptr, bool fuse_tail = true) {
+                 cudaEvent_t* events = nullptr, bool fuse_tail = true, const StepDiag* diag = nullptr) {
   // events (optional, 27): recorded before the stem and after each layer.
   auto mark = [&](int i) {
     if (events) cudaEventRecord(events[i], stream);
+  };
+  auto diagnose = [&](fav::LayerArgs& l, int index) {
+    if (diag && diag->layer == index) {
+      l.wait_limit = diag->wait_limit;
+      l.gate = diag->gate;
+    }
   };
   mark(0);
   const size_t region = (size_t)n_streams * frames * kRegionFloatsPerFrame;
@@ -493,6 +506,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       a.rowmax_parts = 1;
       e = fav::launch_stem_exact(a, stream);
     } else {
+      diagnose(a, 0);
       e = fav::launch_gemm_layer(a, stream);
     }
     act_parts = a.rowmax_parts;
@@ -556,6 +570,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       if ((es = encode_plane_map(&t.tmap, planes, t.rows, st.c_in)) != FAV_OK) return es;
       if ((es = encode_plane_map(&t.tmap2, planes_prev, t.rows, st.c_in)) != FAV_OK) return es;
     }
+    diagnose(t, layer + 1);
     if ((e = fav::launch_gemm_layer(t, stream)) != cudaSuccess) return cuda_fail(e, "transpose launch");
     n *= st.rate;
     if (last_out) *last_out = X[0];
@@ -649,6 +664,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       } else if ((es = encode_input_map(&u.tmap, S[in], u.rows, st.c_out, u.box_rows)) != FAV_OK) {
         return es;
       }
+      diagnose(u, layer + 1);
       if ((e = fav::launch_gemm_layer(u, stream)) != cudaSuccess) return cuda_fail(e, "residual launch");
       if (last_out) *last_out = X[out];
       mark(++layer + 1);
@@ -671,6 +687,18 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
   if ((e = fav::launch_final(f, stream)) != cudaSuccess) return cuda_fail(e, "final launch");
   mark(26);
   if (last_out) *last_out = audio;
+  return FAV_OK;
+}
+
+// The plan's weights live on the device that was current at fav_plan_create;
+// every step must run with that device current (its kernels would otherwise
+// read another GPU's memory).
+int32_t check_device(const fav_plan* plan) {
+  int dev = -1;
+  const cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev != plan->device)
+    return fail(FAV_INVALID_ARGUMENT, "the plan was created on device %d but device %d is current", plan->device, dev);
   return FAV_OK;
 }
 
@@ -813,6 +841,7 @@ int32_t fav_step(const fav_plan* plan, float* state_pool, int32_t num_slots, con
   if (!need) return fail(FAV_SIZE_OVERFLOW, "workspace size overflow");
   if (workspace_bytes < need)
     return fail(FAV_INVALID_ARGUMENT, "workspace too small: %zu < %zu bytes", workspace_bytes, need);
+  if (const int32_t d = check_device(plan)) return d;
   fav::StateRef st{state_pool, slot_codes, num_slots, 0};
   return run_step(plan, st, n_streams, frames, latents, frames, 0, audio, frames * fav::kHop, 0,
                   static_cast<float*>(workspace), status, static_cast<cudaStream_t>(cuda_stream));
@@ -830,10 +859,36 @@ int32_t fav_debug_step_unfused(const fav_plan* plan, float* state_pool, int32_t 
     return fail(FAV_INVALID_ARGUMENT, "state pool, slot codes and num_slots >= n_streams are required");
   if (workspace_bytes < fav_plan_workspace_bytes(plan, n_streams, frames))
     return fail(FAV_INVALID_ARGUMENT, "workspace too small");
+  if (const int32_t d = check_device(plan)) return d;
   fav::StateRef st{state_pool, slot_codes, num_slots, 0};
   return run_step(plan, st, n_streams, frames, latents, frames, 0, audio, frames * fav::kHop, 0,
                   static_cast<float*>(workspace), status, static_cast<cudaStream_t>(cuda_stream), 25, nullptr,
                   nullptr, false);
+}
+
+int32_t fav_debug_step_gated(const fav_plan* plan, float* state_pool, int32_t num_slots, const int32_t* slot_codes,
+                             int32_t n_streams, int32_t frames, const float* latents, float* audio, void* workspace,
+                             size_t workspace_bytes, uint32_t* status, int32_t layer, uint32_t wait_limit,
+                             const uint32_t* gate, void* cuda_stream) {
+  g_error[0] = 0;
+  if (!plan || n_streams <= 0 || frames <= 0 || !latents || !audio || !workspace || !status)
+    return fail(FAV_INVALID_ARGUMENT, "bad gated step arguments");
+  if (layer < 0 || layer > 21 || !gate || wait_limit == 0)
+    return fail(FAV_INVALID_ARGUMENT, "layer must be an engine layer (0..21), gate non-NULL and wait_limit > 0");
+  if (plan->precision != FAV_PRECISION_BF16)
+    return fail(FAV_UNSUPPORTED, "the gated diagnostic step supports FAV_PRECISION_BF16 plans only");
+  if ((int64_t)n_streams * frames * fav::kHop > INT32_MAX)
+    return fail(FAV_SIZE_OVERFLOW, "step too large: %d streams x %d frames", n_streams, frames);
+  if (!state_pool || !slot_codes || num_slots < n_streams)
+    return fail(FAV_INVALID_ARGUMENT, "state pool, slot codes and num_slots >= n_streams are required");
+  if (workspace_bytes < fav_plan_workspace_bytes(plan, n_streams, frames))
+    return fail(FAV_INVALID_ARGUMENT, "workspace too small");
+  if (const int32_t d = check_device(plan)) return d;
+  fav::StateRef st{state_pool, slot_codes, num_slots, 0};
+  const StepDiag diag{layer, wait_limit, gate};
+  return run_step(plan, st, n_streams, frames, latents, frames, 0, audio, frames * fav::kHop, 0,
+                  static_cast<float*>(workspace), status, static_cast<cudaStream_t>(cuda_stream), 25, nullptr,
+                  nullptr, true, &diag);
 }
 
 int32_t fav_step_static(const fav_plan* plan, float* state_pool, int32_t num_slots, const int32_t* slot_codes,
@@ -851,6 +906,7 @@ int32_t fav_step_static(const fav_plan* plan, float* state_pool, int32_t num_slo
     return fail(FAV_INVALID_ARGUMENT, "state pool, slot codes and num_slots >= n_streams are required");
   if (plan->precision != FAV_PRECISION_BF16)
     return fail(FAV_UNSUPPORTED, "the allocation-free step supports FAV_PRECISION_BF16 plans only");
+  if (const int32_t d = check_device(plan)) return d;
   float* ws = nullptr;
   const int32_t st = static_workspace(&ws);
   if (st != FAV_OK) return st;
@@ -893,6 +949,7 @@ int32_t fav_decode_batch(const fav_plan* plan, const float* latents, int32_t n_c
   const size_t need = fav_plan_batch_workspace_bytes(plan, n_clips, chunk_frames);
   if (!need || workspace_bytes < need)
     return fail(FAV_INVALID_ARGUMENT, "workspace too small: %zu < %zu bytes", workspace_bytes, need);
+  if (const int32_t d = check_device(plan)) return d;
   float* ws = static_cast<float*>(workspace);
   float* pool = ws + fav_plan_workspace_bytes(plan, n_clips, chunk_frames) / sizeof(float);
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
@@ -917,6 +974,7 @@ int32_t fav_step_profile(const fav_plan* plan, float* state_pool, int32_t num_sl
     return fail(FAV_INVALID_ARGUMENT, "bad profile step arguments");
   if (workspace_bytes < fav_plan_workspace_bytes(plan, n_streams, frames))
     return fail(FAV_INVALID_ARGUMENT, "workspace too small");
+  if (const int32_t d = check_device(plan)) return d;
   cudaEvent_t ev[27];
   for (int i = 0; i < 27; ++i) {
     cudaError_t e = cudaEventCreate(&ev[i]);
@@ -950,6 +1008,7 @@ int32_t fav_debug_step_layers(const fav_plan* plan, float* state_pool, int32_t n
     return fail(FAV_INVALID_ARGUMENT, "workspace too small");
   if (state_pool && (!slot_codes || num_slots < n_streams))
     return fail(FAV_INVALID_ARGUMENT, "slot codes and num_slots >= n_streams are required with a state pool");
+  if (const int32_t d = check_device(plan)) return d;
   fav::StateRef st{state_pool, state_pool ? slot_codes : nullptr, num_slots, 0};
   return run_step(plan, st, n_streams, frames, latents, frames, 0, nullptr, 0, 0, static_cast<float*>(workspace),
                   status, static_cast<cudaStream_t>(cuda_stream), last_layer, layer_out);

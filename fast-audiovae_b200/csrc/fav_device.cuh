@@ -19,6 +19,7 @@ enum DeviceError : uint32_t {
   kDevTimeoutEpilogue = 0x104,
   kDevBadLaunch = 0x105,
   kDevNonFinite = 0x106,  // the step produced a non-finite audio sample
+  kDevTimeoutGate = 0x107,  // a diagnostic launch's gate flag was never set
 };
 
 // A wait that has not completed after this many polls is a bug; the kernel
@@ -60,10 +61,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait for the phase with ``parity`` to complete. Returns false (and
-// records ``code``) after kWaitLimit polls.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t code) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+// records ``code``) after ``limit`` polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t code,
+                                          uint32_t limit = kWaitLimit) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+  }
+  record_error(status, code);
+  return false;
+}
+
+// Bounded wait for a device flag (global memory) to become nonzero. Returns
+// false (and records ``code``) after ``limit`` polls.
+__device__ __forceinline__ bool flag_wait(const uint32_t* flag, uint32_t* status, uint32_t code, uint32_t limit) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    uint32_t v;
+    asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v) return true;
+    __nanosleep(64);
   }
   record_error(status, code);
   return false;

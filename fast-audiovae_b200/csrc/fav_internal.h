@@ -136,6 +136,12 @@ struct LayerArgs {
   StateRef state;
   HistRef hist;
   uint32_t* status;
+  // Diagnostics (zero in every ordinary launch): polls after which a wait of
+  // this launch gives up (0 = kWaitLimit), and a device flag the MMA issuer
+  // waits for before its first MMA (nullptr = none). A flag that nothing sets
+  // makes every role's wait run out, which tests the timeout path.
+  uint32_t wait_limit;
+  const uint32_t* gate;
 };
 
 struct FinalArgs {

@@ -228,6 +228,16 @@ __device__ __forceinline__ int walk_row(uint32_t lo, uint32_t hi, int u) {
   return ((u < 4 ? lo : hi) >> (8 * (u & 3))) & 255;
 }
 
+// A loader's last fills of a ring of n full barriers: waits (with the full
+// kWaitLimit, whatever the launch's own limit) until the copies of the last
+// min(issued, n) fills have landed, so that no CTA exits, after a timeout
+// elsewhere, with an asynchronous copy still writing its shared memory. A fill
+// whose copies have landed (every fill on the success path) returns at once.
+__device__ __forceinline__ void drain_fills(uint64_t* full, uint32_t issued, uint32_t n, uint32_t* status,
+                                            uint32_t code) {
+  for (uint32_t i = issued > n ? issued - n : 0; i < issued; ++i) mbar_wait(&full[i % n], (i / n) & 1, status, code);
+}
+
 // ------------------------------------------------------------------ producers
 // Stem: depthwise causal conv k=7 (d=1) on latents [S][64][z_stride]; history =
 // last six raw latent frames [6][64]. Two channels per lane, one row per warp step.
@@ -651,12 +661,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   uint64_t* table_empty = bars + 3 * S + 10;  // [2]
   uint64_t* scale_full = bars + 3 * S + 12;   // [2] int8: a tile's row scales are written
   uint64_t* scale_empty = bars + 3 * S + 14;  // [2] int8: the epilogue has read them
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 16);
-  int* table = reinterpret_cast<int*>(bars + 3 * S + 17);
+  uint64_t* mma_drain = bars + 3 * S + 16;    // every MMA the issuer started has finished
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 17);
+  int* table = reinterpret_cast<int*>(bars + 3 * S + 18);
   float* scales = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 512 + Cfg::kTable);  // [2][2][128]
   uint32_t* rowmax = reinterpret_cast<uint32_t*>(scales + 4 * kTileM);                            // [128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t wl = a.wait_limit ? a.wait_limit : kWaitLimit;  // polls before a wait gives up
   const int num_kb = a.num_kblocks;
   const int num_m = (a.rows + kTileM - 1) / kTileM;
   const int num_n = a.n_total / NT;
@@ -684,6 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       mbar_init(&scale_full[b], kI8Res ? kProducerWarps : 1);
       mbar_init(&scale_empty[b], kEpilogueWarps);
     }
+    mbar_init(mma_drain, 1);
     fence_mbar_init();
   }
   if (kI8Res && threadIdx.x < kTileM) rowmax[threadIdx.x] = 0u;
@@ -738,7 +751,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       bool regular = false;
       if (KIND != kTestGemm) {
         ok = named_barrier_and(2, kProducerThreads,
-                               mbar_wait(&table_full[ti & 1], (ti >> 1) & 1, a.status, kDevTimeoutProducer));
+                               mbar_wait(&table_full[ti & 1], (ti >> 1) & 1, a.status, kDevTimeoutProducer, wl));
         if (!ok) break;
         if (KIND == kResidual && chain) {
           const int r0 = walk_lo & 255, rl = walk_row(walk_lo, walk_hi, kRpg - 1), e0 = tab.row_e[r0];
@@ -754,7 +767,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         for (int kb = 0; kb < res_boxes && ok; ++kb, ++g2) {
           const int rb = g2 & 1;
           ok = named_barrier_and(2, kProducerThreads,
-                                 mbar_wait(&raw_full[rb], (g2 >> 1) & 1, a.status, kDevTimeoutProducer));
+                                 mbar_wait(&raw_full[rb], (g2 >> 1) & 1, a.status, kDevTimeoutProducer, wl));
           if (!ok) break;
           produce_residual<MODE, kLpr>(a, m0, kb, nullptr, reinterpret_cast<const float*>(raw_base + rb * Cfg::kRaw),
                                        warp, lane, kb % num_n == tile_n(t), tab, partial ? iwalk_lo : walk_lo,
@@ -766,7 +779,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         // Row scales into this tile's buffer, once the epilogue has read the
         // buffer's previous tile.
         bool ready = true;
-        if (threadIdx.x == 0) ready = mbar_wait(&scale_empty[ti & 1], ((ti >> 1) & 1) ^ 1, a.status, kDevTimeoutProducer);
+        if (threadIdx.x == 0) ready = mbar_wait(&scale_empty[ti & 1], ((ti >> 1) & 1) ^ 1, a.status, kDevTimeoutProducer, wl);
         ok = named_barrier_and(2, kProducerThreads, ready);
         if (!ok) break;
         float* sx = scales + (ti & 1) * 2 * kTileM;
@@ -780,7 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
-          ok = named_barrier_and(2, kProducerThreads, mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer));
+          ok = named_barrier_and(2, kProducerThreads, mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer, wl));
           if (!ok) break;
           quantize_residual_i8(a, kb, a_base + s * Cfg::kAStage, sx, warp, lane);
           fence_async_smem();
@@ -792,13 +805,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         for (int kb = 0; kb < num_kb && ok; ++kb, ++g) {
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
-          ok = named_barrier_and(2, kProducerThreads, mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer));
+          ok = named_barrier_and(2, kProducerThreads, mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer, wl));
           if (!ok) break;
           uint8_t* a_stage = a_base + s * Cfg::kAStage;
           for (int h = 0; h < 2 && ok; ++h, ++g2) {
             const int rb = g2 & 1;
             ok = named_barrier_and(2, kProducerThreads,
-                                   mbar_wait(&raw_full[rb], (g2 >> 1) & 1, a.status, kDevTimeoutProducer));
+                                   mbar_wait(&raw_full[rb], (g2 >> 1) & 1, a.status, kDevTimeoutProducer, wl));
             if (!ok) break;
             produce_tconv_i8(a, kb, h, a_stage, reinterpret_cast<const float*>(raw_base + rb * Cfg::kRaw), sc,
                              sc + kTileM, warp, lane, tab);
@@ -817,8 +830,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           const int rb = g & 1;
           // All producer threads leave together on a timeout, so none is left
           // waiting at a named barrier inside a producer.
-          bool ready = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer);
-          if (kStaged && ready) ready = mbar_wait(&raw_full[rb], (g >> 1) & 1, a.status, kDevTimeoutProducer);
+          bool ready = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer, wl);
+          if (kStaged && ready) ready = mbar_wait(&raw_full[rb], (g >> 1) & 1, a.status, kDevTimeoutProducer, wl);
           ok = named_barrier_and(2, kProducerThreads, ready);
           if (!ok) break;
           uint8_t* a_stage = a_base + s * Cfg::kAStage;
@@ -932,12 +945,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         for (int j = 0; j < 4; ++j)
           hw[j] = hist_old ? __ldg(reinterpret_cast<const uint4*>(hist_old + n0) + j) : make_uint4(0u, 0u, 0u, 0u);
       }
-      if (!(ok = mbar_wait(&acc_full[buf], (i >> 1) & 1, a.status, kDevTimeoutEpilogue))) continue;
+      // Waits whose outcome steers warp-collective code (tcgen05.ld, __syncwarp)
+      // are made warp-uniform: a warp goes on only if every lane saw the phase.
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (i >> 1) & 1, a.status, kDevTimeoutEpilogue, wl))))
+        continue;
       tc_fence_after();
       // int8: this row's activation scales (current and previous tap).
       float sx = 1.f, sxp = 1.f;
       if constexpr (kI8 && KIND != kTestGemm) {
-        if (!(ok = mbar_wait(&scale_full[buf], (i >> 1) & 1, a.status, kDevTimeoutEpilogue))) continue;
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&scale_full[buf], (i >> 1) & 1, a.status, kDevTimeoutEpilogue, wl))))
+          continue;
         const float* sb = scales + buf * 2 * kTileM;
         sx = sb[q * 32 + lane];
         if (kI8Tconv) sxp = sb[kTileM + q * 32 + lane];
@@ -1103,11 +1120,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
-          if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader))) break;
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader, wl))) break;
           mbar_arrive_expect_tx(&b_full[s], Cfg::kBStage);
           bulk_g2s(b_base + s * Cfg::kBStage, src + (size_t)kb * Cfg::kBStage, Cfg::kBStage, &b_full[s]);
         }
       }
+      drain_fills(b_full, g, S, a.status, kDevTimeoutLoader);
     }
   } else if (warp == kRawWarp) {
     if (lane == 0 && KIND == kResidualPre) {
@@ -1119,11 +1137,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
-          if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader))) break;
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader, wl))) break;
           mbar_arrive_expect_tx(&a_full[s], Cfg::kAStage);
           tma_load_2d(a_base + s * Cfg::kAStage, &a.tmap, kb * kKBlock, m0, &a_full[s]);
         }
       }
+      drain_fills(a_full, g, S, a.status, kDevTimeoutLoader);
     } else if (lane == 0 && KIND == kTconvPre) {
       // ---- preformed int8 transposed-conv taps: one 128-channel x 128-row s8
       // box per tap per K block
@@ -1134,12 +1153,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
-          if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader))) break;
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader, wl))) break;
           mbar_arrive_expect_tx(&a_full[s], Cfg::kAStage);
           tma_load_2d(a_base + s * Cfg::kAStage, &a.tmap, kb * kKBlockI8, m0, &a_full[s]);
           tma_load_2d(a_base + s * Cfg::kAStage + Cfg::kATile, &a.tmap2, kb * kKBlockI8, m0, &a_full[s]);
         }
       }
+      drain_fills(a_full, g, S, a.status, kDevTimeoutLoader);
     } else if (lane == 0 && KIND == kTconv && !kI8) {
       // ---- transposed-conv A operand: tap 0 from the planes, tap 1 from the
       // shifted planes, hi and lo tiles in one 3-D box
@@ -1151,12 +1171,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
-          if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader))) break;
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader, wl))) break;
           const int tap = kb / kpt, cb = kb - tap * kpt;
           mbar_arrive_expect_tx(&a_full[s], Cfg::kAStage);
           tma_load_3d(a_base + s * Cfg::kAStage, tap ? &a.tmap2 : &a.tmap, cb * kKBlock, m0, 0, &a_full[s]);
         }
       }
+      drain_fills(a_full, g, S, a.status, kDevTimeoutLoader);
     } else if (lane == 0 && (KIND == kResidual || kI8Tconv)) {
       // ---- staged producer inputs. Residual: per 64-channel block the tile +
       // causal halo rows of s and the block's coefficients. int8 transposed
@@ -1171,7 +1192,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         const int m0 = tile_m(t) * kTileM;
         for (int kb = 0; kb < boxes; ++kb, ++g) {
           const int rb = g & 1;
-          if (!(ok = mbar_wait(&raw_empty[rb], ((g >> 1) & 1) ^ 1, a.status, kDevTimeoutLoader))) break;
+          if (!(ok = mbar_wait(&raw_empty[rb], ((g >> 1) & 1) ^ 1, a.status, kDevTimeoutLoader, wl))) break;
           uint8_t* dst = raw_base + rb * Cfg::kRaw;
           mbar_arrive_expect_tx(&raw_full[rb], bytes);
           tma_load_2d(dst, &a.tmap, kb * kKBlock, m0 - halo, &raw_full[rb]);
@@ -1179,6 +1200,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
             bulk_g2s(dst + kResBoxBytes, a.coef + (size_t)kb * kCoefResidual * 64, kResCoefBytes, &raw_full[rb]);
         }
       }
+      drain_fills(raw_full, g, 2, a.status, kDevTimeoutLoader);
     }
   } else if (warp == kSchedWarp) {
     // ---- scheduler: per-tile stream/row tables (and the int8 transposed
@@ -1198,7 +1220,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++ti) {
         const int m0 = tile_m(t) * kTileM;
         // (A TMA-fed int8 conv has no producers to hand the table to.)
-        if (!kTmaA && !mbar_wait(&table_empty[ti & 1], ((ti >> 1) & 1) ^ 1, a.status, kDevTimeoutProducer)) break;
+        if (!kTmaA && !__all_sync(0xffffffffu, mbar_wait(&table_empty[ti & 1], ((ti >> 1) & 1) ^ 1, a.status,
+                                                         kDevTimeoutProducer, wl)))
+          break;
         int* tbase = table + (ti & 1) * Cfg::kTableI;
         const StreamTable tab = table_at(tbase, m0, a.rows_per_stream);
         fill_table(a, m0, tab, lane);
@@ -1231,7 +1255,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
             sc[kTileM + r] = quant_scale(prev);
           }
           __syncwarp();
-          if (!mbar_wait(&scale_empty[ti & 1], ((ti >> 1) & 1) ^ 1, a.status, kDevTimeoutProducer)) break;
+          if (!__all_sync(0xffffffffu, mbar_wait(&scale_empty[ti & 1], ((ti >> 1) & 1) ^ 1, a.status,
+                                                 kDevTimeoutProducer, wl)))
+            break;
           float* sb = scales + (ti & 1) * 2 * kTileM;
           for (int r = lane; r < 2 * kTileM; r += 32) sb[r] = sc[r];
           __syncwarp();
@@ -1246,17 +1272,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
     // ---- MMA issuer
     if (lane == 0) {
       uint32_t g = 0, i = 0;
-      bool ok = true;
+      bool ok = a.gate == nullptr || flag_wait(a.gate, a.status, kDevTimeoutGate, wl);
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++i) {
         const int buf = i & 1;
-        if (!(ok = mbar_wait(&acc_empty[buf], ((i >> 1) & 1) ^ 1, a.status, kDevTimeoutMma))) break;
+        if (!(ok = mbar_wait(&acc_empty[buf], ((i >> 1) & 1) ^ 1, a.status, kDevTimeoutMma, wl))) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(buf * Cfg::kAccCols);
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
-          ok = mbar_wait(&a_full[s], ph, a.status, kDevTimeoutMma) &&
-               mbar_wait(&b_full[s], ph, a.status, kDevTimeoutMma);
+          ok = mbar_wait(&a_full[s], ph, a.status, kDevTimeoutMma, wl) &&
+               mbar_wait(&b_full[s], ph, a.status, kDevTimeoutMma, wl);
           if (!ok) break;
           tc_fence_after();
           const uint32_t a0 = smem_u32(a_base + s * Cfg::kAStage);
@@ -1285,6 +1311,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         }
         if (ok) mma_commit(&acc_full[buf]);
       }
+      // Every MMA this thread issued has finished before TMEM is freed (after a
+      // timeout, MMAs committed to a stage barrier nobody waits for may still run).
+      mma_commit(mma_drain);
+      mbar_wait(mma_drain, 0, a.status, kDevTimeoutMma);
     }
   }
 done:

@@ -47,6 +47,8 @@ SIGNATURES = {
                           ct.POINTER(ct.c_float), _P], ct.c_int32),
     "fav_debug_step_layers": ([_P, _P, ct.c_int32, _P, ct.c_int32, ct.c_int32, _P, _P, ct.c_size_t, _P,
                                ct.c_int32, ct.POINTER(ct.c_void_p), _P], ct.c_int32),
+    "fav_debug_step_gated": ([_P, _P, ct.c_int32, _P, ct.c_int32, ct.c_int32, _P, _P, _P, ct.c_size_t, _P,
+                              ct.c_int32, ct.c_uint32, _P, _P], ct.c_int32),
     "fav_test_gemm": ([_P, ct.c_int32, ct.c_int32, _P, ct.c_int32, ct.c_int32, _P, _P], ct.c_int32),
     "fav_test_sine": ([_P, ct.c_int32, _P, _P], ct.c_int32),
 }

@@ -14,6 +14,9 @@
  * Conventions
  *   - Every function returns an fav_status (0 = FAV_OK) unless noted.
  *   - Device buffers are raw CUDA device pointers owned by the caller.
+ *   - A plan belongs to the device that was current when it was created; every
+ *     call that takes a plan must run with that device current
+ *     (FAV_INVALID_ARGUMENT otherwise).
  *   - Work is enqueued on the caller's cudaStream_t (passed as void*); calls
  *     return without synchronising. Kernel-side failures (a bounded wait that
  *     expired) are reported through the caller's device status word.
@@ -159,7 +162,9 @@ FAV_API int32_t fav_step(const fav_plan *plan, float *state_pool, int32_t num_sl
  * The step's scratch is a library-owned, file-scope device array sized for
  * n_streams * frames <= FAV_STATIC_MAX_FRAMES (22.5 MiB, held on every GPU
  * that loads the library until the process exits); larger calls are rejected
- * with FAV_SIZE_OVERFLOW. The first call on a device looks up that array's
+ * with FAV_SIZE_OVERFLOW. Only FAV_PRECISION_BF16 plans are accepted: an int8
+ * plan's residual units need a further 78 MB of scratch, which the static
+ * array does not hold (FAV_UNSUPPORTED). The first call on a device looks up that array's
  * device address (cudaGetSymbolAddress) with the device current; make that
  * first call before any stream capture. Every call shares the one array and
  * it keeps the last call's contents (nothing in it needs to start at zero:
@@ -213,6 +218,23 @@ FAV_API int32_t fav_debug_step_unfused(const fav_plan *plan, float *state_pool, 
                                        const int32_t *slot_codes, int32_t n_streams, int32_t frames,
                                        const float *latents, float *audio, void *workspace, size_t workspace_bytes,
                                        uint32_t *status, void *cuda_stream);
+
+/* Diagnostic (no reference counterpart; the reference's transactional contract
+ * is gpu.py:216-225): fav_step in which the GEMM-engine launch of `layer`
+ * (0 = stem, 1+4i = stage i transposed conv, 2+4i+j = stage i residual unit j;
+ * at most 21) gives up every mbarrier wait after `wait_limit` polls and whose
+ * MMA issuer first waits for the device flag `gate` to become nonzero. With a
+ * gate that nothing sets, every role of that launch runs out of its waits: the
+ * kernel drains the copies and MMAs it started, records a timeout code
+ * (0x101-0x104, 0x107) in `status` (required here) and returns; the later
+ * layers run on whatever the workspace holds. As with any failed step, the
+ * history windows the slot codes name stay committed. FAV_PRECISION_BF16 plans
+ * only. Same other arguments as fav_step. */
+FAV_API int32_t fav_debug_step_gated(const fav_plan *plan, float *state_pool, int32_t num_slots,
+                                     const int32_t *slot_codes, int32_t n_streams, int32_t frames,
+                                     const float *latents, float *audio, void *workspace, size_t workspace_bytes,
+                                     uint32_t *status, int32_t layer, uint32_t wait_limit, const uint32_t *gate,
+                                     void *cuda_stream);
 
 /* Engine self-test (diagnostic, no reference counterpart): C[M][N] = A[M][K] * B[N][K]^T
  * through the tcgen05 GEMM engine. a, c device fp32; b host fp32.

@@ -11,7 +11,9 @@
   C sources compiled by ``oracle/Makefile`` into ``oracle/_ref``.
 
 The reference tree exists only in the build container; callers skip when
-``REFERENCE_ROOT`` is missing.
+``REFERENCE_ROOT`` is missing. ``REFERENCE_ROOT`` is the one place that says
+where it is mounted (``$FAST_AUDIOVAE_REFERENCE`` overrides it); the golden
+generator and the build read it from here.
 """
 from __future__ import annotations
 

@@ -1,7 +1,7 @@
 """Generate the golden vectors that pin the oracle to the reference.
 
 Run in a checkout where the reference tree is present (it is read from
-``$FAST_AUDIOVAE_REFERENCE``, default ``/root/reference``) after
+``oracle.reference.REFERENCE_ROOT``) after
 ``make -C oracle ref``:
 
     python tests/golden/make_golden.py

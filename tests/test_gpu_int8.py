@@ -169,3 +169,29 @@ def test_int8_many_streams_equal_single_streams(int8_stream):
             alone = np.concatenate([one.decode_chunk(z[..., t:t + 2]) for t in range(0, 4, 2)], axis=-1)
         joined = np.concatenate([many[0][i], many[1][i]], axis=-1)
         assert np.array_equal(joined.view(np.uint32), alone.view(np.uint32)), i
+
+
+def test_int8_serving_shape_matches_recipe(lib, weights0):
+    """cfg5's per-GPU shard on the int8 plan: 512 streams x 1-frame chunks
+    (seed = stream id), three carried steps in one launch per layer per step.
+    Eight of the streams (first and last slot among them) meet the 35 dB gate
+    against the recipe oracle, and each equals its own batch decode bit for bit."""
+    from fast_audiovae.cuda import CUDADecoder
+    n, steps = 512, 3
+    dec = CUDADecoder(weights0, {}, "streaming", max_streams=n, precision=INT8)
+    zs = [W.seeded_latents(s, steps) for s in range(n)]
+    streams = [dec.stream() for _ in range(n)]
+    got = [[] for _ in range(n)]
+    for t in range(steps):
+        for i, audio in enumerate(dec.decode_streams(streams, [z[..., t:t + 1] for z in zs])):
+            got[i].append(audio)
+    for s in streams:
+        s.close()
+    dec.close()
+    batch = CUDADecoder(weights0, {}, "batch", precision=INT8)
+    recipe = Int8RecipeDecoder(weights0)
+    for s in (0, 1, 63, 64, 255, 256, 510, 511):
+        joined = np.concatenate(got[s], axis=-1)
+        assert np.array_equal(joined.view(np.uint32), batch.decode(zs[s]).view(np.uint32)), s
+        d = discrepancy(recipe.decode_numpy(zs[s]), joined)
+        assert d["snr_db"] >= SNR_VS_RECIPE_DB, (s, d)

@@ -314,16 +314,61 @@ def test_repeat_is_deterministic(batch_dec):
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
-def test_long_clip_chunking_is_bitwise(lib, weights0):
-    """A cfg4-length clip (750 frames): chunk sizes 128 and 50 give identical bits; SNR vs oracle on it."""
+def test_long_clip_chunking_is_bitwise(lib, weights0, oracle0):
+    """cfg4's clip length (750 frames, 30 s): chunk sizes 128 and 50 give
+    identical bits, and the whole clip meets the fp32 gates against the oracle."""
     from fast_audiovae.cuda import CUDADecoder
     z = W.seeded_latents(63, 750)
     a = CUDADecoder(weights0, {}, "batch", batch_chunk_frames=128).decode(z)
     b = CUDADecoder(weights0, {}, "batch", batch_chunk_frames=50).decode(z)
     assert np.array_equal(a, b)
-    ref = Decoder(weights0).decode_numpy(z[..., :100])
-    d = discrepancy(ref, a[..., :100 * 1920])
+    d = discrepancy(oracle0.decode_numpy(z), a)
     assert d["max_abs"] <= MAX_ABS and d["snr_db"] >= SNR_DB, d
+
+
+def test_benchmarked_step_matches_oracle(lib, plan, oracle0):
+    """The benchmark's own step: 512 streams x 1-frame chunks (seed = stream id)
+    through fav_step, three carried steps; eight of the streams (first and
+    last slot among them) against the oracle's decode of the same three frames."""
+    S, steps = 512, 3
+    lat = np.stack([W.seeded_latents(s, steps)[0] for s in range(S)])  # [S, 64, steps]
+    pool = torch.zeros(lib.fav_state_pool_bytes(S) // 4, device="cuda")
+    ws_bytes = lib.fav_plan_workspace_bytes(plan.handle, S, 1)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    audio = torch.empty(steps, S, 1920, device="cuda")
+    for t in range(steps):
+        codes = torch.tensor([(s << 2) | (2 if t == 0 else 0) | (t & 1) for s in range(S)], dtype=torch.int32,
+                             device="cuda")
+        z = torch.from_numpy(np.ascontiguousarray(lat[:, :, t:t + 1])).cuda()
+        _native.check(lib, lib.fav_step(plan.handle, ptr(pool), S, ptr(codes), S, 1, ptr(z), ptr(audio[t]), ptr(ws),
+                                        ws_bytes, ptr(status), stream_handle()))
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    got = audio.permute(1, 0, 2).reshape(S, 1, 1, steps * 1920).cpu().numpy()
+    for s in (0, 1, 63, 64, 255, 256, 510, 511):
+        d = discrepancy(oracle0.decode_numpy(lat[s:s + 1]), got[s])
+        assert d["max_abs"] <= MAX_ABS and d["snr_db"] >= SNR_DB, (s, d)
+
+
+def test_cfg3_full_run_is_bitwise_batch(lib, weights0, stream_dec):
+    """cfg3 in full: 256 streams x 2-frame chunks for 125 steps (10 s per
+    stream), one step per chunk for all streams; every stream equals its batch
+    decode bit for bit."""
+    from fast_audiovae.cuda import CUDADecoder
+    n, steps, F = 256, 125, 2
+    zs = [W.seeded_latents(s, F * steps) for s in range(n)]
+    streams = [stream_dec.stream() for _ in range(n)]
+    got = np.empty((n, 1920 * F * steps), np.float32)
+    for t in range(steps):
+        for i, audio in enumerate(stream_dec.decode_streams(streams, [z[..., F * t:F * (t + 1)] for z in zs])):
+            got[i, 1920 * F * t:1920 * F * (t + 1)] = audio[0, 0]
+    for s in streams:
+        s.close()
+    batch = CUDADecoder(weights0, {}, "batch", batch_chunk_frames=25)
+    for g in range(0, n, 64):
+        for i, ref in enumerate(batch.decode_many(zs[g:g + 64])):
+            assert np.array_equal(got[g + i].view(np.uint32), ref[0, 0].view(np.uint32)), g + i
 
 
 def test_public_load_api(lib):

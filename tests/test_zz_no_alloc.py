@@ -38,27 +38,46 @@ def lib():
 
 
 def test_static_step_matches_fav_step_twice(lib):
+    """Two calls in a row at the largest accepted size (fresh, then carried),
+    then a smaller carried call over a subset of the streams. The ``fav_step``
+    arm's workspace is filled with NaN bytes before every call, so a step that
+    read scratch it had not written would differ between the two arms."""
     plan = _native.Plan(W.seeded_weights(0))
-    n, frames = 4, 2
+    n_max = 8
     stream = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
-    pools = [torch.zeros(lib.fav_state_pool_bytes(n) // 4, device="cuda") for _ in range(2)]
-    ws_bytes = lib.fav_step_workspace_bytes(n, frames)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    pools = [torch.zeros(lib.fav_state_pool_bytes(n_max) // 4, device="cuda") for _ in range(2)]
     status = torch.zeros(2, dtype=torch.int32, device="cuda")
-    first = torch.tensor([(s << 2) | 2 for s in range(n)], dtype=torch.int32, device="cuda")   # fresh, read half 0
-    second = torch.tensor([(s << 2) | 1 for s in range(n)], dtype=torch.int32, device="cuda")  # read half 1
-    for call, codes in enumerate((first, second)):
+    calls = [(8, 2, 2), (8, 2, 1), (3, 1, 0)]  # (streams, frames, fresh / read-table bits)
+    assert calls[0][0] * calls[0][1] == 16  # FAV_STATIC_MAX_FRAMES
+    for call, (n, frames, bits) in enumerate(calls):
+        codes = torch.tensor([(s << 2) | bits for s in range(n)], dtype=torch.int32, device="cuda")
         z = torch.from_numpy(np.concatenate([W.seeded_latents(50 + 10 * call + s, frames) for s in range(n)])).cuda()
+        ws_bytes = lib.fav_step_workspace_bytes(n, frames)
+        ws = torch.full((ws_bytes,), 0xFF, dtype=torch.uint8, device="cuda")
         audio = [torch.full((n, 1920 * frames), float("nan"), device="cuda") for _ in range(2)]
-        _native.check(lib, lib.fav_step(plan.handle, ptr(pools[0]), n, ptr(codes), n, frames, ptr(z), ptr(audio[0]),
-                                        ptr(ws), ws_bytes, ptr(status[0:1]), stream))
-        _native.check(lib, lib.fav_step_static(plan.handle, ptr(pools[1]), n, ptr(codes), n, frames, ptr(z),
+        status.zero_()
+        _native.check(lib, lib.fav_step(plan.handle, ptr(pools[0]), n_max, ptr(codes), n, frames, ptr(z),
+                                        ptr(audio[0]), ptr(ws), ws_bytes, ptr(status[0:1]), stream))
+        _native.check(lib, lib.fav_step_static(plan.handle, ptr(pools[1]), n_max, ptr(codes), n, frames, ptr(z),
                                                ptr(audio[1]), ptr(status[1:2]), stream))
         torch.cuda.synchronize()
         assert status.tolist() == [0, 0]
         assert torch.isfinite(audio[1]).all()
         assert torch.equal(audio[0], audio[1]), call
-        assert torch.equal(pools[0], pools[1]), call
+        assert torch.equal(pools[0].view(torch.int32), pools[1].view(torch.int32)), call
+
+
+def test_static_step_rejects_int8_plans(lib):
+    """The static array holds a bf16 step's scratch only; an int8 plan is refused before any launch."""
+    plan = _native.Plan(W.seeded_weights(0), precision=1)
+    pool = torch.zeros(lib.fav_state_pool_bytes(1) // 4, device="cuda")
+    codes = torch.tensor([2], dtype=torch.int32, device="cuda")
+    z = torch.zeros(1, 64, 1, device="cuda")
+    audio = torch.zeros(1, 1920, device="cuda")
+    stream = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
+    st = lib.fav_step_static(plan.handle, ptr(pool), 1, ptr(codes), 1, 1, ptr(z), ptr(audio), None, stream)
+    assert st == 2  # FAV_UNSUPPORTED
+    assert b"FAV_PRECISION_BF16" in lib.fav_last_error()
 
 
 def test_static_step_rejects_sizes_beyond_its_limit(lib):
