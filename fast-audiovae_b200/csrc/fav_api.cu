@@ -368,8 +368,9 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
       }
       r.pw_b = up(rb + 7);
       {
-        // [block][w0..w6, bias, alpha2, recip2][64], zero padded past C. The
-        // first Snake's alpha1/recip1 go to the previous layer's epilogue.
+        // [block][w0..w6, bias, alpha2, recip2, alpha1, recip1][64], zero padded
+        // past C. The first Snake's alpha1/recip1 are applied either by the
+        // previous layer's epilogue or by this unit's producers (pre_snake).
         const int c = st.c_out, blocks = (c + 63) / 64;
         std::vector<float> cf((size_t)blocks * fav::kCoefResidual * 64, 0.f);
         for (int b = 0; b < blocks; ++b)
@@ -380,6 +381,8 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
             o[7 * 64] = w[rb + 3][cc];
             o[8 * 64] = w[rb + 4][cc];
             o[9 * 64] = w[rb + 5][cc];
+            o[10 * 64] = w[rb + 0][cc];
+            o[11 * 64] = w[rb + 1][cc];
           }
         r.coef = plan->mem.upload(cf.data(), cf.size(), &e);
       }
@@ -525,7 +528,10 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     t.kind = fav::kTconv;
     t.mode = fav::kModeSplit;
     const bool into_tail = tail && i + 1 == fav::kStages;
-    t.epi = fav::kEpiX | (into_tail ? 0 : fav::kEpiS);
+    // Stages 2-4 of a bf16 plan: the residual units read y and apply their first
+    // Snake themselves (pre_snake), so this conv and units 0-1 write y only.
+    const bool x_only = p->precision == FAV_PRECISION_BF16 && i >= 2 && i + 1 < fav::kStages;
+    t.epi = fav::kEpiX | (into_tail || x_only ? 0 : fav::kEpiS);
     t.rows = n_streams * n;
     t.rows_per_stream = n;
     t.k_channels = st.c_in;
@@ -639,7 +645,9 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       const bool debug_y = layer + 1 == last_layer;
       u.out_x = X[out];
       u.out_s = S[out];
-      if (j < 2) {
+      if (j < 2 && x_only) {
+        u.epi = fav::kEpiX;
+      } else if (j < 2) {
         u.epi = fav::kEpiX | fav::kEpiS;
         u.next_alpha = st.res[j + 1].pre_a;
         u.next_recip = st.res[j + 1].pre_r;
@@ -661,6 +669,9 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
         if ((e = fav::launch_depthwise(dw, stream)) != cudaSuccess) return cuda_fail(e, "depthwise launch");
         u.kind = fav::kResidualPre;
         if ((es = encode_operand_map(&u.tmap, a_op, u.rows, st.c_out)) != FAV_OK) return es;
+      } else if (x_only) {
+        u.pre_snake = 1;
+        if ((es = encode_input_map(&u.tmap, X[in], u.rows, st.c_out, u.box_rows)) != FAV_OK) return es;
       } else if ((es = encode_input_map(&u.tmap, S[in], u.rows, st.c_out, u.box_rows)) != FAV_OK) {
         return es;
       }

@@ -126,8 +126,12 @@ struct LayerArgs {
   const float* dw_w;    // stem depthwise taps [64][7]
   const float* dw_b;
   // Residual: per-64-channel-block coefficients packed for one bulk copy per K
-  // block, [block][w0..w6, bias, alpha2, recip2][64] (zero padded).
+  // block, [block][w0..w6, bias, alpha2, recip2, alpha1, recip1][64] (zero padded).
   const float* coef;
+  // Residual: the staged input is the unit's input y itself (not Snake_pre(y)
+  // written by the previous epilogue); the producers apply Snake_pre (alpha1,
+  // recip1) to each staged row once, in shared memory, before the depthwise conv.
+  int pre_snake;
   const float* next_scale;  // coefficients of the pointwise prologue the epilogue applies
   const float* next_offset;
   const float* next_alpha;
@@ -250,7 +254,10 @@ cudaError_t launch_sine_test(const float* x, int n, float* out, cudaStream_t str
 cudaError_t launch_final(const FinalArgs& a, cudaStream_t stream);
 cudaError_t prepare_kernels();
 
-constexpr int kCoefResidual = 10;  // coefficient vectors per 64-channel block
+// Coefficient vectors per 64-channel block of a residual unit: depthwise taps
+// w0..w6, depthwise bias, the second Snake's alpha and reciprocal, then the
+// first Snake's alpha and reciprocal (used when the unit reads y itself).
+constexpr int kCoefResidual = 12;
 
 // Rows of the TMA input box of a residual unit: the 128-row tile plus the
 // causal halo of 6*dilation rows.

@@ -454,6 +454,25 @@ __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_
   }
 }
 
+// Residual unit reading its input y (LayerArgs::pre_snake): Snake_pre (block
+// coefficient vectors 10 and 11) applied in place to every staged row of the
+// K block's box, each row once, before the depthwise conv reads the box; the
+// box then holds exactly what the previous epilogue would have written as
+// Snake_pre(y), and the history window keeps those values as before.
+// Producer-collective: the caller synchronises the producers afterwards.
+__device__ __forceinline__ void snake_box(const LayerArgs& a, float* raw, int tid) {
+  const int quads = a.raw_pitch / 4;  // 16 (64-channel blocks) or 8
+  const int q = tid % quads;
+  const float* cf = raw + kResBoxBytes / 4;
+  const float4 al = lds4(cf + 10 * 64 + 4 * q), rc = lds4(cf + 11 * 64 + 4 * q);
+  const int step = kProducerThreads / quads;
+#pragma unroll 4
+  for (int r = tid / quads; r < a.box_rows; r += step) {
+    float4* p = reinterpret_cast<float4*>(raw + r * a.raw_pitch + 4 * q);
+    *p = snake4(*p, al, rc);
+  }
+}
+
 // Residual unit, int8 pass 2, K block kb8 (128 channels): the depthwise +
 // Snake result staged by pass 1 in the CTA's scratch, quantised with each
 // row's scale into the s8 A tile. Warp w covers rows w, w + 8, ...; a lane
@@ -838,9 +857,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           if (KIND == kStem) {
             produce_stem<MODE>(a, a_stage, warp, lane, write_state, tab);
           } else if (KIND == kResidual) {
-            produce_residual<MODE, kLpr>(a, m0, kb, a_stage, reinterpret_cast<const float*>(raw_base + rb * Cfg::kRaw),
-                                         warp, lane, kb % num_n == tile_n(t), tab, partial ? iwalk_lo : walk_lo,
-                                         partial ? iwalk_hi : walk_hi, regular, nullptr);
+            float* raw = reinterpret_cast<float*>(raw_base + rb * Cfg::kRaw);
+            if (a.pre_snake) {
+              snake_box(a, raw, threadIdx.x);
+              named_barrier(2, kProducerThreads);
+            }
+            produce_residual<MODE, kLpr>(a, m0, kb, a_stage, raw, warp, lane, kb % num_n == tile_n(t), tab,
+                                         partial ? iwalk_lo : walk_lo, partial ? iwalk_hi : walk_hi, regular, nullptr);
           } else {
             produce_test<MODE>(a, m0, kb, a_stage, warp, lane);
           }
@@ -1351,7 +1374,8 @@ static cudaError_t set_smem() {
   X(256, kModeSplit4, kStem, kOutAct)                                                                      \
   X(256, kModeSplit, kTconv, kOutS) X(128, kModeSplit, kTconv, kOutS) X(64, kModeSplit, kTconv, kOutS)      \
   X(128, kModeI8, kTconv, kOutS) X(128, kModeI8, kTconvPre, kOutS)                                        \
-  X(64, kModeSplit, kTconv, kOutNone)                                                                      \
+  X(256, kModeSplit, kTconv, kOutNone) X(128, kModeSplit, kTconv, kOutNone) X(64, kModeSplit, kTconv, kOutNone) \
+  X(256, kModeF16, kResidual, kOutNone) X(128, kModeF16, kResidual, kOutNone) X(64, kModeF16, kResidual, kOutNone) \
   X(256, kModeF16, kResidual, kOutS) X(128, kModeF16, kResidual, kOutS) X(64, kModeF16, kResidual, kOutS)  \
   X(256, kModeF16, kResidualPre, kOutS) X(256, kModeF16, kResidualPre, kOutPlanes)                          \
   X(32, kModeF16, kResidual, kOutS) X(256, kModeF16, kResidual, kOutPlanes)                                \

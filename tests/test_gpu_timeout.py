@@ -70,8 +70,11 @@ class Run:
         """Runs the next step; returns (audio, status). Commits (flips the read table) only on success."""
         audio = torch.full((S, 1920 * F), float("nan"), device="cuda")
         self.status.zero_()
-        args = (self.plan.handle, ptr(self.pool), S, ptr(self.codes()), S, F, ptr(self.latents(self.steps)),
-                ptr(audio), ptr(self.ws), self.ws_bytes, ptr(self.status))
+        # Held until the step has finished: a device pointer taken from a tensor
+        # that is then freed may be handed to the next allocation on this stream.
+        codes, z = self.codes(), self.latents(self.steps)
+        args = (self.plan.handle, ptr(self.pool), S, ptr(codes), S, F, ptr(z), ptr(audio), ptr(self.ws),
+                self.ws_bytes, ptr(self.status))
         if gated_layer is None:
             _native.check(self.lib, self.lib.fav_step(*args, self.stream))
         else:
