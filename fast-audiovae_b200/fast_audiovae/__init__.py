@@ -7,9 +7,12 @@ returns a decoder with ``.decode`` (batch), ``.stream()`` (streaming) and
 and Apple routes are outside this package.
 
 Coefficients: the reference loads a checksum-pinned ONNX export
-(``assets.py:6-11``). Without it, ``load`` takes ``weights=`` (a coefficient
-dict, names from ``fast_audiovae.weights.weight_shapes()``), ``source=`` (an
-``.npz`` file with those names) or, by default, the seeded random init of
+(``assets.py:6-11``); ``load(source="<dir>/audio_vae_decoder.onnx")`` reads it
+the same way (``fast_audiovae.onnx_import``, no ``onnx`` package needed; the
+pinned digests are required unless ``pinned_export=False``). ``load`` also
+takes ``weights=`` (a coefficient dict, names from
+``fast_audiovae.weights.weight_shapes()``), ``source=`` an ``.npz`` file with
+those names, or, by default, the seeded random init of
 ``fast_audiovae.weights.seeded_weights(weight_seed)``.
 """
 from __future__ import annotations
@@ -44,12 +47,16 @@ PRECISIONS = {
 }
 
 
-def _coefficients(weights_arg, source, weight_seed):
+def _coefficients(weights_arg, source, weight_seed, pinned=True):
     if weights_arg is not None and source is not None:
         raise ValueError("Pass weights or source, not both")
     if weights_arg is not None:
         coeffs = {k: np.array(v, dtype=np.float32, copy=True) for k, v in weights_arg.items()}
         origin = "caller_coefficients"
+    elif source is not None and str(source).endswith(".onnx"):
+        from . import onnx_import
+        coeffs = onnx_import.load_coefficients(Path(source).expanduser(), pinned=pinned)
+        origin = "onnx:" + str(Path(source).expanduser().resolve()) + (" (pinned)" if pinned else "")
     elif source is not None:
         with np.load(Path(source).expanduser(), allow_pickle=False) as archive:
             coeffs = {k: np.array(archive[k], dtype=np.float32, copy=True) for k in archive.files}
@@ -81,15 +88,18 @@ def setup(*, mode="streaming", threads=1, device="cuda", cache_dir=None, source=
 
 
 def load(*, mode="streaming", threads=1, device="cuda", cache_dir=None, source=None, offline=False,
-         prefer_custom=True, weights=None, weight_seed=0, max_streams=256, device_index=0, precision="bf16"):
+         prefer_custom=True, weights=None, weight_seed=0, max_streams=256, device_index=0, precision="bf16",
+         pinned_export=True):
     """Load the CUDA decoder; ``mode="stream"`` is accepted as an alias of ``"streaming"``.
 
     ``precision="int8"`` runs the reference's W8A8 int8 recipe on its selected
     projections (experiments/intel-precision), the rest as ``"bf16"``.
+    ``source`` may name the AudioVAE2 ONNX export (``*.onnx`` beside its
+    ``.onnx.data``), read as ``MPSModel.from_onnx`` does (mps_decoder.py:190-286).
     """
     info = setup(mode=mode, threads=threads, device=device, cache_dir=cache_dir, source=source,
                  offline=offline, prefer_custom=prefer_custom, weight_seed=weight_seed, precision=precision)
-    coeffs, origin = _coefficients(weights, source, weight_seed)
+    coeffs, origin = _coefficients(weights, source, weight_seed, pinned_export)
     from .cuda import CUDADecoder
     decoder = CUDADecoder(coeffs, {**info, "coefficient_source": origin}, info["mode"],
                           max_streams=max_streams, device=device_index, precision=PRECISIONS[precision][0])
