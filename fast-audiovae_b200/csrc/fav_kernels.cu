@@ -473,6 +473,136 @@ __device__ __forceinline__ void snake_box(const LayerArgs& a, float* raw, int ti
   }
 }
 
+// The one stream start that bears on a residual tile's depthwise taps, for
+// units that read y (pre_snake) on streams of at least 128 + 6d rows: the
+// start b of the stream holding the tile's last row, when it lies after
+// m0 - 6d (its first 6d rows, which reach into the stream's history, overlap
+// the tile); at most one stream starts in (m0 - 6d, m0 + 128).
+struct TileStart {
+  int b;      // global row of the start; meaningless when !on
+  int entry;  // its stream's table entry
+  bool on;
+};
+__device__ __forceinline__ TileStart tile_start(const LayerArgs& a, int m0, const StreamTable& tab) {
+  const int N = a.rows_per_stream;
+  const int s = (min(m0 + kTileM, a.rows) - 1) / N;
+  const int b = s * N;
+  return TileStart{b, s - tab.s_lo, b > m0 - 6 * a.dilation};
+}
+
+// Residual unit reading its input y (pre_snake), K block kb, 64-channel
+// blocks: depthwise k=7 (dilation d) + Snake_post of the box that snake_box
+// turned into s = Snake_pre(y). Every lane group walks its eight rows in
+// residue-class order with a sliding window of taps from the box: rows
+// r, r + d, ... of one class, and where its positions cross into the next
+// class (at most once: classes hold at least 14 rows) the window is reloaded
+// once. The walk ignores streams; rows whose taps reach before their stream's
+// start (its first 6d rows) get wrong taps there and are recomputed after the
+// walk: the producers overwrite the box rows before that start (the previous
+// stream's last rows, no longer read) with the stream's history window, which
+// they loaded into registers (hist_reg) before the walk, and recompute those
+// rows one (row, channel quad) per thread. ``hist_writer``: this N tile writes
+// the new window rows of streams ending in the tile (first, from the box).
+// Producer-collective (named barrier 2).
+__device__ void produce_residual_y(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, float* raw, int warp,
+                                   int lane, bool hist_writer, const StreamTable& tab, uint32_t walk_lo,
+                                   uint32_t walk_hi, int ubreak, const TileStart& ts, const float4 (&hist_reg)[4]) {
+  const int d = a.dilation;
+  const int H = 6 * d;
+  const int N = a.rows_per_stream;
+  constexpr int P = kKBlock;
+  const int q = lane & 15;
+  const int kl = 4 * q;
+  const int tid = warp * 32 + lane;
+  const float* cf = raw + kResBoxBytes / 4 + kl;
+  if (hist_writer && a.state.pool) {
+    // New window rows (the last min(N, H) rows of s) of the streams whose last row lies in this tile.
+    const int g_end = min(m0 + kTileM, a.rows);
+    const int ns = g_end / N - tab.s_lo;
+    const int per = H * (P / 4);
+#pragma unroll 2
+    for (int it = tid; it < ns * per; it += kProducerThreads) {
+      const int e = it / per, rem = it - e * per;
+      const int row = rem / (P / 4), k4 = 4 * (rem - row * (P / 4));
+      const int tp = N - H + row;
+      *reinterpret_cast<float4*>(hist_new_row(a.state, a.hist, tab.code[e], tab.head[e], tp, N) + kb * kKBlock + k4) =
+          lds4(raw + ((tab.s_lo + e) * N + tp - m0 + H) * P + k4);
+    }
+    if (kb == 0)
+      for (int e = tid; e < ns; e += kProducerThreads) hist_commit_head(a.state, a.hist, tab.code[e], tab.head[e], N);
+  }
+  float4 w[7];
+#pragma unroll
+  for (int j = 0; j < 7; ++j) w[j] = lds4(cf + j * 64);
+  const float4 bias = lds4(cf + 7 * 64), al2 = lds4(cf + 8 * 64), rc2 = lds4(cf + 9 * 64);
+  {
+    const int r0 = walk_row(walk_lo, walk_hi, 0);
+    const int r1 = ubreak < 8 ? walk_row(walk_lo, walk_hi, ubreak) : 0;
+    float4 win[7];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int r = u < ubreak ? r0 + u * d : r1 + (u - ubreak) * d;
+      if (u == 0 || u == ubreak) {
+#pragma unroll
+        for (int j = 0; j < 6; ++j) win[j] = lds4(raw + (r - (6 - j) * d + H) * P + kl);
+      }
+      win[6] = lds4(raw + (r + H) * P + kl);
+      put_a4<kModeF16>(a_stage, r, kl, snake4(dw7<false>(w, win, bias), al2, rc2));
+#pragma unroll
+      for (int j = 0; j < 6; ++j) win[j] = win[j + 1];
+    }
+  }
+  if (!ts.on) return;
+  // Rows [b, b + H) of the stream starting at b: its history window replaces
+  // box rows [b - H, b) (box position of global row g: g - m0 + H), then those
+  // rows are recomputed. Every walk has finished reading the box first.
+  named_barrier(2, kProducerThreads);
+  const int pos0 = ts.b - m0;  // box position of history row 0
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int it = tid + k * kProducerThreads;
+    const int j = it >> 4;  // history row; quad = it & 15 = q
+    if (j < H && pos0 + j >= 0) *reinterpret_cast<float4*>(raw + (pos0 + j) * P + 4 * (it & 15)) = hist_reg[k];
+  }
+  named_barrier(2, kProducerThreads);
+  const int lo = max(ts.b, m0) - m0, hi = min(min(ts.b + H, m0 + kTileM), a.rows) - m0;
+  for (int it = tid; it < (hi - lo) * 16; it += kProducerThreads) {
+    const int r = lo + (it >> 4), k4 = 4 * (it & 15);
+    float4 wq[7], win[7];
+#pragma unroll
+    for (int j = 0; j < 7; ++j) {
+      wq[j] = lds4(raw + kResBoxBytes / 4 + k4 + j * 64);
+      win[j] = lds4(raw + (r - (6 - j) * d + H) * P + k4);
+    }
+    const float4 bq = lds4(raw + kResBoxBytes / 4 + k4 + 7 * 64);
+    const float4 aq = lds4(raw + kResBoxBytes / 4 + k4 + 8 * 64), rq = lds4(raw + kResBoxBytes / 4 + k4 + 9 * 64);
+    put_a4<kModeF16>(a_stage, r, k4, snake4(dw7<false>(wq, win, bq), aq, rq));
+  }
+}
+
+// The history window rows a producer thread loads for produce_residual_y:
+// items tid + k * 256 (k < 4) of [H rows][16 quads] of K block kb, zero for a
+// fresh stream, without a pool, or past the rows the tile can reach.
+__device__ __forceinline__ void load_tile_history(const LayerArgs& a, int m0, int kb, const StreamTable& tab,
+                                                  const TileStart& ts, int tid, float4 (&hist_reg)[4]) {
+  const int H = 6 * a.dilation;
+  const int code = tab.code[ts.entry];
+  const bool have = a.state.pool && !(code & 2);
+  const float* ring = have ? slot_base(a.state, code) + a.hist.ring + kb * kKBlock : nullptr;
+  const int head = tab.head[ts.entry];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int it = tid + k * kProducerThreads;
+    const int j = it >> 4;
+    hist_reg[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (have && j < H && ts.b - m0 + j >= 0) {
+      int row = head + j;  // window row j (time j - H), ring of 2H rows
+      if (row >= 2 * H) row -= 2 * H;
+      hist_reg[k] = ldg4(ring + row * a.hist.width + 4 * (it & 15));
+    }
+  }
+}
+
 // Residual unit, int8 pass 2, K block kb8 (128 channels): the depthwise +
 // Snake result staged by pass 1 in the CTA's scratch, quantised with each
 // row's scale into the s8 A tile. Warp w covers rows w, w + 8, ...; a lane
@@ -744,6 +874,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
     uint32_t walk_lo = 0, walk_hi = 0;
     constexpr int kRpg = 16 * kLpr / 32;
     bool chain = false;  // this lane group's rows form one arithmetic chain of step d
+    int ubreak = 8;      // position where this lane group's rows move to the next residue class (8: none)
     // A tile with empty rows (the last M tile, e.g. one stream) walks rows
     // interleaved across the lane groups instead, so the valid rows spread
     // over every warp.
@@ -758,8 +889,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       }
       class_rows(a.dilation, warp, lane / kLpr, kRpg, walk_lo, walk_hi);
       chain = true;
-      for (int u = 1; u < kRpg; ++u)
+      for (int u = 1; u < kRpg; ++u) {
+        const bool step = walk_row(walk_lo, walk_hi, u) == walk_row(walk_lo, walk_hi, u - 1) + a.dilation;
         chain = chain && walk_row(walk_lo, walk_hi, u) == (int)(walk_lo & 255) + u * a.dilation;
+        if (!step && ubreak == 8) ubreak = u;
+      }
     }
     const int res_boxes = a.k_channels < kKBlock ? 1 : a.k_channels / kKBlock;  // residual boxes per tile
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++ti) {
@@ -858,12 +992,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
             produce_stem<MODE>(a, a_stage, warp, lane, write_state, tab);
           } else if (KIND == kResidual) {
             float* raw = reinterpret_cast<float*>(raw_base + rb * Cfg::kRaw);
-            if (a.pre_snake) {
+            if (kLpr == 16 && !kI8 && a.pre_snake) {
+              const TileStart ts = tile_start(a, m0, tab);
+              float4 hist_reg[4];
+              if (ts.on) load_tile_history(a, m0, kb, tab, ts, threadIdx.x, hist_reg);
               snake_box(a, raw, threadIdx.x);
               named_barrier(2, kProducerThreads);
+              produce_residual_y(a, m0, kb, a_stage, raw, warp, lane, kb % num_n == tile_n(t), tab, walk_lo, walk_hi,
+                                 ubreak, ts, hist_reg);
+            } else {
+              produce_residual<MODE, kLpr>(a, m0, kb, a_stage, raw, warp, lane, kb % num_n == tile_n(t), tab,
+                                           partial ? iwalk_lo : walk_lo, partial ? iwalk_hi : walk_hi, regular,
+                                           nullptr);
             }
-            produce_residual<MODE, kLpr>(a, m0, kb, a_stage, raw, warp, lane, kb % num_n == tile_n(t), tab,
-                                         partial ? iwalk_lo : walk_lo, partial ? iwalk_hi : walk_hi, regular, nullptr);
           } else {
             produce_test<MODE>(a, m0, kb, a_stage, warp, lane);
           }
