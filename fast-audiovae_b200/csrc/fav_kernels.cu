@@ -490,6 +490,37 @@ __device__ __forceinline__ TileStart tile_start(const LayerArgs& a, int m0, cons
   return TileStart{b, s - tab.s_lo, b > m0 - 6 * a.dilation};
 }
 
+// The history window rows a producer thread loads for produce_residual_y:
+// items tid + k * 256 (k < 4) of [H rows][16 quads] of K block kb, zero for a
+// fresh stream, without a pool, or past the rows the tile can reach. With
+// ``prefetch`` the thread only asks for their lines in L1 (no registers held
+// across the walk); the loads after the walk then hit L1.
+template <bool PREFETCH>
+__device__ __forceinline__ void load_tile_history(const LayerArgs& a, int m0, int kb, const StreamTable& tab,
+                                                  const TileStart& ts, int tid, float4 (&hist_reg)[4]) {
+  const int H = 6 * a.dilation;
+  const int code = tab.code[ts.entry];
+  const bool have = a.state.pool && !(code & 2);
+  const float* ring = have ? slot_base(a.state, code) + a.hist.ring + kb * kKBlock : nullptr;
+  const int head = tab.head[ts.entry];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int it = tid + k * kProducerThreads;
+    const int j = it >> 4;
+    hist_reg[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (have && j < H && ts.b - m0 + j >= 0) {
+      int row = head + j;  // window row j (time j - H), ring of 2H rows
+      if (row >= 2 * H) row -= 2 * H;
+      const float* src = ring + row * a.hist.width + 4 * (it & 15);
+      if constexpr (PREFETCH) {
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(src));
+      } else {
+        hist_reg[k] = ldg4(src);
+      }
+    }
+  }
+}
+
 // Residual unit reading its input y (pre_snake), K block kb, 64-channel
 // blocks: depthwise k=7 (dilation d) + Snake_post of the box that snake_box
 // turned into s = Snake_pre(y). Every lane group walks its eight rows in
@@ -499,14 +530,14 @@ __device__ __forceinline__ TileStart tile_start(const LayerArgs& a, int m0, cons
 // once. The walk ignores streams; rows whose taps reach before their stream's
 // start (its first 6d rows) get wrong taps there and are recomputed after the
 // walk: the producers overwrite the box rows before that start (the previous
-// stream's last rows, no longer read) with the stream's history window, which
-// they loaded into registers (hist_reg) before the walk, and recompute those
-// rows one (row, channel quad) per thread. ``hist_writer``: this N tile writes
+// stream's last rows, no longer read) with the stream's history window (whose
+// lines they prefetched into L1 before the walk), and recompute those rows one
+// (row, channel quad) per thread. ``hist_writer``: this N tile writes
 // the new window rows of streams ending in the tile (first, from the box).
 // Producer-collective (named barrier 2).
 __device__ void produce_residual_y(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, float* raw, int warp,
                                    int lane, bool hist_writer, const StreamTable& tab, uint32_t walk_lo,
-                                   uint32_t walk_hi, int ubreak, const TileStart& ts, const float4 (&hist_reg)[4]) {
+                                   uint32_t walk_hi, int ubreak, const TileStart& ts) {
   const int d = a.dilation;
   const int H = 6 * d;
   const int N = a.rows_per_stream;
@@ -556,6 +587,8 @@ __device__ void produce_residual_y(const LayerArgs& a, int m0, int kb, uint8_t* 
   // Rows [b, b + H) of the stream starting at b: its history window replaces
   // box rows [b - H, b) (box position of global row g: g - m0 + H), then those
   // rows are recomputed. Every walk has finished reading the box first.
+  float4 hist_reg[4];
+  load_tile_history<false>(a, m0, kb, tab, ts, tid, hist_reg);
   named_barrier(2, kProducerThreads);
   const int pos0 = ts.b - m0;  // box position of history row 0
 #pragma unroll
@@ -577,29 +610,6 @@ __device__ void produce_residual_y(const LayerArgs& a, int m0, int kb, uint8_t* 
     const float4 bq = lds4(raw + kResBoxBytes / 4 + k4 + 7 * 64);
     const float4 aq = lds4(raw + kResBoxBytes / 4 + k4 + 8 * 64), rq = lds4(raw + kResBoxBytes / 4 + k4 + 9 * 64);
     put_a4<kModeF16>(a_stage, r, k4, snake4(dw7<false>(wq, win, bq), aq, rq));
-  }
-}
-
-// The history window rows a producer thread loads for produce_residual_y:
-// items tid + k * 256 (k < 4) of [H rows][16 quads] of K block kb, zero for a
-// fresh stream, without a pool, or past the rows the tile can reach.
-__device__ __forceinline__ void load_tile_history(const LayerArgs& a, int m0, int kb, const StreamTable& tab,
-                                                  const TileStart& ts, int tid, float4 (&hist_reg)[4]) {
-  const int H = 6 * a.dilation;
-  const int code = tab.code[ts.entry];
-  const bool have = a.state.pool && !(code & 2);
-  const float* ring = have ? slot_base(a.state, code) + a.hist.ring + kb * kKBlock : nullptr;
-  const int head = tab.head[ts.entry];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int it = tid + k * kProducerThreads;
-    const int j = it >> 4;
-    hist_reg[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (have && j < H && ts.b - m0 + j >= 0) {
-      int row = head + j;  // window row j (time j - H), ring of 2H rows
-      if (row >= 2 * H) row -= 2 * H;
-      hist_reg[k] = ldg4(ring + row * a.hist.width + 4 * (it & 15));
-    }
   }
 }
 
@@ -994,12 +1004,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
             float* raw = reinterpret_cast<float*>(raw_base + rb * Cfg::kRaw);
             if (kLpr == 16 && !kI8 && a.pre_snake) {
               const TileStart ts = tile_start(a, m0, tab);
-              float4 hist_reg[4];
-              if (ts.on) load_tile_history(a, m0, kb, tab, ts, threadIdx.x, hist_reg);
+              if (ts.on) {
+                float4 unused[4];
+                load_tile_history<true>(a, m0, kb, tab, ts, threadIdx.x, unused);
+              }
               snake_box(a, raw, threadIdx.x);
               named_barrier(2, kProducerThreads);
               produce_residual_y(a, m0, kb, a_stage, raw, warp, lane, kb % num_n == tile_n(t), tab, walk_lo, walk_hi,
-                                 ubreak, ts, hist_reg);
+                                 ubreak, ts);
             } else {
               produce_residual<MODE, kLpr>(a, m0, kb, a_stage, raw, warp, lane, kb % num_n == tile_n(t), tab,
                                            partial ? iwalk_lo : walk_lo, partial ? iwalk_hi : walk_hi, regular,
