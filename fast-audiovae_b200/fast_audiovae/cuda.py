@@ -41,7 +41,7 @@ _FRESH = 2
 # Per-stream fields read with ``map`` so a step over hundreds of streams loops in C.
 _DTYPE, _SHAPE = attrgetter("dtype"), attrgetter("shape")
 _DECODER, _LOCK, _CLOSED = attrgetter("_decoder"), attrgetter("_lock"), attrgetter("_closed")
-_SLOT, _FRESH_FLAG, _PARITY = attrgetter("_slot"), attrgetter("_fresh"), attrgetter("_parity")
+_SLOT = attrgetter("_slot")
 _LOCK_ACQUIRE, _LOCK_RELEASE = type(threading.Lock()).acquire, type(threading.Lock()).release
 
 
@@ -59,28 +59,35 @@ def _latents(value):
     return np.array(value, copy=True, order="C") if value.shape[2] else value
 
 
-def _latents_step(chunks):
+def _latents_step(chunks, stage=None):
     """``gpu.py:115-122`` for one step of many streams: every chunk a float32
     ``[1,64,L]`` array of one common L, all finite. Returns the chunks stacked
-    as an owned ``[n,64,L]`` array (one copy, one vectorised finiteness check)."""
+    as an owned ``[n,64,L]`` array (one copy, one vectorised finiteness check),
+    written into ``stage(n, L)`` (a backend's staging buffer) when given."""
     if not chunks:
         return np.empty((0, 64, 0), dtype=np.float32)
-    # One pass each over types, dtypes and shapes (a server step carries
-    # hundreds of chunks); the per-chunk loop below only names the failure.
+    # One pass each over types, dtypes and first dimensions (a server step
+    # carries hundreds of chunks); concatenation then checks the other
+    # dimensions. The per-chunk loop below only names a failure.
+    first = chunks[0]
     if (set(map(type, chunks)) == {np.ndarray} and set(map(_DTYPE, chunks)) == {np.dtype(np.float32)}
-            and len(shapes := set(map(_SHAPE, chunks))) == 1):
-        (shape,) = shapes
-        if len(shape) != 3 or shape[:2] != (1, 64):
-            raise ValueError("Latents must be a float32 NumPy array with shape [1,64,L]")
+            and set(map(len, chunks)) == {1} and first.ndim == 3 and first.shape[1] == 64):
+        n, frames = len(chunks), first.shape[2]
+        out = stage(n, frames) if stage is not None else None
+        try:
+            stacked = np.concatenate(chunks, axis=0, out=out)
+        except ValueError:
+            stacked = None
+        if stacked is None or stacked.shape != (n, 64, frames):
+            if any(c.ndim != 3 or c.shape[1] != 64 for c in chunks):
+                raise ValueError("Latents must be a float32 NumPy array with shape [1,64,L]")
+            raise ValueError("decode_streams requires chunks of equal length")
     else:
         for value in chunks:
             if (not isinstance(value, np.ndarray) or value.dtype != np.float32
                     or value.ndim != 3 or value.shape[:2] != (1, 64)):
                 raise ValueError("Latents must be a float32 NumPy array with shape [1,64,L]")
-        frames = chunks[0].shape[2]
-        if any(c.shape[2] != frames for c in chunks):
-            raise ValueError("decode_streams requires chunks of equal length")
-    stacked = np.concatenate(chunks, axis=0)
+        raise ValueError("decode_streams requires chunks of equal length")
     if not np.isfinite(stacked).all():
         raise ValueError("Latents must contain only finite values")
     return stacked
@@ -203,6 +210,14 @@ class DeviceBackend:
     def _stream(self):
         return ct.c_void_p(self.torch.cuda.current_stream(self.device).cuda_stream)
 
+    def stage(self, n, frames):
+        """Pinned host staging of one streaming step: latents ``[n, 64, frames]``
+        fp32, then the slot codes and a zero status word, uploaded together by
+        one copy. Returns the latents part as a writable NumPy view."""
+        count = n * 64 * frames
+        host = self._buffer("stage_host", (count + n + 1,), self.torch.float32, pinned=True)
+        return host.numpy()[:count].reshape(n, 64, frames)
+
     def _upload(self, arrays, frames):
         n = len(arrays)
         host = self._buffer("z_host", (n, 64, frames), self.torch.float32, pinned=True)
@@ -225,10 +240,11 @@ class DeviceBackend:
             self.mapped[key] = dev.value if ok else None
         return self.mapped[key]
 
-    def _finish(self, lent):
+    def _finish(self, lent, status=None):
         """Synchronise and read the kernels' status; on failure the lent buffer
         goes back to the pool and the step raises."""
-        self.status_host.copy_(self.status, non_blocking=True)
+        self.status_host.copy_(self.status if status is None else status.view(self.torch.int32),
+                               non_blocking=True)
         self.torch.cuda.current_stream(self.device).synchronize()
         status = int(self.status_host.item())
         if status:
@@ -238,7 +254,7 @@ class DeviceBackend:
                 raise RuntimeError("CUDA model returned nonfinite audio")
             raise RuntimeError("CUDA decoder kernel reported status 0x%x" % status)
 
-    def _download(self, audio_dev):
+    def _download(self, audio_dev, status=None):
         """The step's audio as host fp32: in a lent pinned buffer (no host copy),
         or, while too many earlier results are still held, an owned copy."""
         shape = tuple(audio_dev.shape)
@@ -246,7 +262,7 @@ class DeviceBackend:
         host = (lent[:audio_dev.numel()].view(*shape) if lent is not None
                 else self._buffer("a_host", shape, self.torch.float32, pinned=True))
         host.copy_(audio_dev, non_blocking=True)
-        self._finish(lent)
+        self._finish(lent, status)
         if lent is None:
             return host.numpy().copy()
         return self.out_buffers.lend(lent, host.numpy())
@@ -255,9 +271,26 @@ class DeviceBackend:
         from ._native import check
         torch, lib = self.torch, self.lib
         n = len(arrays)
+        count = n * 64 * frames
         with torch.cuda.device(self.device):
-            self.status.zero_()
-            z = self._upload(arrays, frames)
+            # Latents (already in the staging buffer when the caller stacked
+            # them there), slot codes and a zero status word: one upload.
+            host = self._buffer("stage_host", (count + n + 1,), torch.float32, pinned=True)
+            hn = host.numpy()
+            if not (isinstance(arrays, np.ndarray) and arrays.ctypes.data == hn.ctypes.data):
+                view = hn[:count].reshape(n, 64, frames)
+                if isinstance(arrays, np.ndarray):
+                    view[...] = arrays
+                else:
+                    for i, a in enumerate(arrays):
+                        view[i] = a[0]
+            hn[count:count + n].view(np.int32)[:] = codes
+            hn[count + n:].view(np.int32)[:] = 0
+            block = self._buffer("stage_dev", (count + n + 1,), torch.float32)
+            block.copy_(host, non_blocking=True)
+            z = block[:count]
+            codes_dev = block[count:count + n]
+            status = block[count + n:]
             # The kernels write the audio straight into a lent pinned buffer
             # when it has a device address (no device-to-host copy after the
             # step); otherwise into device memory, downloaded afterwards.
@@ -270,14 +303,10 @@ class DeviceBackend:
                     lent = None
                 audio = self._buffer("audio_dev", shape, torch.float32)
                 target = audio.data_ptr()
-            codes_host = self._buffer("codes_host", (n,), torch.int32, pinned=True)
-            codes_host.numpy()[:] = codes
-            codes_dev = self._buffer("codes_dev", (n,), torch.int32)
-            codes_dev.copy_(codes_host, non_blocking=True)
             ws_bytes = int(lib.fav_plan_workspace_bytes(self.plan.handle, n, frames))
             ws = self._buffer("workspace", (ws_bytes,), torch.uint8)
             args = (self.plan.handle, self._ptr(self.pool), self.max_streams, self._ptr(codes_dev), n, frames,
-                    self._ptr(z), ct.c_void_p(target), self._ptr(ws), ws_bytes, self._ptr(self.status))
+                    self._ptr(z), ct.c_void_p(target), self._ptr(ws), ws_bytes, self._ptr(status))
             key = (n, frames, z.data_ptr(), target, codes_dev.data_ptr(), ws.data_ptr())
             try:
                 graph = self.graphs.get(key) if self.graphs_enabled else None
@@ -299,8 +328,8 @@ class DeviceBackend:
                     self.out_buffers.release(lent)
                 raise
             if lent is None:
-                return self._download(audio)
-            self._finish(lent)
+                return self._download(audio, status)
+            self._finish(lent, status)
             return self.out_buffers.lend(lent, lent[:n * HOP * frames].view(*shape).numpy())
 
     def decode_many(self, arrays, frames):
@@ -340,6 +369,12 @@ class CUDADecoder:
             precision=precision)
         self._lock = threading.Lock()
         self._free_slots = list(range(self._max_streams - 1, -1, -1))
+        # Per-slot stream state (CUDAStream reads and writes it through its
+        # slot), so a step over hundreds of streams builds its slot codes and
+        # commits its histories with array operations.
+        self._slot_parity = np.zeros(self._max_streams, np.int32)  # head table the history is read from
+        self._slot_fresh = np.ones(self._max_streams, np.int32)    # 1: start from zero history
+        self._slot_frames = np.zeros(self._max_streams, np.int64)  # frames decoded since (re)start
         self.state_bytes = STATE_BYTES
         self.info = {**info, "mode": mode, "state_bytes_per_stream": STATE_BYTES,
                      "state_device": "cuda", "output_device": "cpu", "output_ready": True,
@@ -347,28 +382,30 @@ class CUDADecoder:
                      "plan_device_bytes": getattr(self._backend, "plan_bytes", None)}
 
     # ------------------------------------------------------------ internals
-    def _step(self, streams, arrays, frames):
-        """One device step for ``streams``; commits their histories only on success."""
-        n = len(streams)  # CUDAStream._code, over all streams at once
-        codes = ((np.fromiter(map(_SLOT, streams), np.int32, n) << 2)
-                 | np.fromiter(map(_FRESH_FLAG, streams), np.bool_, n).astype(np.int32) * _FRESH
-                 | np.fromiter(map(_PARITY, streams), np.int32, n))
+    def _step(self, slots, arrays, frames):
+        """One device step for the streams in ``slots`` (distinct); commits
+        their histories only on success. Returns audio ``[n, 1, 1, 1920*frames]``."""
+        n = len(slots)  # CUDAStream._code, over all streams at once
+        codes = (slots << 2) | (self._slot_fresh[slots] * _FRESH) | self._slot_parity[slots]
         audio = self._backend.step(codes, arrays, frames)
         if (not isinstance(audio, np.ndarray) or audio.dtype != np.float32
-                or audio.shape != (len(streams), HOP * frames)):
+                or audio.shape != (n, HOP * frames)):
             raise RuntimeError("CUDA model returned invalid audio")
-        for s in streams:  # CUDAStream._commit
-            s._parity ^= 1
-            s._fresh = False
-            s.frames_decoded += frames
-        return list(audio.reshape(len(streams), 1, 1, HOP * frames))
+        self._slot_parity[slots] ^= 1  # CUDAStream._commit, over all streams at once
+        self._slot_fresh[slots] = 0
+        self._slot_frames[slots] += frames
+        return audio.reshape(n, 1, 1, HOP * frames)
 
     def _acquire_slot(self):
         with self._lock:
             if not self._free_slots:
                 raise RuntimeError("All %d CUDA stream slots are in use; close a stream or raise max_streams"
                                    % self._max_streams)
-            return self._free_slots.pop()
+            slot = self._free_slots.pop()
+            self._slot_parity[slot] = 0
+            self._slot_fresh[slot] = 1
+            self._slot_frames[slot] = 0
+            return slot
 
     def _release_slot(self, slot):
         with self._lock:
@@ -420,31 +457,40 @@ class CUDADecoder:
         """Decode one chunk for each of ``streams`` in a single step.
 
         All chunks must have the same frame count; each stream's history
-        advances only if the whole step succeeds.
+        advances only if the whole step succeeds. Returns the audio as one
+        float32 array ``[n, 1, 1, 1920*L]``; row i (``[1, 1, 1920*L]``) belongs
+        to ``streams[i]``.
         """
         if self.mode != "streaming":
             raise RuntimeError("Load mode='streaming' to create an audio stream")
         if len(streams) != len(chunks):
             raise ValueError("One chunk per stream required")
-        chunks = _latents_step(chunks)
-        if not streams:
-            return []
-        if len(set(map(id, streams))) != len(streams):
-            raise ValueError("A stream may appear only once per step")
-        frames = chunks.shape[2]
+        n = len(streams)
+        if not n:
+            _latents_step(chunks)
+            return np.empty((0, 1, 1, 0), dtype=np.float32)
         if any(d is not self for d in set(map(_DECODER, streams))):
             raise ValueError("Stream belongs to another decoder")
-        # Stream locks in one global (address) order, so concurrent steps over
+        slots = np.fromiter(map(_SLOT, streams), np.int32, n)
+        seen = np.zeros(self._max_streams, np.bool_)
+        seen[slots] = True
+        if int(seen.sum()) != n and len(set(map(id, streams))) != n:
+            raise ValueError("A stream may appear only once per step")
+        # Stream locks in one global (slot) order, so concurrent steps over
         # overlapping streams cannot deadlock.
-        locks = list(map(_LOCK, sorted(streams, key=id)))
+        locks = list(map(_LOCK, map(streams.__getitem__, np.argsort(slots, kind="stable").tolist())))
         _drain(map(_LOCK_ACQUIRE, locks))
         try:
-            if any(map(_CLOSED, streams)):
+            if any(map(_CLOSED, streams)):  # (a closed stream's slot may belong to a live one)
                 next(s for s in streams if s._closed)._check_open()
-            if not frames:
-                return [np.empty((1, 1, 0), dtype=np.float32) for _ in streams]
             with self._lock:
-                return self._step(streams, chunks, frames)
+                # Validated (and stacked straight into the backend's upload
+                # buffer) before any device work.
+                stacked = _latents_step(chunks, getattr(self._backend, "stage", None))
+                frames = stacked.shape[2]
+                if not frames:
+                    return np.empty((n, 1, 1, 0), dtype=np.float32)
+                return self._step(slots, stacked, frames)
         finally:
             _drain(map(_LOCK_RELEASE, reversed(locks)))
 
@@ -461,18 +507,24 @@ class CUDAStream:
         self._decoder = decoder
         self._lock = threading.Lock()
         self._slot = decoder._acquire_slot()
-        self._parity = 0
-        self._fresh = True
         self._closed = False
-        self.frames_decoded = 0
+        self._frames_at_close = 0
+
+    # The stream's state lives in its decoder's per-slot arrays.
+    @property
+    def frames_decoded(self):
+        return self._frames_at_close if self._closed else int(self._decoder._slot_frames[self._slot])
+
+    @property
+    def _parity(self):
+        return int(self._decoder._slot_parity[self._slot])
+
+    @property
+    def _fresh(self):
+        return bool(self._decoder._slot_fresh[self._slot])
 
     def _code(self):
         return (self._slot << 2) | (_FRESH if self._fresh else 0) | self._parity
-
-    def _commit(self, frames):
-        self._parity ^= 1
-        self._fresh = False
-        self.frames_decoded += frames
 
     def _check_open(self):
         if self._closed:
@@ -486,13 +538,13 @@ class CUDAStream:
             if not latents.shape[2]:
                 return np.empty((1, 1, 0), dtype=np.float32)
             with self._decoder._lock:
-                return self._decoder._step([self], [latents], latents.shape[2])[0]
+                return self._decoder._step(np.array([self._slot], np.int32), latents, latents.shape[2])[0]
 
     def reset(self):
         with self._lock:
             self._check_open()
-            self._fresh = True
-            self.frames_decoded = 0
+            self._decoder._slot_fresh[self._slot] = 1
+            self._decoder._slot_frames[self._slot] = 0
 
     def flush(self):
         with self._lock:
@@ -502,6 +554,7 @@ class CUDAStream:
     def close(self):
         with self._lock:
             if not self._closed:
+                self._frames_at_close = self.frames_decoded
                 self._closed = True
                 self._decoder._release_slot(self._slot)
 
