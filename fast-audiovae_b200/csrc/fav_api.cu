@@ -449,11 +449,10 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     return fav::HistRef{1 + 4 * i, 2 * st.state_t, 1, st.c_in};
   };
   // int8 plans: the activated input of an int8 transposed conv (fp32) takes
-  // the planes' region, its per-row partial maxima the shifted planes' region,
-  // and the residual units' scratch follows the six regions.
+  // the planes' region, its per-row partial maxima the shifted planes' region
+  // (followed there by the int8 residual units' s8 operand and row scales).
   float* act = reinterpret_cast<float*>(planes);
   float* rowmax = reinterpret_cast<float*>(planes_prev);
-  float* scratch = ws + kWorkspaceRegions * region;
   int act_parts = 0;  // partial row maxima per row of the activation feeding the next int8 conv
   // Sets the epilogue of a layer whose output feeds stage ``i``'s transposed
   // conv: split-bf16 planes, or (int8 conv) the fp32 activation and row maxima.
@@ -474,6 +473,16 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       l.out_planes = planes;
       l.out_planes_prev = planes_prev;
     }
+  };
+  // A bf16 layer whose tiles would occupy few SMs (a step of few rows, e.g.
+  // one stream's 40 ms chunk) runs 64-column N tiles read from its wider
+  // weight image, so more SMs stream its weights.
+  auto narrow = [](fav::LayerArgs& l, int img_nt) {
+    const int m_tiles = (l.rows + fav::kTileM - 1) / fav::kTileM;
+    l.n_tile = img_nt;
+    l.img_nt = img_nt;
+    if (l.mode != fav::kModeI8 && img_nt > 64 && l.n_total % 64 == 0 && m_tiles * (l.n_total / img_nt) < 64)
+      l.n_tile = 64;
   };
   int32_t es = FAV_OK;
   cudaError_t e = cudaSuccess;
@@ -558,6 +567,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       t.w_scale2 = st.tsw + t.n_total;
       t.hist_max_slot = fav::kNumHistories + i;
     }
+    narrow(t, t.n_tile);
     if (st.int8 && t.n_total / t.n_tile < 4) {
       // Few N tiles (stages 3-4): the producers quantise staged fp32 rows.
       if ((es = encode_input_map(&t.tmap, act, t.rows, st.c_in, fav::kTileM + 1)) != FAV_OK) return es;
@@ -636,11 +646,9 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       u.box_rows = fav::box_rows_for(fav::kResidual, r.dilation);
       u.raw_pitch = st.c_out < fav::kKBlock ? st.c_out : fav::kKBlock;
       if (r.int8) {
-        // W8A8: two-pass producers (depthwise + Snake to scratch, then quantise per row).
         u.mode = fav::kModeI8;
         u.num_kblocks = st.c_out / fav::kKBlockI8;
         u.w_scale = r.sw;
-        u.scratch = scratch;
       }
       const bool debug_y = layer + 1 == last_layer;
       u.out_x = X[out];
@@ -659,7 +667,19 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
         u.next_alpha = p->fin_a;
         u.next_recip = p->fin_r;
       }
-      if (!r.int8 && i <= 1) {
+      if (r.int8) {
+        // W8A8: the quantising pre-pass writes the s8 A operand and its row
+        // scales into the shifted planes' region (idle in int8 plans but for
+        // the up to four partial row maxima per row the stage's last unit
+        // writes at its start for the next int8 conv); the engine TMA-loads it.
+        uint8_t* q8 = reinterpret_cast<uint8_t*>(rowmax + (size_t)u.rows * 4);
+        float* qscale = reinterpret_cast<float*>(q8 + (size_t)u.rows * st.c_out);
+        const fav::QuantResidualArgs qa{S[in], q8, qscale, r.coef, u.rows, n, st.c_out, r.dilation, state, u.hist};
+        if ((e = fav::launch_quantize_residual(qa, stream)) != cudaSuccess) return cuda_fail(e, "quantize launch");
+        u.kind = fav::kResidualPre;
+        u.row_scale = qscale;
+        if ((es = encode_s8_map(&u.tmap, q8, u.rows, st.c_out)) != FAV_OK) return es;
+      } else if (i <= 1) {
         // Stages 0-1 (8 and 48 rows per stream and frame, mostly history taps,
         // N split over 4 and 2 tiles): the depthwise pre-pass writes the f16 A
         // operand once, behind this layer's Snake output in S[out] (both fit:
@@ -675,6 +695,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       } else if ((es = encode_input_map(&u.tmap, S[in], u.rows, st.c_out, u.box_rows)) != FAV_OK) {
         return es;
       }
+      narrow(u, u.n_tile);
       diagnose(u, layer + 1);
       if ((e = fav::launch_gemm_layer(u, stream)) != cudaSuccess) return cuda_fail(e, "residual launch");
       if (last_out) *last_out = X[out];
@@ -915,8 +936,6 @@ int32_t fav_step_static(const fav_plan* plan, float* state_pool, int32_t num_slo
   if (!latents || !audio) return fail(FAV_INVALID_ARGUMENT, "NULL latents or audio");
   if (!state_pool || !slot_codes || num_slots < n_streams)
     return fail(FAV_INVALID_ARGUMENT, "state pool, slot codes and num_slots >= n_streams are required");
-  if (plan->precision != FAV_PRECISION_BF16)
-    return fail(FAV_UNSUPPORTED, "the allocation-free step supports FAV_PRECISION_BF16 plans only");
   if (const int32_t d = check_device(plan)) return d;
   float* ws = nullptr;
   const int32_t st = static_workspace(&ws);
@@ -933,9 +952,8 @@ size_t fav_batch_workspace_bytes(int32_t n_clips, int32_t chunk_frames) {
 }
 
 size_t fav_plan_workspace_bytes(const fav_plan* plan, int32_t n_streams, int32_t frames) {
-  const size_t act = fav_step_workspace_bytes(n_streams, frames);
-  if (!plan || !act) return 0;
-  return act + (plan->precision == FAV_PRECISION_INT8 ? fav::kScratchFloats * sizeof(float) : 0);
+  if (!plan) return 0;
+  return fav_step_workspace_bytes(n_streams, frames);
 }
 
 size_t fav_plan_batch_workspace_bytes(const fav_plan* plan, int32_t n_clips, int32_t chunk_frames) {

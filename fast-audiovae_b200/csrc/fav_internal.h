@@ -46,11 +46,6 @@ enum GemmMode : int {
 
 // K elements of one int8 pipeline stage (128 bytes per operand row).
 constexpr int kKBlockI8 = 128;
-// int8 residual units stage their depthwise + Snake result per CTA in a global
-// scratch of [CTA][128 rows][up to 1024 channels] fp32; the launch caps the grid
-// at kScratchCtas.
-constexpr int kScratchCtas = 148;
-constexpr size_t kScratchFloats = (size_t)kScratchCtas * 128 * 1024;
 
 // Stream slot codes passed to a step: (slot << 2) | (fresh << 1) | read_parity.
 // ``fresh`` starts the stream from an all-zero history.
@@ -101,7 +96,7 @@ struct LayerArgs {
   int rowmax_in_parts;
   const float* w_scale;      // per-GEMM-column weight scale (transposed conv: current tap)
   const float* w_scale2;     // transposed conv: previous tap
-  float* scratch;            // residual: per-CTA [128][k] fp32 of the depthwise + Snake result
+  const float* row_scale;    // int8 kResidualPre: activation scale of each input row (quantize_residual)
   int hist_max_slot;         // transposed conv: head-table entry holding the history row's max |x|
   const float* dense_w;      // int8 plan's stem on CUDA cores: 1x1 weights [n_total][k] fp32
   int kind;
@@ -136,7 +131,11 @@ struct LayerArgs {
   const float* next_offset;
   const float* next_alpha;
   const float* next_recip;
-  const uint8_t* wimg;  // packed weight tiles [n_tile][kblock][term][n_tile rows][128 B]
+  const uint8_t* wimg;  // packed weight tiles [N / img_nt][kblock][term][img_nt rows][128 B]
+  // N tile the weight image was packed for (0: n_tile). A launch with a
+  // smaller n_tile (more CTAs for a step of few rows) reads its NT rows of
+  // each packed block: a contiguous run with the same 128-byte swizzle.
+  int img_nt;
   StateRef state;
   HistRef hist;
   uint32_t* status;
@@ -242,6 +241,25 @@ struct QuantizeArgs {
   int hist_max_slot;     // head-table entry holding the history row's max |x|
 };
 cudaError_t launch_quantize(const QuantizeArgs& a, cudaStream_t stream);
+
+// Pre-pass of an int8 residual unit (fav_prepass.cu): the unit's A operand,
+// Snake_post(depthwise_k7(s)) in the int8 path's fixed operation order,
+// quantised per row with the recipe's per-time-step scale over all channels
+// (s8 [rows][channels]) plus that scale per row, and the layer's new history
+// window.
+struct QuantResidualArgs {
+  const float* s;        // Snake_pre(x) [rows][channels] fp32
+  uint8_t* q;            // A operand [rows][channels] s8
+  float* scale;          // [rows]
+  const float* coef;     // [channels / 64][w0..w6, bias, alpha2, recip2, alpha1, recip1][64]
+  int rows;
+  int rows_per_stream;
+  int channels;          // 128, 256, 512 or 1024
+  int dilation;
+  StateRef state;
+  HistRef hist;
+};
+cudaError_t launch_quantize_residual(const QuantResidualArgs& a, cudaStream_t stream);
 cudaError_t prepare_tail();
 
 // Kernel launchers (fav_kernels.cu). Return cudaError_t of the launch.

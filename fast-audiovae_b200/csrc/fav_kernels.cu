@@ -72,8 +72,8 @@ struct GemmCfg {
   // Per-tile tables: streams and rows, plus the int8 transposed conv's row scales.
   static constexpr int kTableI = kTableInts + (kI8Tconv ? 2 * kTileM : 0);
   static constexpr int kTable = KIND == kTestGemm ? 0 : 2 * ((kTableI * 4 + 15) / 16) * 16;  // two tiles
-  // int8: row scales for the epilogue [2 buffers][current, previous tap][128], and pass-1 row maxima [128].
-  static constexpr int kScales = kI8 ? (2 * 2 * kTileM + kTileM) * 4 : 0;
+  // int8 transposed conv: row scales for the epilogue [2 buffers][current, previous tap][128].
+  static constexpr int kScales = kI8 ? 2 * 2 * kTileM * 4 : 0;
   static constexpr int kFixed = 1024 /*align slack*/ + 512 /*barriers*/ + kTable + kScales;
   // Epilogue column coefficients, double-buffered per tile.
   static constexpr int kEpi = 2 * 7 * NT * 4;
@@ -324,28 +324,10 @@ __device__ void produce_stem(const LayerArgs& a, uint8_t* a_stage, int warp, int
 // through registers; a regular chain (one stream, every tap inside the chunk)
 // runs branch-free. History = last 6d rows of s [6d][C]. LPR lanes cover one
 // row (16 for 64-channel K blocks, 8 for C = 32).
-// Output of a residual producer for row r, channels kl..kl+3 of K block kb:
-// into the A tile, or (int8 pass 1) into the CTA's fp32 scratch with the row's
-// max |value| folded into rowmax. All 16 lanes of a row group call it together.
-template <int MODE>
-__device__ __forceinline__ void residual_out(const LayerArgs& a, uint8_t* a_stage, uint32_t* rowmax, int kb, int r,
-                                             int kl, int lane, float4 y) {
-  if constexpr (MODE == kModeI8) {
-    *reinterpret_cast<float4*>(a.scratch + ((size_t)blockIdx.x * kTileM + r) * a.k_channels + kb * kKBlock + kl) = y;
-    float m = fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w)));
-    const unsigned group = 0xffffu << (lane & 16);
-#pragma unroll
-    for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(group, m, o));
-    if ((lane & 15) == 0) atomicMax(rowmax + r, __float_as_uint(m));
-  } else {
-    put_a4<MODE>(a_stage, r, kl, y);
-  }
-}
-
 template <int MODE, int LPR>
 __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, const float* raw, int warp,
                                  int lane, bool hist_writer, const StreamTable& tab, uint32_t walk_lo,
-                                 uint32_t walk_hi, bool regular, uint32_t* rowmax) {
+                                 uint32_t walk_hi, bool regular) {
   constexpr int kRpg = 16 * LPR / 32;  // rows walked per lane group
   const int C = a.k_channels;
   const int d = a.dilation;
@@ -409,8 +391,8 @@ __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_
 #pragma unroll
     for (int u = 0; u < kRpg; ++u) {
       win[6] = valid ? lds4(base + (6 + u) * step) : zero4;
-      const float4 h = dw7<MODE == kModeI8>(w, win, bias);
-      residual_out<MODE>(a, a_stage, rowmax, kb, r0 + u * d, kl, lane, valid ? snake4<MODE == kModeI8>(h, al2, rc2) : zero4);
+      const float4 h = dw7<false>(w, win, bias);
+      put_a4<MODE>(a_stage, r0 + u * d, kl, valid ? snake4(h, al2, rc2) : zero4);
 #pragma unroll
       for (int j = 0; j < 6; ++j) win[j] = win[j + 1];
     }
@@ -443,14 +425,14 @@ __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_
         }
       }
       win[6] = lds4(raw + (r + H) * P + kl);
-      const float4 h = dw7<MODE == kModeI8>(w, win, bias);
-      y = snake4<MODE == kModeI8>(h, al2, rc2);
+      const float4 h = dw7<false>(w, win, bias);
+      y = snake4(h, al2, rc2);
       prev_r = r;
       prev_e = e;
     } else {
       prev_e = -2;
     }
-    residual_out<MODE>(a, a_stage, rowmax, kb, r, kl, lane, y);
+    put_a4<MODE>(a_stage, r, kl, y);
   }
 }
 
@@ -610,21 +592,6 @@ __device__ void produce_residual_y(const LayerArgs& a, int m0, int kb, uint8_t* 
     const float4 bq = lds4(raw + kResBoxBytes / 4 + k4 + 7 * 64);
     const float4 aq = lds4(raw + kResBoxBytes / 4 + k4 + 8 * 64), rq = lds4(raw + kResBoxBytes / 4 + k4 + 9 * 64);
     put_a4<kModeF16>(a_stage, r, k4, snake4(dw7<false>(wq, win, bq), aq, rq));
-  }
-}
-
-// Residual unit, int8 pass 2, K block kb8 (128 channels): the depthwise +
-// Snake result staged by pass 1 in the CTA's scratch, quantised with each
-// row's scale into the s8 A tile. Warp w covers rows w, w + 8, ...; a lane
-// covers 4 channels.
-__device__ void quantize_residual_i8(const LayerArgs& a, int kb8, uint8_t* a_stage, const float* row_scale,
-                                     int warp, int lane) {
-  const float* src = a.scratch + (size_t)blockIdx.x * kTileM * a.k_channels + kb8 * kKBlockI8 + 4 * lane;
-#pragma unroll 4
-  for (int j = 0; j < 16; ++j) {
-    const int r = warp + 8 * j;
-    const float4 v = *reinterpret_cast<const float4*>(src + (size_t)r * a.k_channels);
-    *reinterpret_cast<uint32_t*>(a_stage + sw128_offset(r, 2 * lane)) = quant4(v, row_scale[r]);
   }
 }
 
@@ -793,7 +760,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   constexpr int S = Cfg::kStages;
   constexpr bool kI8 = Cfg::kI8;
   constexpr bool kI8Tconv = Cfg::kI8Tconv;
-  constexpr bool kI8Res = kI8 && KIND == kResidual;
   constexpr bool kStaged = KIND == kResidual || (kI8 && KIND == kTconv);  // producers read TMA-staged boxes
   constexpr bool kConv = KIND == kTconv || KIND == kTconvPre;
   constexpr bool kSkipAdd = KIND == kResidual || KIND == kResidualPre;  // y = x + (D + b)
@@ -824,7 +790,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 17);
   int* table = reinterpret_cast<int*>(bars + 3 * S + 18);
   float* scales = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 512 + Cfg::kTable);  // [2][2][128]
-  uint32_t* rowmax = reinterpret_cast<uint32_t*>(scales + 4 * kTileM);                            // [128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t wl = a.wait_limit ? a.wait_limit : kWaitLimit;  // polls before a wait gives up
@@ -852,13 +817,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       mbar_init(&raw_empty[b], kProducerWarps);
       mbar_init(&table_full[b], 1);
       mbar_init(&table_empty[b], kProducerWarps);
-      mbar_init(&scale_full[b], kI8Res ? kProducerWarps : 1);
+      mbar_init(&scale_full[b], 1);
       mbar_init(&scale_empty[b], kEpilogueWarps);
     }
     mbar_init(mma_drain, 1);
     fence_mbar_init();
   }
-  if (kI8Res && threadIdx.x < kTileM) rowmax[threadIdx.x] = 0u;
   if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
@@ -923,47 +887,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         if (KIND == kResidual && a.rows - m0 < kTileM) regular = false;
       }
       const bool partial = a.rows - m0 < kTileM;
-      if constexpr (kI8Res) {
-        // Pass 1: depthwise + Snake of every 64-channel block into the CTA's
-        // scratch, with each row's max |value| (reference ip_prepare: one
-        // activation scale per time step over all input channels).
-        for (int kb = 0; kb < res_boxes && ok; ++kb, ++g2) {
-          const int rb = g2 & 1;
-          ok = named_barrier_and(2, kProducerThreads,
-                                 mbar_wait(&raw_full[rb], (g2 >> 1) & 1, a.status, kDevTimeoutProducer, wl));
-          if (!ok) break;
-          produce_residual<MODE, kLpr>(a, m0, kb, nullptr, reinterpret_cast<const float*>(raw_base + rb * Cfg::kRaw),
-                                       warp, lane, kb % num_n == tile_n(t), tab, partial ? iwalk_lo : walk_lo,
-                                       partial ? iwalk_hi : walk_hi, regular, rowmax);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&raw_empty[rb]);
-        }
-        if (!ok) break;
-        // Row scales into this tile's buffer, once the epilogue has read the
-        // buffer's previous tile.
-        bool ready = true;
-        if (threadIdx.x == 0) ready = mbar_wait(&scale_empty[ti & 1], ((ti >> 1) & 1) ^ 1, a.status, kDevTimeoutProducer, wl);
-        ok = named_barrier_and(2, kProducerThreads, ready);
-        if (!ok) break;
-        float* sx = scales + (ti & 1) * 2 * kTileM;
-        if (threadIdx.x < kTileM) {
-          sx[threadIdx.x] = quant_scale(__uint_as_float(rowmax[threadIdx.x]));
-          rowmax[threadIdx.x] = 0u;
-        }
-        named_barrier(2, kProducerThreads);
-        if (lane == 0) mbar_arrive(&scale_full[ti & 1]);
-        // Pass 2: quantise 128-channel blocks into the s8 A tiles.
-        for (int kb = 0; kb < num_kb; ++kb, ++g) {
-          const int s = g % S;
-          const uint32_t ph = (g / S) & 1;
-          ok = named_barrier_and(2, kProducerThreads, mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutProducer, wl));
-          if (!ok) break;
-          quantize_residual_i8(a, kb, a_base + s * Cfg::kAStage, sx, warp, lane);
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&a_full[s]);
-        }
-      } else if constexpr (kI8Tconv) {
+      if constexpr (kI8Tconv) {
         const float* sc = reinterpret_cast<const float*>(tbase + kTableInts);
         for (int kb = 0; kb < num_kb && ok; ++kb, ++g) {
           const int s = g % S;
@@ -1014,8 +938,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
                                  ubreak, ts);
             } else {
               produce_residual<MODE, kLpr>(a, m0, kb, a_stage, raw, warp, lane, kb % num_n == tile_n(t), tab,
-                                           partial ? iwalk_lo : walk_lo, partial ? iwalk_hi : walk_hi, regular,
-                                           nullptr);
+                                           partial ? iwalk_lo : walk_lo, partial ? iwalk_hi : walk_hi, regular);
             }
           } else {
             produce_test<MODE>(a, m0, kb, a_stage, warp, lane);
@@ -1128,7 +1051,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       tc_fence_after();
       // int8: this row's activation scales (current and previous tap).
       float sx = 1.f, sxp = 1.f;
-      if constexpr (kI8 && KIND != kTestGemm) {
+      if constexpr (kI8 && KIND == kResidualPre) {
+        sx = g < a.rows ? __ldg(a.row_scale + g) : 1.f;  // written by the quantising pre-pass
+      } else if constexpr (kI8 && KIND != kTestGemm) {
         if (!(ok = __all_sync(0xffffffffu, mbar_wait(&scale_full[buf], (i >> 1) & 1, a.status, kDevTimeoutEpilogue, wl))))
           continue;
         const float* sb = scales + buf * 2 * kTileM;
@@ -1288,24 +1213,36 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
     }
   } else if (warp == kLoaderWarp) {
     if (lane == 0) {
-      // ---- weight tiles
+      // ---- weight tiles: one bulk copy per stage, or, from an image packed
+      // for wider N tiles, one copy per operand term of this tile's rows
+      const int img_nt = a.img_nt ? a.img_nt : NT;
       uint32_t g = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const uint8_t* src = a.wimg + (size_t)tile_n(t) * num_kb * Cfg::kBStage;
+        const int n0 = tile_n(t) * NT;
+        const uint8_t* src = a.wimg + (size_t)(n0 / img_nt) * num_kb * Cfg::kTerms * img_nt * 128 +
+                             (size_t)(n0 % img_nt) * 128;
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
           if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader, wl))) break;
           mbar_arrive_expect_tx(&b_full[s], Cfg::kBStage);
-          bulk_g2s(b_base + s * Cfg::kBStage, src + (size_t)kb * Cfg::kBStage, Cfg::kBStage, &b_full[s]);
+          if (img_nt == NT) {
+            bulk_g2s(b_base + s * Cfg::kBStage, src + (size_t)kb * Cfg::kBStage, Cfg::kBStage, &b_full[s]);
+          } else {
+#pragma unroll
+            for (int term = 0; term < Cfg::kTerms; ++term)
+              bulk_g2s(b_base + s * Cfg::kBStage + term * Cfg::kBTile,
+                       src + ((size_t)kb * Cfg::kTerms + term) * img_nt * 128, Cfg::kBTile, &b_full[s]);
+          }
         }
       }
       drain_fills(b_full, g, S, a.status, kDevTimeoutLoader);
     }
   } else if (warp == kRawWarp) {
     if (lane == 0 && KIND == kResidualPre) {
-      // ---- preformed residual A operand: one 64-channel x 128-row f16 box per K block
+      // ---- preformed residual A operand: one 128-row box of 128 bytes per row
+      // per K block (64 f16 channels, or an int8 plan's 128 s8 channels)
       uint32_t g = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
@@ -1315,7 +1252,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           const uint32_t ph = (g / S) & 1;
           if (!(ok = mbar_wait(&empty[s], ph ^ 1, a.status, kDevTimeoutLoader, wl))) break;
           mbar_arrive_expect_tx(&a_full[s], Cfg::kAStage);
-          tma_load_2d(a_base + s * Cfg::kAStage, &a.tmap, kb * kKBlock, m0, &a_full[s]);
+          tma_load_2d(a_base + s * Cfg::kAStage, &a.tmap, kb * (kI8 ? kKBlockI8 : kKBlock), m0, &a_full[s]);
         }
       }
       drain_fills(a_full, g, S, a.status, kDevTimeoutLoader);
@@ -1509,7 +1446,6 @@ static cudaError_t launch_cfg(const LayerArgs& a, cudaStream_t stream) {
   using Cfg = GemmCfg<NT, MODE, KIND>;
   const int tiles = ((a.rows + kTileM - 1) / kTileM) * (a.n_total / NT);
   int grid = tiles < g_sm_count ? tiles : g_sm_count;
-  if (MODE == kModeI8 && KIND == kResidual && grid > kScratchCtas) grid = kScratchCtas;
   return launch_overlapped(gemm_layer_kernel<NT, MODE, KIND, OUT>, grid, kThreads, Cfg::kSmem, stream, a);
 }
 
@@ -1531,10 +1467,11 @@ static cudaError_t set_smem() {
   X(256, kModeF16, kResidual, kOutNone) X(128, kModeF16, kResidual, kOutNone) X(64, kModeF16, kResidual, kOutNone) \
   X(256, kModeF16, kResidual, kOutS) X(128, kModeF16, kResidual, kOutS) X(64, kModeF16, kResidual, kOutS)  \
   X(256, kModeF16, kResidualPre, kOutS) X(256, kModeF16, kResidualPre, kOutPlanes)                          \
+  X(64, kModeF16, kResidualPre, kOutS) X(64, kModeF16, kResidualPre, kOutPlanes)                            \
+  X(256, kModeI8, kResidualPre, kOutS) X(128, kModeI8, kResidualPre, kOutS)                                \
+  X(256, kModeI8, kResidualPre, kOutAct) X(128, kModeI8, kResidualPre, kOutAct)                            \
   X(32, kModeF16, kResidual, kOutS) X(256, kModeF16, kResidual, kOutPlanes)                                \
   X(128, kModeF16, kResidual, kOutPlanes) X(64, kModeF16, kResidual, kOutPlanes)                           \
-  X(256, kModeI8, kResidual, kOutS) X(128, kModeI8, kResidual, kOutS) X(256, kModeI8, kResidual, kOutAct)  \
-  X(128, kModeI8, kResidual, kOutAct)                                                                       \
   X(256, kModeF16, kTestGemm, kOutNone) X(128, kModeF16, kTestGemm, kOutNone)                              \
   X(64, kModeF16, kTestGemm, kOutNone) X(32, kModeF16, kTestGemm, kOutNone)                                \
   X(256, kModeSplit, kTestGemm, kOutNone) X(128, kModeSplit, kTestGemm, kOutNone)                          \
@@ -1557,6 +1494,7 @@ cudaError_t prepare_kernels() {
 cudaError_t launch_gemm_layer(const LayerArgs& a, cudaStream_t stream) {
   if (a.rows <= 0) return cudaSuccess;
   if (a.n_total % a.n_tile) return cudaErrorInvalidValue;
+  if (a.img_nt && (a.img_nt % a.n_tile || a.n_total % a.img_nt)) return cudaErrorInvalidValue;
   const int out = (a.epi & kEpiPlanes) ? kOutPlanes : (a.epi & kEpiAct) ? kOutAct : (a.epi & kEpiS) ? kOutS : kOutNone;
 #define FAV_LAUNCH(NT, MODE, KIND, OUT) \
   if (a.n_tile == NT && a.mode == MODE && a.kind == KIND && out == OUT) return launch_cfg<NT, MODE, KIND, OUT>(a, stream);

@@ -116,7 +116,90 @@ __global__ void __launch_bounds__(kDwThreads) quantize_kernel(const __grid_const
   }
 }
 
+// Pre-pass of an int8 residual unit: one thread per (row, channel quad), a
+// block of 256 threads covering 1024 / C whole rows, so each row's maximum
+// |h| over all C channels (the recipe's per-time-step activation scale,
+// precision.cpp ip_prepare) is reduced inside the block. h = Snake_post(
+// depthwise_k7(s)) runs in the int8 oracle's fixed operation order (every
+// product and sum rounded, the fixed-order sine), as the engine's producers
+// did; the s8 values and scales are the recipe's round-half-to-even
+// quantisation. History taps, the new window rows and the heads as in
+// depthwise_kernel.
+__global__ void __launch_bounds__(kDwThreads) quantize_residual_kernel(const __grid_constant__ QuantResidualArgs a) {
+  __shared__ float part[kDwThreads / 32];
+  grid_dependency_sync();
+  const int C = a.channels, quads = C / 4;
+  const int g = blockIdx.x * (kDwThreads / quads) + threadIdx.x / quads;
+  const int q = threadIdx.x % quads;
+  const bool valid = g < a.rows;
+  const int N = a.rows_per_stream, d = a.dilation, H = 6 * d;
+  const int s = valid ? g / N : 0, t = valid ? g - s * N : 0;
+  const int n_new = N < H ? N : H;
+  const bool pool = a.state.pool != nullptr;
+  int code = 0, head = 0;
+  float* slot = nullptr;
+  if (pool && valid) {
+    code = a.state.slot_codes ? a.state.slot_codes[s] : ((s << 2) | a.state.uniform_code);
+    slot = slot_base(a.state, code);
+    if (!(code & 2)) head = head_table(slot, code & 1)[a.hist.index];
+  }
+  const int kl = (4 * q) & (kKBlock - 1);
+  const float* cf = a.coef + (size_t)(4 * q / kKBlock) * kCoefResidual * 64 + kl;
+  const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 y = zero4, win[7];
+  if (valid) {
+    float4 w[7];
+#pragma unroll
+    for (int j = 0; j < 7; ++j) w[j] = ldg4(cf + j * 64);
+#pragma unroll
+    for (int j = 0; j < 7; ++j) {
+      const int back = (6 - j) * d;
+      const int tp = t - back;
+      if (tp >= 0) {
+        win[j] = ldg4(a.s + (size_t)(g - back) * C + 4 * q);
+      } else if (pool && !(code & 2)) {
+        int row = head + H + tp;  // window [head, head + H)
+        if (row >= 2 * H) row -= 2 * H;
+        win[j] = ldg4(slot + a.hist.ring + row * a.hist.width + 4 * q);
+      } else {
+        win[j] = zero4;
+      }
+    }
+    y = snake4<true>(dw7<true>(w, win, ldg4(cf + 7 * 64)), ldg4(cf + 8 * 64), ldg4(cf + 9 * 64));
+  }
+  // Row maximum of |y| over the row's C / 4 threads (whole warps for C >= 128).
+  float m = fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
+  __syncthreads();
+  const int w0 = (threadIdx.x / quads) * (quads / 32), nw = quads / 32;
+  m = part[w0];
+  for (int k = 1; k < nw; ++k) m = fmaxf(m, part[w0 + k]);
+  if (!valid) return;
+  const float sc = quant_scale(m);
+  *reinterpret_cast<uint32_t*>(a.q + (size_t)g * C + 4 * q) = quant4(y, sc);
+  if (q == 0) a.scale[g] = sc;
+  if (!pool) return;
+  if (t >= N - n_new)
+    *reinterpret_cast<float4*>(hist_new_row(a.state, a.hist, code, head, t, N) + 4 * q) = win[6];
+  if ((code & 2) && N < H) {
+    // A fresh stream's window starts as H - N zero rows before its N new ones.
+    for (int r = N + t; r < H; r += N)
+      *reinterpret_cast<float4*>(slot + a.hist.ring + r * a.hist.width + 4 * q) = zero4;
+  }
+  if (t == 0 && q == 0) hist_commit_head(a.state, a.hist, code, head, N);
+}
+
 }  // namespace
+
+cudaError_t launch_quantize_residual(const QuantResidualArgs& a, cudaStream_t stream) {
+  if (a.rows <= 0) return cudaSuccess;
+  if (a.channels < 128 || a.channels > 1024 || (a.channels & (a.channels - 1))) return cudaErrorInvalidValue;
+  const int rows_per_block = kDwThreads / (a.channels / 4);
+  return launch_overlapped(quantize_residual_kernel, (unsigned)((a.rows + rows_per_block - 1) / rows_per_block),
+                           kDwThreads, 0, stream, a);
+}
 
 cudaError_t launch_quantize(const QuantizeArgs& a, cudaStream_t stream) {
   if (a.rows <= 0) return cudaSuccess;

@@ -128,8 +128,8 @@ FAV_API size_t fav_plan_bytes(const fav_plan *plan);
 FAV_API size_t fav_state_pool_bytes(int32_t num_slots);
 /* Workspace bytes one fav_step with n_streams x frames needs. */
 FAV_API size_t fav_step_workspace_bytes(int32_t n_streams, int32_t frames);
-/* Workspace bytes one fav_step with this plan needs: fav_step_workspace_bytes
- * plus, for a FAV_PRECISION_INT8 plan, the int8 residual units' scratch. */
+/* Workspace bytes one fav_step with this plan needs (fav_step_workspace_bytes
+ * for either precision; kept so that callers need not know the plan's). */
 FAV_API size_t fav_plan_workspace_bytes(const fav_plan *plan, int32_t n_streams, int32_t frames);
 /* The plan's precision (fav_precision), -1 for NULL. */
 FAV_API int32_t fav_plan_precision(const fav_plan *plan);
@@ -162,9 +162,7 @@ FAV_API int32_t fav_step(const fav_plan *plan, float *state_pool, int32_t num_sl
  * The step's scratch is a library-owned, file-scope device array sized for
  * n_streams * frames <= FAV_STATIC_MAX_FRAMES (22.5 MiB, held on every GPU
  * that loads the library until the process exits); larger calls are rejected
- * with FAV_SIZE_OVERFLOW. Only FAV_PRECISION_BF16 plans are accepted: an int8
- * plan's residual units need a further 78 MB of scratch, which the static
- * array does not hold (FAV_UNSUPPORTED). The first call on a device looks up that array's
+ * with FAV_SIZE_OVERFLOW. Either precision. The first call on a device looks up that array's
  * device address (cudaGetSymbolAddress) with the device current; make that
  * first call before any stream capture. Every call shares the one array and
  * it keeps the last call's contents (nothing in it needs to start at zero:

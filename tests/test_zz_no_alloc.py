@@ -67,17 +67,29 @@ def test_static_step_matches_fav_step_twice(lib):
         assert torch.equal(pools[0].view(torch.int32), pools[1].view(torch.int32)), call
 
 
-def test_static_step_rejects_int8_plans(lib):
-    """The static array holds a bf16 step's scratch only; an int8 plan is refused before any launch."""
+def test_static_step_matches_fav_step_on_an_int8_plan(lib):
+    """An int8 (W8A8) plan needs no scratch beyond a bf16 one: the static step
+    equals fav_step bit for bit on it too (fresh, then carried)."""
     plan = _native.Plan(W.seeded_weights(0), precision=1)
-    pool = torch.zeros(lib.fav_state_pool_bytes(1) // 4, device="cuda")
-    codes = torch.tensor([2], dtype=torch.int32, device="cuda")
-    z = torch.zeros(1, 64, 1, device="cuda")
-    audio = torch.zeros(1, 1920, device="cuda")
+    n, frames = 4, 2
     stream = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
-    st = lib.fav_step_static(plan.handle, ptr(pool), 1, ptr(codes), 1, 1, ptr(z), ptr(audio), None, stream)
-    assert st == 2  # FAV_UNSUPPORTED
-    assert b"FAV_PRECISION_BF16" in lib.fav_last_error()
+    pools = [torch.zeros(lib.fav_state_pool_bytes(n) // 4, device="cuda") for _ in range(2)]
+    ws_bytes = lib.fav_plan_workspace_bytes(plan.handle, n, frames)
+    status = torch.zeros(2, dtype=torch.int32, device="cuda")
+    for call, bits in enumerate((2, 1)):
+        codes = torch.tensor([(s << 2) | bits for s in range(n)], dtype=torch.int32, device="cuda")
+        z = torch.from_numpy(np.concatenate([W.seeded_latents(90 + 10 * call + s, frames) for s in range(n)])).cuda()
+        ws = torch.full((ws_bytes,), 0xFF, dtype=torch.uint8, device="cuda")
+        audio = [torch.full((n, 1920 * frames), float("nan"), device="cuda") for _ in range(2)]
+        status.zero_()
+        _native.check(lib, lib.fav_step(plan.handle, ptr(pools[0]), n, ptr(codes), n, frames, ptr(z), ptr(audio[0]),
+                                        ptr(ws), ws_bytes, ptr(status[0:1]), stream))
+        _native.check(lib, lib.fav_step_static(plan.handle, ptr(pools[1]), n, ptr(codes), n, frames, ptr(z),
+                                               ptr(audio[1]), ptr(status[1:2]), stream))
+        torch.cuda.synchronize()
+        assert status.tolist() == [0, 0]
+        assert torch.equal(audio[0], audio[1]), call
+        assert torch.equal(pools[0].view(torch.int32), pools[1].view(torch.int32)), call
 
 
 def test_static_step_rejects_sizes_beyond_its_limit(lib):
