@@ -472,6 +472,7 @@ def run_stream(args, wl, world, rank, local):
     from fast_audiovae import weights as W
     from fast_audiovae.cuda import CUDADecoder
 
+    torch.cuda.set_device(local)  # the plan, buffers and every ABI call on this rank's GPU
     S = args.streams or wl.streams
     F = wl.frames
     K, Wm = args.steps, args.warmup
@@ -577,6 +578,7 @@ def run_batch(args, wl, world, rank, local):
     from fast_audiovae import weights as W
     from fast_audiovae.cuda import CUDADecoder
 
+    torch.cuda.set_device(local)  # the plan, buffers and every ABI call on this rank's GPU
     K, Wm = args.steps, args.warmup
     T = wl.frames
     if wl.strong:
