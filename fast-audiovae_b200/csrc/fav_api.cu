@@ -106,10 +106,10 @@ int32_t encode_s8_map(CUtensorMap* map, const uint8_t* q, int rows, int channels
 }
 
 // Stage-5 input y [rows][32] fp32 for the fused tail: boxes of 32 channels x
-// (128 + 84) rows in the 128-byte swizzle.
-int32_t encode_tail_map(CUtensorMap* map, const float* x, int rows) {
+// box_rows rows in the 128-byte swizzle.
+int32_t encode_tail_map(CUtensorMap* map, const float* x, int rows, int box_rows) {
   const cuuint64_t dims[2] = {(cuuint64_t)fav::kTailC, (cuuint64_t)rows};
-  const cuuint32_t box[2] = {(cuuint32_t)fav::kTailC, (cuuint32_t)(fav::kTileM + 84)};
+  const cuuint32_t box[2] = {(cuuint32_t)fav::kTailC, (cuuint32_t)box_rows};
   return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_128B, "tail");
 }
 
@@ -611,7 +611,8 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       ta.audio_offset = audio_offset;
       ta.state = state;
       ta.status = status;
-      if ((es = encode_tail_map(&ta.xmap, X[0], ta.rows)) != FAV_OK) return es;
+      if ((es = encode_tail_map(&ta.xmap, X[0], ta.rows, fav::kTailBoxRows)) != FAV_OK) return es;
+      if ((es = encode_tail_map(&ta.xmap_c, X[0], ta.rows, fav::kTailCompactBoxRows)) != FAV_OK) return es;
       if ((e = fav::launch_tail(ta, stream)) != cudaSuccess) return cuda_fail(e, "tail launch");
       // The fused kernel's time counts as stage 5's first residual unit.
       for (int l = 23; l <= 26; ++l) mark(l);

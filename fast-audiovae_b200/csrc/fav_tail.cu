@@ -5,29 +5,31 @@
 //
 // Stage 5 has 32 channels and 1920 rows per frame, so its per-layer kernels
 // move whole [rows][32] activations through HBM four times per unit for a
-// 32 x 32 projection. Here each CTA takes 128 output rows (audio samples) at a
-// time and keeps every intermediate in shared memory:
+// 32 x 32 projection. Here each CTA takes a contiguous range of 128-row tiles
+// (audio samples) and keeps every intermediate in shared memory. Within a tile,
+// with row 0 its first output row:
 //
-//   x              rows [-84, 128)   TMA box, 128-byte swizzle
-//   Snake_pre1(x)  rows [-84, 128) -> depthwise d=1 -> Snake -> f16 A -> MMA
-//   y1             rows [-78, 128)   = x + (A W1 + b1)
-//   Snake_pre2(y1) rows [-78, 128) -> depthwise d=3 -> ...
-//   y2             rows [-60, 128)
-//   Snake_pre3(y2) rows [-60, 128) -> depthwise d=9 -> ...
+//   Snake_pre1(x)  rows [-6, 128)  -> depthwise d=1 -> Snake -> f16 A -> MMA
+//   y1             rows [0, 128)   = x + (A W1 + b1)
+//   Snake_pre2(y1) rows [-18, 128) -> depthwise d=3 -> ...
+//   y2             rows [0, 128)
+//   Snake_pre3(y2) rows [-54, 128) -> depthwise d=9 -> ...
 //   Snake_f(y3)    rows [-6, 128)  -> final conv -> audio rows [0, 128)
 //
-// (row 0 = the tile's first output row). The halo rows before the tile are
-// recomputed from x, except where a stream starts at the tile: rows before a
-// stream's first row come from the layers' history rings instead (the rows of
-// the previous stream, or of no stream, only feed rows that are discarded).
-// Stage 5 has 1920 rows per frame, a multiple of 128, so a tile never straddles
-// two streams. The tile holding a stream's last row writes the new windows.
-// Every row is computed by the same instructions wherever it falls in a tile,
-// so halo rows equal the rows the neighbouring tile keeps, and a stream decoded
-// in chunks equals the same stream decoded at once, bit for bit.
+// The rows before row 0 of each Snake_pre input (6d of them) and of Snake_f(y3)
+// are the previous tile's last rows, kept in shared memory from one tile to the
+// next of the same stream. At a stream's first tile they come from the layers'
+// history rings instead, and the stream's last tile writes the new windows.
+// A range that starts inside a stream has no previous tile: its first tile
+// recomputes the halo from x rows [-84, 128) (6 + 18 + 54 + 6 rows, two M
+// tiles per unit). Stage 5 has 1920 rows per frame, a multiple of 128, so a
+// tile never straddles two streams. Every row is computed by the same
+// instructions wherever it is computed, so carried, recomputed and history
+// rows agree, and a stream decoded in chunks equals the same stream decoded at
+// once, bit for bit.
 //
 // The 32 x 32 projections run on the tensor cores (tcgen05.mma kind::f16, M =
-// 128 x 2 tiles, N = 32, K = 32, fp32 accumulators in TMEM); depthwise convs,
+// 128 (x 2 for a recomputed halo), N = 32, K = 32, fp32 accumulators in TMEM); depthwise convs,
 // Snake, skip adds and the final conv run on the CUDA cores, 512 threads per
 // CTA, in the operation order of the per-layer kernels.
 #include "fav_common.cuh"
@@ -39,6 +41,12 @@ constexpr int kTailThreads = 512;
 constexpr int kTailRows = 128;   // output rows per tile
 constexpr int kTailHalo = 84;    // x rows before the tile: 6 + 18 + 54 + 6
 constexpr int kTailIn = kTailRows + kTailHalo;
+static_assert(kTailIn == kTailBoxRows, "x box of a tile with its halo");
+constexpr int kCompactRow0 = kTailIn - kTailCompactBoxRows;  // buffer row of a carried tile's box
+static_assert(kCompactRow0 % 8 == 0, "a box starts on a 1024-byte boundary of the swizzled buffer");
+constexpr uint32_t kBoxBytes = kTailBoxRows * 128;
+constexpr uint32_t kCompactBoxBytes = kTailCompactBoxRows * 128;
+constexpr int kCarryRows = 6 + 18 + 54 + 6;  // carried input rows of units 0-2 and the final conv
 constexpr int kTailBuf = ((kTailIn * 128 + 1023) / 1024) * 1024;  // one row buffer (fp32 rows of 128 B)
 constexpr int kTailA = 256 * 128;                                 // f16 A operand: 2 M tiles
 constexpr int kTailW = kTailC * 128;                              // one unit's B operand
@@ -52,7 +60,8 @@ struct TailSmem {
   static constexpr int kQ = 3 * kTailBuf;
   static constexpr int kA = 4 * kTailBuf;
   static constexpr int kW = kA + kTailA;
-  static constexpr int kCoefs = kW + 3 * kTailW;                 // floats from here on
+  static constexpr int kCarry = kW + 3 * kTailW;                 // float[kCarryRows][32], plain rows
+  static constexpr int kCoefs = kCarry + kCarryRows * 128;       // floats from here on
   static constexpr int kUnitCoef = 0;                            // [3][kTailCoef]
   static constexpr int kPwBias = 3 * kTailCoef;                  // [3][32]
   static constexpr int kPreA = kPwBias + 3 * kTailC;             // [3][32]
@@ -88,11 +97,12 @@ __device__ __forceinline__ float4 hist_quad(const StateRef& st, const HistRef& h
   return ldg4(slot_base(st, code) + h.ring + row * h.width + 4 * q);
 }
 
-// Depthwise k=7 (dilation d) + Snake_post of rows [0, n_out) into the f16 A
-// operand, for this thread's chain of L rows in channel quad q.
+// Depthwise k=7 (dilation d) + Snake_post of A rows [0, n_out) into the f16 A
+// operand, A row i from p rows base + i + j*d (j = 0..6), for this thread's
+// chain of L rows in channel quad q.
 template <int L>
 __device__ __forceinline__ void depthwise_chains(const float* uc, const float* pbuf, uint8_t* aop, int rg, int q, int d,
-                                                 int n_out) {
+                                                 int n_out, int base) {
   const int i0 = (rg / d) * L * d + rg % d;
   if (i0 >= n_out) return;
   float4 w[7], win[7];
@@ -100,18 +110,31 @@ __device__ __forceinline__ void depthwise_chains(const float* uc, const float* p
   for (int j = 0; j < 7; ++j) w[j] = lds4(uc + j * 64 + 4 * q);
   const float4 bias = lds4(uc + 7 * 64 + 4 * q), al2 = lds4(uc + 8 * 64 + 4 * q), rc2 = lds4(uc + 9 * 64 + 4 * q);
 #pragma unroll
-  for (int j = 0; j < 6; ++j) win[j] = lds4(pbuf + swq(i0 + j * d, q));
+  for (int j = 0; j < 6; ++j) win[j] = lds4(pbuf + swq(base + i0 + j * d, q));
 #pragma unroll
   for (int c = 0; c < L; ++c) {
     const int i = i0 + c * d;
     if (i >= n_out) break;
-    win[6] = lds4(pbuf + swq(i + 6 * d, q));
+    win[6] = lds4(pbuf + swq(base + i + 6 * d, q));
     const float4 y = snake4(dw7<false>(w, win, bias), al2, rc2);
     *reinterpret_cast<uint2*>(aop + sw128_offset(i, 4 * q)) = make_uint2(pack_f16(y.x, y.y), pack_f16(y.z, y.w));
 #pragma unroll
     for (int j = 0; j < 6; ++j) win[j] = win[j + 1];
   }
 }
+
+// 32 lanes x 8 consecutive fp32 accumulator columns.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+}
+
+// First carry-buffer row of unit u's carried rows (u = 3: the final conv's).
+__device__ __forceinline__ constexpr int carry_off(int u) { return u == 0 ? 0 : u == 1 ? 6 : u == 2 ? 24 : 78; }
 
 __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_constant__ TailArgs a) {
   extern __shared__ uint8_t tail_smem_raw[];
@@ -121,6 +144,7 @@ __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_cons
   float* qbuf = reinterpret_cast<float*>(sm + TailSmem::kQ);
   uint8_t* aop = sm + TailSmem::kA;
   uint8_t* wop = sm + TailSmem::kW;
+  float* carry = reinterpret_cast<float*>(sm + TailSmem::kCarry);
   float* cf = reinterpret_cast<float*>(sm + TailSmem::kCoefs);
   int* misc = reinterpret_cast<int*>(sm + TailSmem::kMisc);
   float* obuf = reinterpret_cast<float*>(sm + TailSmem::kOut);
@@ -132,7 +156,12 @@ __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_cons
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int N = a.rows_per_stream;
   const int num_tiles = a.rows / kTailRows;
-  constexpr uint32_t kBoxBytes = kTailIn * 128;
+  // This CTA's contiguous range of tiles: consecutive tiles of one stream
+  // carry each unit's last 6d input rows (and the final conv's last six) in
+  // shared memory instead of recomputing them. Only a range that starts inside
+  // a stream recomputes its first tile's 84-row halo from x.
+  const int t_begin = (int)((long long)blockIdx.x * num_tiles / gridDim.x);
+  const int t_end = (int)((long long)(blockIdx.x + 1) * num_tiles / gridDim.x);
 
   // ---- one-time setup: barriers, TMEM, coefficients and weights
   if (tid == 0) {
@@ -169,26 +198,34 @@ __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_cons
   const uint32_t tmem = *tmem_slot;
   grid_dependency_sync();  // plan constants above; the stage input and histories below
 
-  if (tid == 0 && blockIdx.x < num_tiles) {
-    mbar_arrive_expect_tx(&xfull[0], kBoxBytes);
-    tma_load_2d(xbuf[0], &a.xmap, 0, (int)blockIdx.x * kTailRows - kTailHalo, &xfull[0]);
-  }
+  // x of tile t into buffer b: a warm tile (its 84-row halo recomputed) takes
+  // relative rows [-84, 128) into buffer rows [0, 212); any other tile rows
+  // [-4, 128) into buffer rows [80, 212) (row 80: a 1024-byte boundary of the
+  // swizzled buffer).
+  auto load_x = [&](int t, int b, bool warm) {
+    if (warm) {
+      mbar_arrive_expect_tx(&xfull[b], kBoxBytes);
+      tma_load_2d(xbuf[b], &a.xmap, 0, t * kTailRows - kTailHalo, &xfull[b]);
+    } else {
+      mbar_arrive_expect_tx(&xfull[b], kCompactBoxBytes);
+      tma_load_2d(xbuf[b] + kCompactRow0 * 32, &a.xmap_c, 0, t * kTailRows - (kTailHalo - kCompactRow0), &xfull[b]);
+    }
+  };
+  if (tid == 0 && t_begin < t_end) load_x(t_begin, 0, (t_begin * kTailRows) % N != 0);
 
   bool ok = true;
   bool issued_next = false;  // this iteration started the next tile's x load
   uint32_t n_mma = 0;
   int k = 0;
-  for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++k) {
+  for (int t = t_begin; t < t_end && ok; ++t, ++k) {
     const int buf = k & 1;
     const int m0 = t * kTailRows;
     const int s = m0 / N, t0 = m0 - s * N;  // stream and its first time step in this tile
     const bool first = t0 == 0, last = t0 + kTailRows == N;
+    const bool warm = k == 0 && !first;  // the range starts inside a stream: halo recomputed
     // Next tile's x into the other buffer (free: the previous tile has ended).
-    issued_next = t + (int)gridDim.x < num_tiles;
-    if (tid == 0 && issued_next) {
-      mbar_arrive_expect_tx(&xfull[buf ^ 1], kBoxBytes);
-      tma_load_2d(xbuf[buf ^ 1], &a.xmap, 0, (t + (int)gridDim.x) * kTailRows - kTailHalo, &xfull[buf ^ 1]);
-    }
+    issued_next = t + 1 < t_end;
+    if (tid == 0 && issued_next) load_x(t + 1, buf ^ 1, false);
     // Stream slot and window heads (units 0-2, final), when the tile reads or writes a window.
     if (tid < 4 && (first || last)) {
       const int code = stream_code(a.state, s);
@@ -205,54 +242,62 @@ __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_cons
     for (int u = 0; u < 3; ++u) {
       const int d = u == 0 ? 1 : u == 1 ? 3 : 9, H = 6 * d;
       const int in_off = u == 0 ? 84 : u == 1 ? 78 : 60;  // input buffer row of relative row 0
-      const int n_in = kTailRows + in_off;      // input rows
-      const int n_out = n_in - H;               // depthwise / projection rows
+      const int hb = in_off - H;                          // buffer row of relative row -H
       const float* in = u == 1 ? qbuf : xb;     // unit input y (x for unit 0)
       float* out = u == 0 ? qbuf : u == 1 ? xb : qbuf;  // y1 -> q, y2 -> x buffer, Snake_f(y3) -> q
       const HistRef& hist = a.unit[u].hist;
       const float* uc = cf + TailSmem::kUnitCoef + u * kTailCoef;
-      // (a) p = Snake_pre(input) (units 1 and 2: written by the previous
-      // unit's epilogue); a stream's first tile takes the rows before the
-      // stream from the history window.
-      // Each thread keeps one channel quad (q = tid % 8) in (a) and (b).
+      // A warm tile computes relative rows [H - in_off, 128) (its halo too:
+      // two M tiles), A row i = relative row i + H - in_off; any other tile
+      // relative rows [0, 128) (one M tile), A row i = relative row i.
+      const int n_out = warm ? kTailRows + in_off - H : kTailRows;
+      const int a_base = warm ? 0 : hb;  // p row of A row 0's oldest tap
       const int q = tid & 7, rg = tid >> 3;
+      // (a) p = Snake_pre(input) over the rows this tile computes (units 1 and
+      // 2: written by the previous unit's epilogue), and the H rows before
+      // relative row 0: the history window at a stream's first tile, the
+      // previous tile's carried rows inside a stream.
       if (u == 0) {
         const float4 pa = lds4(cf + TailSmem::kPreA + 4 * q);
         const float4 pr = lds4(cf + TailSmem::kPreR + 4 * q);
-        for (int i = rg; i < n_in; i += kTailThreads / 8)
+        for (int i = (warm ? 0 : in_off) + rg; i < kTailIn; i += kTailThreads / 8)
           *reinterpret_cast<float4*>(pbuf + swq(i, q)) = snake4(lds4(in + swq(i, q)), pa, pr);
       }
       if (first) {
-        if (u == 0) __syncthreads();
-        for (int i = in_off - H + rg; i < in_off; i += kTailThreads / 8)
-          *reinterpret_cast<float4*>(pbuf + swq(i, q)) = hist_quad(a.state, hist, code, misc[u], i - in_off, q);
+        for (int j = rg; j < H; j += kTailThreads / 8)
+          *reinterpret_cast<float4*>(pbuf + swq(hb + j, q)) = hist_quad(a.state, hist, code, misc[u], j - H, q);
+      } else if (!warm) {
+        for (int j = rg; j < H; j += kTailThreads / 8)
+          *reinterpret_cast<float4*>(pbuf + swq(hb + j, q)) = lds4(carry + (carry_off(u) + j) * 32 + 4 * q);
       }
-      if (u == 0 || first) __syncthreads();
-      // (b) A = Snake_post(depthwise(p)) in f16; the stream's last tile also
-      // writes the new window (the last H rows of p).
-      // A thread's rows form a chain i0, i0 + d, ... (blocks of L*d rows split
-      // into d chains of L), so the seven taps slide through registers: L = 4
-      // covers unit 0's 206 rows with 64 row groups, L = 3 the others'.
-      if (u == 0) {
-        depthwise_chains<4>(uc, pbuf, aop, rg, q, 1, n_out);
+      __syncthreads();
+      // (b) A = Snake_post(depthwise(p)) in f16. A thread's rows form a chain
+      // i0, i0 + d, ... (blocks of L*d rows split into d chains of L), so the
+      // seven taps slide through registers: L = 4 covers a warm unit 0's 206
+      // rows with 64 row groups, L = 2 a carried unit 0's 128, L = 3 the others.
+      if (warm && u == 0) {
+        depthwise_chains<4>(uc, pbuf, aop, rg, q, 1, n_out, a_base);
+      } else if (u == 0) {
+        depthwise_chains<2>(uc, pbuf, aop, rg, q, 1, n_out, a_base);
       } else {
-        depthwise_chains<3>(uc, pbuf, aop, rg, q, d, n_out);
+        depthwise_chains<3>(uc, pbuf, aop, rg, q, d, n_out, a_base);
       }
-      if (last && a.state.pool && tid < H * 8) {
-        const int m = tid >> 3, q = tid & 7;  // window row m = time N - H + m
-        *reinterpret_cast<float4*>(hist_new_row(a.state, hist, code, misc[u], N - H + m, N) + 4 * q) =
-            lds4(pbuf + swq(in_off + kTailRows - H + m, q));
+      // The unit's last H input rows: carried to the next tile, and at the
+      // stream's last tile the new history window.
+      for (int j = rg; j < H; j += kTailThreads / 8) {
+        const float4 v = lds4(pbuf + swq(in_off + kTailRows - H + j, q));
+        *reinterpret_cast<float4*>(carry + (carry_off(u) + j) * 32 + 4 * q) = v;
+        if (last && a.state.pool) *reinterpret_cast<float4*>(hist_new_row(a.state, hist, code, misc[u], N - H + j, N) + 4 * q) = v;
       }
       fence_async_smem();
       tc_fence_before();
       __syncthreads();
-      // (c) D[mt] = A[mt] W^T for the two 128-row M tiles, K = 32 (two K = 16 steps).
+      // (c) D[mt] = A[mt] W^T for the M tiles, K = 32 (two K = 16 steps).
       if (tid == 0) {
         tc_fence_after();
         const uint32_t a0 = smem_u32(aop), b0 = smem_u32(wop + u * kTailW);
         constexpr uint32_t idesc = instr_desc_f16(0u, kTailC);
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
+        for (int mt = 0; mt < (warm ? 2 : 1); ++mt)
 #pragma unroll
           for (int ks = 0; ks < 2; ++ks)
             mma_f16(tmem + mt * kTailC, smem_desc_sw128(a0 + mt * kTileM * 128 + ks * 32),
@@ -263,44 +308,58 @@ __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_cons
       ++n_mma;
       tc_fence_after();
       if (!ok) break;
-      // (d) y = input + (D + b) for rows [0, n_out), with Snake_pre of the next
-      // unit into p (the next unit's input rows); unit 2 keeps Snake_final(y).
-      {
-        const int lq = warp & 3, mt = (warp >> 2) & 1, half = warp >> 3;
+      // (d) y = input + (D + b), with Snake_pre of the next unit into p (the
+      // next unit's input rows); unit 2 keeps Snake_final(y). A row i lands
+      // in buffer row a_base + i of the output (whose relative row 0 is at
+      // in_off - H) and reads its skip from input row a_base + i + H.
+      const int lq = warp & 3;
+      const float* pb = cf + TailSmem::kPwBias + u * kTailC;
+      auto finish = [&](int i, int q4, const uint32_t* r) {
+        const int ob = a_base + i;  // out / p buffer row of A row i
+        const float4 b = lds4(pb + 4 * q4);
+        const float4 x = lds4(in + swq(ob + H, q4));
+        float4 y = make_float4(x.x + (__uint_as_float(r[0]) + b.x), x.y + (__uint_as_float(r[1]) + b.y),
+                               x.z + (__uint_as_float(r[2]) + b.z), x.w + (__uint_as_float(r[3]) + b.w));
+        if (u == 2) {
+          y = snake4(y, lds4(cf + TailSmem::kFinA + 4 * q4), lds4(cf + TailSmem::kFinR + 4 * q4));
+        } else {
+          *reinterpret_cast<float4*>(pbuf + swq(ob, q4)) =
+              snake4(y, lds4(cf + TailSmem::kPreA + (u + 1) * kTailC + 4 * q4),
+                     lds4(cf + TailSmem::kPreR + (u + 1) * kTailC + 4 * q4));
+        }
+        *reinterpret_cast<float4*>(out + swq(ob, q4)) = y;
+      };
+      if (warm) {
+        const int mt = (warp >> 2) & 1, half = warp >> 3;
         const int i = mt * kTileM + lq * 32 + lane;
         uint32_t r[16];
         tmem_ld16_async(tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(mt * kTailC + half * 16), r);
         tmem_wait_ld(r);
         if (i < n_out) {
-          const float* pb = cf + TailSmem::kPwBias + u * kTailC;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int q = half * 4 + j;
-            const float4 b = lds4(pb + 4 * q);
-            const float4 x = lds4(in + swq(i + H, q));
-            float4 y = make_float4(x.x + (__uint_as_float(r[4 * j]) + b.x), x.y + (__uint_as_float(r[4 * j + 1]) + b.y),
-                                   x.z + (__uint_as_float(r[4 * j + 2]) + b.z), x.w + (__uint_as_float(r[4 * j + 3]) + b.w));
-            if (u == 2) {
-              y = snake4(y, lds4(cf + TailSmem::kFinA + 4 * q), lds4(cf + TailSmem::kFinR + 4 * q));
-            } else {
-              *reinterpret_cast<float4*>(pbuf + swq(i, q)) =
-                  snake4(y, lds4(cf + TailSmem::kPreA + (u + 1) * kTailC + 4 * q),
-                         lds4(cf + TailSmem::kPreR + (u + 1) * kTailC + 4 * q));
-            }
-            *reinterpret_cast<float4*>(out + swq(i, q)) = y;
-          }
+          for (int j = 0; j < 4; ++j) finish(i, half * 4 + j, r + 4 * j);
         }
+      } else {
+        // One M tile: 16 warps as 4 lane quarters x 4 groups of 8 columns.
+        const int cg = warp >> 2;
+        uint32_t r[8];
+        tmem_ld8(tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(cg * 8), r);
+        const int i = lq * 32 + lane;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) finish(i, cg * 2 + j, r + 4 * j);
       }
       tc_fence_before();
       __syncthreads();
     }
     if (!ok) break;
     // Final conv over q = Snake_final(y3), rows [0, 134) = relative [-6, 128):
-    // a stream's first tile takes rows [0, 6) from the final history; its last
-    // tile writes the new window (relative rows [122, 128)).
-    if (first && tid < 48) {
+    // rows [0, 6) from the final history at a stream's first tile, from the
+    // previous tile inside a stream (computed by a warm tile); the last six
+    // rows are carried on, and written as the new window at the stream's end.
+    if (tid < 48 && !warm) {
       const int m = tid >> 3, q = tid & 7;
-      *reinterpret_cast<float4*>(qbuf + swq(m, q)) = hist_quad(a.state, a.fin_hist, code, misc[3], m - 6, q);
+      *reinterpret_cast<float4*>(qbuf + swq(m, q)) =
+          first ? hist_quad(a.state, a.fin_hist, code, misc[3], m - 6, q) : lds4(carry + (carry_off(3) + m) * 32 + 4 * q);
     }
     if (last && a.state.pool && tid >= 64 && tid < 64 + 48) {
       const int m = (tid - 64) >> 3, q = (tid - 64) & 7;
@@ -339,6 +398,11 @@ __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_cons
         // The reference checks the audio is finite (gpu.py:182-184).
         if (!(fabsf(y) <= 1.f)) record_error(a.status, kDevNonFinite);
         obuf[o] = y;
+      }
+      // The final conv's last six rows, carried to the next tile.
+      if (tid >= 128 && tid < 128 + 48) {
+        const int m = (tid - 128) >> 3, q = (tid - 128) & 7;
+        *reinterpret_cast<float4*>(carry + (carry_off(3) + m) * 32 + 4 * q) = lds4(qbuf + swq(kTailRows + m, q));
       }
     }
     fence_async_smem();  // this tile's generic writes to the x buffer precede the next TMA into it
