@@ -768,7 +768,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   constexpr bool kTmaA = (KIND == kTconv && !kI8) || KIND == kResidualPre || KIND == kTconvPre;
   constexpr int kLpr = NT == 32 ? 8 : 16;  // residual lanes per row (C = 32 uses eight)
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Aligned by an offset from the shared array (not through an integer), so
+  // the compiler keeps every access through it in the shared state space.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* a_base = smem;
   uint8_t* b_base = a_base + S * Cfg::kAStage;
   float* epi_coef = reinterpret_cast<float*>(b_base + S * Cfg::kBStage);  // [2][kEpiCoefVectors][NT]

@@ -138,7 +138,9 @@ __device__ __forceinline__ constexpr int carry_off(int u) { return u == 0 ? 0 : 
 
 __global__ void __launch_bounds__(kTailThreads, 1) tail_kernel(const __grid_constant__ TailArgs a) {
   extern __shared__ uint8_t tail_smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tail_smem_raw) + 1023) & ~uintptr_t(1023));
+  // Aligned by an offset from the shared array (not through an integer), so
+  // the compiler keeps every access through it in the shared state space.
+  uint8_t* sm = tail_smem_raw + ((1024u - (smem_u32(tail_smem_raw) & 1023u)) & 1023u);
   float* xbuf[2] = {reinterpret_cast<float*>(sm + TailSmem::kX0), reinterpret_cast<float*>(sm + TailSmem::kX1)};
   float* pbuf = reinterpret_cast<float*>(sm + TailSmem::kP);
   float* qbuf = reinterpret_cast<float*>(sm + TailSmem::kQ);
