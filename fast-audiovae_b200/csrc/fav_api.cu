@@ -612,7 +612,6 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       ta.state = state;
       ta.status = status;
       if ((es = encode_tail_map(&ta.xmap, X[0], ta.rows, fav::kTailBoxRows)) != FAV_OK) return es;
-      if ((es = encode_tail_map(&ta.xmap_c, X[0], ta.rows, fav::kTailCompactBoxRows)) != FAV_OK) return es;
       if ((e = fav::launch_tail(ta, stream)) != cudaSuccess) return cuda_fail(e, "tail launch");
       // The fused kernel's time counts as stage 5's first residual unit.
       for (int l = 23; l <= 26; ++l) mark(l);

@@ -190,13 +190,10 @@ struct TailUnitArgs {
   const uint8_t* wimg;   // 1x1 weights, 32 rows x 128 B (f16, K-major, 128-byte swizzle)
   HistRef hist;          // window of Snake_pre(input), 6 * dilation rows
 };
-// Rows of the fused tail's x boxes: a tile whose 84-row halo is recomputed
-// takes relative rows [-84, 128); a tile whose halo is carried, [-4, 128).
-constexpr int kTailBoxRows = 212;
-constexpr int kTailCompactBoxRows = 132;
+// Rows of the fused tail's x boxes: one 128-row tile.
+constexpr int kTailBoxRows = 128;
 struct TailArgs {
   CUtensorMap xmap;      // stage input y [rows][32] fp32: boxes of 32 x kTailBoxRows, 128-byte swizzle
-  CUtensorMap xmap_c;    // the same tensor in boxes of 32 x kTailCompactBoxRows
   int rows;              // all streams' rows (multiple of 128)
   int rows_per_stream;   // multiple of 128
   TailUnitArgs unit[3];
