@@ -703,7 +703,8 @@ def ingest_ncu(path):
         rows.setdefault(key, {"name": rec["Kernel Name"]})
         unit = rec["Metric Unit"]
         val = float(rec["Metric Value"].replace(",", ""))
-        scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "nsecond": 1e-3, "usecond": 1, "msecond": 1e3}
+        scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "ns": 1e-3, "nsecond": 1e-3, "us": 1, "usecond": 1,
+                 "ms": 1e3, "msecond": 1e3}
         rows[key][rec["Metric Name"]] = val * scale.get(unit, 1)
     launches = [rows[k] for k in sorted(rows, key=int)]
     if len(launches) != len(LAUNCH_ORDER):
@@ -712,7 +713,7 @@ def ingest_ncu(path):
     for name, rec in zip(LAUNCH_ORDER, launches):
         layers[name] = layers.get(name, 0) + int(rec.get("dram__bytes_read.sum", 0) + rec.get("dram__bytes_write.sum", 0))
     out = {"workload": "stream40ms", "streams": 512, "frames": 1,
-           "source": "ncu launch list of one step of `python bench.py --steps 3 --warmup 3 --no-cpu-baseline` "
+           "source": "ncu launch list of one step of `python bench.py --steps 2 --warmup 3 --no-cpu-baseline` "
                      "(profiles/step_launches_stream40ms_512.md)",
            "layers": layers}
     TRAFFIC_FILE.write_text(json.dumps(out, indent=1) + "\n")
