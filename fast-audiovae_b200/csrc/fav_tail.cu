@@ -355,33 +355,43 @@ __global__ void __launch_bounds__(kThreads, 512 / kThreads) tail_kernel(const __
     }
     if (!ok) break;
     // Final conv over Q = Snake_final(y3), rows [0, 134) = relative [-6, 128).
-    // Four lanes per output row, eight channels each: one accumulator per
-    // channel of a quad (taps oldest first), summed in a fixed tree.
-    for (int o = tid >> 2; o < kTailRows; o += kThreads / 4) {
-      const int grp = tid & 3;
+    // Each row group of eight lanes (one channel quad each) walks a chain of
+    // consecutive output rows with the seven taps sliding through registers:
+    // one accumulator per channel (taps oldest first), then the quad's sum and
+    // a butterfly over the eight lanes, which leaves every lane the same total.
+    {
+      constexpr int L = kTailRows / kGroups;
       const float* fw = cf + TailSmem::kFinW;
-      float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 w[7], win[7];
 #pragma unroll
-      for (int j = 0; j < 7; ++j) {
+      for (int j = 0; j < 7; ++j) w[j] = lds4(fw + j * kTailC + 4 * q);
 #pragma unroll
-        for (int qq = 0; qq < 2; ++qq) {
-          const int qd = 2 * grp + qq;
-          const float4 v = lds4(qbuf + swq(o + j, qd));
-          const float4 wj = lds4(fw + j * kTailC + 4 * qd);
-          acc4.x = fmaf(wj.x, v.x, acc4.x);
-          acc4.y = fmaf(wj.y, v.y, acc4.y);
-          acc4.z = fmaf(wj.z, v.z, acc4.z);
-          acc4.w = fmaf(wj.w, v.w, acc4.w);
+      for (int j = 0; j < 6; ++j) win[j] = lds4(qbuf + swq(rg * L + j, q));
+      const float fb = cf[TailSmem::kFinB];
+#pragma unroll
+      for (int c = 0; c < L; ++c) {
+        const int o = rg * L + c;
+        win[6] = lds4(qbuf + swq(o + 6, q));
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 7; ++j) {
+          acc.x = fmaf(w[j].x, win[j].x, acc.x);
+          acc.y = fmaf(w[j].y, win[j].y, acc.y);
+          acc.z = fmaf(w[j].z, win[j].z, acc.z);
+          acc.w = fmaf(w[j].w, win[j].w, acc.w);
         }
-      }
-      float acc = (acc4.x + acc4.y) + (acc4.z + acc4.w);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-      if (grp == 0) {
-        const float y = tanhf(acc + cf[TailSmem::kFinB]);
-        // The reference checks the audio is finite (gpu.py:182-184).
-        if (!discard && !(fabsf(y) <= 1.f)) record_error(a.status, kDevNonFinite);
-        obuf[o] = y;
+        float sum = (acc.x + acc.y) + (acc.z + acc.w);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        if (q == 0) {
+          const float y = tanhf(sum + fb);
+          // The reference checks the audio is finite (gpu.py:182-184).
+          if (!discard && !(fabsf(y) <= 1.f)) record_error(a.status, kDevNonFinite);
+          obuf[o] = y;
+        }
+#pragma unroll
+        for (int j = 0; j < 6; ++j) win[j] = win[j + 1];
       }
     }
     // The final conv's last six input rows (relative [122, 128)): carried on,
