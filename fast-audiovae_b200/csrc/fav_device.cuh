@@ -23,8 +23,11 @@ enum DeviceError : uint32_t {
 };
 
 // A wait that has not completed after this many polls is a bug; the kernel
-// records the error and returns instead of spinning forever.
-constexpr uint32_t kWaitLimit = 1u << 24;
+// records the error and returns instead of spinning forever. Each poll may
+// suspend the warp for up to kSuspendNs (it resumes when the phase completes),
+// so a wait gives up after at most ~kWaitLimit * kSuspendNs (about 2.6 s).
+constexpr uint32_t kWaitLimit = 1u << 18;
+constexpr uint32_t kSuspendNs = 10000;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -54,9 +57,9 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
