@@ -50,6 +50,7 @@ import json
 import os
 import subprocess
 import sys
+import threading
 import time
 from dataclasses import dataclass
 from pathlib import Path
@@ -247,12 +248,38 @@ def kernel_ms(layer_ms26):
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
+    """SM clock and clock-event reasons of one GPU while the timed region runs:
+    read through NVML (read-only queries) every 5 ms from a background thread,
+    so a timed region of tens of milliseconds still gets several samples;
+    ``nvidia-smi -lms 100`` is the fallback when NVML cannot be used."""
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits (nvmlClocksEventReason*)
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
     def __init__(self, index):
-        self.proc = None
+        self.proc = self.thread = None
+        self.rows, self.done = [], threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            handle = self._handle(pynvml, index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+
+            def run():
+                while not self.done.is_set():
+                    self.rows.append((float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)),
+                                      int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))))
+                    self.done.wait(0.005)
+            self.rows.append((float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)),
+                              int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))))
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            return
+        except Exception:  # no NVML binding or device: the nvidia-smi loop instead
+            self.rows = []
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
                                           "-lms", "100", "-i", str(index)], stdout=subprocess.PIPE,
@@ -260,7 +287,28 @@ class ClockSampler:
         except (OSError, FileNotFoundError):
             self.proc = None
 
+    @staticmethod
+    def _handle(pynvml, index):
+        """NVML handle of CUDA device ``index`` (by UUID; the index as listed
+        in CUDA_VISIBLE_DEVICES otherwise)."""
+        import torch
+        try:
+            return pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + str(torch.cuda.get_device_properties(index).uuid)).encode())
+        except Exception:
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+            if index < len(visible) and visible[index].strip().isdigit():
+                index = int(visible[index])
+            return pynvml.nvmlDeviceGetHandleByIndex(index)
+
     def stop(self):
+        if self.thread is not None:
+            self.done.set()
+            self.thread.join(timeout=5)
+            rows = list(self.rows)
+            busy = [mhz for mhz, _ in rows if mhz > 0]
+            reasons = sorted({name for _, bits in rows for name, bit in self.REASONS if bits & bit})
+            return {"sm_mhz": float(np.median(busy)) if busy else None, "sm_max_mhz": self.max_mhz,
+                    "reasons": reasons, "samples": len(rows), "source": "nvml, 5 ms"}
         if not self.proc:
             return None
         self.proc.terminate()
@@ -281,7 +329,7 @@ class ClockSampler:
                     reasons.add(name)
         busy = [v for v in sm if v > 0]
         return {"sm_mhz": float(np.median(busy)) if busy else None, "sm_max_mhz": float(rows[0][2]),
-                "reasons": sorted(reasons), "samples": len(rows)}
+                "reasons": sorted(reasons), "samples": len(rows), "source": "nvidia-smi, 100 ms"}
 
 
 # ------------------------------------------------------------------ CPU legs
@@ -448,22 +496,23 @@ def count_kernels(torch, launch):
     return int(kernels)
 
 
-def profile_layers(lib, _native, plan, S, F, z_dev, audio, ws, ws_bytes, status, stream, reps=5):
-    """Per-kernel CUDA-event durations (ms) of a step of S streams x F frames."""
+def profile_layers(lib, _native, plan, S, F, z_dev, audio, ws, ws_bytes, status, stream, reps=20, warm=3):
+    """Per-kernel CUDA-event durations (ms) of a step of S streams x F frames:
+    the median over ``reps`` profiled steps after ``warm`` uncounted ones."""
     import torch
     pool = torch.zeros(lib.fav_state_pool_bytes(S) // 4, device="cuda")
     fresh = torch.tensor([(s << 2) | 2 for s in range(S)], dtype=torch.int32, device="cuda")
     parity = [torch.tensor([(s << 2) | p for s in range(S)], dtype=torch.int32, device="cuda") for p in (0, 1)]
     P = lambda t: ct.c_void_p(t.data_ptr())
     buf = (ct.c_float * 26)()
-    acc = np.zeros(26)
-    for r in range(reps + 1):  # call 0 starts the streams (fresh) and is not counted; call r reads table r % 2
+    runs = []
+    for r in range(warm + reps):  # call 0 starts the streams (fresh); call r reads table r % 2
         codes = fresh if r == 0 else parity[r & 1]
         _native.check(lib, lib.fav_step_profile(plan.handle, P(pool), S, P(codes), S, F, P(z_dev), P(audio), P(ws),
                                                 ws_bytes, P(status), buf, stream))
-        if r:
-            acc += np.array(buf[:])
-    return kernel_ms(acc / reps)
+        if r >= warm:
+            runs.append(np.array(buf[:]))
+    return kernel_ms(np.median(np.stack(runs), axis=0))
 
 
 def run_stream(args, wl, world, rank, local):
