@@ -79,6 +79,14 @@ int32_t encode_input_map(CUtensorMap* map, const float* x, int rows, int channel
   return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_NONE, "input");
 }
 
+// f16 residual input s [rows][channels] (Snake_pre(y) written by the previous
+// epilogue with kEpiS16): boxes of 64 channels (128 bytes) x box_rows rows.
+int32_t encode_input_map_f16(CUtensorMap* map, const void* s, int rows, int channels, int box_rows) {
+  const cuuint64_t dims[2] = {(cuuint64_t)channels, (cuuint64_t)rows};
+  const cuuint32_t box[2] = {(cuuint32_t)fav::kKBlock, (cuuint32_t)box_rows};
+  return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, s, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_NONE, "s16");
+}
+
 // Split-bf16 planes [2][rows][channels] (hi, then lo) of a transposed conv's
 // activated input, loaded in 64 x 128 x 2 boxes (hi tile, then lo tile) in the
 // 128-byte swizzle, which is the MMA's K-major A layout.
@@ -537,10 +545,10 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     t.kind = fav::kTconv;
     t.mode = fav::kModeSplit;
     const bool into_tail = tail && i + 1 == fav::kStages;
-    // Stages 2-4 of a bf16 plan: the residual units read y and apply their first
-    // Snake themselves (pre_snake), so this conv and units 0-1 write y only.
-    const bool x_only = p->precision == FAV_PRECISION_BF16 && i >= 2 && i + 1 < fav::kStages;
-    t.epi = fav::kEpiX | (into_tail || x_only ? 0 : fav::kEpiS);
+    // Stages 2-4 of a bf16 plan: this conv and units 0-1 write the next unit's
+    // Snake_pre(y) in f16 (kEpiS16), which the unit's producers stage as is.
+    const bool s16 = p->precision == FAV_PRECISION_BF16 && i >= 2 && i + 1 < fav::kStages;
+    t.epi = fav::kEpiX | (into_tail ? 0 : s16 ? fav::kEpiS16 : fav::kEpiS);
     t.rows = n_streams * n;
     t.rows_per_stream = n;
     t.k_channels = st.c_in;
@@ -653,10 +661,8 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       const bool debug_y = layer + 1 == last_layer;
       u.out_x = X[out];
       u.out_s = S[out];
-      if (j < 2 && x_only) {
-        u.epi = fav::kEpiX;
-      } else if (j < 2) {
-        u.epi = fav::kEpiX | fav::kEpiS;
+      if (j < 2) {
+        u.epi = fav::kEpiX | (s16 ? fav::kEpiS16 : fav::kEpiS);
         u.next_alpha = st.res[j + 1].pre_a;
         u.next_recip = st.res[j + 1].pre_r;
       } else if (i + 1 < fav::kStages) {
@@ -689,9 +695,9 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
         if ((e = fav::launch_depthwise(dw, stream)) != cudaSuccess) return cuda_fail(e, "depthwise launch");
         u.kind = fav::kResidualPre;
         if ((es = encode_operand_map(&u.tmap, a_op, u.rows, st.c_out)) != FAV_OK) return es;
-      } else if (x_only) {
-        u.pre_snake = 1;
-        if ((es = encode_input_map(&u.tmap, X[in], u.rows, st.c_out, u.box_rows)) != FAV_OK) return es;
+      } else if (s16) {
+        u.s16 = 1;
+        if ((es = encode_input_map_f16(&u.tmap, S[in], u.rows, st.c_out, u.box_rows)) != FAV_OK) return es;
       } else if ((es = encode_input_map(&u.tmap, S[in], u.rows, st.c_out, u.box_rows)) != FAV_OK) {
         return es;
       }

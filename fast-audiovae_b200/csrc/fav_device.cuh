@@ -98,6 +98,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Bulk prefetch of a global range into L2 (no shared memory involved).
+// Address 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // 2-D TMA tile load (no multicast) of the box at coordinates (x = innermost,
 // y) into own shared memory, completion counted on ``bar``. Out-of-range
 // coordinates read as zero. ``map`` must live in param/const/global space.

@@ -75,6 +75,8 @@ enum EpilogueFlags : int {
                    // stream's first row holds the next layer's history), and the next layer's history
   kEpiAct = 16,    // int8 path: Snake(y * next_scale + next_offset) fp32 to out_s, this tile's per-row max of
                    // its magnitude to rowmax_out[row * rowmax_parts + n_tile], and the next layer's history
+  kEpiS16 = 32,    // Snake(y) with next_alpha/next_recip rounded to f16, to out_s read as f16 (same layout
+                   // as kEpiS at half the bytes)
 };
 
 struct LayerArgs {
@@ -127,6 +129,10 @@ struct LayerArgs {
   // written by the previous epilogue); the producers apply Snake_pre (alpha1,
   // recip1) to each staged row once, in shared memory, before the depthwise conv.
   int pre_snake;
+  // Residual: the staged input is s = Snake_pre(y) in f16 (written by the
+  // previous epilogue with kEpiS16; boxes of 64 channels x box_rows rows, 128
+  // bytes per row); the producers read the box as is.
+  int s16;
   const float* next_scale;  // coefficients of the pointwise prologue the epilogue applies
   const float* next_offset;
   const float* next_alpha;

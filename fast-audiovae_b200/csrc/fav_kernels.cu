@@ -517,6 +517,32 @@ __device__ __forceinline__ void load_tile_history(const LayerArgs& a, int m0, in
 // (row, channel quad) per thread. ``hist_writer``: this N tile writes
 // the new window rows of streams ending in the tile (first, from the box).
 // Producer-collective (named barrier 2).
+// Channel quad k .. k+3 of box row r of a residual producer's staged input:
+// fp32 rows of 64 channels, or (S16) f16 rows of 64 channels.
+template <bool S16>
+__device__ __forceinline__ float4 box_quad(const float* raw, int r, int k) {
+  if constexpr (S16) {
+    const uint2 h = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(raw) + r * kKBlock + k);
+    const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+    const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
+  } else {
+    return lds4(raw + r * kKBlock + k);
+  }
+}
+// Stores a quad into box row r (S16: rounded to f16; exact for history rows,
+// which hold f16 values).
+template <bool S16>
+__device__ __forceinline__ void put_box_quad(float* raw, int r, int k, float4 v) {
+  if constexpr (S16) {
+    *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(raw) + r * kKBlock + k) =
+        make_uint2(pack_f16(v.x, v.y), pack_f16(v.z, v.w));
+  } else {
+    *reinterpret_cast<float4*>(raw + r * kKBlock + k) = v;
+  }
+}
+
+template <bool S16>
 __device__ void produce_residual_y(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, float* raw, int warp,
                                    int lane, bool hist_writer, const StreamTable& tab, uint32_t walk_lo,
                                    uint32_t walk_hi, int ubreak, const TileStart& ts) {
@@ -539,7 +565,7 @@ __device__ void produce_residual_y(const LayerArgs& a, int m0, int kb, uint8_t* 
       const int row = rem / (P / 4), k4 = 4 * (rem - row * (P / 4));
       const int tp = N - H + row;
       *reinterpret_cast<float4*>(hist_new_row(a.state, a.hist, tab.code[e], tab.head[e], tp, N) + kb * kKBlock + k4) =
-          lds4(raw + ((tab.s_lo + e) * N + tp - m0 + H) * P + k4);
+          box_quad<S16>(raw, (tab.s_lo + e) * N + tp - m0 + H, k4);
     }
     if (kb == 0)
       for (int e = tid; e < ns; e += kProducerThreads) hist_commit_head(a.state, a.hist, tab.code[e], tab.head[e], N);
@@ -557,9 +583,9 @@ __device__ void produce_residual_y(const LayerArgs& a, int m0, int kb, uint8_t* 
       const int r = u < ubreak ? r0 + u * d : r1 + (u - ubreak) * d;
       if (u == 0 || u == ubreak) {
 #pragma unroll
-        for (int j = 0; j < 6; ++j) win[j] = lds4(raw + (r - (6 - j) * d + H) * P + kl);
+        for (int j = 0; j < 6; ++j) win[j] = box_quad<S16>(raw, r - (6 - j) * d + H, kl);
       }
-      win[6] = lds4(raw + (r + H) * P + kl);
+      win[6] = box_quad<S16>(raw, r + H, kl);
       put_a4<kModeF16>(a_stage, r, kl, snake4(dw7<false>(w, win, bias), al2, rc2));
 #pragma unroll
       for (int j = 0; j < 6; ++j) win[j] = win[j + 1];
@@ -577,7 +603,7 @@ __device__ void produce_residual_y(const LayerArgs& a, int m0, int kb, uint8_t* 
   for (int k = 0; k < 4; ++k) {
     const int it = tid + k * kProducerThreads;
     const int j = it >> 4;  // history row; quad = it & 15 = q
-    if (j < H && pos0 + j >= 0) *reinterpret_cast<float4*>(raw + (pos0 + j) * P + 4 * (it & 15)) = hist_reg[k];
+    if (j < H && pos0 + j >= 0) put_box_quad<S16>(raw, pos0 + j, 4 * (it & 15), hist_reg[k]);
   }
   named_barrier(2, kProducerThreads);
   const int lo = max(ts.b, m0) - m0, hi = min(min(ts.b + H, m0 + kTileM), a.rows) - m0;
@@ -587,7 +613,7 @@ __device__ void produce_residual_y(const LayerArgs& a, int m0, int kb, uint8_t* 
 #pragma unroll
     for (int j = 0; j < 7; ++j) {
       wq[j] = lds4(raw + kResBoxBytes / 4 + k4 + j * 64);
-      win[j] = lds4(raw + (r - (6 - j) * d + H) * P + k4);
+      win[j] = box_quad<S16>(raw, r - (6 - j) * d + H, k4);
     }
     const float4 bq = lds4(raw + kResBoxBytes / 4 + k4 + 7 * 64);
     const float4 aq = lds4(raw + kResBoxBytes / 4 + k4 + 8 * 64), rq = lds4(raw + kResBoxBytes / 4 + k4 + 9 * 64);
@@ -750,7 +776,7 @@ constexpr int kEpiCoefVectors = 7;
 
 // --------------------------------------------------------------------- engine
 // Epilogue output class (besides y, written when the layer's kEpiX flag is set).
-enum EpilogueOut : int { kOutNone = 0, kOutS = 1, kOutPlanes = 2, kOutAct = 3 };
+enum EpilogueOut : int { kOutNone = 0, kOutS = 1, kOutPlanes = 2, kOutAct = 3, kOutS16 = 4 };
 
 template <int NT, int MODE, int KIND, int OUT>
 __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_constant__ LayerArgs a) {
@@ -928,16 +954,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
             produce_stem<MODE>(a, a_stage, warp, lane, write_state, tab);
           } else if (KIND == kResidual) {
             float* raw = reinterpret_cast<float*>(raw_base + rb * Cfg::kRaw);
-            if (kLpr == 16 && !kI8 && a.pre_snake) {
+            if (kLpr == 16 && !kI8 && (a.pre_snake || a.s16)) {
               const TileStart ts = tile_start(a, m0, tab);
               if (ts.on) {
                 float4 unused[4];
                 load_tile_history<true>(a, m0, kb, tab, ts, threadIdx.x, unused);
               }
-              snake_box(a, raw, threadIdx.x);
-              named_barrier(2, kProducerThreads);
-              produce_residual_y(a, m0, kb, a_stage, raw, warp, lane, kb % num_n == tile_n(t), tab, walk_lo, walk_hi,
-                                 ubreak, ts);
+              if (a.s16) {  // the box already holds Snake_pre(y) (f16)
+                produce_residual_y<true>(a, m0, kb, a_stage, raw, warp, lane, kb % num_n == tile_n(t), tab, walk_lo,
+                                         walk_hi, ubreak, ts);
+              } else {
+                snake_box(a, raw, threadIdx.x);
+                named_barrier(2, kProducerThreads);
+                produce_residual_y<false>(a, m0, kb, a_stage, raw, warp, lane, kb % num_n == tile_n(t), tab, walk_lo,
+                                          walk_hi, ubreak, ts);
+              }
             } else {
               produce_residual<MODE, kLpr>(a, m0, kb, a_stage, raw, warp, lane, kb % num_n == tile_n(t), tab,
                                            partial ? iwalk_lo : walk_lo, partial ? iwalk_hi : walk_hi, regular);
@@ -1038,6 +1069,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
           tq[k] = gr < a.rows ? gr - (gr / N) * N : -1;
         }
       }
+      // The tile's skip input rows into L2 while the accumulator is produced
+      // (one bulk prefetch per row), so the chunk loads below hit L2.
+      if (kSkipAdd && g < a.rows) prefetch_l2(a.x + (size_t)g * a.c_out + n0, NT * 4);
       float4 xr[4];  // skip input of the current chunk, coalesced order
       load_skip<KIND>(a, row0, n0, lane, xr);
       uint4 hw[4];  // stem: history bits of this chunk (zero without a history row)
@@ -1185,6 +1219,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
                 }
               }
               }
+            } else if constexpr (OUT == kOutS16) {
+              // f16 Snake output: this lane's row, 16 columns as 32 contiguous bytes.
+              if (g < a.rows) {
+                uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.out_s) + off0 + (size_t)lane * pitch);
+                dst[0] = make_uint4(pack_f16(s[0], s[1]), pack_f16(s[2], s[3]), pack_f16(s[4], s[5]), pack_f16(s[6], s[7]));
+                dst[1] = make_uint4(pack_f16(s[8], s[9]), pack_f16(s[10], s[11]), pack_f16(s[12], s[13]),
+                                    pack_f16(s[14], s[15]));
+              }
             } else {
               store_chunk(stage, lane, s, a.out_s + off0, pitch, a.rows - row0);
               if constexpr (kOutA) {
@@ -1298,7 +1340,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       // causal halo rows of s and the block's coefficients. int8 transposed
       // conv: per 64-channel half of a K block, input rows m0-1 .. m0+127.
       const int halo = KIND == kResidual ? a.box_rows - kTileM : 1;
-      const uint32_t bytes = KIND == kResidual ? (uint32_t)a.box_rows * a.raw_pitch * 4 + kResCoefBytes
+      const uint32_t bytes = KIND == kResidual ? (uint32_t)a.box_rows * a.raw_pitch * (a.s16 ? 2 : 4) + kResCoefBytes
                                                : (uint32_t)(kTileM + 1) * 64 * 4;
       const int boxes = KIND == kResidual ? (a.k_channels < kKBlock ? 1 : a.k_channels / kKBlock) : 2 * num_kb;
       uint32_t g = 0;
@@ -1468,6 +1510,8 @@ static cudaError_t set_smem() {
   X(256, kModeSplit, kTconv, kOutNone) X(128, kModeSplit, kTconv, kOutNone) X(64, kModeSplit, kTconv, kOutNone) \
   X(256, kModeF16, kResidual, kOutNone) X(128, kModeF16, kResidual, kOutNone) X(64, kModeF16, kResidual, kOutNone) \
   X(256, kModeF16, kResidual, kOutS) X(128, kModeF16, kResidual, kOutS) X(64, kModeF16, kResidual, kOutS)  \
+  X(256, kModeSplit, kTconv, kOutS16) X(128, kModeSplit, kTconv, kOutS16) X(64, kModeSplit, kTconv, kOutS16)   \
+  X(256, kModeF16, kResidual, kOutS16) X(128, kModeF16, kResidual, kOutS16) X(64, kModeF16, kResidual, kOutS16) \
   X(256, kModeF16, kResidualPre, kOutS) X(256, kModeF16, kResidualPre, kOutPlanes)                          \
   X(64, kModeF16, kResidualPre, kOutS) X(64, kModeF16, kResidualPre, kOutPlanes)                            \
   X(256, kModeI8, kResidualPre, kOutS) X(128, kModeI8, kResidualPre, kOutS)                                \
@@ -1497,7 +1541,8 @@ cudaError_t launch_gemm_layer(const LayerArgs& a, cudaStream_t stream) {
   if (a.rows <= 0) return cudaSuccess;
   if (a.n_total % a.n_tile) return cudaErrorInvalidValue;
   if (a.img_nt && (a.img_nt % a.n_tile || a.n_total % a.img_nt)) return cudaErrorInvalidValue;
-  const int out = (a.epi & kEpiPlanes) ? kOutPlanes : (a.epi & kEpiAct) ? kOutAct : (a.epi & kEpiS) ? kOutS : kOutNone;
+  const int out = (a.epi & kEpiPlanes) ? kOutPlanes : (a.epi & kEpiAct) ? kOutAct : (a.epi & kEpiS) ? kOutS
+                  : (a.epi & kEpiS16) ? kOutS16 : kOutNone;
 #define FAV_LAUNCH(NT, MODE, KIND, OUT) \
   if (a.n_tile == NT && a.mode == MODE && a.kind == KIND && out == OUT) return launch_cfg<NT, MODE, KIND, OUT>(a, stream);
   FAV_CONFIGS(FAV_LAUNCH)
