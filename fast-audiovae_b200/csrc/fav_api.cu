@@ -376,9 +376,8 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
       }
       r.pw_b = up(rb + 7);
       {
-        // [block][w0..w6, bias, alpha2, recip2, alpha1, recip1][64], zero padded
-        // past C. The first Snake's alpha1/recip1 are applied either by the
-        // previous layer's epilogue or by this unit's producers (pre_snake).
+        // [block][w0..w6, bias, alpha2, recip2][64], zero padded past C (the
+        // first Snake is applied by the previous layer's epilogue).
         const int c = st.c_out, blocks = (c + 63) / 64;
         std::vector<float> cf((size_t)blocks * fav::kCoefResidual * 64, 0.f);
         for (int b = 0; b < blocks; ++b)
@@ -389,8 +388,6 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
             o[7 * 64] = w[rb + 3][cc];
             o[8 * 64] = w[rb + 4][cc];
             o[9 * 64] = w[rb + 5][cc];
-            o[10 * 64] = w[rb + 0][cc];
-            o[11 * 64] = w[rb + 1][cc];
           }
         r.coef = plan->mem.upload(cf.data(), cf.size(), &e);
       }
@@ -545,9 +542,10 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     t.kind = fav::kTconv;
     t.mode = fav::kModeSplit;
     const bool into_tail = tail && i + 1 == fav::kStages;
-    // Stages 2-4 of a bf16 plan: this conv and units 0-1 write the next unit's
+    // Stages 2-4 with bf16 residual units (all of them in a bf16 plan, stage 4
+    // in an int8 plan): this conv and units 0-1 write the next unit's
     // Snake_pre(y) in f16 (kEpiS16), which the unit's producers stage as is.
-    const bool s16 = p->precision == FAV_PRECISION_BF16 && i >= 2 && i + 1 < fav::kStages;
+    const bool s16 = i >= 2 && i + 1 < fav::kStages && !st.res[0].int8;
     t.epi = fav::kEpiX | (into_tail ? 0 : s16 ? fav::kEpiS16 : fav::kEpiS);
     t.rows = n_streams * n;
     t.rows_per_stream = n;

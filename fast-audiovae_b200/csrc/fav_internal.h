@@ -123,12 +123,8 @@ struct LayerArgs {
   const float* dw_w;    // stem depthwise taps [64][7]
   const float* dw_b;
   // Residual: per-64-channel-block coefficients packed for one bulk copy per K
-  // block, [block][w0..w6, bias, alpha2, recip2, alpha1, recip1][64] (zero padded).
+  // block, [block][w0..w6, bias, alpha2, recip2][64] (zero padded).
   const float* coef;
-  // Residual: the staged input is the unit's input y itself (not Snake_pre(y)
-  // written by the previous epilogue); the producers apply Snake_pre (alpha1,
-  // recip1) to each staged row once, in shared memory, before the depthwise conv.
-  int pre_snake;
   // Residual: the staged input is s = Snake_pre(y) in f16 (written by the
   // previous epilogue with kEpiS16; boxes of 64 channels x box_rows rows, 128
   // bytes per row); the producers read the box as is.
@@ -259,7 +255,7 @@ struct QuantResidualArgs {
   const float* s;        // Snake_pre(x) [rows][channels] fp32
   uint8_t* q;            // A operand [rows][channels] s8
   float* scale;          // [rows]
-  const float* coef;     // [channels / 64][w0..w6, bias, alpha2, recip2, alpha1, recip1][64]
+  const float* coef;     // [channels / 64][w0..w6, bias, alpha2, recip2][64]
   int rows;
   int rows_per_stream;
   int channels;          // 128, 256, 512 or 1024
@@ -283,7 +279,7 @@ cudaError_t prepare_kernels();
 // Coefficient vectors per 64-channel block of a residual unit: depthwise taps
 // w0..w6, depthwise bias, the second Snake's alpha and reciprocal, then the
 // first Snake's alpha and reciprocal (used when the unit reads y itself).
-constexpr int kCoefResidual = 12;
+constexpr int kCoefResidual = 10;
 
 // Rows of the TMA input box of a residual unit: the 128-row tile plus the
 // causal halo of 6*dilation rows.

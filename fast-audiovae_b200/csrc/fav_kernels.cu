@@ -46,9 +46,10 @@ constexpr int kMaxTileStreams = kTileM + 1;  // streams one 128-row tile can tou
 constexpr int kTableInts = 2 * kMaxTileStreams + 2 * kTileM;  // one tile's stream and row tables
 constexpr int kEpiCols = 16;                 // epilogue chunk: 16 columns x 32 rows per warp
 
-// Residual producer input of one K block: the TMA box (tile + halo rows of 64
-// channels) followed by the block's coefficients.
-constexpr int kResBoxBytes = (kTileM + kMaxHalo) * 64 * 4;
+// Residual producer input of one K block: the TMA box (tile + halo rows of 128
+// bytes: 64 channels of f16 s, or stage 5's 32 channels of fp32 s) followed by
+// the block's coefficients.
+constexpr int kResBoxBytes = (kTileM + kMaxHalo) * 128;
 constexpr int kResCoefBytes = kCoefResidual * 64 * 4;
 
 // Split-bf16 operand modes store hi and lo tiles.
@@ -436,27 +437,8 @@ __device__ void produce_residual(const LayerArgs& a, int m0, int kb, uint8_t* a_
   }
 }
 
-// Residual unit reading its input y (LayerArgs::pre_snake): Snake_pre (block
-// coefficient vectors 10 and 11) applied in place to every staged row of the
-// K block's box, each row once, before the depthwise conv reads the box; the
-// box then holds exactly what the previous epilogue would have written as
-// Snake_pre(y), and the history window keeps those values as before.
-// Producer-collective: the caller synchronises the producers afterwards.
-__device__ __forceinline__ void snake_box(const LayerArgs& a, float* raw, int tid) {
-  const int quads = a.raw_pitch / 4;  // 16 (64-channel blocks) or 8
-  const int q = tid % quads;
-  const float* cf = raw + kResBoxBytes / 4;
-  const float4 al = lds4(cf + 10 * 64 + 4 * q), rc = lds4(cf + 11 * 64 + 4 * q);
-  const int step = kProducerThreads / quads;
-#pragma unroll 4
-  for (int r = tid / quads; r < a.box_rows; r += step) {
-    float4* p = reinterpret_cast<float4*>(raw + r * a.raw_pitch + 4 * q);
-    *p = snake4(*p, al, rc);
-  }
-}
-
 // The one stream start that bears on a residual tile's depthwise taps, for
-// units that read y (pre_snake) on streams of at least 128 + 6d rows: the
+// units that stage f16 Snake_pre(y) (s16) on streams of at least 128 + 6d rows: the
 // start b of the stream holding the tile's last row, when it lies after
 // m0 - 6d (its first 6d rows, which reach into the stream's history, overlap
 // the tile); at most one stream starts in (m0 - 6d, m0 + 128).
@@ -472,7 +454,7 @@ __device__ __forceinline__ TileStart tile_start(const LayerArgs& a, int m0, cons
   return TileStart{b, s - tab.s_lo, b > m0 - 6 * a.dilation};
 }
 
-// The history window rows a producer thread loads for produce_residual_y:
+// The history window rows a producer thread loads for produce_residual_s16:
 // items tid + k * 256 (k < 4) of [H rows][16 quads] of K block kb, zero for a
 // fresh stream, without a pool, or past the rows the tile can reach. With
 // ``prefetch`` the thread only asks for their lines in L1 (no registers held
@@ -503,9 +485,22 @@ __device__ __forceinline__ void load_tile_history(const LayerArgs& a, int m0, in
   }
 }
 
-// Residual unit reading its input y (pre_snake), K block kb, 64-channel
-// blocks: depthwise k=7 (dilation d) + Snake_post of the box that snake_box
-// turned into s = Snake_pre(y). Every lane group walks its eight rows in
+// Channel quad k .. k+3 of f16 box row r (64 channels, 128 bytes per row).
+__device__ __forceinline__ float4 box_quad(const float* raw, int r, int k) {
+  const uint2 h = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(raw) + r * kKBlock + k);
+  const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+  const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+  return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+// Stores a quad into f16 box row r (exact for history rows, which hold f16 values).
+__device__ __forceinline__ void put_box_quad(float* raw, int r, int k, float4 v) {
+  *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(raw) + r * kKBlock + k) =
+      make_uint2(pack_f16(v.x, v.y), pack_f16(v.z, v.w));
+}
+
+// Residual unit staging s = Snake_pre(y) in f16 (s16, written by the previous
+// epilogue), K block kb, 64-channel blocks: depthwise k=7 (dilation d) +
+// Snake_post of the box. Every lane group walks its eight rows in
 // residue-class order with a sliding window of taps from the box: rows
 // r, r + d, ... of one class, and where its positions cross into the next
 // class (at most once: classes hold at least 14 rows) the window is reloaded
@@ -517,33 +512,7 @@ __device__ __forceinline__ void load_tile_history(const LayerArgs& a, int m0, in
 // (row, channel quad) per thread. ``hist_writer``: this N tile writes
 // the new window rows of streams ending in the tile (first, from the box).
 // Producer-collective (named barrier 2).
-// Channel quad k .. k+3 of box row r of a residual producer's staged input:
-// fp32 rows of 64 channels, or (S16) f16 rows of 64 channels.
-template <bool S16>
-__device__ __forceinline__ float4 box_quad(const float* raw, int r, int k) {
-  if constexpr (S16) {
-    const uint2 h = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(raw) + r * kKBlock + k);
-    const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
-    const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
-    return make_float4(lo.x, lo.y, hi.x, hi.y);
-  } else {
-    return lds4(raw + r * kKBlock + k);
-  }
-}
-// Stores a quad into box row r (S16: rounded to f16; exact for history rows,
-// which hold f16 values).
-template <bool S16>
-__device__ __forceinline__ void put_box_quad(float* raw, int r, int k, float4 v) {
-  if constexpr (S16) {
-    *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(raw) + r * kKBlock + k) =
-        make_uint2(pack_f16(v.x, v.y), pack_f16(v.z, v.w));
-  } else {
-    *reinterpret_cast<float4*>(raw + r * kKBlock + k) = v;
-  }
-}
-
-template <bool S16>
-__device__ void produce_residual_y(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, float* raw, int warp,
+__device__ void produce_residual_s16(const LayerArgs& a, int m0, int kb, uint8_t* a_stage, float* raw, int warp,
                                    int lane, bool hist_writer, const StreamTable& tab, uint32_t walk_lo,
                                    uint32_t walk_hi, int ubreak, const TileStart& ts) {
   const int d = a.dilation;
@@ -565,7 +534,7 @@ __device__ void produce_residual_y(const LayerArgs& a, int m0, int kb, uint8_t* 
       const int row = rem / (P / 4), k4 = 4 * (rem - row * (P / 4));
       const int tp = N - H + row;
       *reinterpret_cast<float4*>(hist_new_row(a.state, a.hist, tab.code[e], tab.head[e], tp, N) + kb * kKBlock + k4) =
-          box_quad<S16>(raw, (tab.s_lo + e) * N + tp - m0 + H, k4);
+          box_quad(raw, (tab.s_lo + e) * N + tp - m0 + H, k4);
     }
     if (kb == 0)
       for (int e = tid; e < ns; e += kProducerThreads) hist_commit_head(a.state, a.hist, tab.code[e], tab.head[e], N);
@@ -583,9 +552,9 @@ __device__ void produce_residual_y(const LayerArgs& a, int m0, int kb, uint8_t* 
       const int r = u < ubreak ? r0 + u * d : r1 + (u - ubreak) * d;
       if (u == 0 || u == ubreak) {
 #pragma unroll
-        for (int j = 0; j < 6; ++j) win[j] = box_quad<S16>(raw, r - (6 - j) * d + H, kl);
+        for (int j = 0; j < 6; ++j) win[j] = box_quad(raw, r - (6 - j) * d + H, kl);
       }
-      win[6] = box_quad<S16>(raw, r + H, kl);
+      win[6] = box_quad(raw, r + H, kl);
       put_a4<kModeF16>(a_stage, r, kl, snake4(dw7<false>(w, win, bias), al2, rc2));
 #pragma unroll
       for (int j = 0; j < 6; ++j) win[j] = win[j + 1];
@@ -603,7 +572,7 @@ __device__ void produce_residual_y(const LayerArgs& a, int m0, int kb, uint8_t* 
   for (int k = 0; k < 4; ++k) {
     const int it = tid + k * kProducerThreads;
     const int j = it >> 4;  // history row; quad = it & 15 = q
-    if (j < H && pos0 + j >= 0) put_box_quad<S16>(raw, pos0 + j, 4 * (it & 15), hist_reg[k]);
+    if (j < H && pos0 + j >= 0) put_box_quad(raw, pos0 + j, 4 * (it & 15), hist_reg[k]);
   }
   named_barrier(2, kProducerThreads);
   const int lo = max(ts.b, m0) - m0, hi = min(min(ts.b + H, m0 + kTileM), a.rows) - m0;
@@ -613,7 +582,7 @@ __device__ void produce_residual_y(const LayerArgs& a, int m0, int kb, uint8_t* 
 #pragma unroll
     for (int j = 0; j < 7; ++j) {
       wq[j] = lds4(raw + kResBoxBytes / 4 + k4 + j * 64);
-      win[j] = box_quad<S16>(raw, r - (6 - j) * d + H, k4);
+      win[j] = box_quad(raw, r - (6 - j) * d + H, k4);
     }
     const float4 bq = lds4(raw + kResBoxBytes / 4 + k4 + 7 * 64);
     const float4 aq = lds4(raw + kResBoxBytes / 4 + k4 + 8 * 64), rq = lds4(raw + kResBoxBytes / 4 + k4 + 9 * 64);
@@ -954,21 +923,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
             produce_stem<MODE>(a, a_stage, warp, lane, write_state, tab);
           } else if (KIND == kResidual) {
             float* raw = reinterpret_cast<float*>(raw_base + rb * Cfg::kRaw);
-            if (kLpr == 16 && !kI8 && (a.pre_snake || a.s16)) {
+            if (kLpr == 16 && !kI8 && a.s16) {
               const TileStart ts = tile_start(a, m0, tab);
               if (ts.on) {
                 float4 unused[4];
                 load_tile_history<true>(a, m0, kb, tab, ts, threadIdx.x, unused);
               }
-              if (a.s16) {  // the box already holds Snake_pre(y) (f16)
-                produce_residual_y<true>(a, m0, kb, a_stage, raw, warp, lane, kb % num_n == tile_n(t), tab, walk_lo,
-                                         walk_hi, ubreak, ts);
-              } else {
-                snake_box(a, raw, threadIdx.x);
-                named_barrier(2, kProducerThreads);
-                produce_residual_y<false>(a, m0, kb, a_stage, raw, warp, lane, kb % num_n == tile_n(t), tab, walk_lo,
-                                          walk_hi, ubreak, ts);
-              }
+              produce_residual_s16(a, m0, kb, a_stage, raw, warp, lane, kb % num_n == tile_n(t), tab, walk_lo, walk_hi,
+                                   ubreak, ts);
             } else {
               produce_residual<MODE, kLpr>(a, m0, kb, a_stage, raw, warp, lane, kb % num_n == tile_n(t), tab,
                                            partial ? iwalk_lo : walk_lo, partial ? iwalk_hi : walk_hi, regular);
@@ -1506,9 +1468,9 @@ static cudaError_t set_smem() {
   X(256, kModeSplit4, kStem, kOutPlanes) X(64, kModeSplit4, kStem, kOutPlanes)                            \
   X(256, kModeSplit4, kStem, kOutAct)                                                                      \
   X(256, kModeSplit, kTconv, kOutS) X(128, kModeSplit, kTconv, kOutS) X(64, kModeSplit, kTconv, kOutS)      \
-  X(128, kModeI8, kTconv, kOutS) X(128, kModeI8, kTconvPre, kOutS)                                        \
-  X(256, kModeSplit, kTconv, kOutNone) X(128, kModeSplit, kTconv, kOutNone) X(64, kModeSplit, kTconv, kOutNone) \
-  X(256, kModeF16, kResidual, kOutNone) X(128, kModeF16, kResidual, kOutNone) X(64, kModeF16, kResidual, kOutNone) \
+  X(128, kModeI8, kTconv, kOutS) X(128, kModeI8, kTconvPre, kOutS) X(128, kModeI8, kTconv, kOutS16)       \
+  X(128, kModeI8, kTconvPre, kOutS16)                                                                      \
+  X(64, kModeSplit, kTconv, kOutNone)                                                                      \
   X(256, kModeF16, kResidual, kOutS) X(128, kModeF16, kResidual, kOutS) X(64, kModeF16, kResidual, kOutS)  \
   X(256, kModeSplit, kTconv, kOutS16) X(128, kModeSplit, kTconv, kOutS16) X(64, kModeSplit, kTconv, kOutS16)   \
   X(256, kModeF16, kResidual, kOutS16) X(128, kModeF16, kResidual, kOutS16) X(64, kModeF16, kResidual, kOutS16) \
@@ -1541,6 +1503,9 @@ cudaError_t launch_gemm_layer(const LayerArgs& a, cudaStream_t stream) {
   if (a.rows <= 0) return cudaSuccess;
   if (a.n_total % a.n_tile) return cudaErrorInvalidValue;
   if (a.img_nt && (a.img_nt % a.n_tile || a.n_total % a.img_nt)) return cudaErrorInvalidValue;
+  // A residual unit's staged box (tile + halo rows) must fit its raw buffer.
+  if (a.kind == kResidual && (size_t)a.box_rows * a.raw_pitch * (a.s16 ? 2 : 4) > (size_t)kResBoxBytes)
+    return cudaErrorInvalidValue;
   const int out = (a.epi & kEpiPlanes) ? kOutPlanes : (a.epi & kEpiAct) ? kOutAct : (a.epi & kEpiS) ? kOutS
                   : (a.epi & kEpiS16) ? kOutS16 : kOutNone;
 #define FAV_LAUNCH(NT, MODE, KIND, OUT) \
