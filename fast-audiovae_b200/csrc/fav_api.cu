@@ -121,6 +121,14 @@ int32_t encode_tail_map(CUtensorMap* map, const float* x, int rows, int box_rows
   return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_128B, "tail");
 }
 
+// Input y [rows][channels] fp32 of a fused residual stage: boxes of 32
+// channels x 128 rows in the 128-byte swizzle.
+int32_t encode_stage_map(CUtensorMap* map, const float* x, int rows, int channels) {
+  const cuuint64_t dims[2] = {(cuuint64_t)channels, (cuuint64_t)rows};
+  const cuuint32_t box[2] = {32, (cuuint32_t)fav::kTileM};
+  return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_128B, "stage");
+}
+
 std::once_flag g_prepare_once;
 cudaError_t g_prepare_error = cudaSuccess;
 
@@ -414,7 +422,8 @@ int32_t build_plan(fav_plan* plan, const float* const* w) {
 constexpr int kWorkspaceRegions = 6;
 constexpr size_t kRegionFloatsPerFrame = 61440;
 
-// Diagnostic settings for one engine launch of a step (fav_debug_step_gated).
+// Diagnostic settings for one engine launch of a step (fav_debug_step_gated);
+// a residual unit of a fused stage gates the stage's kernel.
 struct StepDiag {
   int layer;                // 0 = stem, 1 + 4i = stage i transposed conv, 2 + 4i + j = residual unit
   uint32_t wait_limit;      // polls before a wait of that launch gives up
@@ -428,7 +437,7 @@ struct StepDiag {
 int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, int frames, const float* z,
                  int z_stride, int z_offset, float* audio, int audio_stride, int audio_offset, float* ws,
                  uint32_t* status, cudaStream_t stream, int last_layer = 25, float** last_out = nullptr,
-                 cudaEvent_t* events = nullptr, bool fuse_tail = true, const StepDiag* diag = nullptr) {
+                 cudaEvent_t* events = nullptr, bool fuse = true, const StepDiag* diag = nullptr) {
   // events (optional, 27): recorded before the stem and after each layer.
   auto mark = [&](int i) {
     if (events) cudaEventRecord(events[i], stream);
@@ -447,8 +456,19 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
   uint16_t* planes_prev = reinterpret_cast<uint16_t*>(ws + 5 * region);  // row t holds time step t - 1
   // A whole step runs stage 5's residual units and the final conv as one fused
   // kernel; a step stopped inside stage 5 (layer checks) runs them one by one.
-  bool tail = fuse_tail && last_layer >= 25 && p->stages[fav::kStages - 1].c_out == fav::kTailC;
+  bool tail = fuse && last_layer >= 25 && p->stages[fav::kStages - 1].c_out == fav::kTailC;
   for (int j = 0; j < 3; ++j) tail = tail && !p->stages[fav::kStages - 1].res[j].int8;
+  // Stages 3-4 (64 and 128 channels, bf16 units feeding a bf16 transposed
+  // conv) run their three residual units and the next conv's planes as one
+  // fused kernel, unless the step stops inside the stage or at its last unit.
+  auto fused_stage = [&](int i) {
+    if (!fuse || i + 1 >= fav::kStages || last_layer <= 4 * i + 4) return false;
+    const StageDev& st = p->stages[i];
+    if (st.c_out != 64 && st.c_out != 128) return false;
+    for (int j = 0; j < 3; ++j)
+      if (st.res[j].int8) return false;
+    return !p->stages[i + 1].int8;
+  };
   auto tconv_hist = [p](int i) {
     const StageDev& st = p->stages[i];
     return fav::HistRef{1 + 4 * i, 2 * st.state_t, 1, st.c_in};
@@ -542,11 +562,12 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     t.kind = fav::kTconv;
     t.mode = fav::kModeSplit;
     const bool into_tail = tail && i + 1 == fav::kStages;
+    const bool into_stage = fused_stage(i);
     // Stages 2-4 with bf16 residual units (all of them in a bf16 plan, stage 4
     // in an int8 plan): this conv and units 0-1 write the next unit's
     // Snake_pre(y) in f16 (kEpiS16), which the unit's producers stage as is.
     const bool s16 = i >= 2 && i + 1 < fav::kStages && !st.res[0].int8;
-    t.epi = fav::kEpiX | (into_tail ? 0 : s16 ? fav::kEpiS16 : fav::kEpiS);
+    t.epi = fav::kEpiX | ((into_tail || into_stage) ? 0 : s16 ? fav::kEpiS16 : fav::kEpiS);
     t.rows = n_streams * n;
     t.rows_per_stream = n;
     t.k_channels = st.c_in;
@@ -623,6 +644,36 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       for (int l = 23; l <= 26; ++l) mark(l);
       if (last_out) *last_out = audio;
       return FAV_OK;
+    }
+    if (into_stage) {
+      fav::StageArgs sa{};
+      sa.channels = st.c_out;
+      sa.rows = n_streams * n;
+      sa.rows_per_stream = n;
+      for (int j = 0; j < 3; ++j) {
+        const auto& r = st.res[j];
+        sa.unit[j] = fav::StageUnitArgs{r.pre_a, r.pre_r, r.coef, r.pw_b, r.img,
+                                        fav::HistRef{2 + 4 * i + j, 2 * r.state_off, 6 * r.dilation, st.c_out}};
+      }
+      const StageDev& nx = p->stages[i + 1];
+      sa.next_scale = nx.scale;
+      sa.next_offset = nx.offset;
+      sa.next_alpha = nx.alpha;
+      sa.next_recip = nx.recip;
+      sa.out_planes = planes;
+      sa.out_planes_prev = planes_prev;
+      sa.hist_next = tconv_hist(i + 1);
+      sa.state = state;
+      sa.status = status;
+      if (diag && diag->layer >= 4 * i + 2 && diag->layer <= 4 * i + 4) {
+        sa.wait_limit = diag->wait_limit;
+        sa.gate = diag->gate;
+      }
+      if ((es = encode_stage_map(&sa.xmap, X[0], sa.rows, st.c_out)) != FAV_OK) return es;
+      if ((e = fav::launch_stage(sa, stream)) != cudaSuccess) return cuda_fail(e, "stage launch");
+      // The fused kernel's time counts as the stage's first residual unit.
+      for (int j = 0; j < 3; ++j) mark(++layer + 1);
+      continue;
     }
     // Residual unit j reads y and Snake_pre(y) from pair j % 2 and writes pair
     // (j + 1) % 2; the last unit writes the next stage's planes instead (stage 5:

@@ -212,6 +212,39 @@ struct TailArgs {
 };
 cudaError_t launch_tail(const TailArgs& a, cudaStream_t stream);
 
+// Fused residual stage (fav_stage.cu): the three residual units of a stage with
+// 64 or 128 channels (stages 4 and 3) and the next transposed conv's planes.
+struct StageUnitArgs {
+  const float* pre_a;    // Snake before the depthwise conv [C]
+  const float* pre_r;
+  const float* coef;     // depthwise blocks [C / 64][w0..w6, bias, alpha2, recip2][64]
+  const float* bias;     // 1x1 bias [C]
+  const uint8_t* wimg;   // 1x1 weights [C / 64][C rows][128 B] (f16, K-major, 128-byte swizzle)
+  HistRef hist;          // window of Snake_pre(input) (f16 values), 6 * dilation rows
+};
+struct StageArgs {
+  CUtensorMap xmap;      // stage input y [rows][C] fp32: boxes of 32 channels x 128 rows, 128-byte swizzle
+  int channels;          // C: 64 or 128
+  int rows;              // all streams' rows
+  int rows_per_stream;
+  StageUnitArgs unit[3];
+  const float* next_scale;   // next stage's affine and Snake [C]
+  const float* next_offset;
+  const float* next_alpha;
+  const float* next_recip;
+  uint16_t* out_planes;      // [2][rows][C] bf16 (hi, then lo)
+  uint16_t* out_planes_prev; // the same one row later per stream (a stream's first row: hist_next's row)
+  HistRef hist_next;         // next transposed conv's one-row history, packed (hi << 16) | lo per channel
+  StateRef state;
+  uint32_t* status;
+  // Diagnostics, as in LayerArgs: polls after which a wait gives up (0 =
+  // kWaitLimit), and a device flag the first MMA waits for (nullptr = none).
+  uint32_t wait_limit;
+  const uint32_t* gate;
+};
+cudaError_t launch_stage(const StageArgs& a, cudaStream_t stream);
+cudaError_t prepare_stage();
+
 // Depthwise pre-pass of a residual unit (fav_prepass.cu): A = Snake_post(
 // depthwise_k7(s)) as f16 [rows][channels] for a kResidualPre GEMM, plus the
 // layer's new history window.

@@ -1470,7 +1470,7 @@ static cudaError_t set_smem() {
   X(256, kModeSplit, kTconv, kOutS) X(128, kModeSplit, kTconv, kOutS) X(64, kModeSplit, kTconv, kOutS)      \
   X(128, kModeI8, kTconv, kOutS) X(128, kModeI8, kTconvPre, kOutS) X(128, kModeI8, kTconv, kOutS16)       \
   X(128, kModeI8, kTconvPre, kOutS16)                                                                      \
-  X(64, kModeSplit, kTconv, kOutNone)                                                                      \
+  X(64, kModeSplit, kTconv, kOutNone) X(128, kModeSplit, kTconv, kOutNone) X(128, kModeI8, kTconv, kOutNone) \
   X(256, kModeF16, kResidual, kOutS) X(128, kModeF16, kResidual, kOutS) X(64, kModeF16, kResidual, kOutS)  \
   X(256, kModeSplit, kTconv, kOutS16) X(128, kModeSplit, kTconv, kOutS16) X(64, kModeSplit, kTconv, kOutS16)   \
   X(256, kModeF16, kResidual, kOutS16) X(128, kModeF16, kResidual, kOutS16) X(64, kModeF16, kResidual, kOutS16) \
@@ -1496,6 +1496,7 @@ cudaError_t prepare_kernels() {
   if ((e = set_smem<NT, MODE, KIND, OUT>()) != cudaSuccess) return e;
   FAV_CONFIGS(FAV_SET)
 #undef FAV_SET
+  if ((e = prepare_stage()) != cudaSuccess) return e;
   return prepare_tail();
 }
 

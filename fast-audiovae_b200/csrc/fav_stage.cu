@@ -1,0 +1,505 @@
+// Fused residual stage: the three residual units of a stage with C = 64 or 128
+// channels (stages 4 and 3) and the split-bf16 planes of the next transposed
+// conv's activated input, in one persistent kernel (the reference's
+// mps_decoder.py _Residual.decode loop and the next _Stage.decode prologue,
+// restated in the fp32 oracle at oracle/decoder.py).
+//
+// As per-layer kernels each unit moves y, its f16 Snake_pre(y) and the skip
+// input through HBM around a C x C projection. Here a CTA takes a contiguous
+// range of 128-row tiles (time steps of one stream; a stream's last tile may
+// be partial) and keeps every intermediate in shared memory. Within a tile,
+// with row 0 its first row:
+//
+//   P = f16 Snake_pre1(x)  rows [-6, 128)  -> depthwise d=1 -> Snake -> f16 A -> MMA
+//   y1 = x + (A W1 + b1)   rows [0, 128)   (over x in X)
+//   P = f16 Snake_pre2(y1) rows [-18, 128) -> depthwise d=3 -> ...
+//   y2                     (over y1)
+//   P = f16 Snake_pre3(y2) rows [-54, 128) -> depthwise d=9 -> ...
+//   y3 -> split-bf16 planes of Snake(y3 * scale + offset) for the next conv
+//
+// The rows before row 0 of each P come from the previous tile of the same
+// stream (kept in a small carry buffer) or, at a stream's first tile, from
+// the unit's history ring; a stream's last tile writes the new windows. A
+// range that starts inside a stream first runs the tile before it as a
+// warm-up tile with zero carried rows and discards its output (the zeros
+// reach its rows [0, 6) of y1, [0, 24) of y2 and [0, 78) of y3; the rows it
+// carries on are exact). Every value is computed with the same operations, in
+// the same order and at the same roundings as the per-layer kernels (f16
+// Snake_pre staging, fused multiply-add depthwise chains, f16 x f16 MMAs over
+// the K blocks in order, the planes epilogue), so the fused stage equals them
+// bit for bit and a chunked stream equals the same stream decoded at once.
+//
+// The C x C projections run on the tensor cores (tcgen05.mma kind::f16, M =
+// 128, N = C, fp32 accumulators in TMEM); the unit's B operand is streamed
+// into shared memory by a bulk copy while the previous unit finishes. The
+// phases of a tile are separated by block barriers: C = 64 runs two CTAs of
+// 256 threads per SM, whose phases interleave (one 512-thread CTA per tile
+// when a launch has at most one tile per SM); C = 128 runs one 512-thread CTA
+// per SM.
+#include "fav_common.cuh"
+
+namespace fav {
+namespace {
+
+constexpr int kSR = 128;                 // rows per tile
+constexpr int kSPOff = 54;               // P row of relative row 0 (rows [-54, 128))
+constexpr int kSPRows = kSPOff + kSR;    // 182
+constexpr int kSCarryRows = 6 + 18 + 54;  // carried P rows of units 0-2
+
+template <int C>
+struct StageSmem {
+  static constexpr int kXBlocks = C / 32;  // fp32 column blocks (128-byte rows, TMA boxes)
+  static constexpr int kKB = C / 64;       // f16 column blocks (128-byte rows): K blocks
+  // byte offsets from the 1024-aligned base
+  static constexpr int kX = 0;                               // y: [kXBlocks][128][32] fp32, 128-byte swizzle
+  static constexpr int kA = kX + kXBlocks * kSR * 128;       // A: [kKB][128][64] f16 (MMA layout)
+  static constexpr int kW = kA + kKB * kSR * 128;            // one unit's B: [kKB][C][64] f16 (MMA layout)
+  static constexpr int kP = kW + kKB * C * 128;              // P: [kKB][182][64] f16, 16-byte chunks swizzled
+  static constexpr int kCarry = kP + kKB * kSPRows * 128;    // [78][C] f16, plain rows
+  static constexpr int kCoefs = kCarry + kSCarryRows * C * 2;  // floats from here on
+  static constexpr int kUnitCoefFloats = kKB * kCoefResidual * 64;
+  static constexpr int kUnitCoef = 0;                        // [3][kKB][w0..w6, bias, alpha2, recip2][64]
+  static constexpr int kPwBias = 3 * kUnitCoefFloats;        // [3][C]
+  static constexpr int kPreA = kPwBias + 3 * C;              // [3][C]
+  static constexpr int kPreR = kPreA + 3 * C;                // [3][C]
+  static constexpr int kNScale = kPreR + 3 * C;              // [C] next stage's affine and Snake
+  static constexpr int kNOffset = kNScale + C;
+  static constexpr int kNAlpha = kNOffset + C;
+  static constexpr int kNRecip = kNAlpha + C;
+  static constexpr int kCoefFloats = kNRecip + C;
+  static constexpr int kMisc = kCoefs + kCoefFloats * 4;     // ints: heads[4], code, pad
+  static constexpr int kBars = ((kMisc + 8 * 4 + 7) / 8) * 8;  // xfull, wfull, mma_done, tmem slot
+  static constexpr int kBytes = kBars + 4 * 8;
+  static constexpr int kAlloc = kBytes + 1024;
+};
+// C = 64: two CTAs per SM (228 KB of shared memory per SM, 1 KB of it reserved per CTA).
+static_assert(2 * (StageSmem<64>::kAlloc + 1024) <= 228 * 1024, "two C=64 stage CTAs per SM");
+static_assert(StageSmem<128>::kAlloc <= 227 * 1024, "one C=128 stage CTA per SM");
+
+// fp32 row buffers (X): row r, channel quad q (< 8) of a 32-channel block in
+// the 128-byte swizzle a TMA box with CU_TENSOR_MAP_SWIZZLE_128B writes.
+__device__ __forceinline__ int xq_off(int r, int q) { return r * 32 + ((q ^ (r & 7)) << 2); }
+
+// P: f16 row pr, channel quad q (4 channels, 8 bytes) of the whole row (block
+// q / 16), with the 16-byte chunks of each 128-byte row swizzled by pr & 7 so
+// a lane per row (epilogue writes) spreads over the banks.
+__device__ __forceinline__ int p_off(int pr, int q) {
+  const int kb = q >> 4, qb = q & 15;
+  return kb * kSPRows * 128 + pr * 128 + ((((qb >> 1) ^ (pr & 7)) << 4) | ((qb & 1) << 3));
+}
+__device__ __forceinline__ float4 p_load(const uint8_t* p, int pr, int q) {
+  const uint2 h = *reinterpret_cast<const uint2*>(p + p_off(pr, q));
+  const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+  const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+  return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+__device__ __forceinline__ uint2 f16x4(float4 v) { return make_uint2(pack_f16(v.x, v.y), pack_f16(v.z, v.w)); }
+__device__ __forceinline__ float4 f16x4_to_float(uint2 h) {
+  const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+  const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+  return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+
+__device__ __forceinline__ int stage_code(const StateRef& st, int s) {
+  return st.slot_codes ? st.slot_codes[s] : ((s << 2) | st.uniform_code);
+}
+
+// Window row of time tp (-H <= tp < 0) of a history whose window starts at head.
+__device__ __forceinline__ float4 stage_hist_quad(const StateRef& st, const HistRef& h, int code, int head, int tp,
+                                                  int q) {
+  if (!st.pool || (code & 2)) return make_float4(0.f, 0.f, 0.f, 0.f);
+  int row = head + h.rows + tp;
+  if (row >= 2 * h.rows) row -= 2 * h.rows;
+  return ldg4(slot_base(st, code) + h.ring + row * h.width + 4 * q);
+}
+
+// First carry row of unit u's carried P rows.
+__device__ __forceinline__ constexpr int scarry_off(int u) { return u == 0 ? 0 : u == 1 ? 6 : 24; }
+
+// Chain length covering 128 rows with `groups` row groups at dilation d.
+__host__ __device__ constexpr int stage_chain(int groups, int d) {
+  for (int L = 1; L <= kSR; ++L) {
+    const int full = kSR / (L * d), rest = kSR - full * L * d;
+    if (full * d + (rest < d ? rest : d) <= groups) return L;
+  }
+  return kSR;
+}
+
+// Depthwise k=7 (dilation d) + Snake_post of A rows [0, 128) into the f16 A
+// operand, A row i from P rows kSPOff - 6d + i + j*d (j = 0..6), for this
+// thread's chain of L rows i0, i0 + d, ... in channel quad q: blocks of L*d
+// rows split into d chains of L, so the seven taps slide through registers.
+template <int L>
+__device__ __forceinline__ void stage_chains(const float* ucoef, const uint8_t* pbuf, uint8_t* aop, int rg, int q,
+                                             int d) {
+  const int i0 = (rg / d) * L * d + rg % d;
+  if (i0 >= kSR) return;
+  const int kb = q >> 4, qb = q & 15;
+  const float* uc = ucoef + kb * kCoefResidual * 64 + 4 * qb;
+  uint8_t* ab = aop + kb * kSR * 128;
+  const int base = kSPOff - 6 * d;
+  float4 w[7], win[7];
+#pragma unroll
+  for (int j = 0; j < 7; ++j) w[j] = lds4(uc + j * 64);
+  const float4 bias = lds4(uc + 7 * 64), al2 = lds4(uc + 8 * 64), rc2 = lds4(uc + 9 * 64);
+#pragma unroll
+  for (int j = 0; j < 6; ++j) win[j] = p_load(pbuf, base + i0 + j * d, q);
+#pragma unroll
+  for (int c = 0; c < L; ++c) {
+    const int i = i0 + c * d;
+    if (i >= kSR) break;
+    win[6] = p_load(pbuf, base + i + 6 * d, q);
+    *reinterpret_cast<uint2*>(ab + sw128_offset(i, 4 * qb)) = f16x4(snake4(dw7<false>(w, win, bias), al2, rc2));
+#pragma unroll
+    for (int j = 0; j < 6; ++j) win[j] = win[j + 1];
+  }
+}
+
+template <int C, int kThreads>
+__global__ void __launch_bounds__(kThreads, 512 / kThreads) stage_kernel(const __grid_constant__ StageArgs a) {
+  using L = StageSmem<C>;
+  constexpr int kQuads = C / 4;                 // channel quads per row
+  constexpr int kGroups = kThreads / kQuads;    // row groups of the row-parallel phases
+  constexpr int kColGroups = kThreads / 128;    // warps per TMEM lane quarter
+  constexpr int kCW = C / kColGroups;           // epilogue columns per thread (16 or 32)
+  constexpr int kKB = L::kKB;
+  constexpr uint32_t kXBytes = L::kXBlocks * kSR * 128;
+  constexpr uint32_t kWBytes = kKB * C * 128;
+  static_assert(kThreads % kQuads == 0 && kCW % 16 == 0, "thread mapping");
+  extern __shared__ uint8_t stage_smem_raw[];
+  // Aligned by an offset from the shared array (not through an integer), so
+  // the compiler keeps every access through it in the shared state space.
+  uint8_t* sm = stage_smem_raw + ((1024u - (smem_u32(stage_smem_raw) & 1023u)) & 1023u);
+  float* xbuf = reinterpret_cast<float*>(sm + L::kX);
+  uint8_t* aop = sm + L::kA;
+  uint8_t* wop = sm + L::kW;
+  uint8_t* pbuf = sm + L::kP;
+  uint8_t* carry = sm + L::kCarry;
+  float* cf = reinterpret_cast<float*>(sm + L::kCoefs);
+  int* misc = reinterpret_cast<int*>(sm + L::kMisc);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBars);
+  uint64_t* xfull = bars;
+  uint64_t* wfull = bars + 1;
+  uint64_t* mma_done = bars + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t wl = a.wait_limit ? a.wait_limit : kWaitLimit;  // polls before a wait gives up
+  const int q = tid % kQuads, rg = tid / kQuads;  // channel quad and row group in the row-parallel phases
+  const int N = a.rows_per_stream;
+  const int tps = (N + kSR - 1) / kSR;  // tiles per stream (the last one may be partial)
+  const int num_tiles = (a.rows / N) * tps;
+  // This CTA's contiguous range of tiles, preceded by a discarded warm-up
+  // tile when the range starts inside a stream.
+  const int t_begin = (int)((long long)blockIdx.x * num_tiles / gridDim.x);
+  const int t_end = (int)((long long)(blockIdx.x + 1) * num_tiles / gridDim.x);
+  const int t_first = (t_begin < t_end && t_begin % tps != 0) ? t_begin - 1 : t_begin;
+
+  // ---- one-time setup: barriers, TMEM, coefficients, zero carries
+  if (tid == 0) {
+    mbar_init(xfull, 1);
+    mbar_init(wfull, 1);
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, C);
+    tmem_relinquish();
+  }
+  for (int u = 0; u < 3; ++u) {
+    const StageUnitArgs& un = a.unit[u];
+    for (int i = tid; i < L::kUnitCoefFloats; i += kThreads) cf[L::kUnitCoef + u * L::kUnitCoefFloats + i] = __ldg(un.coef + i);
+    for (int i = tid; i < C; i += kThreads) {
+      cf[L::kPwBias + u * C + i] = __ldg(un.bias + i);
+      cf[L::kPreA + u * C + i] = __ldg(un.pre_a + i);
+      cf[L::kPreR + u * C + i] = __ldg(un.pre_r + i);
+    }
+  }
+  for (int i = tid; i < C; i += kThreads) {
+    cf[L::kNScale + i] = __ldg(a.next_scale + i);
+    cf[L::kNOffset + i] = __ldg(a.next_offset + i);
+    cf[L::kNAlpha + i] = __ldg(a.next_alpha + i);
+    cf[L::kNRecip + i] = __ldg(a.next_recip + i);
+  }
+  for (int i = tid; i < kSCarryRows * C / 2; i += kThreads) reinterpret_cast<uint32_t*>(carry)[i] = 0u;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  grid_dependency_sync();  // plan constants above; the stage input and histories below
+
+  // y of the tile at global row m0: C / 32 boxes of 32 channels x 128 rows.
+  auto load_x = [&](int m0) {
+    mbar_arrive_expect_tx(xfull, kXBytes);
+#pragma unroll
+    for (int b = 0; b < L::kXBlocks; ++b) tma_load_2d(sm + L::kX + b * kSR * 128, &a.xmap, 32 * b, m0, xfull);
+  };
+  auto load_w = [&](int u) {
+    mbar_arrive_expect_tx(wfull, kWBytes);
+    bulk_g2s(wop, a.unit[u].wimg, kWBytes, wfull);
+  };
+  auto tile_m0 = [&](int t) { return (t / tps) * N + (t % tps) * kSR; };
+  if (tid == 0 && t_first < t_end) {
+    load_x(tile_m0(t_first));
+    load_w(0);
+  }
+  int loads = t_first < t_end ? 1 : 0;   // x loads issued (counted alike by every thread)
+  uint32_t n_w = t_first < t_end ? 1 : 0;  // weight loads issued
+  uint32_t n_mma = 0;                       // MMA groups issued
+  bool ok = true;
+  int k = 0;
+  for (int t = t_first; t < t_end && ok; ++t, ++k) {
+    const bool discard = t < t_begin;  // the warm-up tile: only its carried rows are kept
+    const int s = t / tps, j = t - s * tps;
+    const int m0 = s * N + j * kSR;
+    const int v = min(kSR, N - j * kSR);  // valid rows of the tile
+    const bool first = j == 0, last = !discard && j == tps - 1;
+    // Stream slot and window heads (units 0-2, the next conv), when the tile reads or writes a window.
+    if (tid < 4 && (first || last)) {
+      const int code = stage_code(a.state, s);
+      const HistRef& h = tid < 3 ? a.unit[tid].hist : a.hist_next;
+      misc[tid] = (a.state.pool && !(code & 2)) ? head_table(slot_base(a.state, code), code & 1)[h.index] : 0;
+      if (tid == 0) misc[4] = code;
+    }
+    ok = __syncthreads_and(mbar_wait(xfull, k & 1, a.status, kDevTimeoutLoader, wl));
+    if (!ok) break;
+    const int code = misc[4];
+    // Rows [-H, 0) of unit u's P: the history window at a stream's first
+    // tile, the previous tile's carried rows inside a stream.
+    auto fill_halo = [&](int u) {
+      const int H = u == 0 ? 6 : u == 1 ? 18 : 54;
+      const HistRef& hist = a.unit[u].hist;
+      for (int r = rg; r < H; r += kGroups) {
+        const uint2 val = first ? f16x4(stage_hist_quad(a.state, hist, code, misc[u], r - H, q))
+                                : *reinterpret_cast<const uint2*>(carry + ((scarry_off(u) + r) * C + 4 * q) * 2);
+        *reinterpret_cast<uint2*>(pbuf + p_off(kSPOff - H + r, q)) = val;
+      }
+    };
+    // (a) P = f16 Snake_pre1(x), rows [0, 128), and unit 0's halo rows.
+    {
+      const float4 pa = lds4(cf + L::kPreA + 4 * q);
+      const float4 pr = lds4(cf + L::kPreR + 4 * q);
+      const float* xb = xbuf + (q >> 3) * kSR * 32;
+      for (int i = rg; i < kSR; i += kGroups)
+        *reinterpret_cast<uint2*>(pbuf + p_off(kSPOff + i, q)) = f16x4(snake4(lds4(xb + xq_off(i, q & 7)), pa, pr));
+      fill_halo(0);
+      __syncthreads();
+    }
+#pragma unroll
+    for (int u = 0; u < 3; ++u) {
+      const int d = u == 0 ? 1 : u == 1 ? 3 : 9, H = 6 * d;
+      const HistRef& hist = a.unit[u].hist;
+      const float* uc = cf + L::kUnitCoef + u * L::kUnitCoefFloats;
+      // (b) A = Snake_post(depthwise(P)) in f16.
+      if (u == 0) {
+        stage_chains<stage_chain(kGroups, 1)>(uc, pbuf, aop, rg, q, 1);
+      } else if (u == 1) {
+        stage_chains<stage_chain(kGroups, 3)>(uc, pbuf, aop, rg, q, 3);
+      } else {
+        stage_chains<stage_chain(kGroups, 9)>(uc, pbuf, aop, rg, q, 9);
+      }
+      // The unit's last H input rows: carried to the next tile of the stream
+      // (full tiles), and at the stream's last tile the new history window
+      // (rows [v - H, v), partly carried rows when v < H).
+      if (!last) {
+        for (int r = rg; r < H; r += kGroups)
+          *reinterpret_cast<uint2*>(carry + ((scarry_off(u) + r) * C + 4 * q) * 2) =
+              *reinterpret_cast<const uint2*>(pbuf + p_off(kSPOff + kSR - H + r, q));
+      } else if (a.state.pool) {
+        for (int r = rg; r < H; r += kGroups) {
+          const float4 val = f16x4_to_float(*reinterpret_cast<const uint2*>(pbuf + p_off(kSPOff + v - H + r, q)));
+          *reinterpret_cast<float4*>(hist_new_row(a.state, hist, code, misc[u], N - H + r, N) + 4 * q) = val;
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      // (c) D = A W^T, M = 128, N = C, K = C (K blocks of 64 in order, four K = 16 steps each).
+      if (tid == 0) {
+        ok = (a.gate == nullptr || n_mma > 0 || flag_wait(a.gate, a.status, kDevTimeoutGate, wl)) &&
+             mbar_wait(wfull, (n_w - 1) & 1, a.status, kDevTimeoutLoader, wl);
+        if (ok) {
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(aop), b0 = smem_u32(wop);
+          constexpr uint32_t idesc = instr_desc_f16(0u, C);
+#pragma unroll
+          for (int kb = 0; kb < kKB; ++kb)
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              mma_f16(tmem, smem_desc_sw128(a0 + kb * kSR * 128 + ks * 32), smem_desc_sw128(b0 + kb * C * 128 + ks * 32),
+                      idesc, (kb | ks) ? 1u : 0u);
+          mma_commit(mma_done);
+        }
+      }
+      if (!__syncthreads_and(ok)) {
+        ok = false;
+        break;
+      }
+      ++n_mma;
+      ok = __syncthreads_and(mbar_wait(mma_done, (n_mma - 1) & 1, a.status, kDevTimeoutMma, wl));
+      tc_fence_after();
+      if (!ok) break;
+      // The MMAs have read W: the next unit's weights (after unit 2: unit 0's,
+      // for the next tile) stream in during this epilogue and the next
+      // unit's depthwise phase.
+      if (tid == 0 && (u < 2 || t + 1 < t_end)) load_w(u < 2 ? u + 1 : 0);
+      if (u < 2 || t + 1 < t_end) ++n_w;
+      // (d) y = input + (D + b) over the input in X; units 0-1 write the next
+      // unit's f16 Snake_pre(y) into P rows [0, 128) and fill its halo rows
+      // (disjoint rows); unit 2 writes the next conv's planes. A lane reads
+      // TMEM lane i (its warp's lane quarter) and owns row i's kCW columns.
+      {
+        const int lq = warp & 3, cg = warp >> 2;
+        const int i = lq * 32 + lane;
+        const int c0 = cg * kCW;
+        uint32_t r[kCW];
+#pragma unroll
+        for (int h = 0; h < kCW / 16; ++h)
+          tmem_ld16_async(tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(c0 + 16 * h),
+                          *reinterpret_cast<uint32_t(*)[16]>(r + 16 * h));
+#pragma unroll
+        for (int h = 0; h < kCW / 16; ++h) tmem_wait_ld(*reinterpret_cast<uint32_t(*)[16]>(r + 16 * h));
+        const float* pb = cf + L::kPwBias + u * C;
+        uint32_t hi[kCW / 2], lo[kCW / 2];  // unit 2: split-bf16 planes of this row's columns
+#pragma unroll
+        for (int qq = 0; qq < kCW / 4; ++qq) {
+          const int c = c0 + 4 * qq;
+          float* xp = xbuf + (c >> 5) * kSR * 32 + xq_off(i, (c & 31) >> 2);
+          const float4 x = lds4(xp);
+          const float4 b = lds4(pb + c);
+          const float4 y = make_float4(x.x + (__uint_as_float(r[4 * qq]) + b.x), x.y + (__uint_as_float(r[4 * qq + 1]) + b.y),
+                                       x.z + (__uint_as_float(r[4 * qq + 2]) + b.z),
+                                       x.w + (__uint_as_float(r[4 * qq + 3]) + b.w));
+          if (u < 2) {
+            *reinterpret_cast<float4*>(xp) = y;
+            *reinterpret_cast<uint2*>(pbuf + p_off(kSPOff + i, c >> 2)) =
+                f16x4(snake4(y, lds4(cf + L::kPreA + (u + 1) * C + c), lds4(cf + L::kPreR + (u + 1) * C + c)));
+          } else {
+            const float4 sc = lds4(cf + L::kNScale + c), of = lds4(cf + L::kNOffset + c);
+            float4 w4 = make_float4(__fadd_rn(__fmul_rn(y.x, sc.x), of.x), __fadd_rn(__fmul_rn(y.y, sc.y), of.y),
+                                    __fadd_rn(__fmul_rn(y.z, sc.z), of.z), __fadd_rn(__fmul_rn(y.w, sc.w), of.w));
+            w4 = snake4(w4, lds4(cf + L::kNAlpha + c), lds4(cf + L::kNRecip + c));
+            split_bf16(w4.x, w4.y, hi[2 * qq], lo[2 * qq]);
+            split_bf16(w4.z, w4.w, hi[2 * qq + 1], lo[2 * qq + 1]);
+          }
+        }
+        if (u == 2 && !discard && i < v) {
+          // Row g (time tj of its stream) of both planes; one row later in the
+          // shifted planes unless it is the stream's last row; a stream's first
+          // row of the shifted planes holds the conv's history (the previous
+          // activated input, packed (hi << 16) | lo); the stream's last row
+          // becomes the new history row.
+          const int g = m0 + i, tj = j * kSR + i;
+          const size_t plane = (size_t)a.rows * C;
+          uint4* ph = reinterpret_cast<uint4*>(a.out_planes + (size_t)g * C + c0);
+          uint4* pl = reinterpret_cast<uint4*>(a.out_planes + plane + (size_t)g * C + c0);
+#pragma unroll
+          for (int e = 0; e < kCW / 8; ++e) {
+            ph[e] = make_uint4(hi[4 * e], hi[4 * e + 1], hi[4 * e + 2], hi[4 * e + 3]);
+            pl[e] = make_uint4(lo[4 * e], lo[4 * e + 1], lo[4 * e + 2], lo[4 * e + 3]);
+          }
+          if (tj + 1 < N) {
+            uint4* qh = reinterpret_cast<uint4*>(a.out_planes_prev + (size_t)(g + 1) * C + c0);
+            uint4* ql = reinterpret_cast<uint4*>(a.out_planes_prev + plane + (size_t)(g + 1) * C + c0);
+#pragma unroll
+            for (int e = 0; e < kCW / 8; ++e) {
+              qh[e] = make_uint4(hi[4 * e], hi[4 * e + 1], hi[4 * e + 2], hi[4 * e + 3]);
+              ql[e] = make_uint4(lo[4 * e], lo[4 * e + 1], lo[4 * e + 2], lo[4 * e + 3]);
+            }
+          }
+          const bool have = a.state.pool && !(code & 2);
+          if (tj == 0) {
+            uint4* qh = reinterpret_cast<uint4*>(a.out_planes_prev + (size_t)g * C + c0);
+            uint4* ql = reinterpret_cast<uint4*>(a.out_planes_prev + plane + (size_t)g * C + c0);
+            const uint4* old = have ? reinterpret_cast<const uint4*>(slot_base(a.state, code) + a.hist_next.ring +
+                                                                     misc[3] * a.hist_next.width + c0)
+                                    : nullptr;
+#pragma unroll
+            for (int e = 0; e < kCW / 8; ++e) {
+              const uint4 w0 = old ? __ldg(old + 2 * e) : make_uint4(0u, 0u, 0u, 0u);
+              const uint4 w1 = old ? __ldg(old + 2 * e + 1) : make_uint4(0u, 0u, 0u, 0u);
+              qh[e] = make_uint4(__byte_perm(w0.x, w0.y, 0x7632), __byte_perm(w0.z, w0.w, 0x7632),
+                                 __byte_perm(w1.x, w1.y, 0x7632), __byte_perm(w1.z, w1.w, 0x7632));
+              ql[e] = make_uint4(__byte_perm(w0.x, w0.y, 0x5410), __byte_perm(w0.z, w0.w, 0x5410),
+                                 __byte_perm(w1.x, w1.y, 0x5410), __byte_perm(w1.z, w1.w, 0x5410));
+            }
+          }
+          if (tj == N - 1 && a.state.pool) {  // a fresh stream too (its window starts at head 0)
+            uint4* dst = reinterpret_cast<uint4*>(slot_base(a.state, code) + a.hist_next.ring +
+                                                  (misc[3] ^ 1) * a.hist_next.width + c0);
+#pragma unroll
+            for (int e = 0; e < kCW / 4; ++e)
+              dst[e] = make_uint4(__byte_perm(lo[2 * e], hi[2 * e], 0x5410), __byte_perm(lo[2 * e], hi[2 * e], 0x7632),
+                                  __byte_perm(lo[2 * e + 1], hi[2 * e + 1], 0x5410),
+                                  __byte_perm(lo[2 * e + 1], hi[2 * e + 1], 0x7632));
+          }
+        }
+      }
+      if (u < 2) fill_halo(u + 1);
+      // X was written in place (units 0-1) and the next tile's TMA box goes
+      // over it: order those generic writes before the async copy.
+      if (u == 2) fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+    }
+    if (!ok) break;
+    // X has had its last reader (unit 2's epilogue): the next tile's y goes in now.
+    if (t + 1 < t_end) {
+      if (tid == 0) load_x(tile_m0(t + 1));
+      ++loads;
+    }
+    if (last && a.state.pool && tid == 0) {
+      for (int u = 0; u < 3; ++u) hist_commit_head(a.state, a.unit[u].hist, code, misc[u], N);
+      hist_commit_head(a.state, a.hist_next, code, misc[3], N);
+    }
+  }
+  // After a timeout: let the last loads and MMA group issued finish before the
+  // CTA frees its TMEM and exits (a wait on a finished phase returns at once).
+  if (!ok && tid == 0) {
+    if (loads > 0) mbar_wait(xfull, (loads - 1) & 1, a.status, kDevTimeoutLoader);
+    if (n_w > 0) mbar_wait(wfull, (n_w - 1) & 1, a.status, kDevTimeoutLoader);
+    if (n_mma > 0) mbar_wait(mma_done, (n_mma - 1) & 1, a.status, kDevTimeoutMma);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, C);
+}
+
+int g_stage_sms = 0;
+
+}  // namespace
+
+cudaError_t prepare_stage() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&g_stage_sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(stage_kernel<64, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize, StageSmem<64>::kAlloc);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(stage_kernel<64, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, StageSmem<64>::kAlloc);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(stage_kernel<128, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             StageSmem<128>::kAlloc);
+  return e;
+}
+
+cudaError_t launch_stage(const StageArgs& a, cudaStream_t stream) {
+  if (a.rows <= 0) return cudaSuccess;
+  const int N = a.rows_per_stream;
+  if (N <= 0 || a.rows % N) return cudaErrorInvalidValue;
+  const int tiles = (a.rows / N) * ((N + kSR - 1) / kSR);
+  if (a.channels == 64) {
+    // At most one tile per SM: one 512-thread CTA per tile. Otherwise two
+    // 256-thread CTAs per SM, each over a contiguous range of tiles.
+    if (tiles <= g_stage_sms) return launch_overlapped(stage_kernel<64, 512>, tiles, 512, StageSmem<64>::kAlloc, stream, a);
+    const int grid = tiles < 2 * g_stage_sms ? tiles : 2 * g_stage_sms;
+    return launch_overlapped(stage_kernel<64, 256>, grid, 256, StageSmem<64>::kAlloc, stream, a);
+  }
+  if (a.channels == 128) {
+    const int grid = tiles < g_stage_sms ? tiles : g_stage_sms;
+    return launch_overlapped(stage_kernel<128, 512>, grid, 512, StageSmem<128>::kAlloc, stream, a);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace fav

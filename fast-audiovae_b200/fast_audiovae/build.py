@@ -17,7 +17,7 @@ ROOT = PACKAGE_DIR.parent
 CSRC = ROOT / "csrc"
 INCLUDE = ROOT.parent / "include"
 LIBRARY = PACKAGE_DIR / "libfav_cuda.so"
-SOURCES = ("fav_kernels.cu", "fav_tail.cu", "fav_prepass.cu", "fav_api.cu")
+SOURCES = ("fav_kernels.cu", "fav_tail.cu", "fav_stage.cu", "fav_prepass.cu", "fav_api.cu")
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-shared", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden"]
 

@@ -1,11 +1,11 @@
 """Bounded waits that run out, on a B200 (``-m gpu``).
 
-Every mbarrier wait in the GEMM engine is bounded; when one runs out the
+Every mbarrier wait in the GEMM engine and the fused stage kernels is bounded; when one runs out the
 kernel drains the copies and MMAs it started, records a timeout code in the
 caller's status word and returns, so the CUDA context stays usable. The
 reference's streaming contract (``src/fast_audiovae/gpu.py:216-225``) is that
 a failed step leaves the stream's history as it was. ``fav_debug_step_gated``
-makes one engine launch wait for a device flag that nothing sets, with a
+makes one engine (or fused stage) launch wait for a device flag that nothing sets, with a
 short poll limit on every wait of that launch: nothing faults or hangs, the
 status word reports the timeout, and the next ordinary step from the same
 committed history gives the same audio as a run that never failed.
@@ -105,8 +105,10 @@ def committed_windows(pool, read_table=0):
 @pytest.mark.parametrize("layer", [0, 1, 2, 9, 10, 14, 20])
 def test_gated_launch_times_out_and_history_survives(lib, plan, layer):
     """Layer 0 = stem, 1 = stage 0 transposed conv, 2 = stage 0 residual unit
-    (preformed operand), 9 = stage 2 transposed conv, 10 / 14 / 20 = residual
-    units of stages 2 / 3 / 4 (20 writes stage 5's planes)."""
+    (preformed operand), 9 = stage 2 transposed conv, 10 = a residual unit of
+    stage 2, 14 / 20 = residual units of stages 3 / 4, which run as the fused
+    stage kernels (their first MMA waits for the gate; stage 4's writes stage
+    5's planes)."""
     gate = torch.zeros(1, dtype=torch.int32, device="cuda")  # nothing ever sets it
     failing, clean = Run(lib, plan), Run(lib, plan)
     for _ in range(2):
