@@ -5,7 +5,7 @@ Workloads (``--workload``; the default is what the headline line reports):
   stream40ms  every GPU decodes 512 independent streams (the per-GPU shard of
               cfg5's 4096 streams on 8 GPUs) on 1-frame (40 ms, 1920-sample)
               chunks with carried history, bf16 plan. One step = one chunk for
-              all 512 streams (29 kernel launches). Weak scaling.
+              all 512 streams (25 kernel launches). Weak scaling.
   cfg3        256 streams x 2-frame (80 ms) chunks per step, bf16. Weak scaling.
   int8        stream40ms's shape on the int8 (W8A8) plan (cfg5's precision).
   cfg1        batch decode of one clip [1,64,25] (1 s of audio) per step.
@@ -65,11 +65,24 @@ FRAME_SECONDS = 1920 / 48000
 RATES = (8, 6, 5, 2, 2, 2)
 FLOPS_PER_FRAME = 706_740_224  # 2 x 353,370,112 MAC of the 25 GEMMs per latent frame
 TRAFFIC_FILE = ROOT / "bench_traffic.json"
-# Kernels of one step, in launch order of the per-layer timing: the stem, per
-# stage a transposed conv and three residual units (stage 5: its transposed
-# conv and the fused tail = three residual units + final conv).
-LAYER_NAMES = ["stem"] + [f"stage{i}.{k}" for i in range(5) for k in ("transpose", "res0", "res1", "res2")] + \
-    ["stage5.transpose", "stage5.tail"]
+
+
+def fused_stage(i, precision=0):
+    """Stages whose three residual units and the next conv's planes run as one
+    fused kernel: 3 and 4 (bf16 units), stage 4 only in the int8 plan."""
+    return i == 4 or (i == 3 and precision == 0)
+
+
+def kernel_names(precision=0):
+    """Kernels of one step, in launch order of the per-layer timing: the stem,
+    per stage a transposed conv and three residual units (``stageI.units`` for
+    a fused stage), stage 5's transposed conv and the fused tail (three
+    residual units + final conv)."""
+    names = ["stem"]
+    for i in range(5):
+        names.append(f"stage{i}.transpose")
+        names += [f"stage{i}.units"] if fused_stage(i, precision) else [f"stage{i}.res{j}" for j in range(3)]
+    return names + ["stage5.transpose", "stage5.tail"]
 
 
 @dataclass(frozen=True)
@@ -127,7 +140,7 @@ def peaks():
 
 # ------------------------------------------------------------------ algorithmic cost
 def layer_costs(precision=0):
-    """Per kernel of ``LAYER_NAMES``, per latent frame: algorithmic FLOPs (2*MAC
+    """Per kernel of ``kernel_names(precision)``, per latent frame: algorithmic FLOPs (2*MAC
     of the contractions), HBM bytes of this design's data layout (each
     activation read and written once), CUDA-core work (FP32 instructions and
     special-function sines), and per-launch weight bytes and per-stream history
@@ -135,11 +148,13 @@ def layer_costs(precision=0):
 
     Layout (bf16 plan): a transposed conv reads its input as split-bf16 planes
     (hi + lo, 4 B per element) twice (as they are, and one time step later for
-    its second tap) and writes y in fp32 (plus Snake_pre(y) at stages 0-1,
-    whose units read it); the residual units of stages 2-4 read y and write y (the last unit the
-    next conv's two plane copies); stages 0-1's units read Snake_pre(y), write
-    their f16 operand once and read it back. The fused stage-5 tail reads its
-    input once and writes audio; its intermediates stay on chip.
+    its second tap) and writes y in fp32 (plus Snake_pre(y) at stages 0-2,
+    whose units read it); the residual units of stage 2 read y and write y (the
+    last unit the next conv's two plane copies); stages 0-1's units read
+    Snake_pre(y), write their f16 operand once and read it back. A fused stage
+    (3-4) reads its input y once and writes the next conv's two plane copies;
+    the fused stage-5 tail reads its input once and writes audio; their
+    intermediates stay on chip.
 
     CUDA-core work per element of a residual unit: two Snakes (4 FP32 + 1 sine
     each), the depthwise k=7 tap chain with its bias (8) and the skip/bias add
@@ -152,7 +167,7 @@ def layer_costs(precision=0):
     cin = 2048
     for i, s in enumerate(RATES):
         cout = cin // 2
-        y_only = i == 5 or (precision == 0 and 2 <= i <= 4)
+        y_only = i == 5 or fused_stage(i, precision) or (precision == 0 and i == 2)
         out_elems = n * s * cout
         out.append(dict(flops=2 * cin * cout * 2 * s * n, act=n * cin * 8 + out_elems * (4 if y_only else 8),
                         weights=cin * cout * 2 * s * 4, hist=0,
@@ -164,6 +179,12 @@ def layer_costs(precision=0):
                             hist=(6 + 18 + 54 + 6) * cout * 4 * 2, fp32=rows * 2090, sfu=rows * 225))
             break
         elems = n * cout
+        if fused_stage(i, precision):
+            out.append(dict(flops=3 * 2 * cout * cout * n, act=elems * (4 + 8), weights=3 * cout * cout * 2,
+                            hist=(6 + 18 + 54) * cout * 4 * 2 + cout * 4 * 2,
+                            fp32=elems * (3 * 18 + 9), sfu=elems * (3 * 2 + 1)))
+            cin = cout
+            continue
         for j, d in enumerate((1, 3, 9)):
             last = j == 2
             if precision == 0 and i >= 2:
@@ -174,7 +195,7 @@ def layer_costs(precision=0):
                             hist=6 * d * cout * 4 * 2 + (cout * 4 * 2 if last else 0),
                             fp32=elems * (18 + (9 if last else 0)), sfu=elems * (2 + (1 if last else 0))))
         cin = cout
-    assert len(out) == len(LAYER_NAMES)
+    assert len(out) == len(kernel_names(precision))
     return out
 
 
@@ -198,6 +219,7 @@ def stored_traffic(workload, streams, frames):
 
 def roofline(layer_ms, frames_per_launch, streams, pk, workload, frames, precision):
     costs = layer_costs(precision)
+    names = kernel_names(precision)
     dom = int(np.argmax(layer_ms))
     c = costs[dom]
     flops = c["flops"] * frames_per_launch
@@ -214,8 +236,8 @@ def roofline(layer_ms, frames_per_launch, streams, pk, workload, frames, precisi
         achieved, peak, unit, bound = bytes_ / sec / 1e9, pk["hbm_gbs"], "GB/s", "hbm"
     binding = max((t_tensor, "tensor"), (t_hbm, "hbm"), (t_core, "cuda_core"))[1]
     tr = stored_traffic(workload, streams, frames)
-    traffic = tr["layers"].get(LAYER_NAMES[dom]) if tr else None
-    return {"kernel": LAYER_NAMES[dom], "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+    traffic = tr["layers"].get(names[dom]) if tr else None
+    return {"kernel": names[dom], "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
             "frac": round(achieved / peak, 4), "traffic": traffic,
             "traffic_source": f"ncu dram__bytes_read.sum + dram__bytes_write.sum ({TRAFFIC_FILE.name}: "
                               f"{tr['source']})" if traffic else None,
@@ -226,7 +248,7 @@ def roofline(layer_ms, frames_per_launch, streams, pk, workload, frames, precisi
                                    f"{pk['sm_mhz']:.0f} MHz"},
             "share_of_step": round(float(layer_ms[dom] / np.sum(layer_ms)), 4),
             "algorithmic_per_launch": {"flops": flops, "bytes": bytes_}, "peak_source": pk["source"],
-            "layer_ms": {LAYER_NAMES[i]: round(float(v), 4) for i, v in enumerate(layer_ms)}}
+            "layer_ms": {names[i]: round(float(v), 4) for i, v in enumerate(layer_ms)}}
 
 
 def tensor_roofline(frames, dev_s, e2e_s, pk):
@@ -239,11 +261,18 @@ def tensor_roofline(frames, dev_s, e2e_s, pk):
             "e2e_frac": round(e2e / pk["tflops"], 4), "peak_tflops": pk["tflops"], "peak_source": pk["source"]}
 
 
-def kernel_ms(layer_ms26):
-    """Per-kernel durations from the 26 per-layer event intervals of
-    ``fav_step_profile`` (the fused tail spans layers 22-25)."""
+def kernel_ms(layer_ms26, precision=0):
+    """Per-kernel durations (``kernel_names(precision)``) from the 26 per-layer
+    event intervals of ``fav_step_profile``: interval 0 is the stem, 1 + 4i
+    stage i's transposed conv, 2 + 4i + j its residual unit j (a fused stage's
+    kernel spans its three), 21 stage 5's conv and 22-25 the fused tail."""
     v = np.asarray(layer_ms26, dtype=np.float64)
-    return np.concatenate([v[:22], [v[22:].sum()]])
+    out = [v[0]]
+    for i in range(5):
+        out.append(v[1 + 4 * i])
+        units = v[2 + 4 * i:5 + 4 * i]
+        out += [units.sum()] if fused_stage(i, precision) else list(units)
+    return np.array(out + [v[21], v[22:].sum()])
 
 
 # ------------------------------------------------------------------ clocks
@@ -496,7 +525,7 @@ def count_kernels(torch, launch):
     return int(kernels)
 
 
-def profile_layers(lib, _native, plan, S, F, z_dev, audio, ws, ws_bytes, status, stream, reps=20, warm=3):
+def profile_layers(lib, _native, plan, S, F, z_dev, audio, ws, ws_bytes, status, stream, precision, reps=20, warm=3):
     """Per-kernel CUDA-event durations (ms) of a step of S streams x F frames:
     the median over ``reps`` profiled steps after ``warm`` uncounted ones."""
     import torch
@@ -512,7 +541,7 @@ def profile_layers(lib, _native, plan, S, F, z_dev, audio, ws, ws_bytes, status,
                                                 ws_bytes, P(status), buf, stream))
         if r >= warm:
             runs.append(np.array(buf[:]))
-    return kernel_ms(np.median(np.stack(runs), axis=0))
+    return kernel_ms(np.median(np.stack(runs), axis=0), precision)
 
 
 def run_stream(args, wl, world, rank, local):
@@ -566,7 +595,8 @@ def run_stream(args, wl, world, rank, local):
     clock_info = clocks.stop() if clocks else None
     assert status.item() == 0, "kernel status %x" % status.item()
     barrier(world)
-    layer_ms = profile_layers(lib, _native, be.plan, S, F, z_dev[Wm], audio, ws, ws_bytes, status, stream)
+    layer_ms = profile_layers(lib, _native, be.plan, S, F, z_dev[Wm], audio, ws, ws_bytes, status, stream,
+                              wl.precision)
 
     # end to end through the public API: host chunks in, host audio out
     streams = [dec.stream() for _ in range(S)]
@@ -675,7 +705,8 @@ def run_batch(args, wl, world, rank, local):
     ac = torch.empty(n, 1920 * chunk, device="cuda")
     wsc_bytes = int(lib.fav_plan_workspace_bytes(be.plan.handle, n, chunk))
     wsc = torch.empty(wsc_bytes, dtype=torch.uint8, device="cuda")
-    layer_ms = profile_layers(lib, _native, be.plan, n, chunk, zc, ac, wsc, wsc_bytes, status, stream)
+    layer_ms = profile_layers(lib, _native, be.plan, n, chunk, zc, ac, wsc, wsc_bytes, status, stream,
+                              wl.precision)
     del zc, ac, wsc
 
     # end to end through the public API (shard.decode_clips -> decode_many)
@@ -735,15 +766,17 @@ def base_line(args, wl, world, K, Wm, dev_s, audio_s, scaling):
 LAUNCH_ORDER = (["stem"]
                 + [x for i in (0, 1) for x in [f"stage{i}.transpose"]
                    + [y for j in range(3) for y in (f"stage{i}.res{j}", f"stage{i}.res{j}")]]
-                + [x for i in (2, 3, 4) for x in [f"stage{i}.transpose"] + [f"stage{i}.res{j}" for j in range(3)]]
+                + ["stage2.transpose"] + [f"stage2.res{j}" for j in range(3)]
+                + [x for i in (3, 4) for x in (f"stage{i}.transpose", f"stage{i}.units")]
                 + ["stage5.transpose", "stage5.tail"])
 
 
 def ingest_ncu(path):
     """bench_traffic.json from an ncu launch list (csv) of one default step: the
     launches in order (stem, per stage 0-1 a conv and each unit's depthwise
-    pre-pass + GEMM, per stage 2-4 a conv and three units, stage 5's conv and
-    tail), DRAM bytes per layer (a unit's two launches summed)."""
+    pre-pass + GEMM, stage 2's conv and three units, per stage 3-4 a conv and
+    the fused stage, stage 5's conv and tail), DRAM bytes per kernel (a unit's
+    two launches summed)."""
     rows = {}
     with open(path) as f:
         lines = [l for l in f if l.startswith('"')]

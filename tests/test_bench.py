@@ -1,6 +1,8 @@
 """Host-side checks of bench.py's cost model and launch bookkeeping (CPU)."""
 import json
 
+import numpy as np
+
 import bench
 
 
@@ -10,14 +12,27 @@ def test_layer_costs_sum_to_the_step_contraction():
     32 -> 1 conv runs on CUDA cores and is not counted)."""
     for precision in (0, 1):
         costs = bench.layer_costs(precision)
-        assert len(costs) == len(bench.LAYER_NAMES) == 23
+        assert len(costs) == len(bench.kernel_names(precision)) == (19 if precision == 0 else 21)
         assert sum(c["flops"] for c in costs) == bench.FLOPS_PER_FRAME
 
 
 def test_launch_order_is_one_default_step():
-    # stem; stages 0-1: conv + 3 x (depthwise pre-pass, GEMM); stages 2-4: conv + 3 units; stage 5: conv + tail
-    assert len(bench.LAUNCH_ORDER) == 1 + 2 * 7 + 3 * 4 + 2 == 29
-    assert set(bench.LAUNCH_ORDER) == set(bench.LAYER_NAMES)
+    # stem; stages 0-1: conv + 3 x (depthwise pre-pass, GEMM); stage 2: conv + 3 units;
+    # stages 3-4: conv + fused stage; stage 5: conv + tail
+    assert len(bench.LAUNCH_ORDER) == 1 + 2 * 7 + 4 + 2 * 2 + 2 == 25
+    assert set(bench.LAUNCH_ORDER) == set(bench.kernel_names(0))
+
+
+def test_kernel_ms_folds_fused_layers():
+    v = np.arange(26, dtype=np.float64)
+    k = bench.kernel_ms(v, 0)
+    names = bench.kernel_names(0)
+    assert len(k) == len(names) and abs(k.sum() - v.sum()) < 1e-9
+    assert k[names.index("stage3.units")] == 14 + 15 + 16
+    assert k[names.index("stage5.tail")] == 22 + 23 + 24 + 25
+    k8 = bench.kernel_ms(v, 1)
+    names8 = bench.kernel_names(1)
+    assert k8[names8.index("stage3.res1")] == 15 and k8[names8.index("stage4.units")] == 18 + 19 + 20
 
 
 def test_tensor_roofline_fraction():
@@ -29,7 +44,7 @@ def test_tensor_roofline_fraction():
 
 def test_roofline_names_the_binding_pipe():
     pk = {"hbm_gbs": 6000.0, "tflops": 1400.0, "sm_mhz": 1965.0, "source": "test"}
-    layer_ms = [0.1] * 22 + [0.5]  # the tail dominates
+    layer_ms = [0.1] * 18 + [0.5]  # the tail dominates
     r = bench.roofline(layer_ms, 512, 512, pk, "stream40ms", 1, 0)
     assert r["kernel"] == "stage5.tail" and r["bound"] in ("hbm", "tensor")
     assert r["binding"] == "cuda_core"
