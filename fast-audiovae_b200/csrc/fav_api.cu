@@ -129,6 +129,17 @@ int32_t encode_stage_map(CUtensorMap* map, const float* x, int rows, int channel
   return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_128B, "stage");
 }
 
+// Split-bf16 planes [2][streams][rows_per_stream][channels] written by a fused
+// residual stage: store boxes of 64 channels x 128 rows in the 128-byte
+// swizzle; rows past a stream's end fall outside the box's tensor and are not
+// written.
+int32_t encode_stage_planes_map(CUtensorMap* map, const void* planes, int streams, int rows_per_stream, int channels) {
+  const cuuint64_t dims[4] = {(cuuint64_t)channels, (cuuint64_t)rows_per_stream, (cuuint64_t)streams, 2};
+  const cuuint32_t box[4] = {64, (cuuint32_t)fav::kTileM, 1, 1};
+  return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, planes, 4, dims, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                    "stage planes");
+}
+
 std::once_flag g_prepare_once;
 cudaError_t g_prepare_error = cudaSuccess;
 
@@ -669,7 +680,10 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
         sa.wait_limit = diag->wait_limit;
         sa.gate = diag->gate;
       }
+      sa.x = X[0];
       if ((es = encode_stage_map(&sa.xmap, X[0], sa.rows, st.c_out)) != FAV_OK) return es;
+      if ((es = encode_stage_planes_map(&sa.planes_map, planes, n_streams, n, st.c_out)) != FAV_OK) return es;
+      if ((es = encode_stage_planes_map(&sa.prev_map, planes_prev, n_streams, n, st.c_out)) != FAV_OK) return es;
       if ((e = fav::launch_stage(sa, stream)) != cudaSuccess) return cuda_fail(e, "stage launch");
       // The fused kernel's time counts as the stage's first residual unit.
       for (int j = 0; j < 3; ++j) mark(++layer + 1);

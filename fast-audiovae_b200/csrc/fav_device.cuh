@@ -122,6 +122,23 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// 4-D TMA tile store of the box at coordinates (x = innermost, y, z, w) from
+// own shared memory, in the issuing thread's bulk async-group. Rows outside
+// the tensor are not written; x must be 16-byte aligned and every coordinate
+// non-negative.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(src))
+               : "memory");
+}
+// Closes the issuing thread's current bulk async-group.
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every bulk group of this thread has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until every bulk group of this thread has completed (writes visible).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Programmatic dependent launch. A kernel launched with the programmatic
 // stream serialization attribute may start while the previous kernel in the
 // stream is still draining: it waits here, before touching any memory an

@@ -224,6 +224,11 @@ struct StageUnitArgs {
 };
 struct StageArgs {
   CUtensorMap xmap;      // stage input y [rows][C] fp32: boxes of 32 channels x 128 rows, 128-byte swizzle
+  // out_planes / out_planes_prev as [2 planes][streams][rows_per_stream][C]
+  // bf16: store boxes of 64 channels x 128 rows, 128-byte swizzle.
+  CUtensorMap planes_map;
+  CUtensorMap prev_map;
+  const float* x;        // the stage input (L2 prefetch of the next tile)
   int channels;          // C: 64 or 128
   int rows;              // all streams' rows
   int rows_per_stream;

@@ -261,6 +261,15 @@ __global__ void __launch_bounds__(kThreads, 512 / kThreads) stage_kernel(const _
       misc[tid] = (a.state.pool && !(code & 2)) ? head_table(slot_base(a.state, code), code & 1)[h.index] : 0;
       if (tid == 0) misc[4] = code;
     }
+    // The previous tile's plane stores have read their staging tiles (A and
+    // P) before this tile writes them; the next tile's rows head into L2.
+    if (tid == 0) {
+      bulk_wait_read_all();
+      if (t + 1 < t_end) {
+        const int m1 = tile_m0(t + 1);
+        prefetch_l2(a.x + (size_t)m1 * C, (uint32_t)(min(kSR, a.rows - m1) * C * 4));
+      }
+    }
     ok = __syncthreads_and(mbar_wait(xfull, k & 1, a.status, kDevTimeoutLoader, wl));
     if (!ok) break;
     const int code = misc[4];
@@ -383,30 +392,25 @@ __global__ void __launch_bounds__(kThreads, 512 / kThreads) stage_kernel(const _
             split_bf16(w4.z, w4.w, hi[2 * qq + 1], lo[2 * qq + 1]);
           }
         }
-        if (u == 2 && !discard && i < v) {
-          // Row g (time tj of its stream) of both planes; one row later in the
-          // shifted planes unless it is the stream's last row; a stream's first
-          // row of the shifted planes holds the conv's history (the previous
-          // activated input, packed (hi << 16) | lo); the stream's last row
-          // becomes the new history row.
-          const int g = m0 + i, tj = j * kSR + i;
-          const size_t plane = (size_t)a.rows * C;
-          uint4* ph = reinterpret_cast<uint4*>(a.out_planes + (size_t)g * C + c0);
-          uint4* pl = reinterpret_cast<uint4*>(a.out_planes + plane + (size_t)g * C + c0);
+        if (u == 2) {
+          // This row's planes into the staging tiles the TMA stores read: hi
+          // over A (the MMA has read it), lo over P (the depthwise has read
+          // it), [C / 64][128 rows][128 B] in the 128-byte swizzle.
 #pragma unroll
           for (int e = 0; e < kCW / 8; ++e) {
-            ph[e] = make_uint4(hi[4 * e], hi[4 * e + 1], hi[4 * e + 2], hi[4 * e + 3]);
-            pl[e] = make_uint4(lo[4 * e], lo[4 * e + 1], lo[4 * e + 2], lo[4 * e + 3]);
+            const int c = c0 + 8 * e;
+            const int off = (c >> 6) * kSR * 128 + sw128_offset(i, c & 63);
+            *reinterpret_cast<uint4*>(aop + off) = make_uint4(hi[4 * e], hi[4 * e + 1], hi[4 * e + 2], hi[4 * e + 3]);
+            *reinterpret_cast<uint4*>(pbuf + off) = make_uint4(lo[4 * e], lo[4 * e + 1], lo[4 * e + 2], lo[4 * e + 3]);
           }
-          if (tj + 1 < N) {
-            uint4* qh = reinterpret_cast<uint4*>(a.out_planes_prev + (size_t)(g + 1) * C + c0);
-            uint4* ql = reinterpret_cast<uint4*>(a.out_planes_prev + plane + (size_t)(g + 1) * C + c0);
-#pragma unroll
-            for (int e = 0; e < kCW / 8; ++e) {
-              qh[e] = make_uint4(hi[4 * e], hi[4 * e + 1], hi[4 * e + 2], hi[4 * e + 3]);
-              ql[e] = make_uint4(lo[4 * e], lo[4 * e + 1], lo[4 * e + 2], lo[4 * e + 3]);
-            }
-          }
+        }
+        if (u == 2 && !discard && i < v) {
+          // A stream's first row of the shifted planes holds the conv's history
+          // (the previous activated input, packed (hi << 16) | lo); the
+          // stream's last row becomes the new history row. (The TMA stores
+          // write every other row of both plane copies.)
+          const int g = m0 + i, tj = j * kSR + i;
+          const size_t plane = (size_t)a.rows * C;
           const bool have = a.state.pool && !(code & 2);
           if (tj == 0) {
             uint4* qh = reinterpret_cast<uint4*>(a.out_planes_prev + (size_t)g * C + c0);
@@ -437,12 +441,26 @@ __global__ void __launch_bounds__(kThreads, 512 / kThreads) stage_kernel(const _
       }
       if (u < 2) fill_halo(u + 1);
       // X was written in place (units 0-1) and the next tile's TMA box goes
-      // over it: order those generic writes before the async copy.
+      // over it; the staged planes are read by TMA stores: order those
+      // generic writes before the async proxy's accesses.
       if (u == 2) fence_async_smem();
       tc_fence_before();
       __syncthreads();
     }
     if (!ok) break;
+    // The tile's planes: rows [j*128, j*128 + 128) of stream s, and the same
+    // rows one time step later in the shifted planes; the maps' row extent is
+    // the stream's N, so rows past the stream's end are not written.
+    if (!discard && tid == 0) {
+#pragma unroll
+      for (int kb = 0; kb < kKB; ++kb) {
+        tma_store_4d(&a.planes_map, aop + kb * kSR * 128, 64 * kb, j * kSR, s, 0);
+        tma_store_4d(&a.planes_map, pbuf + kb * kSR * 128, 64 * kb, j * kSR, s, 1);
+        tma_store_4d(&a.prev_map, aop + kb * kSR * 128, 64 * kb, j * kSR + 1, s, 0);
+        tma_store_4d(&a.prev_map, pbuf + kb * kSR * 128, 64 * kb, j * kSR + 1, s, 1);
+      }
+      bulk_commit();
+    }
     // X has had its last reader (unit 2's epilogue): the next tile's y goes in now.
     if (t + 1 < t_end) {
       if (tid == 0) load_x(tile_m0(t + 1));
@@ -460,6 +478,7 @@ __global__ void __launch_bounds__(kThreads, 512 / kThreads) stage_kernel(const _
     if (n_w > 0) mbar_wait(wfull, (n_w - 1) & 1, a.status, kDevTimeoutLoader);
     if (n_mma > 0) mbar_wait(mma_done, (n_mma - 1) & 1, a.status, kDevTimeoutMma);
   }
+  if (tid == 0) bulk_wait_all();  // the last plane stores have landed
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, C);
