@@ -269,6 +269,39 @@ __host__ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t
 }
 
 // --------------------------------------------------------------- numerics
+// Packed fp32 pairs (the sm_100 f32x2 instructions: two lanes per issue slot).
+// Each lane rounds to nearest exactly as the scalar operation does. The
+// assembler may fuse a packed multiply whose result feeds a packed add into
+// one packed fused multiply-add (a single rounding), even with the rounding
+// mode explicit, so these are used only where no product feeds an add: the
+// bf16 path's Snake and depthwise chains. The int8 path's fixed operation
+// order keeps scalar __fmul_rn / __fadd_rn.
+__device__ __forceinline__ uint64_t f2pack(float2 v) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+__device__ __forceinline__ float2 f2unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ float2 f2mul(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2pack(a)), "l"(f2pack(b)));
+  return f2unpack(d);
+}
+__device__ __forceinline__ float2 f2add(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2pack(a)), "l"(f2pack(b)));
+  return f2unpack(d);
+}
+__device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2pack(a)), "l"(f2pack(b)), "l"(f2pack(c)));
+  return f2unpack(d);
+}
+
 // Snake with the stored reciprocal: x + r * sin(a*x)^2.
 __device__ __forceinline__ float snake(float x, float a, float r) {
   const float s = __sinf(a * x);
@@ -310,6 +343,14 @@ __device__ __forceinline__ float sin_cw(float x) {
 __device__ __forceinline__ float snake_exact(float x, float a, float r) {
   const float s = sin_cw(__fmul_rn(a, x));
   return __fadd_rn(x, __fmul_rn(r, __fmul_rn(s, s)));
+}
+// Two lanes of snake: x + r * sin(a*x)^2 with the hardware sine; the
+// products and the fused multiply-add as packed fp32 operations (the same
+// roundings as snake).
+__device__ __forceinline__ float2 snake2(float2 x, float2 a, float2 r) {
+  const float2 ax = f2mul(a, x);
+  const float2 s = make_float2(__sinf(ax.x), __sinf(ax.y));
+  return f2fma(r, f2mul(s, s), x);
 }
 
 // The W8A8 recipe's symmetric quantisation (precision.cpp:82-92 of the

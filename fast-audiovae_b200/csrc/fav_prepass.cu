@@ -63,7 +63,8 @@ __global__ void __launch_bounds__(kDwThreads, 4) depthwise_kernel(const __grid_c
       win[j] = zero4;
     }
   }
-  const float4 y = snake4(dw7<false>(w, win, ldg4(cf + 7 * 64)), ldg4(cf + 8 * 64), ldg4(cf + 9 * 64));
+  const float4 y =
+      snake4<false, false>(dw7<false, false>(w, win, ldg4(cf + 7 * 64)), ldg4(cf + 8 * 64), ldg4(cf + 9 * 64));
   *reinterpret_cast<uint2*>(a.a + (size_t)g * C + 4 * q) = make_uint2(pack_f16(y.x, y.y), pack_f16(y.z, y.w));
   if (!pool) return;
   if (t >= N - n_new)
