@@ -503,7 +503,7 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       l.epi = fav::kEpiAct | (debug_y ? fav::kEpiX : 0);
       l.out_s = act;
       l.rowmax_out = rowmax;
-      l.rowmax_parts = l.n_total / l.n_tile;
+      l.rowmax_parts = l.n_total / l.n_tile;  // the units recount them once their kind and N tile are set
     } else {
       l.epi = fav::kEpiPlanes | (debug_y ? fav::kEpiX : 0);
       l.out_planes = planes;
@@ -730,7 +730,6 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
         u.next_recip = st.res[j + 1].pre_r;
       } else if (i + 1 < fav::kStages) {
         feed_tconv(u, i + 1, debug_y);
-        act_parts = u.rowmax_parts;
       } else {
         u.epi = fav::kEpiS | (debug_y ? fav::kEpiX : 0);
         u.next_alpha = p->fin_a;
@@ -739,9 +738,10 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       if (r.int8) {
         // W8A8: the quantising pre-pass writes the s8 A operand and its row
         // scales into the shifted planes' region (idle in int8 plans but for
-        // the up to four partial row maxima per row the stage's last unit
-        // writes at its start for the next int8 conv); the engine TMA-loads it.
-        uint8_t* q8 = reinterpret_cast<uint8_t*>(rowmax + (size_t)u.rows * 4);
+        // the up to kMaxRowmaxParts partial row maxima per row the stage's
+        // last unit writes at its start for the next int8 conv); the engine
+        // TMA-loads it.
+        uint8_t* q8 = reinterpret_cast<uint8_t*>(rowmax + (size_t)u.rows * fav::kMaxRowmaxParts);
         float* qscale = reinterpret_cast<float*>(q8 + (size_t)u.rows * st.c_out);
         const fav::QuantResidualArgs qa{S[in], q8, qscale, r.coef, u.rows, n, st.c_out, r.dilation, state, u.hist};
         if ((e = fav::launch_quantize_residual(qa, stream)) != cudaSuccess) return cuda_fail(e, "quantize launch");
@@ -765,6 +765,11 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
         return es;
       }
       narrow(u, u.n_tile);
+      if (u.epi & fav::kEpiAct) {
+        // One partial row maximum per N tile and epilogue column group.
+        u.rowmax_parts = (u.n_total / u.n_tile) * fav::epilogue_column_groups(u.n_tile, u.kind);
+        act_parts = u.rowmax_parts;
+      }
       diagnose(u, layer + 1);
       if ((e = fav::launch_gemm_layer(u, stream)) != cudaSuccess) return cuda_fail(e, "residual launch");
       if (last_out) *last_out = X[out];

@@ -73,8 +73,9 @@ enum EpilogueFlags : int {
   kEpiPlanes = 8,  // split-bf16 hi/lo planes of Snake(y * next_scale + next_offset) to out_planes, the
                    // same planes one row later per stream to out_planes_prev (row t holds t - 1; a
                    // stream's first row holds the next layer's history), and the next layer's history
-  kEpiAct = 16,    // int8 path: Snake(y * next_scale + next_offset) fp32 to out_s, this tile's per-row max of
-                   // its magnitude to rowmax_out[row * rowmax_parts + n_tile], and the next layer's history
+  kEpiAct = 16,    // int8 path: Snake(y * next_scale + next_offset) fp32 to out_s, per row the max of its
+                   // magnitude over each column group of each N tile to rowmax_out[row * rowmax_parts + part],
+                   // and the next layer's history
   kEpiS16 = 32,    // Snake(y) with next_alpha/next_recip rounded to f16, to out_s read as f16 (same layout
                    // as kEpiS at half the bytes)
 };
@@ -306,6 +307,11 @@ cudaError_t prepare_tail();
 
 // Kernel launchers (fav_kernels.cu). Return cudaError_t of the launch.
 cudaError_t launch_gemm_layer(const LayerArgs& a, cudaStream_t stream);
+// Epilogue warps per TMEM lane quarter of the engine instance that runs a
+// layer of this N tile and kind (3 for TMA-fed A operands, else 1); a kEpiAct
+// epilogue writes rowmax_parts = (n_total / n_tile) * that partial maxima per row.
+int epilogue_column_groups(int n_tile, int kind);
+constexpr int kMaxRowmaxParts = 12;
 // The int8 plan's stem (depthwise k=7 -> 1x1 -> stage 0's affine + Snake, row
 // maxima and history) on CUDA cores, every sum in the int8 oracle's order.
 cudaError_t launch_stem_exact(const LayerArgs& a, cudaStream_t stream);

@@ -78,8 +78,14 @@ struct GemmCfg {
   static constexpr int kFixed = 1024 /*align slack*/ + 512 /*barriers*/ + kTable + kScales;
   // Epilogue column coefficients, double-buffered per tile.
   static constexpr int kEpi = 2 * 7 * NT * 4;
+  // A layer whose A operand is TMA-loaded by a pre-pass (preformed residual
+  // operand, int8 conv taps) has no producer work: its eight producer warps
+  // join the epilogue, three warps per TMEM lane quarter, each taking every
+  // third 16-column chunk of the tile.
+  static constexpr bool kWide = (KIND == kResidualPre || KIND == kTconvPre) && NT >= 64;
+  static constexpr int kEpiWarps = kWide ? kEpilogueWarps + kProducerWarps : kEpilogueWarps;
   // Per epilogue warp: one 32-row x 16-column fp32 chunk staged for coalesced stores.
-  static constexpr int kEpiStage = kEpilogueWarps * 32 * kEpiCols * 4;
+  static constexpr int kEpiStage = kEpiWarps * 32 * kEpiCols * 4;
   static constexpr int kStagesFit = (kSmemBudget - 2 * kRaw - kFixed - kEpi - kEpiStage) / kStage;
   static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
   static_assert(kStages >= 2, "pipeline needs two stages");
@@ -762,6 +768,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   // conv's planes, or a residual unit's preformed depthwise output.
   constexpr bool kTmaA = (KIND == kTconv && !kI8) || KIND == kResidualPre || KIND == kTconvPre;
   constexpr int kLpr = NT == 32 ? 8 : 16;  // residual lanes per row (C = 32 uses eight)
+  constexpr bool kWide = Cfg::kWide;
+  constexpr int kEW = Cfg::kEpiWarps;               // epilogue warps
+  constexpr int kEpiFirst = kWide ? 0 : kProducerWarps;  // the first of them
+  constexpr int kCG = kEW / 4;                        // epilogue warps per TMEM lane quarter
   extern __shared__ uint8_t smem_raw[];
   // Aligned by an offset from the shared array (not through an integer), so
   // the compiler keeps every access through it in the shared state space.
@@ -809,13 +819,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kEpilogueWarps);
+      mbar_init(&acc_empty[b], kEW);
       mbar_init(&raw_full[b], 1);
       mbar_init(&raw_empty[b], kProducerWarps);
       mbar_init(&table_full[b], 1);
       mbar_init(&table_empty[b], kProducerWarps);
       mbar_init(&scale_full[b], 1);
-      mbar_init(&scale_empty[b], kEpilogueWarps);
+      mbar_init(&scale_empty[b], kEW);
     }
     mbar_init(mma_drain, 1);
     fence_mbar_init();
@@ -830,7 +840,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
   const uint32_t tmem = *tmem_slot;
   grid_dependency_sync();
 
-  if (warp < kProducerWarps) {
+  if (!kWide && warp < kProducerWarps) {
     // ---- A producers (a bf16 transposed conv has none: its A operand is TMA-loaded whole)
     if (kTmaA) goto done;
     if (KIND == kResidual && kLpr == 8) {
@@ -957,8 +967,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
     // chunk computes (bf16 paths).
     constexpr int kChunks = NT / kEpiCols;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int etid = threadIdx.x - kProducerThreads;
-    float* stage = epi_stage + (warp - kProducerWarps) * 32 * kEpiCols;
+    const int cg = (warp - kEpiFirst) >> 2;  // column group: chunks cg, cg + kCG, ...
+    const int etid = threadIdx.x - kEpiFirst * 32;
+    float* stage = epi_stage + (warp - kEpiFirst) * 32 * kEpiCols;
     const int epi = a.epi;
     bool ok = true;
     uint32_t i = 0;
@@ -976,7 +987,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         staged_n0 = n0;
       }
       float* cf = epi_coef + cbuf * kEpiCoefVectors * NT;
-      for (int j = etid; restage && j < NT; j += kEpilogueWarps * 32) {
+      for (int j = etid; restage && j < NT; j += kEW * 32) {
         const int n = n0 + j;
         const int ch = kConv ? n % a.c_out : n;
         cf[j] = a.bias ? __ldg(a.bias + ch) : 0.f;
@@ -991,7 +1002,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         if (kI8 && a.w_scale) cf[5 * NT + j] = __ldg(a.w_scale + n);
         if (kI8Tconv) cf[6 * NT + j] = __ldg(a.w_scale2 + n);
       }
-      if (!named_barrier_and(3, kEpilogueWarps * 32, ok)) break;
+      if (!named_barrier_and(3, kEW * 32, ok)) break;
       const int row0 = m0 + q * 32;
       const int g = row0 + lane;
       const int N = a.rows_per_stream;
@@ -1016,7 +1027,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
             hist_old = reinterpret_cast<const uint32_t*>(slot + h.ring + head * h.width);
           if (t_row == N - 1) {
             hist_new = reinterpret_cast<uint32_t*>(slot + h.ring + (head ^ 1) * h.width);
-            if (n0 == 0) {
+            if (n0 == 0 && cg == 0) {
               head_out = head_table(slot, (code & 1) ^ 1) + h.index;
               head_next = head ^ 1;
             }
@@ -1033,9 +1044,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       }
       // The tile's skip input rows into L2 while the accumulator is produced
       // (one bulk prefetch per row), so the chunk loads below hit L2.
-      if (kSkipAdd && g < a.rows) prefetch_l2(a.x + (size_t)g * a.c_out + n0, NT * 4);
+      if (kSkipAdd && g < a.rows && cg == 0) prefetch_l2(a.x + (size_t)g * a.c_out + n0, NT * 4);
       float4 xr[4];  // skip input of the current chunk, coalesced order
-      load_skip<KIND>(a, row0, n0, lane, xr);
+      load_skip<KIND>(a, row0, n0 + cg * kEpiCols, lane, xr);
       uint4 hw[4];  // stem: history bits of this chunk (zero without a history row)
       if constexpr (kStemPl) {
 #pragma unroll
@@ -1063,10 +1074,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * Cfg::kAccCols);
       float rmax = 0.f;  // kEpiAct: max |output| of this row over the tile's columns
       uint32_t r[16];
-      tmem_ld16_async(base, r);
+      tmem_ld16_async(base + cg * kEpiCols, r);
       tmem_wait_ld(r);
 #pragma unroll 1
-      for (int c = 0; c < kChunks; ++c) {
+      for (int c = cg; c < kChunks; c += kCG) {
         const int n = n0 + c * kEpiCols;
         const int j0 = c * kEpiCols;
         uint32_t rn[16];
@@ -1078,16 +1089,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         // Next chunk's accumulator columns (the last chunk reloads its own):
         // issued and waited for unconditionally, so the registers the load
         // writes asynchronously never meet a control-flow merge before the wait.
-        tmem_ld16_async(base + (c + 1 < kChunks ? c + 1 : c) * kEpiCols, rn);
+        tmem_ld16_async(base + (c + kCG < kChunks ? c + kCG : c) * kEpiCols, rn);
         float4 x[4];  // this lane's row of the skip input
         if (kSkipAdd) transpose_skip(stage, lane, xr, x);
         uint4 wn[4];  // stem: next chunk's history bits
-        if (kStemPl && hist_old && c + 1 < kChunks) {
+        if (kStemPl && hist_old && c + kCG < kChunks) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) wn[j] = __ldg(reinterpret_cast<const uint4*>(hist_old + n + kEpiCols) + j);
+          for (int j = 0; j < 4; ++j) wn[j] = __ldg(reinterpret_cast<const uint4*>(hist_old + n + kCG * kEpiCols) + j);
         }
         float4 xn[4];  // next chunk's skip input
-        load_skip<KIND>(a, c + 1 < kChunks ? row0 : a.rows, n + kEpiCols, lane, xn);
+        load_skip<KIND>(a, c + kCG < kChunks ? row0 : a.rows, n + kCG * kEpiCols, lane, xn);
         float v[16];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -1206,12 +1217,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_layer_kernel(const __grid_co
         for (int j = 0; j < 16; ++j) r[j] = rn[j];
 #pragma unroll
         for (int j = 0; j < 4; ++j) xr[j] = xn[j];
-        if (kStemPl && hist_old && c + 1 < kChunks) {
+        if (kStemPl && hist_old && c + kCG < kChunks) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) hw[j] = wn[j];
         }
       }
-      if (kOutA && g < a.rows) a.rowmax_out[(size_t)g * a.rowmax_parts + n0 / NT] = rmax;
+      // One partial maximum per N tile and column group.
+      if (kOutA && g < a.rows) a.rowmax_out[(size_t)g * a.rowmax_parts + (n0 / NT) * kCG + cg] = rmax;
       if (head_out) *head_out = head_next;
       tc_fence_before();
       __syncwarp();
@@ -1500,8 +1512,16 @@ cudaError_t prepare_kernels() {
   return prepare_tail();
 }
 
+int epilogue_column_groups(int n_tile, int kind) {
+  return (kind == kResidualPre || kind == kTconvPre) && n_tile >= 64 ? (kEpilogueWarps + kProducerWarps) / 4 : 1;
+}
+
 cudaError_t launch_gemm_layer(const LayerArgs& a, cudaStream_t stream) {
   if (a.rows <= 0) return cudaSuccess;
+  if ((a.epi & kEpiAct) &&
+      (a.rowmax_parts != (a.n_total / a.n_tile) * epilogue_column_groups(a.n_tile, a.kind) ||
+       a.rowmax_parts > kMaxRowmaxParts))
+    return cudaErrorInvalidValue;
   if (a.n_total % a.n_tile) return cudaErrorInvalidValue;
   if (a.img_nt && (a.img_nt % a.n_tile || a.n_total % a.img_nt)) return cudaErrorInvalidValue;
   // A residual unit's staged box (tile + halo rows) must fit its raw buffer.
