@@ -606,11 +606,11 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
       t.hist_max_slot = fav::kNumHistories + i;
     }
     narrow(t, t.n_tile);
-    if (st.int8 && t.n_total / t.n_tile < 4) {
-      // Few N tiles (stages 3-4): the producers quantise staged fp32 rows.
+    if (st.int8 && t.n_total / t.n_tile < 2) {
+      // One N tile (stage 4): the producers quantise staged fp32 rows.
       if ((es = encode_input_map(&t.tmap, act, t.rows, st.c_in, fav::kTileM + 1)) != FAV_OK) return es;
     } else if (st.int8) {
-      // Many N tiles (stages 0-2) would each quantise the same rows: quantise
+      // Several N tiles (stages 0-3) would each quantise the same rows: quantise
       // each input row once into both s8 taps (in S[1], unused while the conv
       // runs: 2 * rows * C bytes fit the region); the engine TMA-loads them.
       uint8_t* q0 = reinterpret_cast<uint8_t*>(S[1]);
