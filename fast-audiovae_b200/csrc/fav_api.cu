@@ -469,13 +469,14 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
   // kernel; a step stopped inside stage 5 (layer checks) runs them one by one.
   bool tail = fuse && last_layer >= 25 && p->stages[fav::kStages - 1].c_out == fav::kTailC;
   for (int j = 0; j < 3; ++j) tail = tail && !p->stages[fav::kStages - 1].res[j].int8;
-  // Stages 3-4 (64 and 128 channels, bf16 units feeding a bf16 transposed
-  // conv) run their three residual units and the next conv's planes as one
-  // fused kernel, unless the step stops inside the stage or at its last unit.
+  // Stages 2-4 (256, 128 and 64 channels, bf16 units feeding a bf16
+  // transposed conv) run their three residual units and the next conv's
+  // planes as one fused kernel, unless the step stops inside the stage or at
+  // its last unit.
   auto fused_stage = [&](int i) {
     if (!fuse || i + 1 >= fav::kStages || last_layer <= 4 * i + 4) return false;
     const StageDev& st = p->stages[i];
-    if (st.c_out != 64 && st.c_out != 128) return false;
+    if (st.c_out != 64 && st.c_out != 128 && st.c_out != 256) return false;
     for (int j = 0; j < 3; ++j)
       if (st.res[j].int8) return false;
     return !p->stages[i + 1].int8;

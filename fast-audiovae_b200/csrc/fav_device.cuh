@@ -234,6 +234,19 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
                : "memory");
 }
 
+// 32 lanes x 16 consecutive fp32 columns from registers into the accumulator
+// memory, then a wait until the stores have completed (so a thread that syncs
+// with others afterwards publishes them, with the tcgen05 thread-sync fences).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 // ------------------------------------------------------------ descriptors
 // Instruction descriptor, kind::i8: s32 accumulator, signed 8-bit K-major A and B. M = 128.
 __host__ __device__ constexpr uint32_t instr_desc_i8(uint32_t n) {

@@ -1483,6 +1483,7 @@ static cudaError_t set_smem() {
   X(128, kModeI8, kTconv, kOutS) X(128, kModeI8, kTconvPre, kOutS) X(128, kModeI8, kTconv, kOutS16)       \
   X(128, kModeI8, kTconvPre, kOutS16)                                                                      \
   X(64, kModeSplit, kTconv, kOutNone) X(128, kModeSplit, kTconv, kOutNone) X(128, kModeI8, kTconv, kOutNone) \
+  X(256, kModeSplit, kTconv, kOutNone)                                                                     \
   X(256, kModeF16, kResidual, kOutS) X(128, kModeF16, kResidual, kOutS) X(64, kModeF16, kResidual, kOutS)  \
   X(256, kModeSplit, kTconv, kOutS16) X(128, kModeSplit, kTconv, kOutS16) X(64, kModeSplit, kTconv, kOutS16)   \
   X(256, kModeF16, kResidual, kOutS16) X(128, kModeF16, kResidual, kOutS16) X(64, kModeF16, kResidual, kOutS16) \

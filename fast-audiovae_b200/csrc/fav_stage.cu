@@ -35,7 +35,7 @@
 // phases of a tile are separated by block barriers: C = 64 runs two CTAs of
 // 256 threads per SM, whose phases interleave (one 512-thread CTA per tile
 // when a launch has at most one tile per SM); C = 128 runs one 512-thread CTA
-// per SM.
+// per SM. Stage 2 (C = 256) keeps y in TMEM instead (stage256_kernel below).
 #include "fav_common.cuh"
 
 namespace fav {
@@ -129,7 +129,9 @@ __host__ __device__ constexpr int stage_chain(int groups, int d) {
 // operand, A row i from P rows kSPOff - 6d + i + j*d (j = 0..6), for this
 // thread's chain of L rows i0, i0 + d, ... in channel quad q: blocks of L*d
 // rows split into d chains of L, so the seven taps slide through registers.
-template <int L>
+// GLOBAL: the coefficients are read from global memory (L1-cached) instead of
+// shared memory.
+template <int L, bool GLOBAL = false>
 __device__ __forceinline__ void stage_chains(const float* ucoef, const uint8_t* pbuf, uint8_t* aop, int rg, int q,
                                              int d) {
   const int i0 = (rg / d) * L * d + rg % d;
@@ -138,10 +140,11 @@ __device__ __forceinline__ void stage_chains(const float* ucoef, const uint8_t* 
   const float* uc = ucoef + kb * kCoefResidual * 64 + 4 * qb;
   uint8_t* ab = aop + kb * kSR * 128;
   const int base = kSPOff - 6 * d;
+  auto ld = [](const float* p) { return GLOBAL ? ldg4(p) : lds4(p); };
   float4 w[7], win[7];
 #pragma unroll
-  for (int j = 0; j < 7; ++j) w[j] = lds4(uc + j * 64);
-  const float4 bias = lds4(uc + 7 * 64), al2 = lds4(uc + 8 * 64), rc2 = lds4(uc + 9 * 64);
+  for (int j = 0; j < 7; ++j) w[j] = ld(uc + j * 64);
+  const float4 bias = ld(uc + 7 * 64), al2 = ld(uc + 8 * 64), rc2 = ld(uc + 9 * 64);
 #pragma unroll
   for (int j = 0; j < 6; ++j) win[j] = p_load(pbuf, base + i0 + j * d, q);
 #pragma unroll
@@ -484,6 +487,355 @@ __global__ void __launch_bounds__(kThreads, 512 / kThreads) stage_kernel(const _
   if (warp == 0) tmem_dealloc(tmem, C);
 }
 
+// ------------------------------------------------------------ 256 channels
+// Stage 2 (256 channels, 240 rows per stream and frame): a tile's y (128 rows
+// x 256 channels fp32, 128 KB) does not fit in shared memory beside the
+// operands, so y stays in TMEM, columns [0, 256), beside the projection's
+// accumulator D, columns [256, 512) (a whole SM's TMEM: one CTA per SM). A
+// unit runs two K blocks (128 channels) at a time: f16 Snake_pre of their y
+// columns into P (with their carried or history halo rows), the depthwise
+// chains into their A tiles, and their MMAs into D while the next pair is
+// prepared; then y = y + (D + b) in TMEM. The weights stream through two
+// 32 KB K-block buffers. The operations and their order are those
+// of the per-layer kernels, so the result is the same bit for bit.
+constexpr int kS2C = 256;
+struct Stage2Smem {
+  // byte offsets from the 1024-aligned base
+  static constexpr int kA = 0;                               // A: [4][128][64] f16 (MMA layout); hi-plane staging
+  static constexpr int kW = kA + 4 * kSR * 128;              // W: [2][256][64] f16 K blocks; lo-plane staging
+  static constexpr int kP = kW + 2 * kS2C * 128;             // P of two K blocks: [2][182][64] f16, swizzled chunks
+  static constexpr int kCarry = kP + 2 * kSPRows * 128;      // [78][256] f16, plain rows
+  static constexpr int kMisc = kCarry + kSCarryRows * kS2C * 2;  // ints: heads[4], code, pad
+  static constexpr int kBars = ((kMisc + 8 * 4 + 7) / 8) * 8;    // wfull[2], mma_done[2], tmem slot
+  static constexpr int kBytes = kBars + 5 * 8;
+  static constexpr int kAlloc = kBytes + 1024;
+};
+static_assert(Stage2Smem::kAlloc <= 227 * 1024, "one C=256 stage CTA per SM");
+
+__global__ void __launch_bounds__(512, 1) stage256_kernel(const __grid_constant__ StageArgs a) {
+  using L = Stage2Smem;
+  constexpr int C = kS2C;
+  constexpr int kGroups = 512 / 32;  // row groups of the row-parallel phases over two K blocks (32 quads)
+  constexpr uint32_t kWBytes = C * 128;
+  extern __shared__ uint8_t stage2_smem_raw[];
+  uint8_t* sm = stage2_smem_raw + ((1024u - (smem_u32(stage2_smem_raw) & 1023u)) & 1023u);
+  uint8_t* aop = sm + L::kA;
+  uint8_t* wop = sm + L::kW;
+  uint8_t* pbuf = sm + L::kP;
+  uint8_t* carry = sm + L::kCarry;
+  int* misc = reinterpret_cast<int*>(sm + L::kMisc);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBars);
+  uint64_t* wfull = bars;         // [2]
+  uint64_t* mma_done = bars + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t wl = a.wait_limit ? a.wait_limit : kWaitLimit;
+  const int q = tid & 31, rg = tid >> 5;   // channel quad of a K-block pair and row group
+  const int lq = warp & 3, cg = warp >> 2;  // TMEM lane quarter and column group
+  const int row = lq * 32 + lane;           // this thread's tile row in the TMEM phases
+  const int N = a.rows_per_stream;
+  const int tps = (N + kSR - 1) / kSR;
+  const int num_tiles = (a.rows / N) * tps;
+  const int t_begin = (int)((long long)blockIdx.x * num_tiles / gridDim.x);
+  const int t_end = (int)((long long)(blockIdx.x + 1) * num_tiles / gridDim.x);
+  const int t_first = (t_begin < t_end && t_begin % tps != 0) ? t_begin - 1 : t_begin;
+
+  if (tid == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&wfull[b], 1);
+      mbar_init(&mma_done[b], 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  for (int i = tid; i < kSCarryRows * C / 2; i += 512) reinterpret_cast<uint32_t*>(carry)[i] = 0u;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t trow = tmem + ((uint32_t)(lq * 32) << 16);  // this warp's TMEM lanes
+  grid_dependency_sync();
+
+  // Steps: 12 per tile (unit u, K block kb); step g's weights go to buffer g & 1.
+  auto load_w = [&](uint32_t g, int u, int kb) {
+    mbar_arrive_expect_tx(&wfull[g & 1], kWBytes);
+    bulk_g2s(wop + (g & 1) * kWBytes, a.unit[u].wimg + (size_t)kb * kWBytes, kWBytes, &wfull[g & 1]);
+  };
+  auto tile_m0 = [&](int t) { return (t / tps) * N + (t % tps) * kSR; };
+  if (tid == 0 && t_first < t_end) {
+    load_w(0, 0, 0);
+    load_w(1, 0, 1);
+  }
+  uint32_t g = 0;                             // steps taken (counted alike by every thread)
+  int last_load = t_first < t_end ? 1 : -1;   // thread 0: step of the last weight load issued
+  int last_mma = -1;                          // thread 0: step of the last MMA group issued
+  bool ok = true;
+  for (int t = t_first; t < t_end && ok; ++t) {
+    const bool discard = t < t_begin;
+    const int s = t / tps, j = t - s * tps;
+    const int m0 = s * N + j * kSR;
+    const int v = min(kSR, N - j * kSR);
+    const bool first = j == 0, last = !discard && j == tps - 1;
+    if (tid < 4 && (first || last)) {
+      const int code = stage_code(a.state, s);
+      const HistRef& h = tid < 3 ? a.unit[tid].hist : a.hist_next;
+      misc[tid] = (a.state.pool && !(code & 2)) ? head_table(slot_base(a.state, code), code & 1)[h.index] : 0;
+      if (tid == 0) misc[4] = code;
+    }
+    // The previous tile's plane stores have read their staging (A and W);
+    // then the first weights of this tile, and the next tile's rows into L2.
+    if (tid == 0) {
+      bulk_wait_read_all();
+      if (t != t_first) {
+        load_w(g, 0, 0);
+        load_w(g + 1, 0, 1);
+        last_load = (int)g + 1;
+      }
+      if (t + 1 < t_end) {
+        const int m1 = tile_m0(t + 1);
+        prefetch_l2(a.x + (size_t)m1 * C, (uint32_t)(min(kSR, a.rows - m1) * C * 4));
+      }
+    }
+    // y rows into TMEM columns [0, 256): this thread's row, its 64 columns.
+    {
+      const int gr = m0 + row;
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        uint32_t r[16];
+        const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)gr * C + cg * 64 + h * 16);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float4 f = gr < a.rows ? __ldg(src + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+          r[4 * e] = __float_as_uint(f.x);
+          r[4 * e + 1] = __float_as_uint(f.y);
+          r[4 * e + 2] = __float_as_uint(f.z);
+          r[4 * e + 3] = __float_as_uint(f.w);
+        }
+        tmem_st16(trow + (uint32_t)(cg * 64 + h * 16), r);
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const int code = misc[4];
+#pragma unroll 1
+    for (int u = 0; u < 3 && ok; ++u) {
+      const int d = u == 0 ? 1 : u == 1 ? 3 : 9, H = 6 * d;
+      const HistRef& hist = a.unit[u].hist;
+#pragma unroll 1
+      for (int kp = 0; kp < 2; ++kp) {
+        // (a) P = f16 Snake_pre(y) of K blocks 2kp, 2kp + 1, rows [0, 128) (a
+        // thread per row and 32 columns), and the blocks' halo rows [-H, 0).
+        {
+          uint32_t r[32];
+          const int c = kp * 128 + cg * 32;
+          tmem_ld16_async(trow + (uint32_t)c, *reinterpret_cast<uint32_t(*)[16]>(r));
+          tmem_ld16_async(trow + (uint32_t)(c + 16), *reinterpret_cast<uint32_t(*)[16]>(r + 16));
+          tmem_wait_ld(*reinterpret_cast<uint32_t(*)[16]>(r));
+          tmem_wait_ld(*reinterpret_cast<uint32_t(*)[16]>(r + 16));
+          const float* pa = a.unit[u].pre_a + c;
+          const float* pr = a.unit[u].pre_r + c;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float4 y4 = make_float4(__uint_as_float(r[4 * e]), __uint_as_float(r[4 * e + 1]),
+                                          __uint_as_float(r[4 * e + 2]), __uint_as_float(r[4 * e + 3]));
+            *reinterpret_cast<uint2*>(pbuf + p_off(kSPOff + row, cg * 8 + e)) =
+                f16x4(snake4(y4, ldg4(pa + 4 * e), ldg4(pr + 4 * e)));
+          }
+          for (int hr = rg; hr < H; hr += kGroups) {
+            const uint2 val = first ? f16x4(stage_hist_quad(a.state, hist, code, misc[u], hr - H, kp * 32 + q))
+                                    : *reinterpret_cast<const uint2*>(carry + ((scarry_off(u) + hr) * C + kp * 128 + 4 * q) * 2);
+            *reinterpret_cast<uint2*>(pbuf + p_off(kSPOff - H + hr, q)) = val;
+          }
+          tc_fence_before();
+          __syncthreads();
+        }
+        // (b) depthwise + Snake_post of both blocks into their A tiles; their
+        // carried rows or, at a stream's last tile, their new history rows.
+        {
+          const float* uc = a.unit[u].coef + 2 * kp * kCoefResidual * 64;
+          uint8_t* ab = aop + 2 * kp * kSR * 128;
+          if (u == 0) {
+            stage_chains<stage_chain(kGroups, 1), true>(uc, pbuf, ab, rg, q, 1);
+          } else if (u == 1) {
+            stage_chains<stage_chain(kGroups, 3), true>(uc, pbuf, ab, rg, q, 3);
+          } else {
+            stage_chains<stage_chain(kGroups, 9), true>(uc, pbuf, ab, rg, q, 9);
+          }
+          if (!last) {
+            for (int hr = rg; hr < H; hr += kGroups)
+              *reinterpret_cast<uint2*>(carry + ((scarry_off(u) + hr) * C + kp * 128 + 4 * q) * 2) =
+                  *reinterpret_cast<const uint2*>(pbuf + p_off(kSPOff + kSR - H + hr, q));
+          } else if (a.state.pool) {
+            for (int hr = rg; hr < H; hr += kGroups) {
+              const float4 val = f16x4_to_float(*reinterpret_cast<const uint2*>(pbuf + p_off(kSPOff + v - H + hr, q)));
+              *reinterpret_cast<float4*>(hist_new_row(a.state, hist, code, misc[u], N - H + hr, N) + kp * 128 + 4 * q) = val;
+            }
+          }
+          fence_async_smem();
+          tc_fence_before();
+          __syncthreads();
+        }
+        // (c) the two blocks' MMAs into D (M = 128, N = 256, K = 64 each; one
+        // step per block, its weights in buffer step & 1); then the next two
+        // steps' weights, each once its buffer's last reader (the MMAs two
+        // steps earlier) is done.
+        const bool next_in_tile = kp == 0 || u < 2;
+        if (tid == 0) {
+          ok = a.gate == nullptr || g > 0 || flag_wait(a.gate, a.status, kDevTimeoutGate, wl);
+#pragma unroll 1
+          for (int b = 0; b < 2 && ok; ++b) {
+            const uint32_t gs = g + b;
+            const int kb = 2 * kp + b;
+            if (!(ok = mbar_wait(&wfull[gs & 1], (gs >> 1) & 1, a.status, kDevTimeoutLoader, wl))) break;
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(aop + kb * kSR * 128), b0 = smem_u32(wop + (gs & 1) * kWBytes);
+            constexpr uint32_t idesc = instr_desc_f16(0u, C);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              mma_f16(tmem + C, smem_desc_sw128(a0 + ks * 32), smem_desc_sw128(b0 + ks * 32), idesc, (kb | ks) ? 1u : 0u);
+            mma_commit(&mma_done[gs & 1]);
+            last_mma = (int)gs;
+          }
+          if (ok && next_in_tile) {
+            const int nu = kp == 0 ? u : u + 1, nkb = kp == 0 ? 2 : 0;
+#pragma unroll 1
+            for (int b = 0; b < 2 && ok; ++b) {
+              const uint32_t gs = g + 2 + b;  // its buffer's last reader: step gs - 2
+              if (!(ok = mbar_wait(&mma_done[gs & 1], ((gs - 2) >> 1) & 1, a.status, kDevTimeoutMma, wl))) break;
+              load_w(gs, nu, nkb + b);
+              last_load = (int)gs;
+            }
+          }
+        }
+        g += 2;
+        if (!__syncthreads_and(ok)) {
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) break;
+      // Every MMA of the unit has finished (the last commit tracks them all).
+      ok = __syncthreads_and(mbar_wait(&mma_done[(g - 1) & 1], ((g - 1) >> 1) & 1, a.status, kDevTimeoutMma, wl));
+      tc_fence_after();
+      if (!ok) break;
+      // (d) y = y + (D + b) for this thread's row and 64 columns; unit 2 writes
+      // the next conv's planes instead, staged (hi over A, lo over W: both
+      // idle now) for the TMA stores.
+      {
+        const float* pb = a.unit[u].bias;
+#pragma unroll 1
+        for (int h = 0; h < 4; ++h) {
+          const int c = cg * 64 + h * 16;
+          uint32_t ry[16], rd[16];
+          tmem_ld16_async(trow + (uint32_t)c, ry);
+          tmem_ld16_async(trow + (uint32_t)(C + c), rd);
+          tmem_wait_ld(ry);
+          tmem_wait_ld(rd);
+          float y[16];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float4 b = ldg4(pb + c + 4 * e);
+            y[4 * e] = __uint_as_float(ry[4 * e]) + (__uint_as_float(rd[4 * e]) + b.x);
+            y[4 * e + 1] = __uint_as_float(ry[4 * e + 1]) + (__uint_as_float(rd[4 * e + 1]) + b.y);
+            y[4 * e + 2] = __uint_as_float(ry[4 * e + 2]) + (__uint_as_float(rd[4 * e + 2]) + b.z);
+            y[4 * e + 3] = __uint_as_float(ry[4 * e + 3]) + (__uint_as_float(rd[4 * e + 3]) + b.w);
+          }
+          if (u < 2) {
+            uint32_t w[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(y[e]);
+            tmem_st16(trow + (uint32_t)c, w);
+            continue;
+          }
+          uint32_t hi[8], lo[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float4 sc = ldg4(a.next_scale + c + 4 * e), of = ldg4(a.next_offset + c + 4 * e);
+            float4 w4 = make_float4(__fadd_rn(__fmul_rn(y[4 * e], sc.x), of.x), __fadd_rn(__fmul_rn(y[4 * e + 1], sc.y), of.y),
+                                    __fadd_rn(__fmul_rn(y[4 * e + 2], sc.z), of.z),
+                                    __fadd_rn(__fmul_rn(y[4 * e + 3], sc.w), of.w));
+            w4 = snake4(w4, ldg4(a.next_alpha + c + 4 * e), ldg4(a.next_recip + c + 4 * e));
+            split_bf16(w4.x, w4.y, hi[2 * e], lo[2 * e]);
+            split_bf16(w4.z, w4.w, hi[2 * e + 1], lo[2 * e + 1]);
+          }
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int off = (c >> 6) * kSR * 128 + sw128_offset(row, (c & 63) + 8 * e);
+            *reinterpret_cast<uint4*>(aop + off) = make_uint4(hi[4 * e], hi[4 * e + 1], hi[4 * e + 2], hi[4 * e + 3]);
+            *reinterpret_cast<uint4*>(wop + off) = make_uint4(lo[4 * e], lo[4 * e + 1], lo[4 * e + 2], lo[4 * e + 3]);
+          }
+          if (!discard && row < v) {
+            const int gr = m0 + row, tj = j * kSR + row;
+            const size_t plane = (size_t)a.rows * C;
+            const bool have = a.state.pool && !(code & 2);
+            if (tj == 0) {
+              uint4* qh = reinterpret_cast<uint4*>(a.out_planes_prev + (size_t)gr * C + c);
+              uint4* ql = reinterpret_cast<uint4*>(a.out_planes_prev + plane + (size_t)gr * C + c);
+              const uint4* old = have ? reinterpret_cast<const uint4*>(slot_base(a.state, code) + a.hist_next.ring +
+                                                                       misc[3] * a.hist_next.width + c)
+                                      : nullptr;
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const uint4 w0 = old ? __ldg(old + 2 * e) : make_uint4(0u, 0u, 0u, 0u);
+                const uint4 w1 = old ? __ldg(old + 2 * e + 1) : make_uint4(0u, 0u, 0u, 0u);
+                qh[e] = make_uint4(__byte_perm(w0.x, w0.y, 0x7632), __byte_perm(w0.z, w0.w, 0x7632),
+                                   __byte_perm(w1.x, w1.y, 0x7632), __byte_perm(w1.z, w1.w, 0x7632));
+                ql[e] = make_uint4(__byte_perm(w0.x, w0.y, 0x5410), __byte_perm(w0.z, w0.w, 0x5410),
+                                   __byte_perm(w1.x, w1.y, 0x5410), __byte_perm(w1.z, w1.w, 0x5410));
+              }
+            }
+            if (tj == N - 1 && a.state.pool) {
+              uint4* dst = reinterpret_cast<uint4*>(slot_base(a.state, code) + a.hist_next.ring +
+                                                    (misc[3] ^ 1) * a.hist_next.width + c);
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                dst[e] = make_uint4(__byte_perm(lo[2 * e], hi[2 * e], 0x5410), __byte_perm(lo[2 * e], hi[2 * e], 0x7632),
+                                    __byte_perm(lo[2 * e + 1], hi[2 * e + 1], 0x5410),
+                                    __byte_perm(lo[2 * e + 1], hi[2 * e + 1], 0x7632));
+            }
+          }
+        }
+      }
+      if (u == 2) fence_async_smem();  // the staged planes are read by TMA stores
+      tc_fence_before();
+      __syncthreads();
+      tc_fence_after();
+    }
+    if (!ok) break;
+    if (!discard && tid == 0) {
+#pragma unroll
+      for (int kb = 0; kb < 4; ++kb) {
+        tma_store_4d(&a.planes_map, aop + kb * kSR * 128, 64 * kb, j * kSR, s, 0);
+        tma_store_4d(&a.planes_map, wop + kb * kSR * 128, 64 * kb, j * kSR, s, 1);
+        tma_store_4d(&a.prev_map, aop + kb * kSR * 128, 64 * kb, j * kSR + 1, s, 0);
+        tma_store_4d(&a.prev_map, wop + kb * kSR * 128, 64 * kb, j * kSR + 1, s, 1);
+      }
+      bulk_commit();
+    }
+    if (last && a.state.pool && tid == 0) {
+      for (int u = 0; u < 3; ++u) hist_commit_head(a.state, a.unit[u].hist, code, misc[u], N);
+      hist_commit_head(a.state, a.hist_next, code, misc[3], N);
+    }
+  }
+  // After a timeout: let the last weight load and MMA group issued finish
+  // before the CTA frees its TMEM and exits.
+  if (!ok && tid == 0) {
+    // (The two buffers' latest loads: steps last_load and last_load - 1.)
+    for (int l = last_load; l >= 0 && l >= last_load - 1; --l)
+      mbar_wait(&wfull[l & 1], (l >> 1) & 1, a.status, kDevTimeoutLoader);
+    if (last_mma >= 0) mbar_wait(&mma_done[last_mma & 1], (last_mma >> 1) & 1, a.status, kDevTimeoutMma);
+  }
+  if (tid == 0) bulk_wait_all();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
 int g_stage_sms = 0;
 
 }  // namespace
@@ -499,6 +851,8 @@ cudaError_t prepare_stage() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(stage_kernel<128, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              StageSmem<128>::kAlloc);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(stage256_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Stage2Smem::kAlloc);
   return e;
 }
 
@@ -517,6 +871,10 @@ cudaError_t launch_stage(const StageArgs& a, cudaStream_t stream) {
   if (a.channels == 128) {
     const int grid = tiles < g_stage_sms ? tiles : g_stage_sms;
     return launch_overlapped(stage_kernel<128, 512>, grid, 512, StageSmem<128>::kAlloc, stream, a);
+  }
+  if (a.channels == kS2C) {
+    const int grid = tiles < g_stage_sms ? tiles : g_stage_sms;
+    return launch_overlapped(stage256_kernel, grid, 512, Stage2Smem::kAlloc, stream, a);
   }
   return cudaErrorInvalidValue;
 }

@@ -1,15 +1,15 @@
 """The fused kernels against the per-layer kernels on a B200 (``-m gpu``).
 
 A whole step runs stage 5's three residual units and the final conv as one
-kernel, and the three residual units of stages 3 and 4 (128 and 64 channels)
-with the next transposed conv's planes as one kernel each; all of them keep
+kernel, and the three residual units of stages 2, 3 and 4 (256, 128 and 64
+channels) with the next transposed conv's planes as one kernel each; all of them keep
 each 128-row tile and its halo in shared memory. The same step with every
 layer as its own kernel (``fav_debug_step_unfused``) is the check: both
 compute each row with the same depthwise, Snake and f16 projection
 arithmetic, and differ only in the final conv's summation order, so audio
 agrees to 1e-5 and every history window (what the next step reads) to 1e-5
 over consecutive steps with carried state, fresh streams and stream ends at
-every tile position of the stage. The stage 3-4 windows, which no summation
+every tile position of the stage. The stage 2-4 windows, which no summation
 order touches, are equal bit for bit. The cases cover partial last tiles of
 32, 64 and 96 rows, warm-up tiles (CTA ranges that start inside a stream) and
 both launch shapes of the 64-channel kernel.
@@ -82,17 +82,17 @@ def run_steps(lib, plan, entry, latents, chunk_frames):
     return torch.cat(audio, 1).numpy(), pools
 
 
-# Float offsets of the stage 3-4 residual rings inside a slot, and their end
+# Float offsets of the stage 2-4 residual rings inside a slot, and their end
 # (the stage-5 transposed conv's history ring follows): each history of H rows
 # x C channels owns 2H ring rows at twice its reference state offset.
-def _stage34_rings():
+def _stage_rings():
     off = 6 * 64
     spans = []
     for i in range(6):
         cin = 2048 >> i
         off += cin
         for d in (1, 3, 9):
-            if i in (3, 4):
+            if i in (2, 3, 4):
                 spans.append((2 * off, 2 * (off + 6 * d * cin // 2)))
             off += 6 * d * cin // 2
     return spans
@@ -109,7 +109,7 @@ def test_fused_tail_matches_per_layer_kernels(lib, plan, streams, frames, chunk)
         diff = (a - b).abs().view(streams, stride).amax(0)
         bad = torch.nonzero(diff > STATE_TOL).flatten()
         assert bad.numel() == 0, f"slot floats {bad[:4].tolist()}..{bad[-1:].tolist()} differ by {float(diff.max())}"
-        for lo, hi in _stage34_rings():
+        for lo, hi in _stage_rings():
             sa = a.view(streams, stride)[:, lo:hi]
             sb = b.view(streams, stride)[:, lo:hi]
             assert torch.equal(sa, sb), (lo, hi)
