@@ -505,7 +505,11 @@ struct Stage2Smem {
   static constexpr int kW = kA + 4 * kSR * 128;              // W: [2][256][64] f16 K blocks; lo-plane staging
   static constexpr int kP = kW + 2 * kS2C * 128;             // P of two K blocks: [2][182][64] f16, swizzled chunks
   static constexpr int kCarry = kP + 2 * kSPRows * 128;      // [78][256] f16, plain rows
-  static constexpr int kMisc = kCarry + kSCarryRows * kS2C * 2;  // ints: heads[4], code, pad
+  // The current K-block pair's coefficients: depthwise [2][w0..w6, bias,
+  // alpha2, recip2][64], then Snake_pre alpha and reciprocal [128] each.
+  static constexpr int kRC = kCarry + kSCarryRows * kS2C * 2;
+  static constexpr int kRCFloats = 2 * kCoefResidual * 64 + 2 * 128;
+  static constexpr int kMisc = kRC + kRCFloats * 4;          // ints: heads[4], code, pad
   static constexpr int kBars = ((kMisc + 8 * 4 + 7) / 8) * 8;    // wfull[2], mma_done[2], tmem slot
   static constexpr int kBytes = kBars + 5 * 8;
   static constexpr int kAlloc = kBytes + 1024;
@@ -528,6 +532,11 @@ __global__ void __launch_bounds__(512, 1) stage256_kernel(const __grid_constant_
   uint64_t* wfull = bars;         // [2]
   uint64_t* mma_done = bars + 2;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+  float* rc = reinterpret_cast<float*>(sm + L::kRC);
+  // A unit's epilogue coefficients (bias; unit 2: the next stage's affine and
+  // Snake), [5][256], kept in P while P is idle (after the unit's last
+  // depthwise phase, until the next unit's first Snake_pre phase).
+  float* ec = reinterpret_cast<float*>(pbuf);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t wl = a.wait_limit ? a.wait_limit : kWaitLimit;
@@ -553,6 +562,24 @@ __global__ void __launch_bounds__(512, 1) stage256_kernel(const __grid_constant_
     tmem_relinquish();
   }
   for (int i = tid; i < kSCarryRows * C / 2; i += 512) reinterpret_cast<uint32_t*>(carry)[i] = 0u;
+  // Coefficients of K-block pair kp of unit u into rc (plan constants).
+  auto load_round_coefs = [&](int u, int kp) {
+    const float* src = a.unit[u].coef + 2 * kp * kCoefResidual * 64;
+    for (int i = tid; i < 2 * kCoefResidual * 16; i += 512) reinterpret_cast<float4*>(rc)[i] = ldg4(src + 4 * i);
+    if (tid < 32) {
+      reinterpret_cast<float4*>(rc + 2 * kCoefResidual * 64)[tid] = ldg4(a.unit[u].pre_a + kp * 128 + 4 * tid);
+      reinterpret_cast<float4*>(rc + 2 * kCoefResidual * 64 + 128)[tid] = ldg4(a.unit[u].pre_r + kp * 128 + 4 * tid);
+    }
+  };
+  auto load_epi_coefs = [&](int u) {
+    if (tid < 64) reinterpret_cast<float4*>(ec)[tid] = ldg4(a.unit[u].bias + 4 * tid);
+    if (u == 2 && tid < 256) {
+      const int k = tid >> 6, i = tid & 63;
+      const float* src = k == 0 ? a.next_scale : k == 1 ? a.next_offset : k == 2 ? a.next_alpha : a.next_recip;
+      reinterpret_cast<float4*>(ec + 256 * (k + 1))[i] = ldg4(src + 4 * i);
+    }
+  };
+  load_round_coefs(0, 0);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -637,14 +664,14 @@ __global__ void __launch_bounds__(512, 1) stage256_kernel(const __grid_constant_
           tmem_ld16_async(trow + (uint32_t)(c + 16), *reinterpret_cast<uint32_t(*)[16]>(r + 16));
           tmem_wait_ld(*reinterpret_cast<uint32_t(*)[16]>(r));
           tmem_wait_ld(*reinterpret_cast<uint32_t(*)[16]>(r + 16));
-          const float* pa = a.unit[u].pre_a + c;
-          const float* pr = a.unit[u].pre_r + c;
+          const float* pa = rc + 2 * kCoefResidual * 64 + cg * 32;
+          const float* pr = pa + 128;
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const float4 y4 = make_float4(__uint_as_float(r[4 * e]), __uint_as_float(r[4 * e + 1]),
                                           __uint_as_float(r[4 * e + 2]), __uint_as_float(r[4 * e + 3]));
             *reinterpret_cast<uint2*>(pbuf + p_off(kSPOff + row, cg * 8 + e)) =
-                f16x4(snake4(y4, ldg4(pa + 4 * e), ldg4(pr + 4 * e)));
+                f16x4(snake4(y4, lds4(pa + 4 * e), lds4(pr + 4 * e)));
           }
           for (int hr = rg; hr < H; hr += kGroups) {
             const uint2 val = first ? f16x4(stage_hist_quad(a.state, hist, code, misc[u], hr - H, kp * 32 + q))
@@ -657,14 +684,14 @@ __global__ void __launch_bounds__(512, 1) stage256_kernel(const __grid_constant_
         // (b) depthwise + Snake_post of both blocks into their A tiles; their
         // carried rows or, at a stream's last tile, their new history rows.
         {
-          const float* uc = a.unit[u].coef + 2 * kp * kCoefResidual * 64;
+          const float* uc = rc;
           uint8_t* ab = aop + 2 * kp * kSR * 128;
           if (u == 0) {
-            stage_chains<stage_chain(kGroups, 1), true>(uc, pbuf, ab, rg, q, 1);
+            stage_chains<stage_chain(kGroups, 1)>(uc, pbuf, ab, rg, q, 1);
           } else if (u == 1) {
-            stage_chains<stage_chain(kGroups, 3), true>(uc, pbuf, ab, rg, q, 3);
+            stage_chains<stage_chain(kGroups, 3)>(uc, pbuf, ab, rg, q, 3);
           } else {
-            stage_chains<stage_chain(kGroups, 9), true>(uc, pbuf, ab, rg, q, 9);
+            stage_chains<stage_chain(kGroups, 9)>(uc, pbuf, ab, rg, q, 9);
           }
           if (!last) {
             for (int hr = rg; hr < H; hr += kGroups)
@@ -713,6 +740,11 @@ __global__ void __launch_bounds__(512, 1) stage256_kernel(const __grid_constant_
           }
         }
         g += 2;
+        // Every thread is past this pair's depthwise phase: the next pair's
+        // coefficients go into rc and, after the unit's last pair, its
+        // epilogue coefficients into P (both published by the barrier below).
+        load_round_coefs(kp == 0 ? u : u < 2 ? u + 1 : 0, kp ^ 1);
+        if (kp == 1) load_epi_coefs(u);
         if (!__syncthreads_and(ok)) {
           ok = false;
           break;
@@ -727,7 +759,7 @@ __global__ void __launch_bounds__(512, 1) stage256_kernel(const __grid_constant_
       // the next conv's planes instead, staged (hi over A, lo over W: both
       // idle now) for the TMA stores.
       {
-        const float* pb = a.unit[u].bias;
+        const float* pb = ec;
 #pragma unroll 1
         for (int h = 0; h < 4; ++h) {
           const int c = cg * 64 + h * 16;
@@ -739,7 +771,7 @@ __global__ void __launch_bounds__(512, 1) stage256_kernel(const __grid_constant_
           float y[16];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float4 b = ldg4(pb + c + 4 * e);
+            const float4 b = lds4(pb + c + 4 * e);
             y[4 * e] = __uint_as_float(ry[4 * e]) + (__uint_as_float(rd[4 * e]) + b.x);
             y[4 * e + 1] = __uint_as_float(ry[4 * e + 1]) + (__uint_as_float(rd[4 * e + 1]) + b.y);
             y[4 * e + 2] = __uint_as_float(ry[4 * e + 2]) + (__uint_as_float(rd[4 * e + 2]) + b.z);
@@ -755,11 +787,11 @@ __global__ void __launch_bounds__(512, 1) stage256_kernel(const __grid_constant_
           uint32_t hi[8], lo[8];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float4 sc = ldg4(a.next_scale + c + 4 * e), of = ldg4(a.next_offset + c + 4 * e);
+            const float4 sc = lds4(ec + 256 + c + 4 * e), of = lds4(ec + 512 + c + 4 * e);
             float4 w4 = make_float4(__fadd_rn(__fmul_rn(y[4 * e], sc.x), of.x), __fadd_rn(__fmul_rn(y[4 * e + 1], sc.y), of.y),
                                     __fadd_rn(__fmul_rn(y[4 * e + 2], sc.z), of.z),
                                     __fadd_rn(__fmul_rn(y[4 * e + 3], sc.w), of.w));
-            w4 = snake4(w4, ldg4(a.next_alpha + c + 4 * e), ldg4(a.next_recip + c + 4 * e));
+            w4 = snake4(w4, lds4(ec + 768 + c + 4 * e), lds4(ec + 1024 + c + 4 * e));
             split_bf16(w4.x, w4.y, hi[2 * e], lo[2 * e]);
             split_bf16(w4.z, w4.w, hi[2 * e + 1], lo[2 * e + 1]);
           }
