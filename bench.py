@@ -5,7 +5,7 @@ Workloads (``--workload``; the default is what the headline line reports):
   stream40ms  every GPU decodes 512 independent streams (the per-GPU shard of
               cfg5's 4096 streams on 8 GPUs) on 1-frame (40 ms, 1920-sample)
               chunks with carried history, bf16 plan. One step = one chunk for
-              all 512 streams (25 kernel launches). Weak scaling.
+              all 512 streams (23 kernel launches). Weak scaling.
   cfg3        256 streams x 2-frame (80 ms) chunks per step, bf16. Weak scaling.
   int8        stream40ms's shape on the int8 (W8A8) plan (cfg5's precision).
   cfg1        batch decode of one clip [1,64,25] (1 s of audio) per step.
@@ -69,8 +69,8 @@ TRAFFIC_FILE = ROOT / "bench_traffic.json"
 
 def fused_stage(i, precision=0):
     """Stages whose three residual units and the next conv's planes run as one
-    fused kernel: 3 and 4 (bf16 units), stage 4 only in the int8 plan."""
-    return i == 4 or (i == 3 and precision == 0)
+    fused kernel: 2, 3 and 4 (bf16 units), stage 4 only in the int8 plan."""
+    return i == 4 or (i in (2, 3) and precision == 0)
 
 
 def kernel_names(precision=0):
@@ -148,13 +148,12 @@ def layer_costs(precision=0):
 
     Layout (bf16 plan): a transposed conv reads its input as split-bf16 planes
     (hi + lo, 4 B per element) twice (as they are, and one time step later for
-    its second tap) and writes y in fp32 (plus Snake_pre(y) at stages 0-2,
-    whose units read it); the residual units of stage 2 read y and write y (the
-    last unit the next conv's two plane copies); stages 0-1's units read
-    Snake_pre(y), write their f16 operand once and read it back. A fused stage
-    (3-4) reads its input y once and writes the next conv's two plane copies;
-    the fused stage-5 tail reads its input once and writes audio; their
-    intermediates stay on chip.
+    its second tap) and writes y in fp32 (plus Snake_pre(y) at stages 0-1,
+    whose units read it); stages 0-1's units read Snake_pre(y), write their
+    f16 operand once and read it back. A fused stage (2-4) reads its input y
+    once and writes the next conv's two plane copies; the fused stage-5 tail
+    reads its input once and writes audio; their intermediates stay on chip.
+    (The int8 plan's stages 2-3 run their units as per-layer launches.)
 
     CUDA-core work per element of a residual unit: two Snakes (4 FP32 + 1 sine
     each), the depthwise k=7 tap chain with its bias (8) and the skip/bias add
@@ -167,7 +166,7 @@ def layer_costs(precision=0):
     cin = 2048
     for i, s in enumerate(RATES):
         cout = cin // 2
-        y_only = i == 5 or fused_stage(i, precision) or (precision == 0 and i == 2)
+        y_only = i == 5 or fused_stage(i, precision)
         out_elems = n * s * cout
         out.append(dict(flops=2 * cin * cout * 2 * s * n, act=n * cin * 8 + out_elems * (4 if y_only else 8),
                         weights=cin * cout * 2 * s * 4, hist=0,
@@ -766,17 +765,15 @@ def base_line(args, wl, world, K, Wm, dev_s, audio_s, scaling):
 LAUNCH_ORDER = (["stem"]
                 + [x for i in (0, 1) for x in [f"stage{i}.transpose"]
                    + [y for j in range(3) for y in (f"stage{i}.res{j}", f"stage{i}.res{j}")]]
-                + ["stage2.transpose"] + [f"stage2.res{j}" for j in range(3)]
-                + [x for i in (3, 4) for x in (f"stage{i}.transpose", f"stage{i}.units")]
+                + [x for i in (2, 3, 4) for x in (f"stage{i}.transpose", f"stage{i}.units")]
                 + ["stage5.transpose", "stage5.tail"])
 
 
 def ingest_ncu(path):
     """bench_traffic.json from an ncu launch list (csv) of one default step: the
     launches in order (stem, per stage 0-1 a conv and each unit's depthwise
-    pre-pass + GEMM, stage 2's conv and three units, per stage 3-4 a conv and
-    the fused stage, stage 5's conv and tail), DRAM bytes per kernel (a unit's
-    two launches summed)."""
+    pre-pass + GEMM, per stage 2-4 a conv and the fused stage, stage 5's conv
+    and tail), DRAM bytes per kernel (a unit's two launches summed)."""
     rows = {}
     with open(path) as f:
         lines = [l for l in f if l.startswith('"')]

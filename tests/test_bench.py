@@ -12,14 +12,14 @@ def test_layer_costs_sum_to_the_step_contraction():
     32 -> 1 conv runs on CUDA cores and is not counted)."""
     for precision in (0, 1):
         costs = bench.layer_costs(precision)
-        assert len(costs) == len(bench.kernel_names(precision)) == (19 if precision == 0 else 21)
+        assert len(costs) == len(bench.kernel_names(precision)) == (17 if precision == 0 else 21)
         assert sum(c["flops"] for c in costs) == bench.FLOPS_PER_FRAME
 
 
 def test_launch_order_is_one_default_step():
-    # stem; stages 0-1: conv + 3 x (depthwise pre-pass, GEMM); stage 2: conv + 3 units;
-    # stages 3-4: conv + fused stage; stage 5: conv + tail
-    assert len(bench.LAUNCH_ORDER) == 1 + 2 * 7 + 4 + 2 * 2 + 2 == 25
+    # stem; stages 0-1: conv + 3 x (depthwise pre-pass, GEMM); stages 2-4: conv + fused stage;
+    # stage 5: conv + tail
+    assert len(bench.LAUNCH_ORDER) == 1 + 2 * 7 + 3 * 2 + 2 == 23
     assert set(bench.LAUNCH_ORDER) == set(bench.kernel_names(0))
 
 
@@ -44,7 +44,7 @@ def test_tensor_roofline_fraction():
 
 def test_roofline_names_the_binding_pipe():
     pk = {"hbm_gbs": 6000.0, "tflops": 1400.0, "sm_mhz": 1965.0, "source": "test"}
-    layer_ms = [0.1] * 18 + [0.5]  # the tail dominates
+    layer_ms = [0.1] * 16 + [0.5]  # the tail dominates
     r = bench.roofline(layer_ms, 512, 512, pk, "stream40ms", 1, 0)
     assert r["kernel"] == "stage5.tail" and r["bound"] in ("hbm", "tensor")
     assert r["binding"] == "cuda_core"
