@@ -477,6 +477,15 @@ int32_t run_step(const fav_plan* p, const fav::StateRef& state, int n_streams, i
     if (!fuse || i + 1 >= fav::kStages || last_layer <= 4 * i + 4) return false;
     const StageDev& st = p->stages[i];
     if (st.c_out != 64 && st.c_out != 128 && st.c_out != 256) return false;
+    if (st.c_out == 256) {
+      // Stage 2's fused kernel walks a stream's tiles one after another (a
+      // one-frame stream has two, the second after a warm-up tile); with
+      // fewer tiles than SMs (a step of few streams, latency-bound) the
+      // per-layer kernels, which run every tile at once, finish sooner.
+      int rows = frames;
+      for (int k = 0; k <= i; ++k) rows *= fav::kRates[k];
+      if ((long long)n_streams * ((rows + fav::kTileM - 1) / fav::kTileM) < fav::stage_sm_count()) return false;
+    }
     for (int j = 0; j < 3; ++j)
       if (st.res[j].int8) return false;
     return !p->stages[i + 1].int8;

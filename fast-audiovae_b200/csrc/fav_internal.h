@@ -250,6 +250,7 @@ struct StageArgs {
 };
 cudaError_t launch_stage(const StageArgs& a, cudaStream_t stream);
 cudaError_t prepare_stage();
+int stage_sm_count();  // SMs of the device prepare_stage ran on
 
 // Depthwise pre-pass of a residual unit (fav_prepass.cu): A = Snake_post(
 // depthwise_k7(s)) as f16 [rows][channels] for a kResidualPre GEMM, plus the

@@ -888,6 +888,8 @@ cudaError_t prepare_stage() {
   return e;
 }
 
+int stage_sm_count() { return g_stage_sms; }
+
 cudaError_t launch_stage(const StageArgs& a, cudaStream_t stream) {
   if (a.rows <= 0) return cudaSuccess;
   const int N = a.rows_per_stream;
