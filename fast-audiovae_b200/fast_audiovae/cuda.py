@@ -188,6 +188,9 @@ class DeviceBackend:
         self.graphs_enabled = graphs
         self.graphs = {}
         self.graph_seen = set()
+        # (streams, frames, lent buffer) -> (staging view, graph, status view):
+        # replayed without rebuilding the step's arguments.
+        self.fast = {}
 
     @property
     def plan_bytes(self):
@@ -201,6 +204,7 @@ class DeviceBackend:
             t = (torch.empty(numel, dtype=dtype, pin_memory=True) if pinned
                  else torch.empty(numel, dtype=dtype, device=self.device))
             self.cache[key] = t
+            self.fast = {}  # replay entries point into the buffers they were captured with
         return t[:numel].view(*shape)
 
     @staticmethod
@@ -267,35 +271,69 @@ class DeviceBackend:
             return host.numpy().copy()
         return self.out_buffers.lend(lent, host.numpy())
 
+    def _stage_latents(self, hn, arrays, n, count, frames):
+        """Latents into the staging buffer (unless the caller stacked them there)."""
+        if not (isinstance(arrays, np.ndarray) and arrays.ctypes.data == hn.ctypes.data):
+            view = hn[:count].reshape(n, 64, frames)
+            if isinstance(arrays, np.ndarray):
+                view[...] = arrays
+            else:
+                for i, a in enumerate(arrays):
+                    view[i] = a[0]
+
+    def _check_status(self, status, lent):
+        if status:
+            if lent is not None:
+                self.out_buffers.release(lent)
+            if status == NONFINITE_STATUS:
+                raise RuntimeError("CUDA model returned nonfinite audio")
+            raise RuntimeError("CUDA decoder kernel reported status 0x%x" % status)
+
+    def _replay(self, fast, lent, codes, arrays, n, frames):
+        """A step whose graph (upload, kernels, status download) exists for
+        these streams, frames and lent output buffer: stage, replay, read."""
+        hn, graph, status_np = fast
+        count = n * 64 * frames
+        self._stage_latents(hn, arrays, n, count, frames)
+        hn[count:count + n].view(np.int32)[:] = codes
+        hn[count + n:].view(np.int32)[:] = 0
+        torch = self.torch
+        try:
+            with torch.cuda.device(self.device):
+                graph.replay()
+                torch.cuda.current_stream(self.device).synchronize()
+        except BaseException:
+            self.out_buffers.release(lent)
+            raise
+        self._check_status(int(status_np[0]), lent)
+        return self.out_buffers.lend(lent, lent[:n * HOP * frames].view(n, HOP * frames).numpy())
+
     def step(self, codes, arrays, frames):
         from ._native import check
         torch, lib = self.torch, self.lib
         n = len(arrays)
         count = n * 64 * frames
+        shape = (n, HOP * frames)
+        # The kernels write the audio straight into a lent pinned buffer when
+        # it has a device address (no device-to-host copy after the step);
+        # otherwise into device memory, downloaded afterwards.
+        lent = self.out_buffers.acquire(n * HOP * frames)
+        if lent is not None:
+            fast = self.fast.get((n, frames, lent.data_ptr()))
+            if fast is not None:
+                return self._replay(fast, lent, codes, arrays, n, frames)
         with torch.cuda.device(self.device):
             # Latents (already in the staging buffer when the caller stacked
             # them there), slot codes and a zero status word: one upload.
             host = self._buffer("stage_host", (count + n + 1,), torch.float32, pinned=True)
             hn = host.numpy()
-            if not (isinstance(arrays, np.ndarray) and arrays.ctypes.data == hn.ctypes.data):
-                view = hn[:count].reshape(n, 64, frames)
-                if isinstance(arrays, np.ndarray):
-                    view[...] = arrays
-                else:
-                    for i, a in enumerate(arrays):
-                        view[i] = a[0]
+            self._stage_latents(hn, arrays, n, count, frames)
             hn[count:count + n].view(np.int32)[:] = codes
             hn[count + n:].view(np.int32)[:] = 0
             block = self._buffer("stage_dev", (count + n + 1,), torch.float32)
-            block.copy_(host, non_blocking=True)
             z = block[:count]
             codes_dev = block[count:count + n]
             status = block[count + n:]
-            # The kernels write the audio straight into a lent pinned buffer
-            # when it has a device address (no device-to-host copy after the
-            # step); otherwise into device memory, downloaded afterwards.
-            shape = (n, HOP * frames)
-            lent = self.out_buffers.acquire(n * HOP * frames)
             target = self._mapped(lent) if lent is not None else None
             if target is None:
                 if lent is not None:
@@ -309,27 +347,43 @@ class DeviceBackend:
                     self._ptr(z), ct.c_void_p(target), self._ptr(ws), ws_bytes, self._ptr(status))
             key = (n, frames, z.data_ptr(), target, codes_dev.data_ptr(), ws.data_ptr())
             try:
-                graph = self.graphs.get(key) if self.graphs_enabled else None
-                if graph is None and self.graphs_enabled and key in self.graph_seen:
+                entry = self.graphs.get(key) if self.graphs_enabled else None
+                if entry is None and self.graphs_enabled and key in self.graph_seen:
+                    # The second step of a shape captures the upload, the
+                    # kernels and the status download as one graph.
                     side = torch.cuda.Stream(self.device)
                     side.wait_stream(torch.cuda.current_stream(self.device))
                     graph = torch.cuda.CUDAGraph()
+                    status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
                     with torch.cuda.graph(graph, stream=side):
+                        block.copy_(host, non_blocking=True)
                         check(lib, lib.fav_step(*args, ct.c_void_p(side.cuda_stream)))
+                        status_host.copy_(status.view(torch.int32), non_blocking=True)
                     torch.cuda.current_stream(self.device).wait_stream(side)
-                    self.graphs[key] = graph
-                if graph is not None:
-                    graph.replay()
+                    entry = self.graphs[key] = (graph, status_host)
+                    if lent is not None:
+                        self.fast[(n, frames, lent.data_ptr())] = (hn, graph, status_host.numpy())
+                if entry is not None:
+                    entry[0].replay()
+                    torch.cuda.current_stream(self.device).synchronize()
+                    step_status = int(entry[1].item())
                 else:
                     self.graph_seen.add(key)
+                    block.copy_(host, non_blocking=True)
                     check(lib, lib.fav_step(*args, self._stream()))
+                    step_status = None
             except BaseException:
                 if lent is not None:
                     self.out_buffers.release(lent)
                 raise
             if lent is None:
+                if step_status is not None:
+                    self._check_status(step_status, None)
                 return self._download(audio, status)
-            self._finish(lent, status)
+            if step_status is None:
+                self._finish(lent, status)
+            else:
+                self._check_status(step_status, lent)
             return self.out_buffers.lend(lent, lent[:n * HOP * frames].view(*shape).numpy())
 
     def decode_many(self, arrays, frames):
@@ -349,6 +403,7 @@ class DeviceBackend:
 
     def close(self):
         self.graphs = {}
+        self.fast = {}
         if getattr(self, "plan", None) is not None:
             self.plan.close()
 
