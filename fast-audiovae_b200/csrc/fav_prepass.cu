@@ -125,8 +125,11 @@ __global__ void __launch_bounds__(kDwThreads) quantize_kernel(const __grid_const
 // product and sum rounded, the fixed-order sine), as the engine's producers
 // did; the s8 values and scales are the recipe's round-half-to-even
 // quantisation. History taps, the new window rows and the heads as in
-// depthwise_kernel.
-__global__ void __launch_bounds__(kDwThreads) quantize_residual_kernel(const __grid_constant__ QuantResidualArgs a) {
+// depthwise_kernel. Four blocks per SM (64 registers, a few spilled): the
+// fixed-order arithmetic is a long dependent chain per element, and twice
+// the resident warps of the unconstrained build hide more of its latency
+// (int8 step 4.93 -> 4.35 ms).
+__global__ void __launch_bounds__(kDwThreads, 4) quantize_residual_kernel(const __grid_constant__ QuantResidualArgs a) {
   __shared__ float part[kDwThreads / 32];
   grid_dependency_sync();
   const int C = a.channels, quads = C / 4;
