@@ -222,7 +222,8 @@ FAV_API int32_t fav_debug_step_unfused(const fav_plan *plan, float *state_pool, 
  * (0 = stem, 1+4i = stage i transposed conv, 2+4i+j = stage i residual unit j;
  * at most 21) gives up every mbarrier wait after `wait_limit` polls and whose
  * MMA issuer first waits for the device flag `gate` to become nonzero (a
- * residual unit of stages 3-4 names that stage's fused kernel). With a
+ * residual unit of a stage that the step runs as one fused kernel names that
+ * kernel). With a
  * gate that nothing sets, every role of that launch runs out of its waits: the
  * kernel drains the copies and MMAs it started, records a timeout code
  * (0x101-0x104, 0x107) in `status` (required here) and returns; the later

@@ -105,9 +105,11 @@ def committed_windows(pool, read_table=0):
 @pytest.mark.parametrize("layer", [0, 1, 2, 9, 10, 14, 20])
 def test_gated_launch_times_out_and_history_survives(lib, plan, layer):
     """Layer 0 = stem, 1 = stage 0 transposed conv, 2 = stage 0 residual unit
-    (preformed operand), 9 = stage 2 transposed conv, 10 / 14 / 20 = residual
-    units of stages 2 / 3 / 4, which run as the fused stage kernels (their
-    first MMA waits for the gate; stage 4's writes stage 5's planes)."""
+    (preformed operand), 9 = stage 2 transposed conv, 10 = a stage 2 residual
+    unit (per-layer launch: a four-stream step has fewer stage-2 tiles than
+    SMs), 14 / 20 = residual units of stages 3 / 4, which run as the fused
+    stage kernels (their first MMA waits for the gate; stage 4's writes stage
+    5's planes)."""
     gate = torch.zeros(1, dtype=torch.int32, device="cuda")  # nothing ever sets it
     failing, clean = Run(lib, plan), Run(lib, plan)
     for _ in range(2):
