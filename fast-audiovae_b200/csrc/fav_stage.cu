@@ -443,6 +443,12 @@ __global__ void __launch_bounds__(kThreads, 512 / kThreads) stage_kernel(const _
         }
       }
       if (u < 2) fill_halo(u + 1);
+      // The stream's advanced heads, before the barrier that ends the tile:
+      // after it, threads 1-3 may already write the next tile's heads into misc.
+      if (u == 2 && last && a.state.pool && tid == 0) {
+        for (int v2 = 0; v2 < 3; ++v2) hist_commit_head(a.state, a.unit[v2].hist, code, misc[v2], N);
+        hist_commit_head(a.state, a.hist_next, code, misc[3], N);
+      }
       // X was written in place (units 0-1) and the next tile's TMA box goes
       // over it; the staged planes are read by TMA stores: order those
       // generic writes before the async proxy's accesses.
@@ -468,10 +474,6 @@ __global__ void __launch_bounds__(kThreads, 512 / kThreads) stage_kernel(const _
     if (t + 1 < t_end) {
       if (tid == 0) load_x(tile_m0(t + 1));
       ++loads;
-    }
-    if (last && a.state.pool && tid == 0) {
-      for (int u = 0; u < 3; ++u) hist_commit_head(a.state, a.unit[u].hist, code, misc[u], N);
-      hist_commit_head(a.state, a.hist_next, code, misc[3], N);
     }
   }
   // After a timeout: let the last loads and MMA group issued finish before the
@@ -833,6 +835,12 @@ __global__ void __launch_bounds__(512, 1) stage256_kernel(const __grid_constant_
           }
         }
       }
+      // The stream's advanced heads, before the barrier that ends the tile:
+      // after it, threads 1-3 may already write the next tile's heads into misc.
+      if (u == 2 && last && a.state.pool && tid == 0) {
+        for (int v2 = 0; v2 < 3; ++v2) hist_commit_head(a.state, a.unit[v2].hist, code, misc[v2], N);
+        hist_commit_head(a.state, a.hist_next, code, misc[3], N);
+      }
       if (u == 2) fence_async_smem();  // the staged planes are read by TMA stores
       tc_fence_before();
       __syncthreads();
@@ -848,10 +856,6 @@ __global__ void __launch_bounds__(512, 1) stage256_kernel(const __grid_constant_
         tma_store_4d(&a.prev_map, wop + kb * kSR * 128, 64 * kb, j * kSR + 1, s, 1);
       }
       bulk_commit();
-    }
-    if (last && a.state.pool && tid == 0) {
-      for (int u = 0; u < 3; ++u) hist_commit_head(a.state, a.unit[u].hist, code, misc[u], N);
-      hist_commit_head(a.state, a.hist_next, code, misc[3], N);
     }
   }
   // After a timeout: let the last weight load and MMA group issued finish
