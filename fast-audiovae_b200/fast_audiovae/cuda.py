@@ -345,7 +345,9 @@ class DeviceBackend:
             ws = self._buffer("workspace", (ws_bytes,), torch.uint8)
             args = (self.plan.handle, self._ptr(self.pool), self.max_streams, self._ptr(codes_dev), n, frames,
                     self._ptr(z), ct.c_void_p(target), self._ptr(ws), ws_bytes, self._ptr(status))
-            key = (n, frames, z.data_ptr(), target, codes_dev.data_ptr(), ws.data_ptr())
+            # Every buffer the graph reads or writes is part of its key (the
+            # pinned staging buffer too: the graph's upload reads it).
+            key = (n, frames, host.data_ptr(), z.data_ptr(), target, codes_dev.data_ptr(), ws.data_ptr())
             try:
                 entry = self.graphs.get(key) if self.graphs_enabled else None
                 if entry is None and self.graphs_enabled and key in self.graph_seen:
