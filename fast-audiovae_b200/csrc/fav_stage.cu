@@ -129,9 +129,7 @@ __host__ __device__ constexpr int stage_chain(int groups, int d) {
 // operand, A row i from P rows kSPOff - 6d + i + j*d (j = 0..6), for this
 // thread's chain of L rows i0, i0 + d, ... in channel quad q: blocks of L*d
 // rows split into d chains of L, so the seven taps slide through registers.
-// GLOBAL: the coefficients are read from global memory (L1-cached) instead of
-// shared memory.
-template <int L, bool GLOBAL = false>
+template <int L>
 __device__ __forceinline__ void stage_chains(const float* ucoef, const uint8_t* pbuf, uint8_t* aop, int rg, int q,
                                              int d) {
   const int i0 = (rg / d) * L * d + rg % d;
@@ -140,11 +138,10 @@ __device__ __forceinline__ void stage_chains(const float* ucoef, const uint8_t* 
   const float* uc = ucoef + kb * kCoefResidual * 64 + 4 * qb;
   uint8_t* ab = aop + kb * kSR * 128;
   const int base = kSPOff - 6 * d;
-  auto ld = [](const float* p) { return GLOBAL ? ldg4(p) : lds4(p); };
   float4 w[7], win[7];
 #pragma unroll
-  for (int j = 0; j < 7; ++j) w[j] = ld(uc + j * 64);
-  const float4 bias = ld(uc + 7 * 64), al2 = ld(uc + 8 * 64), rc2 = ld(uc + 9 * 64);
+  for (int j = 0; j < 7; ++j) w[j] = lds4(uc + j * 64);
+  const float4 bias = lds4(uc + 7 * 64), al2 = lds4(uc + 8 * 64), rc2 = lds4(uc + 9 * 64);
 #pragma unroll
   for (int j = 0; j < 6; ++j) win[j] = p_load(pbuf, base + i0 + j * d, q);
 #pragma unroll
